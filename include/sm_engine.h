@@ -1,0 +1,233 @@
+/*
+ * siliceo-motor B200 decode engine — C ABI.
+ *
+ * Drop-in boundary for the qwen2/llama decode path of PROGETTO-SILICEO/
+ * siliceo-motor. Each group below names the reference interface it replaces
+ * (paths relative to the reference repository). All functions return an
+ * sm_status (0 = ok); on error, sm_last_error() gives a message for the
+ * calling thread. Nothing aborts or throws across this boundary. Pointers
+ * named *_dev are CUDA device pointers; everything else is host memory.
+ */
+#ifndef SM_ENGINE_H
+#define SM_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SM_OK = 0,
+  SM_ERR_ARG = 1,         /* invalid argument */
+  SM_ERR_IO = 2,          /* file could not be read or written */
+  SM_ERR_FORMAT = 3,      /* malformed GGUF / missing tensor or key */
+  SM_ERR_UNSUPPORTED = 4, /* architecture, type or shape not supported */
+  SM_ERR_CUDA = 5,        /* CUDA runtime error (message has the CUDA text) */
+  SM_ERR_OOM = 6,         /* device or host allocation failed */
+  SM_ERR_CAPACITY = 7,    /* sequence would exceed the cache capacity */
+  SM_ERR_STATE = 8        /* operation not valid for the object's state */
+} sm_status;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* sm_last_error(void);
+/* ABI version: increments on any incompatible change. */
+int sm_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Model. Replaces `s_models::qwen2::Model` / `s_backend_cuda::model::GpuQwen2`
+ * as the `impl Device` for qwen2/llama (crates/s-models/src/device.rs:20-34,
+ * crates/s-models/src/qwen2.rs:99-150, crates/s-backend-cuda/src/model.rs:146-211).
+ * Quantized weights stay quantized in HBM.
+ * ---------------------------------------------------------------------- */
+typedef struct sm_model sm_model;
+typedef struct sm_cache sm_cache;
+
+/* Mirrors qwen2::Config (crates/s-models/src/qwen2.rs:16-26). */
+typedef struct {
+  uint64_t n_layers, n_embd, n_ff, n_heads, n_kv_heads, head_dim;
+  float rope_theta, rms_eps;
+  uint64_t vocab_size;
+} sm_config;
+
+typedef struct {
+  int32_t device;        /* CUDA device ordinal */
+  uint32_t max_batch;    /* largest decode batch (default 32) */
+  uint32_t max_context;  /* largest position + 1 any cache may reach (default 32768) */
+  uint32_t tp_rank;      /* reserved: tensor-parallel rank (0) */
+  uint32_t tp_size;      /* reserved: tensor-parallel size (0 or 1) */
+} sm_load_opts;
+
+/* Model::load / GpuQwen2::load. opts may be NULL (defaults). */
+int sm_model_load(const char* gguf_path, const sm_load_opts* opts, sm_model** out);
+/* Same, from a GGUF image in host memory (the buffer may be freed after). */
+int sm_model_load_memory(const void* gguf, uint64_t len, const sm_load_opts* opts, sm_model** out);
+int sm_model_free(sm_model* m);
+/* Device::config */
+int sm_model_config(const sm_model* m, sm_config* out);
+/* Quantized weight bytes one decode step streams from HBM (all 2-D weights,
+ * output head included, embedding table excluded: one row is gathered). */
+int sm_model_weight_bytes(const sm_model* m, uint64_t* out);
+/* The CUDA stream the model's work is issued on (a cudaStream_t). */
+int sm_model_stream(const sm_model* m, void** stream);
+/* Bytes one decode step copies host->device (token, position, RNG and
+ * sampler state of every row, one pinned block) and device->host (tokens,
+ * RNG states). */
+int sm_model_step_io_bytes(const sm_model* m, uint64_t* h2d, uint64_t* d2h);
+
+/* ------------------------------------------------------------------------
+ * Sequence state. Replaces `s_models::state::SeqState` for dense models
+ * (crates/s-models/src/state.rs:202-361) and the position counter GpuCache
+ * (crates/s-backend-cuda/src/model.rs:97-105): K/V live in HBM, f32,
+ * [layer][position][kv_dim], owned by the handle.
+ * ---------------------------------------------------------------------- */
+int sm_cache_new(sm_model* m, uint64_t max_seq, sm_cache** out); /* Device::new_cache (qwen2.rs:633-637) */
+int sm_cache_free(sm_cache* c);
+int sm_cache_len(const sm_cache* c, uint64_t* out);          /* SeqState.len */
+int sm_cache_capacity(const sm_cache* c, uint64_t* out);     /* state.rs:309-318 */
+int sm_cache_advance(sm_cache* c, uint64_t n);               /* state.rs:289-291 (len += n, within capacity) */
+int sm_cache_reset(sm_cache* c);                             /* state.rs:297-304 */
+int sm_cache_truncate(sm_cache* c, uint64_t len);            /* state.rs:341-360: error if len > current len */
+int sm_cache_ensure_capacity(sm_cache* c, uint64_t min_cap); /* state.rs:323-329: keeps positions 0..len */
+int sm_cache_clone(const sm_cache* c, sm_cache** out);       /* SeqState: Clone (state.rs:64-69) */
+/* Host copy of the K and V rows (kv_dim floats each) of one position. */
+int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_out, float* v_out);
+
+/* ------------------------------------------------------------------------
+ * Forward. Device::forward_cached (crates/s-models/src/device.rs:33,
+ * crates/s-models/src/qwen2.rs:460-561): processes `n` tokens at absolute
+ * position sm_cache_len(), appends their K/V, and writes the last token's
+ * logits [vocab] to logits_out (host) unless it is NULL.
+ * ---------------------------------------------------------------------- */
+int sm_forward_cached(sm_model* m, sm_cache* c, const uint32_t* tokens, uint64_t n, float* logits_out);
+
+/* Sampler (crates/s-models/src/sampling.rs:43-60, 94-144). temperature <= 0
+ * is greedy (lowest index wins ties); top_k < 0 and top_p < 0 mean None.
+ * The splitmix64 state (sampling.rs:12-41) is passed in and returned. */
+typedef struct {
+  float temperature;
+  int64_t top_k;
+  float top_p;
+} sm_sampler;
+
+/* Initial splitmix64 state for Rng::new(seed). */
+uint64_t sm_rng_seed(uint64_t seed);
+
+/* Forward `n` tokens and sample the next one on the device: only the token
+ * id (and the RNG state) cross PCIe. mask (host, vocab bytes, 0 = forbidden)
+ * may be NULL (sampling.rs:66-88). */
+int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* tokens, uint64_t n, const sm_sampler* s,
+                      uint64_t* rng_state, const uint8_t* mask, uint32_t* out_token);
+/* One decode step for each of n sequences, batched (one token each; each
+ * cache advances by one). samplers and rng_states have n entries. */
+int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* tokens,
+                    const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens);
+
+/* n_steps decode steps for each of n sequences entirely on the device: the
+ * token sampled at step i is the input of step i+1 (no stop checks; the
+ * caller truncates a cache past an EOS). out_tokens[step * n + i]. If
+ * ev_begin / ev_end (cudaEvent_t) are given they are recorded on the model's
+ * stream around the steps. The loop of generate.rs:204-238 without its
+ * per-token callbacks. */
+int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* tokens,
+                  const sm_sampler* samplers, uint64_t* rng_states, uint64_t n_steps, uint32_t* out_tokens,
+                  void* ev_begin, void* ev_end);
+
+/* ------------------------------------------------------------------------
+ * Generation loop. generate_tokens_seeded (crates/s-models/src/generate.rs:149-250)
+ * over any device given as a vtable (the `Device` trait), and over the
+ * engine itself. Stop strings need a detokenizer: stop_cb receives the
+ * generated ids and reports a hit.
+ * ---------------------------------------------------------------------- */
+typedef int (*sm_on_token_fn)(void* ud, uint32_t token);                 /* 0 = abort ("stop") */
+typedef int (*sm_masker_fn)(void* ud, uint8_t* mask, uint64_t vocab);    /* 1 = mask written */
+typedef int (*sm_stop_fn)(void* ud, const uint32_t* ids, uint64_t n);    /* 1 = stop-string hit */
+typedef void (*sm_on_prefill_fn)(void* ud, void* cache);                 /* once, after prefill */
+
+typedef struct {
+  uint64_t max_tokens;
+  float temperature;
+  int64_t top_k;  /* < 0: None */
+  float top_p;    /* < 0: None */
+  int32_t has_seed;
+  uint64_t seed;
+} sm_gen_params;
+
+typedef struct {
+  uint64_t n_ids;
+  int32_t finish_stop; /* 1 = "stop", 0 = "length" */
+  uint64_t prompt_tokens;
+  uint64_t prefix_reused;
+  double elapsed_secs;
+} sm_gen_result;
+
+/* The Device trait as a vtable: new_cache / free_cache, and forward+sample
+ * (forward_cached followed by Sampler::sample[_masked]). */
+typedef struct {
+  int (*new_cache)(void* dev, uint64_t max_seq, void** cache);
+  int (*free_cache)(void* dev, void* cache);
+  int (*forward_sample)(void* dev, void* cache, const uint32_t* tokens, uint64_t n, const sm_sampler* s,
+                        uint64_t* rng_state, const uint8_t* mask, uint32_t* out_token);
+} sm_device_vtbl;
+
+/* out_ids must hold params->max_tokens entries. seed_cache (may be NULL) is
+ * used, not consumed, when 0 < seed_n < n_prompt; its length must be seed_n. */
+int sm_generate_with(const sm_device_vtbl* vt, void* dev, uint64_t vocab, const uint32_t* prompt, uint64_t n_prompt,
+                     const sm_gen_params* params, const uint32_t* eos, uint64_t n_eos, sm_on_token_fn on_token,
+                     sm_masker_fn masker, sm_stop_fn stop, sm_on_prefill_fn on_prefill, void* ud, void* seed_cache,
+                     uint64_t seed_n, uint32_t* out_ids, sm_gen_result* res);
+/* sm_generate_with over the engine (caches are sm_cache*). */
+int sm_generate(sm_model* m, const uint32_t* prompt, uint64_t n_prompt, const sm_gen_params* params,
+                const uint32_t* eos, uint64_t n_eos, sm_on_token_fn on_token, sm_masker_fn masker, sm_stop_fn stop,
+                sm_on_prefill_fn on_prefill, void* ud, sm_cache* seed_cache, uint64_t seed_n, uint32_t* out_ids,
+                sm_gen_result* res);
+
+/* ------------------------------------------------------------------------
+ * Kernel-level entry points (the reference's per-kernel GPU tests drive its
+ * kernels the same way: crates/s-backend-cuda/src/runtime.rs:120-899).
+ * A device weight holds one GGUF tensor [n_out x n_in] in the engine's HBM
+ * layout. Types: Q4_K (12), Q6_K (14), Q5_0 (6), Q8_0 (8).
+ * ---------------------------------------------------------------------- */
+typedef struct sm_dweight sm_dweight;
+/* Uploads GGUF bytes (host) of a row-major [n_out x n_in] tensor. */
+int sm_dweight_upload(uint32_t ggml_type, const void* gguf_bytes, uint64_t n_out, uint64_t n_in, sm_dweight** out);
+int sm_dweight_free(sm_dweight* w);
+/* Bytes of the encoded tensor (what one GEMV must read from HBM). */
+int sm_dweight_bytes(const sm_dweight* w, uint64_t* out);
+/* Bit-exact dequantization of all rows into out_dev[n_out x n_in]
+ * (crates/s-gguf/src/dequant.rs:66-206). stream may be NULL. */
+int sm_dequant(const sm_dweight* w, float* out_dev, void* stream);
+/* Dequant-fused GEMV: y_dev[b][o] = sum_d W[o][d] * x_dev[b][d] for b < batch
+ * (batch 1..32; qwen2.rs:663-674, kernels/src/lib.rs:709-876). */
+int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Synthetic GGUF models (the stand-in for real model files). Shapes and
+ * metadata keys follow qwen2.rs:30-63; values are seeded N(0, weight_std).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t arch; /* 0 = "qwen2", 1 = "llama" */
+  uint32_t n_embd, n_layers, n_heads, n_kv_heads, n_ff, vocab;
+  float rope_theta, rms_eps;
+  int32_t qkv_bias;      /* attn_{q,k,v}.bias present */
+  int32_t tied;          /* no output.weight (tied embeddings) */
+  uint64_t seed;
+  float weight_std;      /* 0.02 */
+  int32_t type_override; /* -1: Q4_K_M mix; else ggml type for every 2-D weight */
+} sm_synth_spec;
+
+/* Presets for the benchmark configurations 0 (Qwen2.5-0.5B), 2 (Qwen2.5-7B),
+ * 3 (Llama-3-8B) and 4 (Llama-3-70B). */
+int sm_synth_preset(int config_index, sm_synth_spec* out);
+int sm_synth_size(const sm_synth_spec* s, uint64_t* len);
+int sm_synth_write(const sm_synth_spec* s, const char* path, int threads);
+int sm_synth_memory(const sm_synth_spec* s, int threads, void** buf, uint64_t* len);
+void sm_synth_free(void* buf);
+/* Encodes n f32 values (whole blocks) as ggml type `type` into out. */
+int sm_quantize(uint32_t type, const float* x, uint64_t n, void* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SM_ENGINE_H */

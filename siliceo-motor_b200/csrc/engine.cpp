@@ -1,0 +1,995 @@
+// Engine runtime: model load into HBM, sequence caches, forward passes,
+// batched decode steps captured in CUDA graphs, and the C ABI over them.
+//
+// Replaces, for qwen2/llama: s_models::qwen2::Model as `impl Device`
+// (crates/s-models/src/qwen2.rs:625-642), s_backend_cuda::model::GpuQwen2
+// (crates/s-backend-cuda/src/model.rs:107-629) and SeqState
+// (crates/s-models/src/state.rs:202-361).
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/sm_engine.h"
+#include "common.hpp"
+#include "gguf.hpp"
+#include "layers.cuh"
+
+using namespace sm;
+
+namespace {
+
+#define CK(expr)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess) {                                                             \
+      set_error(std::string("cuda: ") + cudaGetErrorString(e_) + " at " #expr);         \
+      return SM_ERR_CUDA;                                                                \
+    }                                                                                    \
+  } while (0)
+
+// ------------------------------------------------------ device weights ----
+struct DW {
+  DWDesc d{};
+  void* mem = nullptr;
+  uint64_t enc_bytes = 0;  // bytes of the GGUF encoding
+};
+
+bool engine_type(uint32_t t) { return t == QT_Q4K || t == QT_Q6K || t == QT_Q8_0 || t == QT_Q5_0; }
+
+// GGUF rows -> engine HBM layout (see device.cuh). Returns the status.
+int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_in, DW* out) {
+  if (!engine_type(type)) {
+    set_error("unsupported weight type " + std::to_string(type) + " (engine handles Q4_K, Q6_K, Q5_0, Q8_0)");
+    return SM_ERR_UNSUPPORTED;
+  }
+  uint32_t bs = 1, tb = 4;
+  qtype_layout(type, &bs, &tb);
+  if (n_in % bs != 0 || n_out == 0 || n_out > 0xFFFFFFFFull || n_in > 0xFFFFFFFFull) {
+    set_error("weight shape not supported: n_in must be a multiple of " + std::to_string(bs));
+    return SM_ERR_UNSUPPORTED;
+  }
+  const uint64_t nb = n_in / bs, row_src = nb * tb;
+  uint64_t body_stride = 0, aux_stride = 0;
+  switch (type) {
+    case QT_Q4K: body_stride = nb * 144; break;
+    case QT_Q6K: body_stride = nb * 208; aux_stride = nb * 2; break;
+    case QT_Q8_0: body_stride = nb * 32; aux_stride = nb * 2; break;
+    case QT_Q5_0: body_stride = nb * 16; aux_stride = nb * 8; break;
+  }
+  aux_stride = (aux_stride + 15) / 16 * 16;
+  const uint64_t body_bytes = body_stride * n_out, aux_bytes = aux_stride * n_out;
+  std::vector<uint8_t> body(body_bytes), aux(aux_bytes);
+  for (uint64_t o = 0; o < n_out; o++) {
+    const uint8_t* r = src + o * row_src;
+    uint8_t* bd = body.data() + o * body_stride;
+    uint8_t* ax = aux.data() + o * aux_stride;
+    switch (type) {
+      case QT_Q4K: std::memcpy(bd, r, row_src); break;
+      case QT_Q6K:
+        for (uint64_t b = 0; b < nb; b++) {
+          std::memcpy(bd + b * 208, r + b * 210, 208);
+          std::memcpy(ax + b * 2, r + b * 210 + 208, 2);
+        }
+        break;
+      case QT_Q8_0:
+        for (uint64_t b = 0; b < nb; b++) {
+          std::memcpy(ax + b * 2, r + b * 34, 2);
+          std::memcpy(bd + b * 32, r + b * 34 + 2, 32);
+        }
+        break;
+      case QT_Q5_0:
+        for (uint64_t b = 0; b < nb; b++) {
+          std::memcpy(ax + b * 8 + 4, r + b * 22, 2);  // d
+          std::memcpy(ax + b * 8, r + b * 22 + 2, 4);  // qh
+          std::memcpy(bd + b * 16, r + b * 22 + 6, 16);
+        }
+        break;
+    }
+  }
+  void* mem = nullptr;
+  const uint64_t total = body_bytes + aux_bytes + 256;
+  if (cudaMalloc(&mem, total) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaMalloc failed for a weight of " + std::to_string(total) + " bytes");
+    return SM_ERR_OOM;
+  }
+  uint8_t* base = (uint8_t*)mem;
+  uint8_t* auxp = base + (body_bytes + 255) / 256 * 256;
+  CK(cudaMemcpy(base, body.data(), body_bytes, cudaMemcpyHostToDevice));
+  if (aux_bytes) CK(cudaMemcpy(auxp, aux.data(), aux_bytes, cudaMemcpyHostToDevice));
+  out->mem = mem;
+  out->enc_bytes = row_src * n_out;
+  out->d.body = base;
+  out->d.aux = aux_bytes ? auxp : base;
+  out->d.type = type;
+  out->d.n_out = (uint32_t)n_out;
+  out->d.n_in = (uint32_t)n_in;
+  out->d.body_stride = (uint32_t)body_stride;
+  out->d.aux_stride = (uint32_t)aux_stride;
+  return SM_OK;
+}
+
+void free_weight(DW& w) {
+  if (w.mem) cudaFree(w.mem);
+  w.mem = nullptr;
+}
+
+struct Layer {
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  float* bq = nullptr;
+  float* bk = nullptr;
+  float* bv = nullptr;
+  DW wq, wk, wv, wo, wgate, wup, wdown;
+};
+
+// Per-step host->device state, one pinned block copied with one memcpy.
+struct StepIn {
+  uint32_t* tok;        // [rows]
+  RowDesc* rows;        // [rows]
+  SeqDesc* seqs;        // [rows]
+  SampleParams* sp;     // [rows]
+  uint64_t* rng;        // [rows]
+  uint32_t* sel;        // [rows]
+};
+struct StepOut {
+  uint32_t* tok;  // [rows]
+  uint64_t* rng;  // [rows]
+};
+
+}  // namespace
+
+struct sm_cache {
+  sm_model* m = nullptr;
+  float* k = nullptr;
+  float* v = nullptr;
+  uint64_t cap = 0, len = 0;
+};
+
+struct sm_model {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  sm_config c{};
+  uint32_t kvd = 0;
+  DW tok_embd, output;
+  bool tied = false;
+  float* output_norm = nullptr;
+  std::vector<Layer> layers;
+  float* cos_t = nullptr;
+  float* sin_t = nullptr;
+  uint32_t max_ctx = 0;
+  uint32_t rows_max = 0, max_splits = 32;
+  // workspace
+  float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
+        *u = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr;
+  uint8_t* mask_dev = nullptr;
+  void* in_dev = nullptr;   // StepIn block on the device
+  void* in_host = nullptr;  // pinned
+  void* out_dev = nullptr;  // StepOut block on the device
+  void* out_host = nullptr; // pinned
+  size_t in_bytes = 0, out_bytes = 0;
+  StepIn din{}, hin{};
+  StepOut dout{}, hout{};
+  std::vector<void*> allocs;
+  std::map<uint32_t, cudaGraphExec_t> graphs;       // one step, state from the host
+  std::map<uint32_t, cudaGraphExec_t> run_graphs;   // one step, state carried on the device
+  uint32_t* hist = nullptr;  // [HIST_TOKENS] tokens recorded by decode runs
+  uint32_t* hist_ctr = nullptr;
+  std::mutex mu;
+  uint64_t weight_bytes = 0;
+};
+
+namespace {
+
+constexpr uint32_t HIST_TOKENS = 1u << 16;
+
+template <class T>
+void carve(uint8_t*& p, T*& out, size_t n) {
+  out = reinterpret_cast<T*>(p);
+  p += (n * sizeof(T) + 255) / 256 * 256;
+}
+
+size_t step_in_bytes(uint32_t R) {
+  return 6 * 256 + (size_t)R * (sizeof(uint32_t) * 2 + sizeof(RowDesc) + sizeof(SeqDesc) + sizeof(SampleParams) +
+                                sizeof(uint64_t));
+}
+void layout_in(void* base, uint32_t R, StepIn& s) {
+  uint8_t* p = (uint8_t*)base;
+  carve(p, s.tok, R);
+  carve(p, s.rows, R);
+  carve(p, s.seqs, R);
+  carve(p, s.sp, R);
+  carve(p, s.rng, R);
+  carve(p, s.sel, R);
+}
+size_t step_out_bytes(uint32_t R) { return 2 * 256 + (size_t)R * (sizeof(uint32_t) + sizeof(uint64_t)); }
+void layout_out(void* base, uint32_t R, StepOut& s) {
+  uint8_t* p = (uint8_t*)base;
+  carve(p, s.tok, R);
+  carve(p, s.rng, R);
+}
+
+int dev_alloc(sm_model* m, void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+    return SM_ERR_OOM;
+  }
+  m->allocs.push_back(*p);
+  return SM_OK;
+}
+
+int upload_f32(sm_model* m, const GgufReader& g, const std::string& name, size_t n, float** out) {
+  const GgufTensor* t = g.tensor(name);
+  if (!t) { set_error("tensor not found: " + name); return SM_ERR_FORMAT; }
+  if (t->type != QT_F32 || t->n_elements() != n) {
+    set_error(name + ": expected an F32 tensor of " + std::to_string(n) + " elements");
+    return SM_ERR_UNSUPPORTED;
+  }
+  const uint8_t* src = g.data(*t);
+  if (!src) { set_error(name + ": truncated tensor data"); return SM_ERR_FORMAT; }
+  int rc = dev_alloc(m, (void**)out, n * 4);
+  if (rc) return rc;
+  CK(cudaMemcpy(*out, src, n * 4, cudaMemcpyHostToDevice));
+  return SM_OK;
+}
+
+int upload_2d(const GgufReader& g, const std::string& name, uint64_t n_in, uint64_t n_out, DW* w) {
+  const GgufTensor* t = g.tensor(name);
+  if (!t) { set_error("tensor not found: " + name); return SM_ERR_FORMAT; }
+  if (t->dims.size() != 2 || t->dims[0] != n_in || t->dims[1] != n_out) {
+    set_error(name + ": unexpected shape");
+    return SM_ERR_FORMAT;
+  }
+  const uint8_t* src = g.data(*t);
+  if (!src) { set_error(name + ": truncated tensor data"); return SM_ERR_FORMAT; }
+  int rc = upload_weight(t->type, src, n_out, n_in, w);
+  if (rc) set_error(name + ": " + get_error());
+  return rc;
+}
+
+int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
+  // Famiglia::detect (crates/s-models/src/registry.rs:38-60)
+  const GgufValue* arch = g.meta("general.architecture");
+  if (!arch || arch->type != 8) { set_error("missing metadata: general.architecture"); return SM_ERR_FORMAT; }
+  if (arch->s != "qwen2" && arch->s != "llama") {
+    set_error("architecture '" + arch->s + "' not supported (qwen2, llama)");
+    return SM_ERR_UNSUPPORTED;
+  }
+  // Config::from_gguf (qwen2.rs:30-63): "qwen2." keys first, then "llama."
+  auto get_u = [&](const char* suf, uint64_t* out) -> int {
+    for (const char* pre : {"qwen2", "llama"}) {
+      const GgufValue* v = g.meta(std::string(pre) + "." + suf);
+      if (v) {
+        if (!v->as_u64(out)) { set_error(std::string(pre) + "." + suf + ": unexpected type"); return SM_ERR_FORMAT; }
+        return SM_OK;
+      }
+    }
+    set_error(std::string("missing metadata: ") + suf);
+    return SM_ERR_FORMAT;
+  };
+  auto get_f = [&](const char* suf, float* out) -> int {
+    for (const char* pre : {"qwen2", "llama"}) {
+      const GgufValue* v = g.meta(std::string(pre) + "." + suf);
+      if (v) {
+        if (!v->as_f32(out)) { set_error(std::string(pre) + "." + suf + ": unexpected type"); return SM_ERR_FORMAT; }
+        return SM_OK;
+      }
+    }
+    set_error(std::string("missing metadata: ") + suf);
+    return SM_ERR_FORMAT;
+  };
+  sm_config& c = m->c;
+  int rc;
+  if ((rc = get_u("embedding_length", &c.n_embd)) || (rc = get_u("attention.head_count", &c.n_heads)) ||
+      (rc = get_u("attention.head_count_kv", &c.n_kv_heads)) || (rc = get_u("block_count", &c.n_layers)) ||
+      (rc = get_u("feed_forward_length", &c.n_ff)) || (rc = get_f("rope.freq_base", &c.rope_theta)) ||
+      (rc = get_f("attention.layer_norm_rms_epsilon", &c.rms_eps)))
+    return rc;
+  if (!c.n_heads || !c.n_kv_heads || c.n_heads % c.n_kv_heads) { set_error("bad head counts"); return SM_ERR_FORMAT; }
+  c.head_dim = c.n_embd / c.n_heads;
+  const GgufTensor* te = g.tensor("token_embd.weight");
+  if (!te || te->dims.size() != 2) { set_error("tensor not found: token_embd.weight"); return SM_ERR_FORMAT; }
+  c.vocab_size = te->dims[1];
+  const uint64_t H = c.n_embd, hd = c.head_dim, kvd = c.n_kv_heads * hd, G = c.n_heads / c.n_kv_heads;
+  m->kvd = (uint32_t)kvd;
+  if (c.n_heads * hd != H || hd % 4 || hd > 128 || G > 8 || (G * hd) > 1024 || H % 4 || c.n_ff % 4) {
+    set_error("shape not supported by the attention kernels (head_dim <= 128, heads/kv_heads <= 8)");
+    return SM_ERR_UNSUPPORTED;
+  }
+  if ((rc = upload_2d(g, "token_embd.weight", H, c.vocab_size, &m->tok_embd))) return rc;
+  if (g.tensor("output.weight")) {
+    if ((rc = upload_2d(g, "output.weight", H, c.vocab_size, &m->output))) return rc;
+  } else {
+    m->output = m->tok_embd;  // tied embeddings (qwen2.rs:115-118)
+    m->tied = true;
+  }
+  if ((rc = upload_f32(m, g, "output_norm.weight", H, &m->output_norm))) return rc;
+  m->weight_bytes = m->output.enc_bytes;
+  for (uint64_t i = 0; i < c.n_layers; i++) {
+    Layer L;
+    const std::string p = "blk." + std::to_string(i) + ".";
+    auto opt_bias = [&](const char* n, uint64_t len, float** out) -> int {  // qwen2.rs:687-697
+      if (!g.tensor(p + n)) return SM_OK;
+      return upload_f32(m, g, p + n, len, out);
+    };
+    if ((rc = opt_bias("attn_q.bias", H, &L.bq)) || (rc = opt_bias("attn_k.bias", kvd, &L.bk)) ||
+        (rc = opt_bias("attn_v.bias", kvd, &L.bv)) || (rc = upload_f32(m, g, p + "attn_norm.weight", H, &L.attn_norm)) ||
+        (rc = upload_f32(m, g, p + "ffn_norm.weight", H, &L.ffn_norm)) ||
+        (rc = upload_2d(g, p + "attn_q.weight", H, H, &L.wq)) || (rc = upload_2d(g, p + "attn_k.weight", H, kvd, &L.wk)) ||
+        (rc = upload_2d(g, p + "attn_v.weight", H, kvd, &L.wv)) ||
+        (rc = upload_2d(g, p + "attn_output.weight", H, H, &L.wo)) ||
+        (rc = upload_2d(g, p + "ffn_gate.weight", H, c.n_ff, &L.wgate)) ||
+        (rc = upload_2d(g, p + "ffn_up.weight", H, c.n_ff, &L.wup)) ||
+        (rc = upload_2d(g, p + "ffn_down.weight", c.n_ff, H, &L.wdown))) {
+      m->layers.push_back(L);  // so that free releases what was uploaded
+      return rc;
+    }
+    m->weight_bytes += L.wq.enc_bytes + L.wk.enc_bytes + L.wv.enc_bytes + L.wo.enc_bytes + L.wgate.enc_bytes +
+                       L.wup.enc_bytes + L.wdown.enc_bytes;
+    m->layers.push_back(L);
+  }
+  // RoPE table with the reference's f32 formula (qwen2.rs:712-718).
+  m->max_ctx = opts && opts->max_context ? opts->max_context : 32768;
+  const uint64_t half = hd / 2;
+  std::vector<float> ct(m->max_ctx * half), st(m->max_ctx * half);
+  std::vector<float> freq(half);
+  for (uint64_t i = 0; i < half; i++) freq[i] = powf(c.rope_theta, -(2.0f * (float)i) / (float)hd);
+  for (uint64_t p = 0; p < m->max_ctx; p++)
+    for (uint64_t i = 0; i < half; i++) {
+      const float angle = (float)p * freq[i];
+      ct[p * half + i] = cosf(angle);
+      st[p * half + i] = sinf(angle);
+    }
+  if ((rc = dev_alloc(m, (void**)&m->cos_t, ct.size() * 4)) || (rc = dev_alloc(m, (void**)&m->sin_t, st.size() * 4)))
+    return rc;
+  CK(cudaMemcpy(m->cos_t, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(m->sin_t, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
+  // workspace
+  const uint32_t R = std::max<uint32_t>(32, opts && opts->max_batch ? opts->max_batch : 32);
+  m->rows_max = R;
+  const size_t F = c.n_ff, V = c.vocab_size;
+  if ((rc = dev_alloc(m, (void**)&m->x, R * H * 4)) || (rc = dev_alloc(m, (void**)&m->xn, R * H * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->q, R * H * 4)) || (rc = dev_alloc(m, (void**)&m->k, R * kvd * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->v, R * kvd * 4)) || (rc = dev_alloc(m, (void**)&m->att, R * H * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->g, R * F * 4)) || (rc = dev_alloc(m, (void**)&m->u, R * F * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->logits, R * V * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->part_o, (size_t)R * c.n_heads * m->max_splits * hd * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->part_ml, (size_t)R * c.n_heads * m->max_splits * 2 * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)))
+    return rc;
+  m->in_bytes = step_in_bytes(R);
+  m->out_bytes = step_out_bytes(R);
+  if ((rc = dev_alloc(m, &m->in_dev, m->in_bytes)) || (rc = dev_alloc(m, &m->out_dev, m->out_bytes)) ||
+      (rc = dev_alloc(m, (void**)&m->hist, HIST_TOKENS * 4)) || (rc = dev_alloc(m, (void**)&m->hist_ctr, 256)))
+    return rc;
+  CK(cudaMallocHost(&m->in_host, m->in_bytes));
+  CK(cudaMallocHost(&m->out_host, m->out_bytes));
+  std::memset(m->in_host, 0, m->in_bytes);
+  layout_in(m->in_dev, R, m->din);
+  layout_in(m->in_host, R, m->hin);
+  layout_out(m->out_dev, R, m->dout);
+  layout_out(m->out_host, R, m->hout);
+  for (uint32_t i = 0; i < R; i++) m->hin.sel[i] = i;
+  return SM_OK;
+}
+
+void destroy_model(sm_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : m->run_graphs) cudaGraphExecDestroy(kv.second);
+  free_weight(m->tok_embd);
+  if (!m->tied) free_weight(m->output);
+  for (auto& L : m->layers) {
+    free_weight(L.wq); free_weight(L.wk); free_weight(L.wv); free_weight(L.wo);
+    free_weight(L.wgate); free_weight(L.wup); free_weight(L.wdown);
+  }
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->in_host) cudaFreeHost(m->in_host);
+  if (m->out_host) cudaFreeHost(m->out_host);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, bool add) {
+  GemvSeg s{};
+  s.w = w.d;
+  s.y = y;
+  s.ldy = ldy;
+  s.bias = bias;
+  s.add = add ? 1u : 0u;
+  return s;
+}
+
+// The layer stack for `nrows` rows described in din (tokens, rows, seqs),
+// then final norm + output head for the nsel rows listed in din.sel.
+// qwen2.rs:460-561 with the kernels of gemv.cu / layers.cu.
+cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
+  const sm_config& c = m->c;
+  const uint32_t H = (uint32_t)c.n_embd, F = (uint32_t)c.n_ff, kvd = m->kvd, hd = (uint32_t)c.head_dim;
+  cudaError_t e;
+#define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
+  RK(launch_embed(m->tok_embd.d, m->din.tok, nrows, m->x, H, st));
+  for (uint32_t li = 0; li < c.n_layers; li++) {
+    const Layer& L = m->layers[li];
+    RK(launch_rmsnorm(m->x, H, nullptr, L.attn_norm, m->xn, H, nrows, H, c.rms_eps, st));
+    GemvArgs a{};
+    a.x = m->xn; a.ldx = H; a.batch = nrows; a.nseg = 3;
+    a.seg[0] = seg(L.wq, m->q, H, L.bq, false);
+    a.seg[1] = seg(L.wk, m->k, kvd, L.bk, false);
+    a.seg[2] = seg(L.wv, m->v, kvd, L.bv, false);
+    RK(launch_gemv(a, st));
+    RK(launch_rope_kv(m->q, m->k, m->v, H, kvd, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads,
+                      (uint32_t)c.n_kv_heads, hd, m->cos_t, m->sin_t, st));
+    RK(launch_attention(m->q, H, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads, (uint32_t)c.n_kv_heads, hd,
+                        m->part_o, m->part_ml, m->max_splits, m->att, H, st));
+    GemvArgs o{};
+    o.x = m->att; o.ldx = H; o.batch = nrows; o.nseg = 1;
+    o.seg[0] = seg(L.wo, m->x, H, nullptr, true);
+    RK(launch_gemv(o, st));
+    RK(launch_rmsnorm(m->x, H, nullptr, L.ffn_norm, m->xn, H, nrows, H, c.rms_eps, st));
+    GemvArgs gu{};
+    gu.x = m->xn; gu.ldx = H; gu.batch = nrows; gu.nseg = 2;
+    gu.seg[0] = seg(L.wgate, m->g, F, nullptr, false);
+    gu.seg[1] = seg(L.wup, m->u, F, nullptr, false);
+    RK(launch_gemv(gu, st));
+    RK(launch_silu_mul(m->g, m->u, (size_t)nrows * F, st));
+    GemvArgs dn{};
+    dn.x = m->g; dn.ldx = F; dn.batch = nrows; dn.nseg = 1;
+    dn.seg[0] = seg(L.wdown, m->x, H, nullptr, true);
+    RK(launch_gemv(dn, st));
+  }
+  if (nsel) {
+    RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
+    GemvArgs hd_{};
+    hd_.x = m->xn; hd_.ldx = H; hd_.batch = nsel; hd_.nseg = 1;
+    hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, false);
+    RK(launch_gemv(hd_, st));
+  }
+#undef RK
+  return cudaSuccess;
+}
+
+int check_sampler(const sm_sampler* s) {
+  if (!s) return SM_OK;
+  if (s->temperature > 0.0f && (s->top_k < 1 || s->top_k > SAMPLER_MAX_TOP_K)) {
+    set_error("on-device sampling with temperature > 0 needs 1 <= top_k <= " + std::to_string(SAMPLER_MAX_TOP_K));
+    return SM_ERR_UNSUPPORTED;
+  }
+  return SM_OK;
+}
+
+SampleParams to_params(const sm_sampler* s) {
+  SampleParams p{};
+  if (!s) { p.temperature = 0.f; p.top_k = -1; p.top_p = -1.f; return p; }
+  p.temperature = s->temperature;
+  p.top_k = (int32_t)std::max<int64_t>(-1, std::min<int64_t>(s->top_k, INT32_MAX));
+  p.top_p = s->top_p;
+  return p;
+}
+
+// Prefill / forward of n tokens of one cache, chunked by rows_max. The last
+// token's logits end in m->logits row 0.
+int forward_tokens(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n) {
+  if (n == 0) { set_error("forward_cached: empty token list"); return SM_ERR_ARG; }
+  if (c->len + n > c->cap) {
+    set_error("forward_cached: " + std::to_string(c->len + n) + " positions exceed the cache capacity " +
+              std::to_string(c->cap));
+    return SM_ERR_CAPACITY;
+  }
+  for (uint64_t i = 0; i < n; i++)
+    if (toks[i] >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
+  cudaStream_t st = m->stream;
+  for (uint64_t c0 = 0; c0 < n; c0 += m->rows_max) {
+    const uint32_t rows = (uint32_t)std::min<uint64_t>(m->rows_max, n - c0);
+    const bool last = c0 + rows == n;
+    CK(cudaStreamSynchronize(st));  // pinned staging is reused
+    for (uint32_t r = 0; r < rows; r++) {
+      m->hin.tok[r] = toks[c0 + r];
+      m->hin.rows[r] = RowDesc{0u, (uint32_t)(c->len + c0 + r)};
+    }
+    m->hin.seqs[0] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.sel[0] = rows - 1;
+    CK(cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, st));
+    CK(run_rows(m, rows, last ? 1 : 0, st));
+  }
+  c->len += n;
+  return SM_OK;
+}
+
+int sample_rows(sm_model* m, uint32_t rows, const uint8_t* mask_host, bool advance) {
+  cudaStream_t st = m->stream;
+  const uint8_t* mask = nullptr;
+  if (mask_host) {
+    CK(cudaMemcpyAsync(m->mask_dev, mask_host, (size_t)rows * m->c.vocab_size, cudaMemcpyHostToDevice, st));
+    mask = m->mask_dev;
+  }
+  CK(launch_sample(m->logits, (uint32_t)m->c.vocab_size, rows, mask, m->din.sp, m->din.rng, m->dout.tok,
+                   advance ? m->din.tok : nullptr, advance ? m->din.rows : nullptr, st));
+  CK(cudaMemcpyAsync(m->dout.rng, m->din.rng, rows * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
+  CK(cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st));
+  return SM_OK;
+}
+
+// One decode step of B sequences (one token each) as a CUDA graph:
+// H2D of the step state, layer stack, head, sampler, D2H of tokens + RNG.
+int decode_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
+  auto it = m->graphs.find(B);
+  if (it != m->graphs.end()) { *out = it->second; return SM_OK; }
+  cudaStream_t st = m->stream;
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = run_rows(m, B, B, st);
+  if (e == cudaSuccess)
+    e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
+                      m->din.rows, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->dout.rng, m->din.rng, B * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st);
+  cudaError_t e2 = cudaStreamEndCapture(st, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    set_error(std::string("cuda: decode graph capture failed: ") + cudaGetErrorString(e != cudaSuccess ? e : e2));
+    return SM_ERR_CUDA;
+  }
+  cudaGraphExec_t ex = nullptr;
+  e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    set_error(std::string("cuda: graph instantiate: ") + cudaGetErrorString(e));
+    return SM_ERR_CUDA;
+  }
+  m->graphs[B] = ex;
+  *out = ex;
+  return SM_OK;
+}
+
+// One decode step whose inputs (tokens, positions) were left on the device by
+// the previous step's sampler; records the sampled tokens in m->hist.
+int run_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
+  auto it = m->run_graphs.find(B);
+  if (it != m->run_graphs.end()) { *out = it->second; return SM_OK; }
+  cudaStream_t st = m->stream;
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = run_rows(m, B, B, st);
+  if (e == cudaSuccess)
+    e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
+                      m->din.rows, st);
+  if (e == cudaSuccess) e = launch_record_tokens(m->dout.tok, B, m->hist, m->hist_ctr, HIST_TOKENS / B, st);
+  cudaError_t e2 = cudaStreamEndCapture(st, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    set_error(std::string("cuda: decode-run graph capture failed: ") + cudaGetErrorString(e != cudaSuccess ? e : e2));
+    return SM_ERR_CUDA;
+  }
+  cudaGraphExec_t ex = nullptr;
+  e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    set_error(std::string("cuda: graph instantiate: ") + cudaGetErrorString(e));
+    return SM_ERR_CUDA;
+  }
+  m->run_graphs[B] = ex;
+  *out = ex;
+  return SM_OK;
+}
+
+int guard_model(const sm_model* m) {
+  if (!m) { set_error("null model"); return SM_ERR_ARG; }
+  return SM_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- C ABI ----
+extern "C" {
+
+const char* sm_last_error(void) { return get_error().c_str(); }
+int sm_abi_version(void) { return 1; }
+uint64_t sm_rng_seed(uint64_t seed) { return seed + 0x9E3779B97F4A7C15ull; }
+
+static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* opts, sm_model** out) {
+  if (!r) return SM_ERR_FORMAT;
+  if (!out) { set_error("null out"); return SM_ERR_ARG; }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    set_error("no CUDA device available: the engine runs only on the GPU");
+    return SM_ERR_CUDA;
+  }
+  auto* m = new sm_model();
+  m->device = opts ? opts->device : 0;
+  if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cannot use CUDA device " + std::to_string(m->device));
+    delete m;
+    return SM_ERR_CUDA;
+  }
+  int rc = load_model(*r, opts, m);
+  if (rc) { std::string msg = get_error(); destroy_model(m); set_error(msg); return rc; }
+  *out = m;
+  return SM_OK;
+}
+
+int sm_model_load(const char* path, const sm_load_opts* opts, sm_model** out) {
+  if (!path) { set_error("null path"); return SM_ERR_ARG; }
+  auto r = GgufReader::open_file(path);
+  if (!r) return get_error().rfind("io:", 0) == 0 ? SM_ERR_IO : SM_ERR_FORMAT;
+  return model_from_reader(std::move(r), opts, out);
+}
+
+int sm_model_load_memory(const void* buf, uint64_t len, const sm_load_opts* opts, sm_model** out) {
+  if (!buf) { set_error("null buffer"); return SM_ERR_ARG; }
+  return model_from_reader(GgufReader::open_memory(buf, len), opts, out);
+}
+
+int sm_model_free(sm_model* m) {
+  destroy_model(m);
+  return SM_OK;
+}
+
+int sm_model_config(const sm_model* m, sm_config* out) {
+  if (guard_model(m) || !out) return SM_ERR_ARG;
+  *out = m->c;
+  return SM_OK;
+}
+
+int sm_model_weight_bytes(const sm_model* m, uint64_t* out) {
+  if (guard_model(m) || !out) return SM_ERR_ARG;
+  *out = m->weight_bytes;
+  return SM_OK;
+}
+
+int sm_model_step_io_bytes(const sm_model* m, uint64_t* h2d, uint64_t* d2h) {
+  if (guard_model(m) || !h2d || !d2h) return SM_ERR_ARG;
+  *h2d = m->in_bytes;
+  *d2h = m->out_bytes;
+  return SM_OK;
+}
+
+int sm_model_stream(const sm_model* m, void** stream) {
+  if (guard_model(m) || !stream) return SM_ERR_ARG;
+  *stream = (void*)m->stream;
+  return SM_OK;
+}
+
+// ------------------------------------------------------------- caches ----
+static int alloc_kv(sm_model* m, uint64_t cap, float** k, float** v) {
+  const size_t bytes = (size_t)m->c.n_layers * cap * m->kvd * 4;
+  *k = *v = nullptr;
+  if (cudaMalloc((void**)k, bytes) != cudaSuccess || cudaMalloc((void**)v, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    if (*k) cudaFree(*k);
+    *k = nullptr;
+    set_error("cudaMalloc failed for a KV cache of " + std::to_string(2 * bytes) + " bytes");
+    return SM_ERR_OOM;
+  }
+  return SM_OK;
+}
+
+// copies positions [0, len) of every layer between caches of capacities ca -> cb
+static int copy_kv(sm_model* m, float* dk, float* dv, uint64_t dcap, const float* sk, const float* sv, uint64_t scap,
+                   uint64_t len) {
+  if (!len) return SM_OK;
+  const size_t row = (size_t)m->kvd * 4;
+  CK(cudaMemcpy2DAsync(dk, dcap * row, sk, scap * row, len * row, m->c.n_layers, cudaMemcpyDeviceToDevice, m->stream));
+  CK(cudaMemcpy2DAsync(dv, dcap * row, sv, scap * row, len * row, m->c.n_layers, cudaMemcpyDeviceToDevice, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return SM_OK;
+}
+
+int sm_cache_new(sm_model* m, uint64_t max_seq, sm_cache** out) {
+  if (guard_model(m) || !out) return SM_ERR_ARG;
+  if (max_seq == 0 || max_seq > m->max_ctx) {
+    set_error("sm_cache_new: max_seq must be in 1.." + std::to_string(m->max_ctx) + " (the model's max_context)");
+    return SM_ERR_CAPACITY;
+  }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  auto* c = new sm_cache();
+  c->m = m;
+  c->cap = max_seq;
+  int rc = alloc_kv(m, max_seq, &c->k, &c->v);
+  if (rc) { delete c; return rc; }
+  *out = c;
+  return SM_OK;
+}
+
+int sm_cache_free(sm_cache* c) {
+  if (!c) return SM_OK;
+  std::lock_guard<std::mutex> lk(c->m->mu);
+  cudaSetDevice(c->m->device);
+  cudaStreamSynchronize(c->m->stream);
+  cudaFree(c->k);
+  cudaFree(c->v);
+  delete c;
+  return SM_OK;
+}
+
+int sm_cache_len(const sm_cache* c, uint64_t* out) {
+  if (!c || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  *out = c->len;
+  return SM_OK;
+}
+int sm_cache_capacity(const sm_cache* c, uint64_t* out) {
+  if (!c || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  *out = c->cap;
+  return SM_OK;
+}
+int sm_cache_advance(sm_cache* c, uint64_t n) {
+  if (!c) { set_error("null cache"); return SM_ERR_ARG; }
+  if (c->len + n > c->cap) { set_error("sm_cache_advance: beyond capacity"); return SM_ERR_CAPACITY; }
+  c->len += n;
+  return SM_OK;
+}
+int sm_cache_reset(sm_cache* c) {
+  if (!c) { set_error("null cache"); return SM_ERR_ARG; }
+  c->len = 0;
+  return SM_OK;
+}
+int sm_cache_truncate(sm_cache* c, uint64_t len) {
+  if (!c) { set_error("null cache"); return SM_ERR_ARG; }
+  if (len > c->len) {
+    set_error("truncate: " + std::to_string(len) + " > len=" + std::to_string(c->len) + " (a state cannot grow this way)");
+    return SM_ERR_STATE;
+  }
+  c->len = len;
+  return SM_OK;
+}
+int sm_cache_ensure_capacity(sm_cache* c, uint64_t min_cap) {
+  if (!c) { set_error("null cache"); return SM_ERR_ARG; }
+  if (min_cap <= c->cap) return SM_OK;
+  sm_model* m = c->m;
+  if (min_cap > m->max_ctx) { set_error("ensure_capacity: beyond the model's max_context"); return SM_ERR_CAPACITY; }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  float *k, *v;
+  int rc = alloc_kv(m, min_cap, &k, &v);
+  if (rc) return rc;
+  rc = copy_kv(m, k, v, min_cap, c->k, c->v, c->cap, c->len);
+  if (rc) { cudaFree(k); cudaFree(v); return rc; }
+  cudaFree(c->k);
+  cudaFree(c->v);
+  c->k = k;
+  c->v = v;
+  c->cap = min_cap;
+  return SM_OK;
+}
+int sm_cache_clone(const sm_cache* c, sm_cache** out) {
+  if (!c || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  sm_model* m = c->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  auto* n = new sm_cache();
+  n->m = m;
+  n->cap = c->cap;
+  n->len = c->len;
+  int rc = alloc_kv(m, c->cap, &n->k, &n->v);
+  if (!rc) rc = copy_kv(m, n->k, n->v, n->cap, c->k, c->v, c->cap, c->len);
+  if (rc) { if (n->k) { cudaFree(n->k); cudaFree(n->v); } delete n; return rc; }
+  *out = n;
+  return SM_OK;
+}
+int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_out, float* v_out) {
+  if (!c || !k_out || !v_out) { set_error("null argument"); return SM_ERR_ARG; }
+  sm_model* m = c->m;
+  if (layer >= m->c.n_layers || pos >= c->cap) { set_error("read_kv: index out of range"); return SM_ERR_ARG; }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  const size_t off = ((size_t)layer * c->cap + pos) * m->kvd;
+  CK(cudaStreamSynchronize(m->stream));
+  CK(cudaMemcpy(k_out, c->k + off, m->kvd * 4, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(v_out, c->v + off, m->kvd * 4, cudaMemcpyDeviceToHost));
+  return SM_OK;
+}
+
+// ------------------------------------------------------------ forward ----
+int sm_forward_cached(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n, float* logits_out) {
+  if (guard_model(m) || !c || !toks || c->m != m) { set_error("sm_forward_cached: bad arguments"); return SM_ERR_ARG; }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  int rc = forward_tokens(m, c, toks, n);
+  if (rc) return rc;
+  if (logits_out) {
+    CK(cudaMemcpyAsync(logits_out, m->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+  }
+  CK(cudaStreamSynchronize(m->stream));
+  return SM_OK;
+}
+
+int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n, const sm_sampler* s,
+                      uint64_t* rng_state, const uint8_t* mask, uint32_t* out_token) {
+  if (guard_model(m) || !c || !toks || !rng_state || !out_token || c->m != m) {
+    set_error("sm_forward_sample: bad arguments");
+    return SM_ERR_ARG;
+  }
+  int rc = check_sampler(s);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  if (n == 1 && !mask) {  // the decode step: graph replay
+    if (c->len + 1 > c->cap) {
+      set_error("decode: position " + std::to_string(c->len) + " is beyond the cache capacity " + std::to_string(c->cap));
+      return SM_ERR_CAPACITY;
+    }
+    if (toks[0] >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
+    cudaGraphExec_t ex;
+    if ((rc = decode_graph(m, 1, &ex))) return rc;
+    CK(cudaStreamSynchronize(m->stream));
+    m->hin.tok[0] = toks[0];
+    m->hin.rows[0] = RowDesc{0u, (uint32_t)c->len};
+    m->hin.seqs[0] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.sp[0] = to_params(s);
+    m->hin.rng[0] = *rng_state;
+    m->hin.sel[0] = 0;
+    CK(cudaGraphLaunch(ex, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    c->len += 1;
+    *out_token = m->hout.tok[0];
+    *rng_state = m->hout.rng[0];
+    return SM_OK;
+  }
+  if ((rc = forward_tokens(m, c, toks, n))) return rc;
+  CK(cudaStreamSynchronize(m->stream));  // the staging block is free again
+  m->hin.sp[0] = to_params(s);
+  m->hin.rng[0] = *rng_state;
+  // only sp/rng changed: copy the whole staging block again (small)
+  CK(cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, m->stream));
+  if ((rc = sample_rows(m, 1, mask, false))) return rc;
+  CK(cudaStreamSynchronize(m->stream));
+  *out_token = m->hout.tok[0];
+  *rng_state = m->hout.rng[0];
+  return SM_OK;
+}
+
+int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks, const sm_sampler* samplers,
+                    uint64_t* rng_states, uint32_t* out_tokens) {
+  if (guard_model(m) || !caches || !toks || !rng_states || !out_tokens || n == 0) {
+    set_error("sm_decode_batch: bad arguments");
+    return SM_ERR_ARG;
+  }
+  if (n > m->rows_max) { set_error("sm_decode_batch: batch larger than the model's max_batch"); return SM_ERR_ARG; }
+  for (uint64_t i = 0; i < n; i++) {
+    int rc = check_sampler(samplers ? &samplers[i] : nullptr);
+    if (rc) return rc;
+    if (!caches[i] || caches[i]->m != m) { set_error("sm_decode_batch: cache of another model"); return SM_ERR_ARG; }
+    if (caches[i]->len + 1 > caches[i]->cap) { set_error("sm_decode_batch: cache full"); return SM_ERR_CAPACITY; }
+    if (toks[i] >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
+    for (uint64_t j = 0; j < i; j++)
+      if (caches[j] == caches[i]) { set_error("sm_decode_batch: a cache appears twice"); return SM_ERR_ARG; }
+  }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  cudaGraphExec_t ex;
+  int rc = decode_graph(m, (uint32_t)n, &ex);
+  if (rc) return rc;
+  CK(cudaStreamSynchronize(m->stream));
+  for (uint64_t i = 0; i < n; i++) {
+    sm_cache* c = caches[i];
+    m->hin.tok[i] = toks[i];
+    m->hin.rows[i] = RowDesc{(uint32_t)i, (uint32_t)c->len};
+    m->hin.seqs[i] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.sp[i] = to_params(samplers ? &samplers[i] : nullptr);
+    m->hin.rng[i] = rng_states[i];
+    m->hin.sel[i] = (uint32_t)i;
+  }
+  CK(cudaGraphLaunch(ex, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  for (uint64_t i = 0; i < n; i++) {
+    caches[i]->len += 1;
+    out_tokens[i] = m->hout.tok[i];
+    rng_states[i] = m->hout.rng[i];
+  }
+  return SM_OK;
+}
+
+int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks, const sm_sampler* samplers,
+                  uint64_t* rng_states, uint64_t n_steps, uint32_t* out_tokens, void* ev_begin, void* ev_end) {
+  if (guard_model(m) || !caches || !toks || !rng_states || !out_tokens || n == 0) {
+    set_error("sm_decode_run: bad arguments");
+    return SM_ERR_ARG;
+  }
+  if (n > m->rows_max) { set_error("sm_decode_run: batch larger than the model's max_batch"); return SM_ERR_ARG; }
+  if (n_steps == 0) return SM_OK;
+  for (uint64_t i = 0; i < n; i++) {
+    int rc = check_sampler(samplers ? &samplers[i] : nullptr);
+    if (rc) return rc;
+    if (!caches[i] || caches[i]->m != m) { set_error("sm_decode_run: cache of another model"); return SM_ERR_ARG; }
+    if (caches[i]->len + n_steps > caches[i]->cap) { set_error("sm_decode_run: steps exceed the cache capacity"); return SM_ERR_CAPACITY; }
+    if (toks[i] >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
+    for (uint64_t j = 0; j < i; j++)
+      if (caches[j] == caches[i]) { set_error("sm_decode_run: a cache appears twice"); return SM_ERR_ARG; }
+  }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  cudaGraphExec_t ex;
+  int rc = run_graph(m, (uint32_t)n, &ex);
+  if (rc) return rc;
+  const uint64_t chunk = HIST_TOKENS / n;
+  CK(cudaStreamSynchronize(m->stream));
+  for (uint64_t i = 0; i < n; i++) {
+    sm_cache* c = caches[i];
+    m->hin.tok[i] = toks[i];
+    m->hin.rows[i] = RowDesc{(uint32_t)i, (uint32_t)c->len};
+    m->hin.seqs[i] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.sp[i] = to_params(samplers ? &samplers[i] : nullptr);
+    m->hin.rng[i] = rng_states[i];
+    m->hin.sel[i] = (uint32_t)i;
+  }
+  CK(cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, m->stream));
+  if (ev_begin) CK(cudaEventRecord((cudaEvent_t)ev_begin, m->stream));
+  for (uint64_t s0 = 0; s0 < n_steps; s0 += chunk) {
+    const uint64_t k = std::min(chunk, n_steps - s0);
+    CK(cudaMemsetAsync(m->hist_ctr, 0, 4, m->stream));
+    for (uint64_t s = 0; s < k; s++) CK(cudaGraphLaunch(ex, m->stream));
+    CK(cudaMemcpyAsync(out_tokens + s0 * n, m->hist, k * n * 4, cudaMemcpyDeviceToHost, m->stream));
+  }
+  if (ev_end) CK(cudaEventRecord((cudaEvent_t)ev_end, m->stream));
+  CK(cudaMemcpyAsync(m->hout.rng, m->din.rng, n * sizeof(uint64_t), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  for (uint64_t i = 0; i < n; i++) {
+    caches[i]->len += n_steps;
+    rng_states[i] = m->hout.rng[i];
+  }
+  return SM_OK;
+}
+
+// ------------------------------------------------- kernel-level entries ----
+struct sm_dweight {
+  DW w;
+  int device;
+};
+
+int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t n_in, sm_dweight** out) {
+  if (!bytes || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); set_error("no CUDA device"); return SM_ERR_CUDA; }
+  auto* w = new sm_dweight();
+  w->device = dev;
+  int rc = upload_weight(type, (const uint8_t*)bytes, n_out, n_in, &w->w);
+  if (rc) { delete w; return rc; }
+  *out = w;
+  return SM_OK;
+}
+int sm_dweight_free(sm_dweight* w) {
+  if (!w) return SM_OK;
+  free_weight(w->w);
+  delete w;
+  return SM_OK;
+}
+int sm_dweight_bytes(const sm_dweight* w, uint64_t* out) {
+  if (!w || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  *out = w->w.enc_bytes;
+  return SM_OK;
+}
+int sm_dequant(const sm_dweight* w, float* out_dev, void* stream) {
+  if (!w || !out_dev) { set_error("null argument"); return SM_ERR_ARG; }
+  CK(launch_dequant(w->w.d, out_dev, (cudaStream_t)stream));
+  return SM_OK;
+}
+int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream) {
+  if (!w || !x_dev || !y_dev) { set_error("null argument"); return SM_ERR_ARG; }
+  if (batch < 1 || batch > 32) { set_error("sm_gemv: batch must be 1..32"); return SM_ERR_ARG; }
+  if (((uintptr_t)x_dev & 15) || (w->w.d.n_in & 3)) { set_error("sm_gemv: x must be 16-byte aligned"); return SM_ERR_ARG; }
+  GemvArgs a{};
+  a.x = x_dev;
+  a.ldx = w->w.d.n_in;
+  a.batch = (uint32_t)batch;
+  a.nseg = 1;
+  a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, false);
+  CK(launch_gemv(a, (cudaStream_t)stream));
+  return SM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,429 @@
+// Dequant-fused GEMV for GGUF Q4_K / Q6_K / Q8_0 / Q5_0 weights, batch 1..32,
+// and the bit-exact dequantizer.
+//
+// Reference semantics: y[s,o] = sum_d W[o,d] * x[s,d] with W the f32 values of
+// dequantize() (crates/s-models/src/qwen2.rs:663-674; the reference's fused
+// GPU kernels crates/s-backend-cuda/kernels/src/lib.rs:709-876 do the same one
+// thread per output). Here a warp owns R rows: its lanes stride over the
+// row's 16-byte units with 128-bit streaming loads, and the partial sums are
+// combined with warp shuffles. Within a sub-block the scale is factored out
+// (sum x*(d*sc*q - dmin*m) = d*sc*sum(q*x) - dmin*m*sum(x)), so the inner
+// loop is one exact int->float conversion and one FMA per weight; the result
+// differs from the reference's sequential sum by rounding only.
+#include "device.cuh"
+
+namespace sm {
+
+constexpr int GEMV_WARPS = 4;
+
+// ----------------------------------------------------------- dequant ----
+__device__ __forceinline__ uint32_t rd16(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, uint32_t* d, uint32_t* m) {
+  if (j < 4) {  // dequant.rs:41-49
+    *d = s[j] & 63;
+    *m = s[j + 4] & 63;
+  } else {
+    *d = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+    *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+// Element e of row o, with the reference's f32 operations (no contraction).
+__device__ float dequant_elem(const DWDesc& w, uint32_t o, uint32_t e) {
+  const uint8_t* row = w.body + (size_t)o * w.body_stride;
+  switch (w.type) {
+    case 12: {  // Q4_K, dequant.rs:98-124
+      uint32_t blk = e >> 8, l = e & 255, g = l >> 6, within = l & 63;
+      const uint8_t* b = row + (size_t)blk * 144;
+      float d = fp16_ref(rd16(b)), dmin = fp16_ref(rd16(b + 2));
+      uint32_t is = 2 * g + (within >= 32), sc, m;
+      scale_min_k4((int)is, b + 4, &sc, &m);
+      uint32_t qb = b[16 + 32 * g + (within & 31)];
+      uint32_t q = within < 32 ? (qb & 0x0F) : (qb >> 4);
+      float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+      return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    case 14: {  // Q6_K, dequant.rs:178-206
+      uint32_t blk = e >> 8, l = e & 255, n = l >> 7, wl = l & 127, k = wl >> 5, ll = wl & 31, is = ll >> 4;
+      const uint8_t* b = row + (size_t)blk * 208;
+      float d = fp16_ref(rd16(w.aux + (size_t)o * w.aux_stride + blk * 2));
+      if (!isfinite(d)) return 0.0f;
+      uint32_t qlb = b[n * 64 + ll + ((k & 1) ? 32 : 0)];
+      uint32_t nib = (k & 2) ? (qlb >> 4) : (qlb & 0x0F);
+      uint32_t hb = (b[128 + n * 32 + ll] >> (2 * k)) & 3;
+      int32_t q = (int32_t)(nib | (hb << 4)) - 32;
+      float sc = (float)(int8_t)b[192 + n * 8 + is + 2 * k];
+      return __fmul_rn(__fmul_rn(d, sc), (float)q);
+    }
+    case 8: {  // Q8_0, dequant.rs:66-71
+      uint32_t blk = e >> 5, l = e & 31;
+      float d = fp16_ref(rd16(w.aux + (size_t)o * w.aux_stride + blk * 2));
+      return __fmul_rn((float)(int8_t)row[blk * 32 + l], d);
+    }
+    case 6: {  // Q5_0, dequant.rs:79-94
+      uint32_t blk = e >> 5, l = e & 31;
+      const uint8_t* a = w.aux + (size_t)o * w.aux_stride + blk * 8;
+      uint32_t qh = (uint32_t)a[0] | ((uint32_t)a[1] << 8) | ((uint32_t)a[2] << 16) | ((uint32_t)a[3] << 24);
+      float d = fp16_ref(rd16(a + 4));
+      uint32_t qb = row[blk * 16 + (l & 15)];
+      int32_t q = (int32_t)((l < 16 ? (qb & 0x0F) : (qb >> 4)) | (((qh >> l) & 1u) << 4)) - 16;
+      return __fmul_rn(d, (float)q);
+    }
+    case 0:
+      return reinterpret_cast<const float*>(row)[e];
+  }
+  return 0.0f;
+}
+
+__global__ void dequant_kernel(DWDesc w, float* out) {
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  size_t n = (size_t)w.n_out * w.n_in;
+  if (i >= n) return;
+  uint32_t o = (uint32_t)(i / w.n_in), e = (uint32_t)(i % w.n_in);
+  out[i] = dequant_elem(w, o, e);
+}
+
+// Embedding lookup (qwen2.rs:468-472): row tok of the table, dequantized exactly.
+__global__ void embed_kernel(DWDesc w, const uint32_t* tokens, float* x, uint32_t ldx) {
+  uint32_t r = blockIdx.y, tok = tokens[r];
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < w.n_in; e += gridDim.x * blockDim.x)
+    x[(size_t)r * ldx + e] = dequant_elem(w, tok, e);
+}
+
+// -------------------------------------------------------------- GEMV ----
+// Each unit function adds, for R rows and up to BT columns, one lane's share
+// of a row: acc[r][b] += sum over the unit's weights of W*x.
+
+// Q4_K unit = 16 bytes of qs (32 weights: 16 of sub-block 2j, 16 of 2j+1)
+// plus the block header (d, dmin, 12 scale bytes) read as one 16-byte load.
+template <int R, int BT>
+__device__ __forceinline__ void unit_q4k(const uint8_t* const* rowp, int u, const float* x, uint32_t ldx, int ncols,
+                                         float (&acc)[R][BT]) {
+  const int blk = u >> 3, p = u & 7, j = p >> 1;
+  uint4 hd[R], qs[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const uint8_t* b = rowp[r] + (size_t)blk * 144;
+    hd[r] = ld_stream(b);
+    qs[r] = ld_stream(b + 16 + p * 16);
+  }
+  float d1[R], m1[R], d2[R], m2[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const float d = fp16_ref(hd[r].x & 0xFFFFu), dmin = fp16_ref(hd[r].x >> 16);
+    uint32_t sa, ma, sb, mb;
+    if (j < 2) {  // sub-blocks 2j, 2j+1 < 4
+      const int s0 = 16 * j;
+      sa = (hd[r].y >> s0) & 63u;
+      ma = (hd[r].z >> s0) & 63u;
+      sb = (hd[r].y >> (s0 + 8)) & 63u;
+      mb = (hd[r].z >> (s0 + 8)) & 63u;
+    } else {  // sub-blocks 4..7
+      const int s0 = 16 * (j - 2);
+      const uint32_t a0 = (hd[r].w >> s0) & 0xFFu, a1 = (hd[r].w >> (s0 + 8)) & 0xFFu;
+      sa = (a0 & 0xF) | (((hd[r].y >> (s0 + 6)) & 3u) << 4);
+      ma = (a0 >> 4) | (((hd[r].z >> (s0 + 6)) & 3u) << 4);
+      sb = (a1 & 0xF) | (((hd[r].y >> (s0 + 14)) & 3u) << 4);
+      mb = (a1 >> 4) | (((hd[r].z >> (s0 + 14)) & 3u) << 4);
+    }
+    d1[r] = d * (float)sa;
+    m1[r] = dmin * (float)ma;
+    d2[r] = d * (float)sb;
+    m2[r] = dmin * (float)mb;
+  }
+  const int base = blk * 256 + 64 * j + 16 * (p & 1);
+#pragma unroll
+  for (int b = 0; b < BT; b++) {
+    if (b >= ncols) break;
+    const float* xb = x + (size_t)b * ldx + base;
+    float xl[16], xh[16];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float4 a = ldg4(xb + 4 * i), c = ldg4(xb + 32 + 4 * i);
+      xl[4 * i] = a.x; xl[4 * i + 1] = a.y; xl[4 * i + 2] = a.z; xl[4 * i + 3] = a.w;
+      xh[4 * i] = c.x; xh[4 * i + 1] = c.y; xh[4 * i + 2] = c.z; xh[4 * i + 3] = c.w;
+    }
+    float sxl = 0.f, sxh = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) { sxl += xl[i]; sxh += xh[i]; }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint32_t wv[4] = {qs[r].x, qs[r].y, qs[r].z, qs[r].w};
+      float sl0 = 0.f, sl1 = 0.f, sh0 = 0.f, sh1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t lo = wv[i] & 0x0F0F0F0Fu, hi = (wv[i] >> 4) & 0x0F0F0F0Fu;
+        sl0 = fmaf(byte_f<0>(lo, 8388608.f), xl[4 * i + 0], sl0);
+        sl1 = fmaf(byte_f<1>(lo, 8388608.f), xl[4 * i + 1], sl1);
+        sl0 = fmaf(byte_f<2>(lo, 8388608.f), xl[4 * i + 2], sl0);
+        sl1 = fmaf(byte_f<3>(lo, 8388608.f), xl[4 * i + 3], sl1);
+        sh0 = fmaf(byte_f<0>(hi, 8388608.f), xh[4 * i + 0], sh0);
+        sh1 = fmaf(byte_f<1>(hi, 8388608.f), xh[4 * i + 1], sh1);
+        sh0 = fmaf(byte_f<2>(hi, 8388608.f), xh[4 * i + 2], sh0);
+        sh1 = fmaf(byte_f<3>(hi, 8388608.f), xh[4 * i + 3], sh1);
+      }
+      acc[r][b] += (d1[r] * (sl0 + sl1) - m1[r] * sxl) + (d2[r] * (sh0 + sh1) - m2[r] * sxh);
+    }
+  }
+}
+
+// Q6_K unit = 64 weights of one block: half n, 16-column slice c, all four
+// 32-row groups (ql 2 x 16 B + qh 16 B + 4 scale bytes + d).
+template <int R, int BT>
+__device__ __forceinline__ void unit_q6k(const uint8_t* const* rowp, const uint8_t* const* auxp, int u, const float* x,
+                                         uint32_t ldx, int ncols, float (&acc)[R][BT]) {
+  const int blk = u >> 2, n = (u >> 1) & 1, c = u & 1;
+  uint4 qa[R], qb[R], qh[R];
+  float ds[R][4];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const uint8_t* b = rowp[r] + (size_t)blk * 208;
+    qa[r] = ld_stream(b + n * 64 + c * 16);
+    qb[r] = ld_stream(b + n * 64 + 32 + c * 16);
+    qh[r] = ld_stream(b + 128 + n * 32 + c * 16);
+    const uint2 scw = __ldg(reinterpret_cast<const uint2*>(b + 192 + n * 8));
+    float d = fp16_ref(__ldg(reinterpret_cast<const unsigned short*>(auxp[r]) + blk));
+    if (!isfinite(d)) d = 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
+    const uint32_t s0 = c ? (scw.x >> 8) : scw.x, s1 = c ? (scw.y >> 8) : scw.y;
+    ds[r][0] = d * (float)(int8_t)(s0 & 0xFF);
+    ds[r][1] = d * (float)(int8_t)((s0 >> 16) & 0xFF);
+    ds[r][2] = d * (float)(int8_t)(s1 & 0xFF);
+    ds[r][3] = d * (float)(int8_t)((s1 >> 16) & 0xFF);
+  }
+  const int base = blk * 256 + n * 128 + c * 16;
+#pragma unroll
+  for (int b = 0; b < BT; b++) {
+    if (b >= ncols) break;
+    const float* xb = x + (size_t)b * ldx + base;
+    float xv[4][16];
+#pragma unroll
+    for (int g = 0; g < 4; g++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        float4 a = ldg4(xb + 32 * g + 4 * i);
+        xv[g][4 * i] = a.x; xv[g][4 * i + 1] = a.y; xv[g][4 * i + 2] = a.z; xv[g][4 * i + 3] = a.w;
+      }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint32_t av[4] = {qa[r].x, qa[r].y, qa[r].z, qa[r].w};
+      const uint32_t bv[4] = {qb[r].x, qb[r].y, qb[r].z, qb[r].w};
+      const uint32_t hv[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t w1 = (av[i] & 0x0F0F0F0Fu) | ((hv[i] << 4) & 0x30303030u);
+        const uint32_t w2 = (bv[i] & 0x0F0F0F0Fu) | ((hv[i] << 2) & 0x30303030u);
+        const uint32_t w3 = ((av[i] >> 4) & 0x0F0F0F0Fu) | (hv[i] & 0x30303030u);
+        const uint32_t w4 = ((bv[i] >> 4) & 0x0F0F0F0Fu) | ((hv[i] >> 2) & 0x30303030u);
+        const uint32_t ww[4] = {w1, w2, w3, w4};
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+          s[g] = fmaf(byte_f<0>(ww[g], 8388640.f), xv[g][4 * i + 0], s[g]);
+          s[g] = fmaf(byte_f<1>(ww[g], 8388640.f), xv[g][4 * i + 1], s[g]);
+          s[g] = fmaf(byte_f<2>(ww[g], 8388640.f), xv[g][4 * i + 2], s[g]);
+          s[g] = fmaf(byte_f<3>(ww[g], 8388640.f), xv[g][4 * i + 3], s[g]);
+        }
+      }
+      acc[r][b] += (ds[r][0] * s[0] + ds[r][1] * s[1]) + (ds[r][2] * s[2] + ds[r][3] * s[3]);
+    }
+  }
+}
+
+// Q8_0 unit = 16 int8 weights (half a block) + d.
+template <int R, int BT>
+__device__ __forceinline__ void unit_q80(const uint8_t* const* rowp, const uint8_t* const* auxp, int u, const float* x,
+                                         uint32_t ldx, int ncols, float (&acc)[R][BT]) {
+  const int blk = u >> 1, h = u & 1;
+  uint4 q[R];
+  float d[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    q[r] = ld_stream(rowp[r] + (size_t)blk * 32 + h * 16);
+    d[r] = fp16_ref(__ldg(reinterpret_cast<const unsigned short*>(auxp[r]) + blk));
+  }
+  const int base = blk * 32 + h * 16;
+#pragma unroll
+  for (int b = 0; b < BT; b++) {
+    if (b >= ncols) break;
+    const float* xb = x + (size_t)b * ldx + base;
+    float xv[16];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float4 a = ldg4(xb + 4 * i);
+      xv[4 * i] = a.x; xv[4 * i + 1] = a.y; xv[4 * i + 2] = a.z; xv[4 * i + 3] = a.w;
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint32_t wv[4] = {q[r].x ^ 0x80808080u, q[r].y ^ 0x80808080u, q[r].z ^ 0x80808080u, q[r].w ^ 0x80808080u};
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        s0 = fmaf(byte_f<0>(wv[i], 8388736.f), xv[4 * i + 0], s0);
+        s1 = fmaf(byte_f<1>(wv[i], 8388736.f), xv[4 * i + 1], s1);
+        s0 = fmaf(byte_f<2>(wv[i], 8388736.f), xv[4 * i + 2], s0);
+        s1 = fmaf(byte_f<3>(wv[i], 8388736.f), xv[4 * i + 3], s1);
+      }
+      acc[r][b] += d[r] * (s0 + s1);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t spread4(uint32_t b) {  // 4 bits -> bit 4 of each byte
+  return ((b & 1u) << 4) | ((b & 2u) << 11) | ((b & 4u) << 18) | ((b & 8u) << 25);
+}
+
+// Q5_0 unit = one block (32 weights).
+template <int R, int BT>
+__device__ __forceinline__ void unit_q50(const uint8_t* const* rowp, const uint8_t* const* auxp, int u, const float* x,
+                                         uint32_t ldx, int ncols, float (&acc)[R][BT]) {
+  uint4 q[R];
+  uint32_t qh[R];
+  float d[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    q[r] = ld_stream(rowp[r] + (size_t)u * 16);
+    const uint2 a = __ldg(reinterpret_cast<const uint2*>(auxp[r]) + u);
+    qh[r] = a.x;
+    d[r] = fp16_ref(a.y & 0xFFFFu);
+  }
+  const int base = u * 32;
+#pragma unroll
+  for (int b = 0; b < BT; b++) {
+    if (b >= ncols) break;
+    const float* xb = x + (size_t)b * ldx + base;
+    float xv[32];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      float4 a = ldg4(xb + 4 * i);
+      xv[4 * i] = a.x; xv[4 * i + 1] = a.y; xv[4 * i + 2] = a.z; xv[4 * i + 3] = a.w;
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint32_t wv[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t lo = (wv[i] & 0x0F0F0F0Fu) | spread4((qh[r] >> (4 * i)) & 0xFu);
+        const uint32_t hi = ((wv[i] >> 4) & 0x0F0F0F0Fu) | spread4((qh[r] >> (16 + 4 * i)) & 0xFu);
+        s0 = fmaf(byte_f<0>(lo, 8388624.f), xv[4 * i + 0], s0);
+        s1 = fmaf(byte_f<1>(lo, 8388624.f), xv[4 * i + 1], s1);
+        s0 = fmaf(byte_f<2>(lo, 8388624.f), xv[4 * i + 2], s0);
+        s1 = fmaf(byte_f<3>(lo, 8388624.f), xv[4 * i + 3], s1);
+        s0 = fmaf(byte_f<0>(hi, 8388624.f), xv[16 + 4 * i + 0], s0);
+        s1 = fmaf(byte_f<1>(hi, 8388624.f), xv[16 + 4 * i + 1], s1);
+        s0 = fmaf(byte_f<2>(hi, 8388624.f), xv[16 + 4 * i + 2], s0);
+        s1 = fmaf(byte_f<3>(hi, 8388624.f), xv[16 + 4 * i + 3], s1);
+      }
+      acc[r][b] += d[r] * (s0 + s1);
+    }
+  }
+}
+
+template <int QT, int R, int BT>
+__device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uint32_t ldx, int row0, int col0,
+                                          int ncols) {
+  const DWDesc& w = sg.w;
+  const int lane = threadIdx.x & 31;
+  const uint8_t* rowp[R];
+  const uint8_t* auxp[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const uint32_t o = min((uint32_t)(row0 + r), w.n_out - 1);
+    rowp[r] = w.body + (size_t)o * w.body_stride;
+    auxp[r] = w.aux + (size_t)o * w.aux_stride;
+  }
+  float acc[R][BT];
+#pragma unroll
+  for (int r = 0; r < R; r++)
+#pragma unroll
+    for (int b = 0; b < BT; b++) acc[r][b] = 0.f;
+  const float* xc = x + (size_t)col0 * ldx;
+  if (QT == 12) {
+    const int nu = (int)(w.n_in >> 8) * 8;
+    for (int u = lane; u < nu; u += 32) unit_q4k<R, BT>(rowp, u, xc, ldx, ncols, acc);
+  } else if (QT == 14) {
+    const int nu = (int)(w.n_in >> 8) * 4;
+    for (int u = lane; u < nu; u += 32) unit_q6k<R, BT>(rowp, auxp, u, xc, ldx, ncols, acc);
+  } else if (QT == 8) {
+    const int nu = (int)(w.n_in >> 5) * 2;
+    for (int u = lane; u < nu; u += 32) unit_q80<R, BT>(rowp, auxp, u, xc, ldx, ncols, acc);
+  } else {
+    const int nu = (int)(w.n_in >> 5);
+    for (int u = lane; u < nu; u += 32) unit_q50<R, BT>(rowp, auxp, u, xc, ldx, ncols, acc);
+  }
+#pragma unroll
+  for (int r = 0; r < R; r++)
+#pragma unroll
+    for (int b = 0; b < BT; b++) {
+      const float v = warp_sum(acc[r][b]);
+      const uint32_t o = (uint32_t)(row0 + r);
+      if (lane == 0 && o < w.n_out && b < ncols) {
+        float* dst = sg.y + (size_t)(col0 + b) * sg.ldy + o;
+        float res = v;
+        if (sg.bias) res = res + sg.bias[o];
+        if (sg.add) res = *dst + res;
+        *dst = res;
+      }
+    }
+}
+
+// grid.x = column tiles of BT (fastest, so CTAs sharing weights run together),
+// grid.y = CTAs over the concatenated rows of all segments.
+template <int R, int BT>
+__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(const __grid_constant__ GemvArgs a) {
+  const uint32_t cta = blockIdx.y;
+  GemvSeg sg = a.seg[0];
+  if (a.nseg > 1 && cta >= a.seg[1].cta_begin) sg = a.seg[1];
+  if (a.nseg > 2 && cta >= a.seg[2].cta_begin) sg = a.seg[2];
+  const int warp = threadIdx.x >> 5;
+  const int row0 = (int)(cta - sg.cta_begin) * (GEMV_WARPS * R) + warp * R;
+  if (row0 >= (int)sg.w.n_out) return;
+  const int col0 = blockIdx.x * BT;
+  const int ncols = min(BT, (int)a.batch - col0);
+  switch (sg.w.type) {
+    case 12: gemv_rows<12, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
+    case 14: gemv_rows<14, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
+    case 8: gemv_rows<8, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
+    case 6: gemv_rows<6, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
+  }
+}
+
+// ------------------------------------------------------------ launch ----
+static int rows_per_cta(uint32_t batch) { return GEMV_WARPS * (batch <= 1 ? 4 : 2); }
+
+// Fills cta_begin of each segment; returns the total CTA count along y.
+uint32_t gemv_plan(GemvArgs& a) {
+  const int rpc = rows_per_cta(a.batch);
+  uint32_t c = 0;
+  for (uint32_t i = 0; i < a.nseg; i++) {
+    a.seg[i].cta_begin = c;
+    c += (a.seg[i].w.n_out + rpc - 1) / rpc;
+  }
+  return c;
+}
+
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st) {
+  const uint32_t ny = gemv_plan(a);
+  const dim3 blk(GEMV_WARPS * 32);
+  if (a.batch == 1) gemv_kernel<4, 1><<<dim3(1, ny), blk, 0, st>>>(a);
+  else if (a.batch == 2) gemv_kernel<2, 2><<<dim3(1, ny), blk, 0, st>>>(a);
+  else if (a.batch <= 4) gemv_kernel<2, 4><<<dim3(1, ny), blk, 0, st>>>(a);
+  else gemv_kernel<2, 8><<<dim3((a.batch + 7) / 8, ny), blk, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st) {
+  size_t n = (size_t)w.n_out * w.n_in;
+  if (!n) return cudaSuccess;
+  dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx, cudaStream_t st) {
+  if (!rows) return cudaSuccess;
+  embed_kernel<<<dim3((w.n_in + 255) / 256, rows), 256, 0, st>>>(w, tokens, x, ldx);
+  return cudaGetLastError();
+}
+
+}  // namespace sm

@@ -1,0 +1,58 @@
+// Host-visible declarations of the engine's kernels and their launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "device.cuh"
+
+namespace sm {
+
+// One row of a forward pass (a token): which sequence it belongs to and its
+// absolute position.
+struct RowDesc {
+  uint32_t seq;
+  uint32_t pos;
+};
+
+// A sequence's KV storage: k/v are [n_layers][cap][kv_dim] f32.
+struct SeqDesc {
+  float* k;
+  float* v;
+  uint32_t cap;
+  uint32_t pad;
+};
+
+struct SampleParams {
+  float temperature;
+  int32_t top_k;  // < 0: None
+  float top_p;    // < 0: None
+  int32_t pad;
+};
+
+constexpr int SAMPLER_MAX_TOP_K = 1024;
+
+uint32_t gemv_plan(GemvArgs& a);
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st);
+cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st);
+cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
+                         cudaStream_t st);
+cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
+                           uint32_t rows, uint32_t n, float eps, cudaStream_t st);
+cudaError_t launch_rope_kv(float* q, const float* k, const float* v, uint32_t ldq, uint32_t ldkv, const RowDesc* rows,
+                           const SeqDesc* seqs, uint32_t nrows, uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd,
+                           const float* cos_t, const float* sin_t, cudaStream_t st);
+size_t attn_smem_bytes(uint32_t G, uint32_t hd);
+cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
+                             uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
+                             uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st);
+cudaError_t launch_silu_mul(float* gate, const float* up, size_t n, cudaStream_t st);
+cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const uint8_t* mask,
+                          const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
+                          RowDesc* advance, cudaStream_t st);
+
+cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
+                                 uint32_t cap_steps, cudaStream_t st);
+
+}  // namespace sm
