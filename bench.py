@@ -36,6 +36,7 @@ WORKLOADS = {
              "Llama-3-8B-shape Q4_K_M, 32 sequences, 1024 shared + 1024 own prompt tokens, T=1 top-k 40 top-p 0.9"),
 }
 HBM_FALLBACK_GBS = 6650.0
+GEMV_SHAPES = [(896, 4864), (3584, 18944), (4096, 14336), (8192, 28672)]  # BASELINE config 1 (M x K)
 
 
 def env_int(k, d):
@@ -194,6 +195,60 @@ def run_reference(args, rank, world, local_rank, barrier):
     }), flush=True)
 
 
+def run_gemv(args, rank, world, local_rank, barrier, allmax):
+    """Config 1: the dequant-fused GEMV alone, Q4_K and Q6_K, batch 1/8/32.
+    Each launch is timed between CUDA events after an L2 flush (a 512 MB
+    write), so every launch streams its weights from HBM."""
+    import torch
+    import smotor
+    torch.cuda.set_device(local_rank)
+    st = torch.cuda.current_stream()
+    # L2 flush by reading 512 MB: leaves clean lines, so no write-back lands in the timed launch
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    peak, peak_kind = peaks()
+    rng = np.random.default_rng(1)
+    rows = []
+    only = args.only.split(":") if args.only else None
+    for (M, K) in GEMV_SHAPES:
+        if only and only[0] != f"{M}x{K}":
+            continue
+        wf = rng.normal(0, 1, M * K).astype(np.float32)
+        for qt, name in ((smotor.Q4_K, "Q4_K"), (smotor.Q6_K, "Q6_K")):
+            if only and only[1] != name:
+                continue
+            w = smotor.DWeight(qt, smotor.quantize(qt, wf), M, K)
+            x = torch.randn(32, K, device="cuda")
+            y = torch.empty(32, M, device="cuda")
+            for b in (1, 8, 32):
+                if only and int(only[2]) != b:
+                    continue
+                times = []
+                for it in range(args.warmup + args.steps):
+                    flush.sum()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    w.gemv(x.data_ptr(), y.data_ptr(), b, st.cuda_stream)
+                    e1.record(st)
+                    e1.synchronize()
+                    if it >= args.warmup:
+                        times.append(e0.elapsed_time(e1))
+                ms = statistics.median(times)
+                nbytes = w.nbytes() + 4 * b * (K + M)
+                rows.append({"shape": f"{M}x{K}", "type": name, "batch": b, "us": ms * 1e3,
+                             "gbs": nbytes / (ms / 1e3) / 1e9, "frac": nbytes / (ms / 1e3) / 1e9 / peak})
+            w.free()
+    head = ([r for r in rows if r["shape"] == "3584x18944" and r["type"] == "Q4_K" and r["batch"] == 1] or rows)[0]
+    print(json.dumps({
+        "metric": "gemv_GBps", "value": head["gbs"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["us"] / 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (Q4_K/Q6_K weights)", "data": "synthetic N(0,1) weights, seed 1",
+        "config": {"workload": "gemv", "headline": "Q4_K 3584x18944 batch 1", "l2": "flushed before every launch",
+                   "results": rows},
+        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": head["gbs"] / peak, "traffic": None, "peak_source": peak_kind},
+    }), flush=True)
+
+
 def run_ours(args, rank, world, local_rank, barrier, allmax):
     import torch
     import smotor
@@ -281,8 +336,9 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=list(WORKLOADS))
+    ap.add_argument("--workload", default="cfg2", choices=list(WORKLOADS) + ["gemv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default="", help="gemv workload: one MxK:TYPE:batch case, e.g. 3584x18944:Q4_K:1")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = env_int("WORLD_SIZE", 1)
@@ -310,7 +366,7 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             return float(t.item())
     try:
-        run_ours(args, rank, world, local_rank, barrier, allmax)
+        (run_gemv if args.workload == "gemv" else run_ours)(args, rank, world, local_rank, barrier, allmax)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -7,17 +7,55 @@ namespace sm {
 
 // ---------------------------------------------------------------------------
 // HBM layout of one quantized weight [n_out x n_in] (row-major, a row = one
-// output). Rows of `body` start on 16-byte boundaries so every lane reads its
-// share of a row with 128-bit loads:
-//   Q4_K: body = the GGUF blocks unchanged (144 B = 9 x 16 B per 256 values).
-//   Q6_K: body = 208 B per block (ql 128 | qh 64 | scales 16), aux = fp16 d per
-//         block. The GGUF block is 210 B with d last (dequant.rs:178-182); the
-//         split only moves d so that blocks stay 16-byte aligned.
+// output). Every byte of the GGUF encoding is kept; only its order changes so
+// that the 32 lanes of a warp read 512 contiguous bytes per load. A row is a
+// sequence of groups of up to 8 consecutive 256-weight blocks (nbg blocks in
+// the last group); lane L = 4*bi + u works on block bi of a group.
+//   Q4_K group: [nbg headers x 16 B: d, dmin, 12 scale bytes]
+//               [qs round 0: 4*nbg lanes x 16 B][qs round 1: 4*nbg lanes x 16 B]
+//               lane 4bi+j holds qs bytes 32j..32j+15 (round 0) and
+//               32j+16..32j+31 (round 1) of block bi.   1152 B per 8 blocks.
+//   Q6_K group: [ql a: 4*nbg x 16 B][ql b: 4*nbg x 16 B][qh: 4*nbg x 16 B]
+//               [scales: nbg x 16 B][d: nbg x 2 B, padded to 16 B]
+//               lane 4bi+2n+c holds ql[64n+16c..] (a), ql[64n+32+16c..] (b) and
+//               qh[32n+16c..] of block bi.                 1680 B per 8 blocks.
 //   Q8_0: body = 32 B of qs per block, aux = fp16 d per block.
 //   Q5_0: body = 16 B of qs per block, aux = 8 B per block (qh u32 | d fp16 | 0).
-// Every byte of the GGUF encoding is kept; dequantization reads exactly the
-// reference's bytes.
+// The GGUF block formats are dequant.rs:66-206 (Q6_K keeps d last in GGUF).
 // ---------------------------------------------------------------------------
+#ifdef __CUDACC__
+#define SM_HD __host__ __device__ __forceinline__
+#else
+#define SM_HD inline
+#endif
+SM_HD uint32_t q4k_group_bytes(uint32_t nbg) { return 144u * nbg; }
+SM_HD uint32_t q6k_group_bytes(uint32_t nbg) { return 208u * nbg + (2u * nbg + 15u) / 16u * 16u; }
+SM_HD uint32_t q4k_row_bytes(uint32_t nb) { return nb / 8u * q4k_group_bytes(8) + q4k_group_bytes(nb % 8u); }
+SM_HD uint32_t q6k_row_bytes(uint32_t nb) {
+  return nb / 8u * q6k_group_bytes(8) + (nb % 8u ? q6k_group_bytes(nb % 8u) : 0u);
+}
+// Byte offsets inside a row for block b (of nb).
+struct KqPos {
+  uint32_t base, nbg, bi;
+};
+SM_HD KqPos kq_pos(uint32_t b, uint32_t nb, uint32_t group_bytes8) {
+  KqPos p;
+  p.base = (b >> 3) * group_bytes8;
+  p.nbg = nb - (b & ~7u) < 8u ? nb - (b & ~7u) : 8u;
+  p.bi = b & 7u;
+  return p;
+}
+SM_HD uint32_t q4k_hdr_off(const KqPos& p) { return p.base + 16u * p.bi; }
+SM_HD uint32_t q4k_qs_off(const KqPos& p, uint32_t j, uint32_t round) {
+  return p.base + 16u * p.nbg + 16u * (round * 4u * p.nbg + 4u * p.bi + j);
+}
+// part 0: ql a, 1: ql b, 2: qh
+SM_HD uint32_t q6k_q_off(const KqPos& p, uint32_t n, uint32_t c, uint32_t part) {
+  return p.base + 16u * (part * 4u * p.nbg + 4u * p.bi + 2u * n + c);
+}
+SM_HD uint32_t q6k_sc_off(const KqPos& p) { return p.base + 192u * p.nbg + 16u * p.bi; }
+SM_HD uint32_t q6k_d_off(const KqPos& p) { return p.base + 208u * p.nbg + 2u * p.bi; }
+
 struct DWDesc {
   const uint8_t* body;
   const uint8_t* aux;
@@ -42,7 +80,52 @@ struct GemvArgs {
   const float* x;  // x[b * ldx + d]
   uint32_t ldx;
   uint32_t batch;
+  // Batch 1 reads the activations in the lane order of its K-quant kernels
+  // (xperm_q4k / xperm_q6k below); both copies are written by the kernel
+  // that produced x.
+  const float* xp4;
+  const float* xp6;
 };
+
+// ---------------------------------------------------------------------------
+// Lane-interleaved activation layouts of the batch-1 GEMV. A warp step covers
+// 8 consecutive 256-weight blocks (2048 activations); lane L = 4*bi + u owns 64
+// activations of block bi and reads them as 16 float4 loads k = 0..15. The
+// float4 of (step t, k, lane) is stored at t*2048 + k*128 + 4*lane, so every
+// load instruction of the warp reads 512 contiguous bytes. Rows are padded to
+// whole steps: xperm_len(K) floats.
+//   Q4_K lane (bi, j):    float4 k = activations 64j + 4k .. +3 of the block
+//   Q6_K lane (bi, n, c): float4 k = 4g + i -> 128n + 16c + 32g + 4i .. +3
+// Inside each float4 the four activations e..e+3 are stored as (e, e+2, e+1,
+// e+3): the kernels turn bytes (0, 2) and (1, 3) of a weight word into one
+// half2 each, and the float4's halves are then their f32x2 partners.
+// ---------------------------------------------------------------------------
+#ifdef __CUDACC__
+__host__ __device__ __forceinline__
+#else
+inline
+#endif
+uint32_t xperm_len(uint32_t K) { return (K + 2047u) / 2048u * 2048u; }
+
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t xperm_q4k(uint32_t e) {
+  const uint32_t b = e >> 8, o = e & 255, t = b >> 3, bi = b & 7;
+  const uint32_t j = o >> 6, r = o & 63;
+  return t * 2048u + (r >> 2) * 128u + (4u * bi + j) * 4u + (((r & 1u) << 1) | ((r >> 1) & 1u));
+}
+__device__ __forceinline__ uint32_t xperm_q6k(uint32_t e) {
+  const uint32_t b = e >> 8, o = e & 255, t = b >> 3, bi = b & 7;
+  const uint32_t n = o >> 7, r1 = o & 127, g = r1 >> 5, r2 = r1 & 31, c = r2 >> 4, i = (r2 & 15) >> 2;
+  return t * 2048u + (4u * g + i) * 128u + (4u * bi + 2u * n + c) * 4u + (((r2 & 1u) << 1) | ((r2 >> 1) & 1u));
+}
+// Writes activation e of row `row` in the natural layout and both permuted ones.
+__device__ __forceinline__ void store_act(float* nat, uint32_t ldn, float* p4, float* p6, uint32_t ldp, uint32_t row,
+                                          uint32_t e, float v) {
+  if (nat) nat[(size_t)row * ldn + e] = v;
+  if (p4) p4[(size_t)row * ldp + xperm_q4k(e)] = v;
+  if (p6) p6[(size_t)row * ldp + xperm_q6k(e)] = v;
+}
+#endif
 
 #ifdef __CUDACC__
 // fp16 bit pattern -> f32 as the reference decodes it (dequant.rs:12-33):

@@ -7,6 +7,7 @@
 // (crates/s-models/src/state.rs:202-361).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <map>
@@ -57,24 +58,40 @@ int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_
   const uint64_t nb = n_in / bs, row_src = nb * tb;
   uint64_t body_stride = 0, aux_stride = 0;
   switch (type) {
-    case QT_Q4K: body_stride = nb * 144; break;
-    case QT_Q6K: body_stride = nb * 208; aux_stride = nb * 2; break;
+    case QT_Q4K: body_stride = q4k_row_bytes((uint32_t)nb); break;
+    case QT_Q6K: body_stride = q6k_row_bytes((uint32_t)nb); break;
     case QT_Q8_0: body_stride = nb * 32; aux_stride = nb * 2; break;
     case QT_Q5_0: body_stride = nb * 16; aux_stride = nb * 8; break;
   }
   aux_stride = (aux_stride + 15) / 16 * 16;
   const uint64_t body_bytes = body_stride * n_out, aux_bytes = aux_stride * n_out;
-  std::vector<uint8_t> body(body_bytes), aux(aux_bytes);
+  std::vector<uint8_t> body(body_bytes, 0), aux(aux_bytes, 0);
   for (uint64_t o = 0; o < n_out; o++) {
     const uint8_t* r = src + o * row_src;
     uint8_t* bd = body.data() + o * body_stride;
     uint8_t* ax = aux.data() + o * aux_stride;
     switch (type) {
-      case QT_Q4K: std::memcpy(bd, r, row_src); break;
+      case QT_Q4K:  // groups of 8 blocks, lane-interleaved qs (device.cuh)
+        for (uint32_t b = 0; b < nb; b++) {
+          const uint8_t* blk = r + (size_t)b * 144;
+          const KqPos ps = kq_pos(b, (uint32_t)nb, q4k_group_bytes(8));
+          std::memcpy(bd + q4k_hdr_off(ps), blk, 16);
+          for (uint32_t j = 0; j < 4; j++)
+            for (uint32_t rd = 0; rd < 2; rd++) std::memcpy(bd + q4k_qs_off(ps, j, rd), blk + 16 + 32 * j + 16 * rd, 16);
+        }
+        break;
       case QT_Q6K:
-        for (uint64_t b = 0; b < nb; b++) {
-          std::memcpy(bd + b * 208, r + b * 210, 208);
-          std::memcpy(ax + b * 2, r + b * 210 + 208, 2);
+        for (uint32_t b = 0; b < nb; b++) {
+          const uint8_t* blk = r + (size_t)b * 210;  // ql 128 | qh 64 | scales 16 | d 2
+          const KqPos ps = kq_pos(b, (uint32_t)nb, q6k_group_bytes(8));
+          for (uint32_t n = 0; n < 2; n++)
+            for (uint32_t c = 0; c < 2; c++) {
+              std::memcpy(bd + q6k_q_off(ps, n, c, 0), blk + 64 * n + 16 * c, 16);
+              std::memcpy(bd + q6k_q_off(ps, n, c, 1), blk + 64 * n + 32 + 16 * c, 16);
+              std::memcpy(bd + q6k_q_off(ps, n, c, 2), blk + 128 + 32 * n + 16 * c, 16);
+            }
+          std::memcpy(bd + q6k_sc_off(ps), blk + 192, 16);
+          std::memcpy(bd + q6k_d_off(ps), blk + 208, 2);
         }
         break;
       case QT_Q8_0:
@@ -168,6 +185,8 @@ struct sm_model {
   // workspace
   float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
         *u = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr;
+  // permuted copies of the GEMV inputs for batch 1 (xperm_q4k / xperm_q6k)
+  float *xn4 = nullptr, *xn6 = nullptr, *att4 = nullptr, *att6 = nullptr, *g4 = nullptr, *g6 = nullptr;
   uint8_t* mask_dev = nullptr;
   void* in_dev = nullptr;   // StepIn block on the device
   void* in_host = nullptr;  // pinned
@@ -183,6 +202,9 @@ struct sm_model {
   uint32_t* hist_ctr = nullptr;
   std::mutex mu;
   uint64_t weight_bytes = 0;
+  // The user's handle and every live cache hold a reference; the model (and
+  // its device memory) is destroyed when the last one is released.
+  std::atomic<int> refs{1};
 };
 
 namespace {
@@ -364,6 +386,13 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
       (rc = dev_alloc(m, (void**)&m->part_ml, (size_t)R * c.n_heads * m->max_splits * 2 * 4)) ||
       (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)))
     return rc;
+  {
+    const size_t pH = (size_t)R * xperm_len((uint32_t)H), pF = (size_t)R * xperm_len((uint32_t)F);
+    if ((rc = dev_alloc(m, (void**)&m->xn4, pH * 4)) || (rc = dev_alloc(m, (void**)&m->xn6, pH * 4)) ||
+        (rc = dev_alloc(m, (void**)&m->att4, pH * 4)) || (rc = dev_alloc(m, (void**)&m->att6, pH * 4)) ||
+        (rc = dev_alloc(m, (void**)&m->g4, pF * 4)) || (rc = dev_alloc(m, (void**)&m->g6, pF * 4)))
+      return rc;
+  }
   m->in_bytes = step_in_bytes(R);
   m->out_bytes = step_out_bytes(R);
   if ((rc = dev_alloc(m, &m->in_dev, m->in_bytes)) || (rc = dev_alloc(m, &m->out_dev, m->out_bytes)) ||
@@ -415,14 +444,22 @@ GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, bool add) {
 cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
   const sm_config& c = m->c;
   const uint32_t H = (uint32_t)c.n_embd, F = (uint32_t)c.n_ff, kvd = m->kvd, hd = (uint32_t)c.head_dim;
+  // batch 1 reads permuted activations; larger batches the natural layout
+  const bool b1 = nrows == 1;
+  float* xn4 = b1 ? m->xn4 : nullptr;
+  float* xn6 = b1 ? m->xn6 : nullptr;
+  float* att4 = b1 ? m->att4 : nullptr;
+  float* att6 = b1 ? m->att6 : nullptr;
+  float* g4 = b1 ? m->g4 : nullptr;
+  float* g6 = b1 ? m->g6 : nullptr;
   cudaError_t e;
 #define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
   RK(launch_embed(m->tok_embd.d, m->din.tok, nrows, m->x, H, st));
   for (uint32_t li = 0; li < c.n_layers; li++) {
     const Layer& L = m->layers[li];
-    RK(launch_rmsnorm(m->x, H, nullptr, L.attn_norm, m->xn, H, nrows, H, c.rms_eps, st));
+    RK(launch_rmsnorm(m->x, H, nullptr, L.attn_norm, m->xn, H, xn4, xn6, nrows, H, c.rms_eps, st));
     GemvArgs a{};
-    a.x = m->xn; a.ldx = H; a.batch = nrows; a.nseg = 3;
+    a.x = m->xn; a.ldx = H; a.batch = nrows; a.nseg = 3; a.xp4 = xn4; a.xp6 = xn6;
     a.seg[0] = seg(L.wq, m->q, H, L.bq, false);
     a.seg[1] = seg(L.wk, m->k, kvd, L.bk, false);
     a.seg[2] = seg(L.wv, m->v, kvd, L.bv, false);
@@ -430,27 +467,29 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     RK(launch_rope_kv(m->q, m->k, m->v, H, kvd, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads,
                       (uint32_t)c.n_kv_heads, hd, m->cos_t, m->sin_t, st));
     RK(launch_attention(m->q, H, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads, (uint32_t)c.n_kv_heads, hd,
-                        m->part_o, m->part_ml, m->max_splits, m->att, H, st));
+                        m->part_o, m->part_ml, m->max_splits, m->att, H, att4, att6, st));
     GemvArgs o{};
-    o.x = m->att; o.ldx = H; o.batch = nrows; o.nseg = 1;
+    o.x = m->att; o.ldx = H; o.batch = nrows; o.nseg = 1; o.xp4 = att4; o.xp6 = att6;
     o.seg[0] = seg(L.wo, m->x, H, nullptr, true);
     RK(launch_gemv(o, st));
-    RK(launch_rmsnorm(m->x, H, nullptr, L.ffn_norm, m->xn, H, nrows, H, c.rms_eps, st));
+    RK(launch_rmsnorm(m->x, H, nullptr, L.ffn_norm, m->xn, H, xn4, xn6, nrows, H, c.rms_eps, st));
     GemvArgs gu{};
-    gu.x = m->xn; gu.ldx = H; gu.batch = nrows; gu.nseg = 2;
+    gu.x = m->xn; gu.ldx = H; gu.batch = nrows; gu.nseg = 2; gu.xp4 = xn4; gu.xp6 = xn6;
     gu.seg[0] = seg(L.wgate, m->g, F, nullptr, false);
     gu.seg[1] = seg(L.wup, m->u, F, nullptr, false);
     RK(launch_gemv(gu, st));
-    RK(launch_silu_mul(m->g, m->u, (size_t)nrows * F, st));
+    RK(launch_silu_mul(m->g, m->u, F, (size_t)nrows * F, g4, g6, st));
     GemvArgs dn{};
-    dn.x = m->g; dn.ldx = F; dn.batch = nrows; dn.nseg = 1;
+    dn.x = m->g; dn.ldx = F; dn.batch = nrows; dn.nseg = 1; dn.xp4 = g4; dn.xp6 = g6;
     dn.seg[0] = seg(L.wdown, m->x, H, nullptr, true);
     RK(launch_gemv(dn, st));
   }
   if (nsel) {
-    RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
+    const bool h1 = nsel == 1;
+    RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, h1 ? m->xn4 : nullptr, h1 ? m->xn6 : nullptr, nsel,
+                      H, c.rms_eps, st));
     GemvArgs hd_{};
-    hd_.x = m->xn; hd_.ldx = H; hd_.batch = nsel; hd_.nseg = 1;
+    hd_.x = m->xn; hd_.ldx = H; hd_.batch = nsel; hd_.nseg = 1; hd_.xp4 = m->xn4; hd_.xp6 = m->xn6;
     hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, false);
     RK(launch_gemv(hd_, st));
   }
@@ -590,6 +629,10 @@ int guard_model(const sm_model* m) {
   return SM_OK;
 }
 
+void model_release(sm_model* m) {
+  if (m && m->refs.fetch_sub(1) == 1) destroy_model(m);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- C ABI ----
@@ -635,7 +678,7 @@ int sm_model_load_memory(const void* buf, uint64_t len, const sm_load_opts* opts
 }
 
 int sm_model_free(sm_model* m) {
-  destroy_model(m);
+  model_release(m);
   return SM_OK;
 }
 
@@ -702,18 +745,23 @@ int sm_cache_new(sm_model* m, uint64_t max_seq, sm_cache** out) {
   c->cap = max_seq;
   int rc = alloc_kv(m, max_seq, &c->k, &c->v);
   if (rc) { delete c; return rc; }
+  m->refs++;
   *out = c;
   return SM_OK;
 }
 
 int sm_cache_free(sm_cache* c) {
   if (!c) return SM_OK;
-  std::lock_guard<std::mutex> lk(c->m->mu);
-  cudaSetDevice(c->m->device);
-  cudaStreamSynchronize(c->m->stream);
-  cudaFree(c->k);
-  cudaFree(c->v);
-  delete c;
+  sm_model* m = c->m;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    cudaFree(c->k);
+    cudaFree(c->v);
+    delete c;
+  }
+  model_release(m);
   return SM_OK;
 }
 
@@ -778,6 +826,7 @@ int sm_cache_clone(const sm_cache* c, sm_cache** out) {
   int rc = alloc_kv(m, c->cap, &n->k, &n->v);
   if (!rc) rc = copy_kv(m, n->k, n->v, n->cap, c->k, c->v, c->cap, c->len);
   if (rc) { if (n->k) { cudaFree(n->k); cudaFree(n->v); } delete n; return rc; }
+  m->refs++;
   *out = n;
   return SM_OK;
 }
@@ -949,6 +998,7 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
 struct sm_dweight {
   DW w;
   int device;
+  float* xp = nullptr;  // permuted activations for batch 1 (both layouts), allocated on first use
 };
 
 int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t n_in, sm_dweight** out) {
@@ -964,6 +1014,7 @@ int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t
 }
 int sm_dweight_free(sm_dweight* w) {
   if (!w) return SM_OK;
+  if (w->xp) cudaFree(w->xp);
   free_weight(w->w);
   delete w;
   return SM_OK;
@@ -988,6 +1039,13 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
   a.batch = (uint32_t)batch;
   a.nseg = 1;
   a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, false);
+  if (batch == 1) {
+    const uint32_t lp = xperm_len(w->w.d.n_in);
+    if (!w->xp) CK(cudaMalloc((void**)&w->xp, 2 * (size_t)lp * 4));
+    a.xp4 = w->xp;
+    a.xp6 = w->xp + lp;
+    CK(launch_xpack(x_dev, w->w.d.n_in, w->w.d.n_in, 1, w->xp, w->xp + lp, (cudaStream_t)stream));
+  }
   CK(launch_gemv(a, (cudaStream_t)stream));
   return SM_OK;
 }

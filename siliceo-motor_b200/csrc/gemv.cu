@@ -10,6 +10,8 @@
 // (sum x*(d*sc*q - dmin*m) = d*sc*sum(q*x) - dmin*m*sum(x)), so the inner
 // loop is one exact int->float conversion and one FMA per weight; the result
 // differs from the reference's sequential sum by rounding only.
+#include <cuda_fp16.h>
+
 #include "device.cuh"
 
 namespace sm {
@@ -34,26 +36,27 @@ __device__ float dequant_elem(const DWDesc& w, uint32_t o, uint32_t e) {
   const uint8_t* row = w.body + (size_t)o * w.body_stride;
   switch (w.type) {
     case 12: {  // Q4_K, dequant.rs:98-124
-      uint32_t blk = e >> 8, l = e & 255, g = l >> 6, within = l & 63;
-      const uint8_t* b = row + (size_t)blk * 144;
-      float d = fp16_ref(rd16(b)), dmin = fp16_ref(rd16(b + 2));
+      const uint32_t blk = e >> 8, l = e & 255, g = l >> 6, within = l & 63, w31 = within & 31;
+      const KqPos ps = kq_pos(blk, w.n_in >> 8, q4k_group_bytes(8));
+      const uint8_t* h = row + q4k_hdr_off(ps);
+      float d = fp16_ref(rd16(h)), dmin = fp16_ref(rd16(h + 2));
       uint32_t is = 2 * g + (within >= 32), sc, m;
-      scale_min_k4((int)is, b + 4, &sc, &m);
-      uint32_t qb = b[16 + 32 * g + (within & 31)];
+      scale_min_k4((int)is, h + 4, &sc, &m);
+      uint32_t qb = row[q4k_qs_off(ps, g, w31 >> 4) + (w31 & 15)];
       uint32_t q = within < 32 ? (qb & 0x0F) : (qb >> 4);
       float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
       return __fsub_rn(__fmul_rn(d1, (float)q), m1);
     }
     case 14: {  // Q6_K, dequant.rs:178-206
-      uint32_t blk = e >> 8, l = e & 255, n = l >> 7, wl = l & 127, k = wl >> 5, ll = wl & 31, is = ll >> 4;
-      const uint8_t* b = row + (size_t)blk * 208;
-      float d = fp16_ref(rd16(w.aux + (size_t)o * w.aux_stride + blk * 2));
+      const uint32_t blk = e >> 8, l = e & 255, n = l >> 7, wl = l & 127, k = wl >> 5, ll = wl & 31, is = ll >> 4;
+      const KqPos ps = kq_pos(blk, w.n_in >> 8, q6k_group_bytes(8));
+      float d = fp16_ref(rd16(row + q6k_d_off(ps)));
       if (!isfinite(d)) return 0.0f;
-      uint32_t qlb = b[n * 64 + ll + ((k & 1) ? 32 : 0)];
+      uint32_t qlb = row[q6k_q_off(ps, n, is, (k & 1) ? 1 : 0) + (ll & 15)];
       uint32_t nib = (k & 2) ? (qlb >> 4) : (qlb & 0x0F);
-      uint32_t hb = (b[128 + n * 32 + ll] >> (2 * k)) & 3;
+      uint32_t hb = (row[q6k_q_off(ps, n, is, 2) + (ll & 15)] >> (2 * k)) & 3;
       int32_t q = (int32_t)(nib | (hb << 4)) - 32;
-      float sc = (float)(int8_t)b[192 + n * 8 + is + 2 * k];
+      float sc = (float)(int8_t)row[q6k_sc_off(ps) + n * 8 + is + 2 * k];
       return __fmul_rn(__fmul_rn(d, sc), (float)q);
     }
     case 8: {  // Q8_0, dequant.rs:66-71
@@ -98,15 +101,16 @@ __global__ void embed_kernel(DWDesc w, const uint32_t* tokens, float* x, uint32_
 // Q4_K unit = 16 bytes of qs (32 weights: 16 of sub-block 2j, 16 of 2j+1)
 // plus the block header (d, dmin, 12 scale bytes) read as one 16-byte load.
 template <int R, int BT>
-__device__ __forceinline__ void unit_q4k(const uint8_t* const* rowp, int u, const float* x, uint32_t ldx, int ncols,
-                                         float (&acc)[R][BT]) {
+__device__ __forceinline__ void unit_q4k(const uint8_t* const* rowp, int u, uint32_t nb, const float* x, uint32_t ldx,
+                                         int ncols, float (&acc)[R][BT]) {
   const int blk = u >> 3, p = u & 7, j = p >> 1;
+  const KqPos ps = kq_pos((uint32_t)blk, nb, q4k_group_bytes(8));
+  const uint32_t ho = q4k_hdr_off(ps), qo = q4k_qs_off(ps, (uint32_t)j, (uint32_t)(p & 1));
   uint4 hd[R], qs[R];
 #pragma unroll
   for (int r = 0; r < R; r++) {
-    const uint8_t* b = rowp[r] + (size_t)blk * 144;
-    hd[r] = ld_stream(b);
-    qs[r] = ld_stream(b + 16 + p * 16);
+    hd[r] = ld_stream(rowp[r] + ho);
+    qs[r] = ld_stream(rowp[r] + qo);
   }
   float d1[R], m1[R], d2[R], m2[R];
 #pragma unroll
@@ -171,19 +175,20 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* const* rowp, int u, cons
 // Q6_K unit = 64 weights of one block: half n, 16-column slice c, all four
 // 32-row groups (ql 2 x 16 B + qh 16 B + 4 scale bytes + d).
 template <int R, int BT>
-__device__ __forceinline__ void unit_q6k(const uint8_t* const* rowp, const uint8_t* const* auxp, int u, const float* x,
-                                         uint32_t ldx, int ncols, float (&acc)[R][BT]) {
+__device__ __forceinline__ void unit_q6k(const uint8_t* const* rowp, int u, uint32_t nb, const float* x, uint32_t ldx,
+                                         int ncols, float (&acc)[R][BT]) {
   const int blk = u >> 2, n = (u >> 1) & 1, c = u & 1;
+  const KqPos ps = kq_pos((uint32_t)blk, nb, q6k_group_bytes(8));
   uint4 qa[R], qb[R], qh[R];
   float ds[R][4];
 #pragma unroll
   for (int r = 0; r < R; r++) {
-    const uint8_t* b = rowp[r] + (size_t)blk * 208;
-    qa[r] = ld_stream(b + n * 64 + c * 16);
-    qb[r] = ld_stream(b + n * 64 + 32 + c * 16);
-    qh[r] = ld_stream(b + 128 + n * 32 + c * 16);
-    const uint2 scw = __ldg(reinterpret_cast<const uint2*>(b + 192 + n * 8));
-    float d = fp16_ref(__ldg(reinterpret_cast<const unsigned short*>(auxp[r]) + blk));
+    const uint8_t* b = rowp[r];
+    qa[r] = ld_stream(b + q6k_q_off(ps, n, c, 0));
+    qb[r] = ld_stream(b + q6k_q_off(ps, n, c, 1));
+    qh[r] = ld_stream(b + q6k_q_off(ps, n, c, 2));
+    const uint2 scw = __ldg(reinterpret_cast<const uint2*>(b + q6k_sc_off(ps) + n * 8));
+    float d = fp16_ref(__ldg(reinterpret_cast<const unsigned short*>(b + q6k_d_off(ps))));
     if (!isfinite(d)) d = 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
     const uint32_t s0 = c ? (scw.x >> 8) : scw.x, s1 = c ? (scw.y >> 8) : scw.y;
     ds[r][0] = d * (float)(int8_t)(s0 & 0xFF);
@@ -339,13 +344,14 @@ __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uin
 #pragma unroll
     for (int b = 0; b < BT; b++) acc[r][b] = 0.f;
   const float* xc = x + (size_t)col0 * ldx;
-  if (QT == 12) {
+  const uint32_t qt = QT ? (uint32_t)QT : w.type;
+  if (qt == 12) {
     const int nu = (int)(w.n_in >> 8) * 8;
-    for (int u = lane; u < nu; u += 32) unit_q4k<R, BT>(rowp, u, xc, ldx, ncols, acc);
-  } else if (QT == 14) {
+    for (int u = lane; u < nu; u += 32) unit_q4k<R, BT>(rowp, u, w.n_in >> 8, xc, ldx, ncols, acc);
+  } else if (qt == 14) {
     const int nu = (int)(w.n_in >> 8) * 4;
-    for (int u = lane; u < nu; u += 32) unit_q6k<R, BT>(rowp, auxp, u, xc, ldx, ncols, acc);
-  } else if (QT == 8) {
+    for (int u = lane; u < nu; u += 32) unit_q6k<R, BT>(rowp, u, w.n_in >> 8, xc, ldx, ncols, acc);
+  } else if (qt == 8) {
     const int nu = (int)(w.n_in >> 5) * 2;
     for (int u = lane; u < nu; u += 32) unit_q80<R, BT>(rowp, auxp, u, xc, ldx, ncols, acc);
   } else {
@@ -366,6 +372,190 @@ __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uin
         *dst = res;
       }
     }
+}
+
+// ------------------------------------------------------ batch-1 GEMV ----
+// Batch 1 is the decode hot path. A lane owns 64 weights of one 256-weight
+// block per row (Q4_K: the 32 qs bytes of one sub-block pair; Q6_K: one
+// (half, 16-column) slice of all four 32-row groups) and the warp owns R rows
+// that share the lane's 64 activations. Two weights at a time become exact
+// f32 values with one LOP3 (two fields into the mantissas of a half2 of
+// 1024 + q), one half2 subtract and two f16->f32 converts, and are multiplied
+// into f32x2 accumulators with packed FMAs. The activations arrive
+// pre-permuted (xperm_q4k / xperm_q6k) so every load is coalesced and each
+// float4 holds the partners of bytes (0,2) and (1,3). The GGUF block header
+// is decoded once per 64 weights per row.
+
+// fp16 -> f32 with the reference's NaN -> +-Inf quirk (dequant.rs:25-26).
+__device__ __forceinline__ float h2f_ref(uint32_t h) {
+  const float v = __half2float(__ushort_as_half((unsigned short)h));
+  return ((h & 0x7C00u) == 0x7C00u) ? __uint_as_float(((h & 0x8000u) << 16) | 0x7F800000u) : v;
+}
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+// v = two halves (off + a, off + b), exact: returns (a, b) in f32.
+__device__ __forceinline__ float2 hpair(uint32_t v, __half2 off) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  return __half22float2(__hsub2(h, off));
+}
+// acc01 += pair(bytes 0,2) * (x.x, x.y); acc23 += pair(bytes 1,3) * (x.z, x.w)
+// where pair p02/p13 are half2 of (off + q) for the word's byte fields.
+__device__ __forceinline__ void fma_pairs(uint32_t p02, uint32_t p13, const float4& xv, __half2 off, float2& a0,
+                                          float2& a1) {
+  a0 = __ffma2_rn(hpair(p02, off), f2(xv.x, xv.y), a0);
+  a1 = __ffma2_rn(hpair(p13, off), f2(xv.z, xv.w), a1);
+}
+__device__ __forceinline__ float hsum(const float2& a, const float2& b) { return (a.x + a.y) + (b.x + b.y); }
+__device__ __forceinline__ float sum4(const float4& v) { return (v.x + v.y) + (v.z + v.w); }
+
+template <int R>
+__device__ __forceinline__ void q4k_b1(const DWDesc& w, const float* __restrict__ x, int row0, int slice, int nslice,
+                                       float (&acc)[R]) {
+  const int lane = threadIdx.x & 31, bi = lane >> 2, j = lane & 3;
+  const int nb = (int)(w.n_in >> 8);
+  const uint8_t* rowp[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) rowp[r] = w.body + (size_t)min((uint32_t)(row0 + r), w.n_out - 1) * w.body_stride;
+  // scale/min bit positions of sub-blocks 2j and 2j+1 (get_scale_min_k4, dequant.rs:41-49)
+  const int sh = 16 * (j & 1);
+  const bool hi6 = j >= 2;
+  const uint32_t lo_mask = hi6 ? 0x0Fu : 0x3Fu, hi_mask = hi6 ? 0x30u : 0u;
+  const int m_off = hi6 ? 4 : 0;
+  const __half2 off = __floats2half2_rn(1024.f, 1024.f);
+  for (int b = bi + 8 * slice; b < nb; b += 8 * nslice) {
+    const KqPos ps = kq_pos((uint32_t)b, (uint32_t)nb, q4k_group_bytes(8));
+    const uint32_t ho = q4k_hdr_off(ps), q0 = q4k_qs_off(ps, (uint32_t)j, 0), q1 = q4k_qs_off(ps, (uint32_t)j, 1);
+    uint4 hd[R], qa[R], qb[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      hd[r] = ld_stream(rowp[r] + ho);
+      qa[r] = ld_stream(rowp[r] + q0);
+      qb[r] = ld_stream(rowp[r] + q1);
+    }
+    const float* xs = x + (size_t)(b >> 3) * 2048 + 4 * lane;  // xperm_q4k layout
+#pragma unroll
+    for (int half = 0; half < 2; half++) {  // 0: low nibbles = sub-block 2j, 1: high nibbles (x16) = 2j+1
+      float4 xv[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) xv[i] = ldg4(xs + (8 * half + i) * 128);
+      float sx = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) sx += sum4(xv[i]);
+      const uint32_t nm = half ? 0x00F000F0u : 0x000F000Fu;
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint32_t wv[8] = {qa[r].x, qa[r].y, qa[r].z, qa[r].w, qb[r].x, qb[r].y, qb[r].z, qb[r].w};
+        float2 a0 = f2(0.f, 0.f), a1 = a0;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          fma_pairs((wv[i] & nm) | 0x64006400u, ((wv[i] >> 8) & nm) | 0x64006400u, xv[i], off, a0, a1);
+        const float d = h2f_ref(hd[r].x & 0xFFFFu), dmin = h2f_ref(hd[r].x >> 16);
+        const uint32_t ss = hi6 ? hd[r].w : hd[r].y, sm = hi6 ? hd[r].w : hd[r].z;
+        const int o8 = 8 * half;
+        const uint32_t sc = ((ss >> (sh + o8)) & lo_mask) | ((hd[r].y >> (sh + 2 + o8)) & hi_mask);
+        const uint32_t mn = ((sm >> (sh + o8 + m_off)) & lo_mask) | ((hd[r].z >> (sh + 2 + o8)) & hi_mask);
+        const float ds = half ? d * 0.0625f : d;  // high nibbles were summed as 16*q
+        acc[r] = fmaf(-(dmin * (float)mn), sx, fmaf(ds * (float)sc, hsum(a0, a1), acc[r]));
+      }
+    }
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void q6k_b1(const DWDesc& w, const float* __restrict__ x, int row0, int slice, int nslice,
+                                       float (&acc)[R]) {
+  const int lane = threadIdx.x & 31, bi = lane >> 2, n = (lane >> 1) & 1, c = lane & 1;
+  const int nb = (int)(w.n_in >> 8);
+  const uint8_t* rowp[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) rowp[r] = w.body + (size_t)min((uint32_t)(row0 + r), w.n_out - 1) * w.body_stride;
+  const __half2 off = __floats2half2_rn(1056.f, 1056.f);  // 1024 + 32: yields q - 32
+  for (int b = bi + 8 * slice; b < nb; b += 8 * nslice) {
+    const KqPos ps = kq_pos((uint32_t)b, (uint32_t)nb, q6k_group_bytes(8));
+    const uint32_t oa = q6k_q_off(ps, n, c, 0), ob = q6k_q_off(ps, n, c, 1), oh = q6k_q_off(ps, n, c, 2);
+    const uint32_t os = q6k_sc_off(ps) + 8 * n, od = q6k_d_off(ps);
+    uint4 qa[R], qb[R], qh[R];
+    uint2 sc[R];
+    uint32_t dh[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      qa[r] = ld_stream(rowp[r] + oa);
+      qb[r] = ld_stream(rowp[r] + ob);
+      qh[r] = ld_stream(rowp[r] + oh);
+      sc[r] = __ldg(reinterpret_cast<const uint2*>(rowp[r] + os));
+      dh[r] = __ldg(reinterpret_cast<const unsigned short*>(rowp[r] + od));
+    }
+    const float* xs = x + (size_t)(b >> 3) * 2048 + 4 * lane;  // xperm_q6k layout
+#pragma unroll
+    for (int g = 0; g < 4; g++) {  // group g: rows 32g.. of the slice, scale sc[n*8 + c + 2g]
+      float4 xv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) xv[i] = ldg4(xs + (4 * g + i) * 128);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint32_t src[4] = {(g & 1) ? qb[r].x : qa[r].x, (g & 1) ? qb[r].y : qa[r].y,
+                                 (g & 1) ? qb[r].z : qa[r].z, (g & 1) ? qb[r].w : qa[r].w};
+        const uint32_t hv[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
+        float2 p0 = f2(0.f, 0.f), p1 = p0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          // 6-bit q per byte: nibble | 2 high bits << 4 (dequant.rs:195-198)
+          const uint32_t nib = g < 2 ? (src[i] & 0x0F0F0F0Fu) : ((src[i] >> 4) & 0x0F0F0F0Fu);
+          const int hs = 4 - 2 * g;  // qh bits 2g, 2g+1 -> bits 4, 5
+          const uint32_t q = nib | ((hs >= 0 ? (hv[i] << hs) : (hv[i] >> -hs)) & 0x30303030u);
+          fma_pairs((q & 0x003F003Fu) | 0x64006400u, ((q >> 8) & 0x003F003Fu) | 0x64006400u, xv[i], off, p0, p1);
+        }
+        float d = h2f_ref(dh[r]);
+        if (!isfinite(d)) d = 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
+        const uint32_t sw = (g < 2 ? sc[r].x : sc[r].y) >> (8 * c + 16 * (g & 1));
+        acc[r] = fmaf(d * (float)(int8_t)(sw & 0xFF), hsum(p0, p1), acc[r]);
+      }
+    }
+  }
+}
+
+constexpr int B1_R = 4;
+constexpr int B1_WARPS = 8;
+
+// CTA = 8 warps = (8/S) row groups of B1_R rows x S slices of each row's
+// blocks (slice s takes blocks 8s.., stride 8S); partial sums meet in smem.
+__global__ void __launch_bounds__(B1_WARPS * 32, 2) gemv1_kernel(const __grid_constant__ GemvArgs a, int nslice) {
+  const uint32_t cta = blockIdx.y;
+  GemvSeg sg = a.seg[0];
+  if (a.nseg > 1 && cta >= a.seg[1].cta_begin) sg = a.seg[1];
+  if (a.nseg > 2 && cta >= a.seg[2].cta_begin) sg = a.seg[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = B1_WARPS / nslice, grp = warp / nslice, slice = warp - grp * nslice;
+  const int row0 = (int)(cta - sg.cta_begin) * (groups * B1_R) + grp * B1_R;
+  __shared__ float red[B1_WARPS][B1_R];
+  float acc[B1_R];
+#pragma unroll
+  for (int r = 0; r < B1_R; r++) acc[r] = 0.f;
+  if (row0 < (int)sg.w.n_out) {
+    if (sg.w.type == 12) {
+      q4k_b1<B1_R>(sg.w, a.xp4, row0, slice, nslice, acc);
+    } else if (sg.w.type == 14) {
+      q6k_b1<B1_R>(sg.w, a.xp6, row0, slice, nslice, acc);
+    } else if (slice == 0) {
+      gemv_rows<0, B1_R, 1>(sg, a.x, a.ldx, row0, 0, 1);  // Q8_0 / Q5_0: generic units, unsplit
+    }
+  }
+  if (sg.w.type != 12 && sg.w.type != 14) return;
+#pragma unroll
+  for (int r = 0; r < B1_R; r++) {
+    const float v = warp_sum(acc[r]);
+    if (lane == 0) red[warp][r] = v;
+  }
+  __syncthreads();
+  if (slice == 0 && lane < B1_R) {
+    const uint32_t o = (uint32_t)(row0 + lane);
+    if (row0 < (int)sg.w.n_out && o < sg.w.n_out) {
+      float v = 0.f;
+      for (int k = 0; k < nslice; k++) v += red[warp + k][lane];
+      if (sg.bias) v = v + sg.bias[o];
+      if (sg.add) v = sg.y[o] + v;
+      sg.y[o] = v;
+    }
+  }
 }
 
 // grid.x = column tiles of BT (fastest, so CTAs sharing weights run together),
@@ -389,12 +579,35 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(const __grid_cons
   }
 }
 
+// Writes rows of natural-layout activations in both permuted layouts.
+__global__ void xpack_kernel(const float* x, uint32_t ldx, uint32_t K, float* p4, float* p6, uint32_t ldp) {
+  const uint32_t r = blockIdx.y;
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < K; e += gridDim.x * blockDim.x)
+    store_act(nullptr, 0, p4, p6, ldp, r, e, x[(size_t)r * ldx + e]);
+}
+
 // ------------------------------------------------------------ launch ----
-static int rows_per_cta(uint32_t batch) { return GEMV_WARPS * (batch <= 1 ? 4 : 2); }
+// K-slices per row for batch 1: enough warps to cover every SM several times,
+// at least one 8-block step per slice.
+static int b1_slices(const GemvArgs& a) {
+  uint32_t rows = 0;
+  for (uint32_t i = 0; i < a.nseg; i++) rows += a.seg[i].w.n_out;
+  const uint32_t nb = a.seg[0].w.n_in >> 8;
+  int s = 1;
+  while (s < B1_WARPS && (rows / B1_R) * s < 148u * 24u && nb >= 8u * (uint32_t)(2 * s)) s *= 2;
+  for (uint32_t i = 0; i < a.nseg; i++)
+    if (a.seg[i].w.type != 12 && a.seg[i].w.type != 14) s = 1;
+  return s;
+}
+
+static int rows_per_cta(const GemvArgs& a) {
+  if (a.batch <= 1) return (B1_WARPS / b1_slices(a)) * B1_R;
+  return GEMV_WARPS * 2;
+}
 
 // Fills cta_begin of each segment; returns the total CTA count along y.
 uint32_t gemv_plan(GemvArgs& a) {
-  const int rpc = rows_per_cta(a.batch);
+  const int rpc = rows_per_cta(a);
   uint32_t c = 0;
   for (uint32_t i = 0; i < a.nseg; i++) {
     a.seg[i].cta_begin = c;
@@ -406,10 +619,16 @@ uint32_t gemv_plan(GemvArgs& a) {
 cudaError_t launch_gemv(GemvArgs a, cudaStream_t st) {
   const uint32_t ny = gemv_plan(a);
   const dim3 blk(GEMV_WARPS * 32);
-  if (a.batch == 1) gemv_kernel<4, 1><<<dim3(1, ny), blk, 0, st>>>(a);
+  if (a.batch == 1) gemv1_kernel<<<dim3(1, ny), B1_WARPS * 32, 0, st>>>(a, b1_slices(a));
   else if (a.batch == 2) gemv_kernel<2, 2><<<dim3(1, ny), blk, 0, st>>>(a);
   else if (a.batch <= 4) gemv_kernel<2, 4><<<dim3(1, ny), blk, 0, st>>>(a);
   else gemv_kernel<2, 8><<<dim3((a.batch + 7) / 8, ny), blk, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_xpack(const float* x, uint32_t ldx, uint32_t K, uint32_t rows, float* p4, float* p6, cudaStream_t st) {
+  if (!rows) return cudaSuccess;
+  xpack_kernel<<<dim3((K + 255) / 256, rows), 256, 0, st>>>(x, ldx, K, p4, p6, xperm_len(K));
   return cudaGetLastError();
 }
 

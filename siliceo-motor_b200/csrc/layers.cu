@@ -11,7 +11,7 @@ namespace sm {
 // out = x * (1/sqrt(sum(x^2)/n + eps)) * w  (qwen2.rs:647-660, 748-756).
 // rows: optional row selection (row r of out reads row rows[r] of x).
 __global__ void rmsnorm_kernel(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out,
-                               uint32_t ldo, uint32_t n, float eps) {
+                               uint32_t ldo, float* p4, float* p6, uint32_t n, float eps) {
   const uint32_t r = blockIdx.x;
   const float* xr = x + (size_t)(sel ? sel[r] : r) * ldx;
   float ss = 0.f;
@@ -27,8 +27,9 @@ __global__ void rmsnorm_kernel(const float* x, uint32_t ldx, const uint32_t* sel
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(red[0] / (float)n + eps);
-  float* o = out + (size_t)r * ldo;
-  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+  const uint32_t ldp = xperm_len(n);
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+    store_act(out, ldo, p4, p6, ldp, r, i, __fmul_rn(__fmul_rn(xr[i], inv), w[i]));
 }
 
 // --------------------------------------------------- RoPE + KV append ----
@@ -68,18 +69,28 @@ __global__ void rope_kv_kernel(float* q, const float* k, const float* v, uint32_
 
 // ------------------------------------------------------------ attention ----
 // Split-K decode attention with GQA (qwen2.rs:502-533). CTA (row r, kv head
-// g, split sp) covers a run of 64-position tiles of the row's context
-// [0, pos]; the G = Hq/Hkv query heads of the group share each K/V tile
-// staged in shared memory. Online softmax inside the CTA; splits are merged
-// by attn_combine_kernel.
-constexpr int ATT_T = 64;     // positions per tile
+// g, split sp) covers a run of 32-position tiles of the row's context
+// [0, pos]; the G = Hq/Hkv query heads of the group share each K/V tile.
+// Both tiles of a step are staged with cp.async at once (V arrives while the
+// scores are computed); rows are padded to hd+4 floats so that the float4
+// shared-memory reads of 8 lanes hit distinct banks. Online softmax inside
+// the CTA; splits are merged by attn_combine_kernel.
+constexpr int ATT_T = 32;     // positions per tile
 constexpr int ATT_THREADS = 128;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
 
 __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q, uint32_t ldq, const RowDesc* rows,
                                                                  const SeqDesc* seqs, uint32_t layer, uint32_t Hq,
                                                                  uint32_t Hkv, uint32_t hd, float scale, float* part_o,
                                                                  float* part_ml, uint32_t max_splits) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const uint32_t r = blockIdx.x / Hkv, g = blockIdx.x - r * Hkv, sp = blockIdx.y;
   const RowDesc rd = rows[r];
   const uint32_t L = rd.pos + 1;
@@ -88,56 +99,69 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
   const uint32_t tb = sp * tps;
   if (tb >= tiles) return;
   const uint32_t te = min(tiles, tb + tps);
-  const uint32_t G = Hq / Hkv, kvd = Hkv * hd, hs = hd + 1;
+  const uint32_t G = Hq / Hkv, kvd = Hkv * hd, hs = hd + 4, hd4 = hd / 4;
   const SeqDesc sd = seqs[rd.seq];
   float* qs = smem;                  // [G][hd]
-  float* tile = qs + G * hd;         // [ATT_T][hd+1]
-  float* ps = tile + ATT_T * hs;     // [G][ATT_T]
+  float* kt = qs + G * hd;           // [ATT_T][hd+4]
+  float* vt = kt + ATT_T * hs;       // [ATT_T][hd+4]
+  float* ps = vt + ATT_T * hs;       // [G][ATT_T]
   float* mrun = ps + G * ATT_T;      // [G] running max
   float* lrun = mrun + G;            // [G] running sum
   float* alpha = lrun + G;           // [G] rescale of this tile
   const float* qr = q + (size_t)r * ldq + (size_t)g * G * hd;
-  for (uint32_t i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = qr[i];
+  for (uint32_t i = threadIdx.x; i < G * hd4; i += blockDim.x)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(qr)[i];
   if (threadIdx.x < G) { mrun[threadIdx.x] = -INFINITY; lrun[threadIdx.x] = 0.f; }
-  constexpr int MAXO = 8;  // G*hd/ATT_THREADS <= 8 (G <= 8, hd <= 128)
-  float o[MAXO];
+  constexpr int MAXO = 2;  // (G*hd/4) / ATT_THREADS <= 2 (G <= 8, hd <= 128)
+  float4 o[MAXO];
 #pragma unroll
-  for (int i = 0; i < MAXO; i++) o[i] = 0.f;
+  for (int i = 0; i < MAXO; i++) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   const size_t kbase = (size_t)layer * sd.cap * kvd + (size_t)g * hd;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (uint32_t t = tb; t < te; t++) {
     const uint32_t p0 = t * ATT_T, n = min((uint32_t)ATT_T, L - p0);
     __syncthreads();  // previous tile fully consumed
-    for (uint32_t i = threadIdx.x; i < n * (hd / 4); i += blockDim.x) {
-      const uint32_t pp = i / (hd / 4), d4 = i - pp * (hd / 4);
-      const float4 a = *reinterpret_cast<const float4*>(sd.k + kbase + (size_t)(p0 + pp) * kvd + 4 * d4);
-      float* dst = tile + pp * hs + 4 * d4;
-      dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+    for (uint32_t i = threadIdx.x; i < n * hd4; i += blockDim.x) {
+      const uint32_t pp = i / hd4, d4 = i - pp * hd4;
+      cp_async16(kt + pp * hs + 4 * d4, sd.k + kbase + (size_t)(p0 + pp) * kvd + 4 * d4);
     }
+    cp_async_commit();
+    for (uint32_t i = threadIdx.x; i < n * hd4; i += blockDim.x) {
+      const uint32_t pp = i / hd4, d4 = i - pp * hd4;
+      cp_async16(vt + pp * hs + 4 * d4, sd.v + kbase + (size_t)(p0 + pp) * kvd + 4 * d4);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();  // K landed
     __syncthreads();
+    // scores: (head j, position pp) pairs
     for (uint32_t i = threadIdx.x; i < G * ATT_T; i += blockDim.x) {
       const uint32_t j = i / ATT_T, pp = i - j * ATT_T;
-      float s = -INFINITY;
+      float sc = -INFINITY;
       if (pp < n) {
-        const float* qj = qs + j * hd;
-        const float* kr = tile + pp * hs;
+        const float4* qj = reinterpret_cast<const float4*>(qs + j * hd);
+        const float4* kr = reinterpret_cast<const float4*>(kt + pp * hs);
         float a0 = 0.f, a1 = 0.f;
-        for (uint32_t d = 0; d < hd; d += 2) { a0 = fmaf(qj[d], kr[d], a0); a1 = fmaf(qj[d + 1], kr[d + 1], a1); }
-        s = (a0 + a1) * scale;
+        for (uint32_t d = 0; d < hd4; d++) {
+          const float4 qa = qj[d], ka = kr[d];
+          a0 = fmaf(qa.x, ka.x, a0);
+          a1 = fmaf(qa.y, ka.y, a1);
+          a0 = fmaf(qa.z, ka.z, a0);
+          a1 = fmaf(qa.w, ka.w, a1);
+        }
+        sc = (a0 + a1) * scale;
       }
-      ps[i] = s;
+      ps[i] = sc;
     }
     __syncthreads();
     for (uint32_t j = warp; j < G; j += ATT_THREADS / 32) {
-      float s0 = ps[j * ATT_T + lane], s1 = ps[j * ATT_T + 32 + lane];
-      float m = fmaxf(s0, s1);
+      const float s0 = ps[j * ATT_T + lane];
+      float m = s0;
 #pragma unroll
       for (int of = 16; of > 0; of >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, of));
       const float mold = mrun[j], mnew = fmaxf(mold, m);
-      const float e0 = expf(s0 - mnew), e1 = expf(s1 - mnew);
+      const float e0 = expf(s0 - mnew);
       ps[j * ATT_T + lane] = e0;
-      ps[j * ATT_T + 32 + lane] = e1;
-      const float sum = warp_sum(e0 + e1);
+      const float sum = warp_sum(e0);
       if (lane == 0) {
         const float a = expf(mold - mnew);  // 0 on the first tile (mold = -inf)
         alpha[j] = a;
@@ -145,22 +169,24 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
         mrun[j] = mnew;
       }
     }
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < n * (hd / 4); i += blockDim.x) {
-      const uint32_t pp = i / (hd / 4), d4 = i - pp * (hd / 4);
-      const float4 a = *reinterpret_cast<const float4*>(sd.v + kbase + (size_t)(p0 + pp) * kvd + 4 * d4);
-      float* dst = tile + pp * hs + 4 * d4;
-      dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
-    }
+    cp_async_wait<0>();  // V landed
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < MAXO; k++) {
       const uint32_t i = threadIdx.x + k * ATT_THREADS;
-      if (i < G * hd) {
-        const uint32_t j = i / hd, d = i - j * hd;
+      if (i < G * hd4) {
+        const uint32_t j = i / hd4, d4 = i - j * hd4;
         const float* pj = ps + j * ATT_T;
-        float acc = o[k] * alpha[j];
-        for (uint32_t pp = 0; pp < n; pp++) acc = fmaf(pj[pp], tile[pp * hs + d], acc);
+        const float a = alpha[j];
+        float4 acc = make_float4(o[k].x * a, o[k].y * a, o[k].z * a, o[k].w * a);
+        for (uint32_t pp = 0; pp < n; pp++) {
+          const float p = pj[pp];
+          const float4 v = reinterpret_cast<const float4*>(vt + pp * hs)[d4];
+          acc.x = fmaf(p, v.x, acc.x);
+          acc.y = fmaf(p, v.y, acc.y);
+          acc.z = fmaf(p, v.z, acc.z);
+          acc.w = fmaf(p, v.w, acc.w);
+        }
         o[k] = acc;
       }
     }
@@ -169,9 +195,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
 #pragma unroll
   for (int k = 0; k < MAXO; k++) {
     const uint32_t i = threadIdx.x + k * ATT_THREADS;
-    if (i < G * hd) {
-      const uint32_t j = i / hd, d = i - j * hd, h = g * G + j;
-      part_o[(((size_t)r * Hq + h) * max_splits + sp) * hd + d] = o[k];
+    if (i < G * hd4) {
+      const uint32_t j = i / hd4, d4 = i - j * hd4, h = g * G + j;
+      reinterpret_cast<float4*>(part_o + (((size_t)r * Hq + h) * max_splits + sp) * hd)[d4] = o[k];
     }
   }
   if (threadIdx.x < G) {
@@ -183,7 +209,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
 }
 
 __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const RowDesc* rows, uint32_t Hq,
-                                    uint32_t hd, uint32_t max_splits, float* out, uint32_t ldo) {
+                                    uint32_t hd, uint32_t max_splits, float* out, uint32_t ldo, float* p4, float* p6) {
   const uint32_t r = blockIdx.x / Hq, h = blockIdx.x - r * Hq;
   const uint32_t L = rows[r].pos + 1;
   const uint32_t tiles = (L + ATT_T - 1) / ATT_T;
@@ -198,16 +224,18 @@ __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, c
   for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
     float acc = 0.f;
     for (uint32_t s = 0; s < ns; s++) acc = fmaf(po[(size_t)s * hd + d], expf(ml[2 * s] - M), acc);
-    out[(size_t)r * ldo + h * hd + d] = acc / den;
+    store_act(out, ldo, p4, p6, xperm_len(Hq * hd), r, h * hd + d, acc / den);
   }
 }
 
 // -------------------------------------------------------------- SwiGLU ----
 // gate = silu(gate) * up, silu(x) = x / (1 + exp(-x)) (qwen2.rs:743-745, 546-548).
-__global__ void silu_mul_kernel(float* gate, const float* up, size_t n) {
+__global__ void silu_mul_kernel(float* gate, const float* up, uint32_t F, size_t n, float* p4, float* p6) {
+  const uint32_t ldp = xperm_len(F);
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float gv = gate[i];
-    gate[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), up[i]);
+    const uint32_t r = (uint32_t)(i / F), e = (uint32_t)(i - (size_t)r * F);
+    store_act(gate, F, p4, p6, ldp, r, e, __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), up[i]));
   }
 }
 
@@ -443,9 +471,9 @@ __global__ void record_tokens_kernel(const uint32_t* tok, uint32_t rows, uint32_
 
 // --------------------------------------------------------------- launch ----
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
-                           uint32_t rows, uint32_t n, float eps, cudaStream_t st) {
+                           float* p4, float* p6, uint32_t rows, uint32_t n, float eps, cudaStream_t st) {
   if (!rows) return cudaSuccess;
-  rmsnorm_kernel<<<rows, n >= 4096 ? 1024 : 512, 0, st>>>(x, ldx, sel, w, out, ldo, n, eps);
+  rmsnorm_kernel<<<rows, n >= 4096 ? 1024 : 512, 0, st>>>(x, ldx, sel, w, out, ldo, p4, p6, n, eps);
   return cudaGetLastError();
 }
 
@@ -458,12 +486,12 @@ cudaError_t launch_rope_kv(float* q, const float* k, const float* v, uint32_t ld
 }
 
 size_t attn_smem_bytes(uint32_t G, uint32_t hd) {
-  return sizeof(float) * ((size_t)G * hd + (size_t)ATT_T * (hd + 1) + (size_t)G * ATT_T + 3 * G);
+  return sizeof(float) * ((size_t)G * hd + 2 * (size_t)ATT_T * (hd + 4) + (size_t)G * ATT_T + 3 * G);
 }
 
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
-                             uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st) {
+                             uint32_t max_splits, float* out, uint32_t ldo, float* p4, float* p6, cudaStream_t st) {
   if (!nrows) return cudaSuccess;
   const uint32_t G = Hq / Hkv;
   const size_t sm = attn_smem_bytes(G, hd);
@@ -472,14 +500,14 @@ cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, 
                                                                             scale, part_o, part_ml, max_splits);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo);
+  attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo, p4, p6);
   return cudaGetLastError();
 }
 
-cudaError_t launch_silu_mul(float* gate, const float* up, size_t n, cudaStream_t st) {
+cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, float* p4, float* p6, cudaStream_t st) {
   if (!n) return cudaSuccess;
   const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 16);
-  silu_mul_kernel<<<blocks, 256, 0, st>>>(gate, up, n);
+  silu_mul_kernel<<<blocks, 256, 0, st>>>(gate, up, F, n, p4, p6);
   return cudaGetLastError();
 }
 

@@ -149,6 +149,19 @@ def test_batched_decode_matches_single(models):
     assert [len(c) for c in caches] == [len(p) - 1 + 6 for p in prompts]
 
 
+def test_cache_outlives_model_handle(tmp_path):
+    p = str(tmp_path / "m.gguf")
+    smotor.synth_write(smotor.synth_spec(n_layers=1, vocab=300), p)
+    m = smotor.Model.load(p, max_context=256)
+    c = m.new_cache(16)
+    m.forward_cached(c, [1, 2, 3], logits=False)
+    c2 = c.clone()
+    m.free()  # the caches keep the model alive
+    assert len(c2) == 3
+    c.free()
+    c2.free()
+
+
 def test_cache_ops(models):
     eng, _ = models["qwen2_tiny"]
     c = eng.new_cache(40)
@@ -189,7 +202,7 @@ def test_seeded_generation_equals_plain(models):
 def test_decode_run_matches_stepwise(models):
     eng, _ = models["llama_tiny"]
     V = eng.config.vocab_size
-    prompts = [[5, 6, 7], list(range(40, 110)), [9]]
+    prompts = [[5, 6, 7], list(range(40, 110)), [9, 10]]
     samplers = [smotor.Sampler(), smotor.Sampler(1.0, 40, 0.9), smotor.Sampler(0.9, 7, None)]
     runs, steps = [], []
     for p in prompts:
