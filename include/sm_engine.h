@@ -201,6 +201,17 @@ int sm_dequant(const sm_dweight* w, float* out_dev, void* stream);
 /* Dequant-fused GEMV: y_dev[b][o] = sum_d W[o][d] * x_dev[b][d] for b < batch
  * (batch 1..32; qwen2.rs:663-674, kernels/src/lib.rs:709-876). */
 int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream);
+/* sm_gemv for callers that cannot allocate device memory: hosts that hand out
+ * all device memory from their own pool, and latency-critical paths that may
+ * not call cudaMalloc (it can synchronize the device). No counterpart in the
+ * reference. It allocates nothing: batch 1 packs x into a fixed 256 KB device
+ * array of the library instead of scratch that sm_gemv allocates on first
+ * use, so n_in is limited to 32768 (larger n_in returns SM_ERR_ARG). Every
+ * call on a device shares that array, so calls that overlap on the GPU race;
+ * nothing in it needs clearing between calls. The first call on a device
+ * looks the array's address up (once per device, with the weight's device
+ * current); make that first call before any stream capture. */
+int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream);
 
 /* ------------------------------------------------------------------------
  * Synthetic GGUF models (the stand-in for real model files). Shapes and

@@ -1050,4 +1050,32 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
   return SM_OK;
 }
 
+// Same product as sm_gemv, for callers that cannot allocate device memory: the
+// batch-1 scratch is a fixed device array of the library (see gemv.cu).
+int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream) {
+  if (!w || !x_dev || !y_dev) { set_error("null argument"); return SM_ERR_ARG; }
+  if (batch < 1 || batch > 32) { set_error("sm_gemv_noalloc: batch must be 1..32"); return SM_ERR_ARG; }
+  if (((uintptr_t)x_dev & 15) || (w->w.d.n_in & 3)) { set_error("sm_gemv_noalloc: x must be 16-byte aligned"); return SM_ERR_ARG; }
+  if (w->w.d.n_in > gemv_noalloc_max_k()) {
+    set_error("sm_gemv_noalloc: n_in " + std::to_string(w->w.d.n_in) + " exceeds the fixed scratch limit of " +
+              std::to_string(gemv_noalloc_max_k()) + " inputs");
+    return SM_ERR_ARG;
+  }
+  int dev = -1;
+  CK(cudaGetDevice(&dev));
+  if (dev != w->device) {
+    set_error("sm_gemv_noalloc: the weight lives on device " + std::to_string(w->device) + ", current device is " +
+              std::to_string(dev));
+    return SM_ERR_ARG;
+  }
+  GemvArgs a{};
+  a.x = x_dev;
+  a.ldx = w->w.d.n_in;
+  a.batch = (uint32_t)batch;
+  a.nseg = 1;
+  a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, false);
+  CK(launch_gemv_noalloc(a, (cudaStream_t)stream));
+  return SM_OK;
+}
+
 }  // extern "C"

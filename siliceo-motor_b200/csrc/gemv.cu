@@ -12,6 +12,8 @@
 // differs from the reference's sequential sum by rounding only.
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "device.cuh"
 
 namespace sm {
@@ -643,6 +645,56 @@ cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows,
   if (!rows) return cudaSuccess;
   embed_kernel<<<dim3((w.n_in + 255) / 256, rows), 256, 0, st>>>(w, tokens, x, ldx);
   return cudaGetLastError();
+}
+
+// ------------------------------------------------- no-allocation GEMV ----
+// Scratch of sm_gemv_noalloc: the two permuted copies of one batch-1 input
+// vector, in a fixed device array instead of memory the call allocates. Every
+// call on a device shares it; the pack kernel of a call writes every entry its
+// GEMV reads, so nothing needs clearing, and calls that overlap on the GPU
+// race on it.
+constexpr uint32_t NOALLOC_MAX_K = 32768;
+static __device__ __align__(256) float g_noalloc_xp[2 * NOALLOC_MAX_K];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+uint32_t gemv_noalloc_max_k() { return NOALLOC_MAX_K; }
+
+// The scratch's device address on the current device, looked up once per
+// device with that device current (host code cannot use the symbol itself).
+static cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    float* p = nullptr;
+    e = cudaGetSymbolAddress((void**)&p, g_noalloc_xp);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+// sm_gemv without any allocation: batch 1 packs x into the fixed scratch;
+// larger batches read x directly and need no scratch. n_in must not exceed
+// NOALLOC_MAX_K (checked by the caller).
+cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st) {
+  if (a.batch == 1) {
+    float* xp = nullptr;
+    cudaError_t e = noalloc_scratch(&xp);
+    if (e != cudaSuccess) return e;
+    const uint32_t K = a.seg[0].w.n_in;
+    a.xp4 = xp;
+    a.xp6 = xp + NOALLOC_MAX_K;
+    e = launch_xpack(a.x, a.ldx, K, 1, xp, xp + NOALLOC_MAX_K, st);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_gemv(a, st);
 }
 
 }  // namespace sm

@@ -53,6 +53,8 @@ cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const 
                           const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
                           RowDesc* advance, cudaStream_t st);
 
+uint32_t gemv_noalloc_max_k();
+cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st);
 cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
                                  uint32_t cap_steps, cudaStream_t st);
 

@@ -122,6 +122,7 @@ SIGNATURES = {
     "sm_dweight_bytes": (C.c_int, [P, PU64]),
     "sm_dequant": (C.c_int, [P, P, P]),
     "sm_gemv": (C.c_int, [P, P, P, U64, P]),
+    "sm_gemv_noalloc": (C.c_int, [P, P, P, U64, P]),
     "sm_synth_preset": (C.c_int, [C.c_int, C.POINTER(sm_synth_spec)]),
     "sm_synth_size": (C.c_int, [C.POINTER(sm_synth_spec), PU64]),
     "sm_synth_write": (C.c_int, [C.POINTER(sm_synth_spec), C.c_char_p, C.c_int]),
@@ -448,6 +449,10 @@ class DWeight:
 
     def gemv(self, x_ptr: int, y_ptr: int, batch: int, stream: int = 0) -> None:
         _check(lib().sm_gemv(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), batch, C.c_void_p(stream)))
+
+    def gemv_noalloc(self, x_ptr: int, y_ptr: int, batch: int, stream: int = 0) -> None:
+        """sm_gemv without allocating: scratch is a fixed library array (n_in <= 32768)."""
+        _check(lib().sm_gemv_noalloc(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), batch, C.c_void_p(stream)))
 
     def free(self) -> None:
         if self.h:
