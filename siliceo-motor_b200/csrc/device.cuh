@@ -64,13 +64,41 @@ struct DWDesc {
   uint32_t aux_stride;   // bytes per row
 };
 
+// One row of a forward pass (a token): which sequence it belongs to and its
+// absolute position.
+struct RowDesc {
+  uint32_t seq;
+  uint32_t pos;
+};
+
+// A sequence's KV storage: k/v are [n_layers][cap][kv_dim] f32.
+struct SeqDesc {
+  float* k;
+  float* v;
+  uint32_t cap;
+  uint32_t pad;
+};
+
+// What a GEMV does with the dot product v of (physical row o, column b).
+// Pair kinds act on physical rows (2m, 2m+1) together.
+enum GemvEpi : uint32_t {
+  EPI_STORE = 0,   // y = v (+ bias)
+  EPI_ADD = 1,     // y += v
+  EPI_RESID = 2,   // x = y += v; xn = x * nw (natural and permuted); per-CTA sum of x^2
+  EPI_ROPE_Q = 3,  // pair (dim m, dim m + hd/2) of a head: RoPE, store q (natural order)
+  EPI_ROPE_K = 4,  // same, store into the K cache
+  EPI_V = 5,       // store into the V cache
+  EPI_SILU = 6,    // pair (gate m, up m): h[m] = silu(gate) * up (natural and permuted)
+};
+__host__ __device__ inline bool epi_is_pair(uint32_t e) { return e == EPI_ROPE_Q || e == EPI_ROPE_K || e == EPI_SILU; }
+
 // One output segment of a (possibly fused) GEMV launch.
 struct GemvSeg {
   DWDesc w;
   float* y;            // y[b * ldy + o]
-  const float* bias;   // optional, added to every column
+  const float* bias;   // optional, physical-row order
   uint32_t ldy;
-  uint32_t add;        // 1: y += result (residual), 0: y = result
+  uint32_t epi;        // GemvEpi
   uint32_t cta_begin;  // first CTA index of this segment
 };
 
@@ -85,6 +113,27 @@ struct GemvArgs {
   // that produced x.
   const float* xp4;
   const float* xp6;
+  // Input RMSNorm (qwen2.rs:647-660) folded into the GEMV: x holds x*w of the
+  // un-normalized residual, and the dot products of column b are scaled by
+  // 1/sqrt(sum(in_parts[b*in_np .. +in_np]) / in_n + in_eps) when in_parts is set.
+  const float* in_parts;
+  uint32_t in_np, in_n;
+  float in_eps;
+  // EPI_RESID outputs: xn = x * nw, and per-CTA partial sums of x^2
+  // (out_parts[b * gridDim.y + cta]).
+  const float* nw;
+  float *xn, *xn4, *xn6;
+  uint32_t ldxn;
+  float* out_parts;
+  // EPI_SILU outputs
+  float *h, *h4, *h6;
+  uint32_t ldh;
+  // RoPE and KV-cache epilogues
+  const RowDesc* rows;
+  const SeqDesc* seqs;
+  const float* cos_t;
+  const float* sin_t;
+  uint32_t layer, hd, kvd;
 };
 
 // ---------------------------------------------------------------------------

@@ -137,13 +137,17 @@ void free_weight(DW& w) {
   w.mem = nullptr;
 }
 
+// Per-layer weights. wq / wk (and bq / bk) hold their rows in RoPE-pair
+// order: physical row h*hd + 2m + s is logical row h*hd + m + s*hd/2, so one
+// warp sees both halves of every rotated pair. wgu interleaves ffn_gate and
+// ffn_up: physical row 2m is gate row m, 2m+1 is up row m.
 struct Layer {
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
   float* bq = nullptr;
   float* bk = nullptr;
   float* bv = nullptr;
-  DW wq, wk, wv, wo, wgate, wup, wdown;
+  DW wq, wk, wv, wo, wgu, wdown;
 };
 
 // Per-step host->device state, one pinned block copied with one memcpy.
@@ -187,6 +191,9 @@ struct sm_model {
         *u = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr;
   // permuted copies of the GEMV inputs for batch 1 (xperm_q4k / xperm_q6k)
   float *xn4 = nullptr, *xn6 = nullptr, *att4 = nullptr, *att6 = nullptr, *g4 = nullptr, *g6 = nullptr;
+  // per-CTA partial sums of x^2 written by residual GEMVs, read by the next GEMV
+  float *parts_a = nullptr, *parts_b = nullptr;
+  uint32_t parts_cap = 0;
   uint8_t* mask_dev = nullptr;
   void* in_dev = nullptr;   // StepIn block on the device
   void* in_host = nullptr;  // pinned
@@ -276,6 +283,54 @@ int upload_2d(const GgufReader& g, const std::string& name, uint64_t n_in, uint6
   return rc;
 }
 
+// Uploads a 2-D tensor with its rows reordered: physical row p is logical row map[p].
+int upload_2d_rows(const GgufReader& g, const std::string& name, uint64_t n_in, uint64_t n_out,
+                   const std::vector<uint32_t>& map, DW* w) {
+  const GgufTensor* t = g.tensor(name);
+  if (!t) { set_error("tensor not found: " + name); return SM_ERR_FORMAT; }
+  if (t->dims.size() != 2 || t->dims[0] != n_in || t->dims[1] != n_out) { set_error(name + ": unexpected shape"); return SM_ERR_FORMAT; }
+  const uint8_t* src = g.data(*t);
+  if (!src) { set_error(name + ": truncated tensor data"); return SM_ERR_FORMAT; }
+  const uint64_t rb = qtype_row_bytes(t->type, n_in);
+  std::vector<uint8_t> buf(rb * n_out);
+  for (uint64_t p = 0; p < n_out; p++) std::memcpy(buf.data() + p * rb, src + (uint64_t)map[p] * rb, rb);
+  int rc = upload_weight(t->type, buf.data(), n_out, n_in, w);
+  if (rc) set_error(name + ": " + get_error());
+  return rc;
+}
+
+// RoPE-pair row order for a [n_heads * hd] projection (see Layer).
+std::vector<uint32_t> rope_pair_map(uint64_t n_heads, uint64_t hd) {
+  std::vector<uint32_t> map(n_heads * hd);
+  const uint64_t half = hd / 2;
+  for (uint64_t h = 0; h < n_heads; h++)
+    for (uint64_t mm = 0; mm < half; mm++)
+      for (uint64_t sdx = 0; sdx < 2; sdx++) map[h * hd + 2 * mm + sdx] = (uint32_t)(h * hd + mm + sdx * half);
+  return map;
+}
+
+// ffn_gate and ffn_up interleaved row by row into one weight (see Layer).
+int upload_gate_up(const GgufReader& g, const std::string& pg, const std::string& pu, uint64_t n_in, uint64_t n_ff, DW* w) {
+  const GgufTensor* tg = g.tensor(pg);
+  const GgufTensor* tu = g.tensor(pu);
+  if (!tg || !tu) { set_error("tensor not found: " + (tg ? pu : pg)); return SM_ERR_FORMAT; }
+  for (const GgufTensor* t : {tg, tu})
+    if (t->dims.size() != 2 || t->dims[0] != n_in || t->dims[1] != n_ff) { set_error(t->name + ": unexpected shape"); return SM_ERR_FORMAT; }
+  if (tg->type != tu->type) { set_error(pg + " and " + pu + " have different types"); return SM_ERR_UNSUPPORTED; }
+  const uint8_t* sg_ = g.data(*tg);
+  const uint8_t* su = g.data(*tu);
+  if (!sg_ || !su) { set_error(pg + ": truncated tensor data"); return SM_ERR_FORMAT; }
+  const uint64_t rb = qtype_row_bytes(tg->type, n_in);
+  std::vector<uint8_t> buf(rb * 2 * n_ff);
+  for (uint64_t r = 0; r < n_ff; r++) {
+    std::memcpy(buf.data() + (2 * r) * rb, sg_ + r * rb, rb);
+    std::memcpy(buf.data() + (2 * r + 1) * rb, su + r * rb, rb);
+  }
+  int rc = upload_weight(tg->type, buf.data(), 2 * n_ff, n_in, w);
+  if (rc) set_error(pg + ": " + get_error());
+  return rc;
+}
+
 int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   // Famiglia::detect (crates/s-models/src/registry.rs:38-60)
   const GgufValue* arch = g.meta("general.architecture");
@@ -334,27 +389,38 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   }
   if ((rc = upload_f32(m, g, "output_norm.weight", H, &m->output_norm))) return rc;
   m->weight_bytes = m->output.enc_bytes;
+  const std::vector<uint32_t> qmap = rope_pair_map(c.n_heads, hd), kmap = rope_pair_map(c.n_kv_heads, hd);
   for (uint64_t i = 0; i < c.n_layers; i++) {
     Layer L;
     const std::string p = "blk." + std::to_string(i) + ".";
-    auto opt_bias = [&](const char* n, uint64_t len, float** out) -> int {  // qwen2.rs:687-697
-      if (!g.tensor(p + n)) return SM_OK;
-      return upload_f32(m, g, p + n, len, out);
+    auto opt_bias = [&](const char* n, uint64_t len, const std::vector<uint32_t>* map, float** out) -> int {
+      if (!g.tensor(p + n)) return SM_OK;  // opt_bias (qwen2.rs:687-697)
+      const GgufTensor* t = g.tensor(p + n);
+      if (t->type != QT_F32 || t->n_elements() != len) { set_error(p + n + ": expected F32"); return SM_ERR_UNSUPPORTED; }
+      const float* src = reinterpret_cast<const float*>(g.data(*t));
+      if (!src) { set_error(p + n + ": truncated tensor data"); return SM_ERR_FORMAT; }
+      std::vector<float> b(len);
+      for (uint64_t k = 0; k < len; k++) b[k] = src[map ? (*map)[k] : k];
+      int rc2 = dev_alloc(m, (void**)out, len * 4);
+      if (rc2) return rc2;
+      CK(cudaMemcpy(*out, b.data(), len * 4, cudaMemcpyHostToDevice));
+      return SM_OK;
     };
-    if ((rc = opt_bias("attn_q.bias", H, &L.bq)) || (rc = opt_bias("attn_k.bias", kvd, &L.bk)) ||
-        (rc = opt_bias("attn_v.bias", kvd, &L.bv)) || (rc = upload_f32(m, g, p + "attn_norm.weight", H, &L.attn_norm)) ||
+    if ((rc = opt_bias("attn_q.bias", H, &qmap, &L.bq)) || (rc = opt_bias("attn_k.bias", kvd, &kmap, &L.bk)) ||
+        (rc = opt_bias("attn_v.bias", kvd, nullptr, &L.bv)) ||
+        (rc = upload_f32(m, g, p + "attn_norm.weight", H, &L.attn_norm)) ||
         (rc = upload_f32(m, g, p + "ffn_norm.weight", H, &L.ffn_norm)) ||
-        (rc = upload_2d(g, p + "attn_q.weight", H, H, &L.wq)) || (rc = upload_2d(g, p + "attn_k.weight", H, kvd, &L.wk)) ||
+        (rc = upload_2d_rows(g, p + "attn_q.weight", H, H, qmap, &L.wq)) ||
+        (rc = upload_2d_rows(g, p + "attn_k.weight", H, kvd, kmap, &L.wk)) ||
         (rc = upload_2d(g, p + "attn_v.weight", H, kvd, &L.wv)) ||
         (rc = upload_2d(g, p + "attn_output.weight", H, H, &L.wo)) ||
-        (rc = upload_2d(g, p + "ffn_gate.weight", H, c.n_ff, &L.wgate)) ||
-        (rc = upload_2d(g, p + "ffn_up.weight", H, c.n_ff, &L.wup)) ||
+        (rc = upload_gate_up(g, p + "ffn_gate.weight", p + "ffn_up.weight", H, c.n_ff, &L.wgu)) ||
         (rc = upload_2d(g, p + "ffn_down.weight", c.n_ff, H, &L.wdown))) {
       m->layers.push_back(L);  // so that free releases what was uploaded
       return rc;
     }
-    m->weight_bytes += L.wq.enc_bytes + L.wk.enc_bytes + L.wv.enc_bytes + L.wo.enc_bytes + L.wgate.enc_bytes +
-                       L.wup.enc_bytes + L.wdown.enc_bytes;
+    m->weight_bytes += L.wq.enc_bytes + L.wk.enc_bytes + L.wv.enc_bytes + L.wo.enc_bytes + L.wgu.enc_bytes +
+                       L.wdown.enc_bytes;
     m->layers.push_back(L);
   }
   // RoPE table with the reference's f32 formula (qwen2.rs:712-718).
@@ -392,6 +458,10 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
         (rc = dev_alloc(m, (void**)&m->att4, pH * 4)) || (rc = dev_alloc(m, (void**)&m->att6, pH * 4)) ||
         (rc = dev_alloc(m, (void**)&m->g4, pF * 4)) || (rc = dev_alloc(m, (void**)&m->g6, pF * 4)))
       return rc;
+    m->parts_cap = (uint32_t)(H / 4 + 64);
+    if ((rc = dev_alloc(m, (void**)&m->parts_a, (size_t)R * m->parts_cap * 4)) ||
+        (rc = dev_alloc(m, (void**)&m->parts_b, (size_t)R * m->parts_cap * 4)))
+      return rc;
   }
   m->in_bytes = step_in_bytes(R);
   m->out_bytes = step_out_bytes(R);
@@ -419,7 +489,7 @@ void destroy_model(sm_model* m) {
   if (!m->tied) free_weight(m->output);
   for (auto& L : m->layers) {
     free_weight(L.wq); free_weight(L.wk); free_weight(L.wv); free_weight(L.wo);
-    free_weight(L.wgate); free_weight(L.wup); free_weight(L.wdown);
+    free_weight(L.wgu); free_weight(L.wdown);
   }
   for (void* p : m->allocs) cudaFree(p);
   if (m->in_host) cudaFreeHost(m->in_host);
@@ -428,19 +498,24 @@ void destroy_model(sm_model* m) {
   delete m;
 }
 
-GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, bool add) {
+GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, uint32_t epi) {
   GemvSeg s{};
   s.w = w.d;
   s.y = y;
   s.ldy = ldy;
   s.bias = bias;
-  s.add = add ? 1u : 0u;
+  s.epi = epi;
   return s;
 }
 
 // The layer stack for `nrows` rows described in din (tokens, rows, seqs),
 // then final norm + output head for the nsel rows listed in din.sel.
 // qwen2.rs:460-561 with the kernels of gemv.cu / layers.cu.
+// The layer stack for `nrows` rows described in din (tokens, rows, seqs),
+// then final norm + output head for the nsel rows listed in din.sel
+// (qwen2.rs:460-561). Per layer: QKV GEMV (input RMSNorm, bias, RoPE, KV
+// append in its epilogue), attention, O GEMV (+ residual, next norm's input),
+// gate/up GEMV (+ SwiGLU), down GEMV (+ residual, next norm's input).
 cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
   const sm_config& c = m->c;
   const uint32_t H = (uint32_t)c.n_embd, F = (uint32_t)c.n_ff, kvd = m->kvd, hd = (uint32_t)c.head_dim;
@@ -454,43 +529,70 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   float* g6 = b1 ? m->g6 : nullptr;
   cudaError_t e;
 #define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
-  RK(launch_embed(m->tok_embd.d, m->din.tok, nrows, m->x, H, st));
+  GemvArgs base{};
+  base.batch = nrows;
+  base.in_n = H;
+  base.in_eps = c.rms_eps;
+  base.rows = m->din.rows;
+  base.seqs = m->din.seqs;
+  base.cos_t = m->cos_t;
+  base.sin_t = m->sin_t;
+  base.hd = hd;
+  base.kvd = kvd;
+  RK(launch_embed_norm(m->tok_embd.d, m->din.tok, nrows, m->x, H, m->layers[0].attn_norm, m->xn, xn4, xn6, H,
+                       m->parts_a, st));
+  uint32_t np_a = 1, np_b = 0;
   for (uint32_t li = 0; li < c.n_layers; li++) {
     const Layer& L = m->layers[li];
-    RK(launch_rmsnorm(m->x, H, nullptr, L.attn_norm, m->xn, H, xn4, xn6, nrows, H, c.rms_eps, st));
-    GemvArgs a{};
-    a.x = m->xn; a.ldx = H; a.batch = nrows; a.nseg = 3; a.xp4 = xn4; a.xp6 = xn6;
-    a.seg[0] = seg(L.wq, m->q, H, L.bq, false);
-    a.seg[1] = seg(L.wk, m->k, kvd, L.bk, false);
-    a.seg[2] = seg(L.wv, m->v, kvd, L.bv, false);
+    GemvArgs a = base;
+    a.layer = li;
+    a.x = m->xn; a.ldx = H; a.xp4 = xn4; a.xp6 = xn6;
+    a.in_parts = m->parts_a; a.in_np = np_a;
+    a.nseg = 3;
+    a.seg[0] = seg(L.wq, m->q, H, L.bq, EPI_ROPE_Q);
+    a.seg[1] = seg(L.wk, nullptr, 0, L.bk, EPI_ROPE_K);
+    a.seg[2] = seg(L.wv, nullptr, 0, L.bv, EPI_V);
     RK(launch_gemv(a, st));
-    RK(launch_rope_kv(m->q, m->k, m->v, H, kvd, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads,
-                      (uint32_t)c.n_kv_heads, hd, m->cos_t, m->sin_t, st));
     RK(launch_attention(m->q, H, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads, (uint32_t)c.n_kv_heads, hd,
                         m->part_o, m->part_ml, m->max_splits, m->att, H, att4, att6, st));
-    GemvArgs o{};
-    o.x = m->att; o.ldx = H; o.batch = nrows; o.nseg = 1; o.xp4 = att4; o.xp6 = att6;
-    o.seg[0] = seg(L.wo, m->x, H, nullptr, true);
-    RK(launch_gemv(o, st));
-    RK(launch_rmsnorm(m->x, H, nullptr, L.ffn_norm, m->xn, H, xn4, xn6, nrows, H, c.rms_eps, st));
-    GemvArgs gu{};
-    gu.x = m->xn; gu.ldx = H; gu.batch = nrows; gu.nseg = 2; gu.xp4 = xn4; gu.xp6 = xn6;
-    gu.seg[0] = seg(L.wgate, m->g, F, nullptr, false);
-    gu.seg[1] = seg(L.wup, m->u, F, nullptr, false);
+    GemvArgs o = base;
+    o.layer = li;
+    o.x = m->att; o.ldx = H; o.xp4 = att4; o.xp6 = att6;
+    o.nseg = 1;
+    o.seg[0] = seg(L.wo, m->x, H, nullptr, EPI_RESID);
+    o.nw = L.ffn_norm; o.xn = m->xn; o.xn4 = xn4; o.xn6 = xn6; o.ldxn = H; o.out_parts = m->parts_b;
+    RK(launch_gemv(o, st, &np_b));
+    GemvArgs gu = base;
+    gu.layer = li;
+    gu.x = m->xn; gu.ldx = H; gu.xp4 = xn4; gu.xp6 = xn6;
+    gu.in_parts = m->parts_b; gu.in_np = np_b;
+    gu.nseg = 1;
+    gu.seg[0] = seg(L.wgu, nullptr, 0, nullptr, EPI_SILU);
+    gu.h = m->g; gu.h4 = g4; gu.h6 = g6; gu.ldh = F;
     RK(launch_gemv(gu, st));
-    RK(launch_silu_mul(m->g, m->u, F, (size_t)nrows * F, g4, g6, st));
-    GemvArgs dn{};
-    dn.x = m->g; dn.ldx = F; dn.batch = nrows; dn.nseg = 1; dn.xp4 = g4; dn.xp6 = g6;
-    dn.seg[0] = seg(L.wdown, m->x, H, nullptr, true);
-    RK(launch_gemv(dn, st));
+    GemvArgs dn = base;
+    dn.layer = li;
+    dn.x = m->g; dn.ldx = F; dn.xp4 = g4; dn.xp6 = g6;
+    dn.nseg = 1;
+    dn.seg[0] = seg(L.wdown, m->x, H, nullptr, EPI_RESID);
+    dn.nw = li + 1 < c.n_layers ? m->layers[li + 1].attn_norm : m->output_norm;
+    dn.xn = m->xn; dn.xn4 = xn4; dn.xn6 = xn6; dn.ldxn = H; dn.out_parts = m->parts_a;
+    RK(launch_gemv(dn, st, &np_a));
   }
   if (nsel) {
-    const bool h1 = nsel == 1;
-    RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, h1 ? m->xn4 : nullptr, h1 ? m->xn6 : nullptr, nsel,
-                      H, c.rms_eps, st));
-    GemvArgs hd_{};
-    hd_.x = m->xn; hd_.ldx = H; hd_.batch = nsel; hd_.nseg = 1; hd_.xp4 = m->xn4; hd_.xp6 = m->xn6;
-    hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, false);
+    GemvArgs hd_ = base;
+    hd_.batch = nsel;
+    hd_.nseg = 1;
+    hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, EPI_STORE);
+    hd_.x = m->xn; hd_.ldx = H; hd_.xp4 = m->xn4; hd_.xp6 = m->xn6;
+    if (nsel == nrows) {  // every row: the last down GEMV prepared the final norm's input
+      hd_.in_parts = m->parts_a;
+      hd_.in_np = np_a;
+    } else {  // a selection (prefill): normalize the selected rows here (qwen2.rs:555-560)
+      const bool h1 = nsel == 1;
+      RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, h1 ? m->xn4 : nullptr, h1 ? m->xn6 : nullptr,
+                        nsel, H, c.rms_eps, st));
+    }
     RK(launch_gemv(hd_, st));
   }
 #undef RK
@@ -1038,7 +1140,7 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
   a.ldx = w->w.d.n_in;
   a.batch = (uint32_t)batch;
   a.nseg = 1;
-  a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, false);
+  a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, EPI_STORE);
   if (batch == 1) {
     const uint32_t lp = xperm_len(w->w.d.n_in);
     if (!w->xp) CK(cudaMalloc((void**)&w->xp, 2 * (size_t)lp * 4));
@@ -1073,7 +1175,7 @@ int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint6
   a.ldx = w->w.d.n_in;
   a.batch = (uint32_t)batch;
   a.nseg = 1;
-  a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, false);
+  a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, EPI_STORE);
   CK(launch_gemv_noalloc(a, (cudaStream_t)stream));
   return SM_OK;
 }

@@ -327,9 +327,11 @@ __device__ __forceinline__ void unit_q50(const uint8_t* const* rowp, const uint8
   }
 }
 
+// Dot products of rows row0..row0+R-1 with columns col0..col0+ncols-1;
+// returns the warp-reduced sums (every lane holds them).
 template <int QT, int R, int BT>
 __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uint32_t ldx, int row0, int col0,
-                                          int ncols) {
+                                          int ncols, float (&acc)[R][BT]) {
   const DWDesc& w = sg.w;
   const int lane = threadIdx.x & 31;
   const uint8_t* rowp[R];
@@ -340,7 +342,6 @@ __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uin
     rowp[r] = w.body + (size_t)o * w.body_stride;
     auxp[r] = w.aux + (size_t)o * w.aux_stride;
   }
-  float acc[R][BT];
 #pragma unroll
   for (int r = 0; r < R; r++)
 #pragma unroll
@@ -363,17 +364,103 @@ __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uin
 #pragma unroll
   for (int r = 0; r < R; r++)
 #pragma unroll
-    for (int b = 0; b < BT; b++) {
-      const float v = warp_sum(acc[r][b]);
-      const uint32_t o = (uint32_t)(row0 + r);
-      if (lane == 0 && o < w.n_out && b < ncols) {
-        float* dst = sg.y + (size_t)(col0 + b) * sg.ldy + o;
-        float res = v;
-        if (sg.bias) res = res + sg.bias[o];
-        if (sg.add) res = *dst + res;
-        *dst = res;
-      }
+    for (int b = 0; b < BT; b++) acc[r][b] = warp_sum(acc[r][b]);
+}
+
+// ------------------------------------------------------------ epilogue ----
+// Input RMSNorm scale of column col (1 when the input is not normalized):
+// the sum of the producer's per-CTA partials in a fixed order (deterministic).
+__device__ float input_scale(const GemvArgs& a, uint32_t col) {
+  if (!a.in_parts) return 1.0f;
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+  for (uint32_t i = lane; i < a.in_np; i += 32) s += a.in_parts[(size_t)col * a.in_np + i];
+  s = warp_sum(s);
+  return 1.0f / sqrtf(s / (float)a.in_n + a.in_eps);
+}
+
+// Single-row epilogues; returns the new residual value for EPI_RESID, else 0.
+__device__ __forceinline__ float epi_single(const GemvArgs& a, const GemvSeg& sg, uint32_t o, uint32_t col, float v) {
+  if (sg.bias) v = v + sg.bias[o];
+  float* y = sg.y + (size_t)col * sg.ldy + o;
+  switch (sg.epi) {
+    case EPI_STORE: *y = v; return 0.f;
+    case EPI_ADD: *y = *y + v; return 0.f;
+    case EPI_RESID: {  // x += v (qwen2.rs:536-538, 549-551)
+      const float xn = *y + v;
+      *y = xn;
+      store_act(a.xn, a.ldxn, a.xn4, a.xn6, xperm_len(sg.w.n_out), col, o, xn * a.nw[o]);
+      return xn;
     }
+    case EPI_V: {  // v row into the cache at the row's position (qwen2.rs:498)
+      const RowDesc rd = a.rows[col];
+      const SeqDesc sd = a.seqs[rd.seq];
+      sd.v[((size_t)a.layer * sd.cap + rd.pos) * a.kvd + o] = v;
+      return 0.f;
+    }
+  }
+  return 0.f;
+}
+
+// Pair epilogues on physical rows (o, o+1), o even.
+__device__ __forceinline__ void epi_pair(const GemvArgs& a, const GemvSeg& sg, uint32_t o, uint32_t col, float v0,
+                                         float v1) {
+  if (sg.bias) { v0 = v0 + sg.bias[o]; v1 = v1 + sg.bias[o + 1]; }
+  if (sg.epi == EPI_SILU) {  // gate = silu(gate) * up (qwen2.rs:546-548, 743-745)
+    const uint32_t m = o >> 1;
+    const float hv = __fmul_rn(__fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0))), v1);
+    store_act(a.h, a.ldh, a.h4, a.h6, xperm_len(sg.w.n_out >> 1), col, m, hv);
+    return;
+  }
+  // NEOX RoPE of the pair (dim m, dim m + hd/2) at the row's position
+  // (qwen2.rs:708-724); cos/sin from the host table.
+  const uint32_t half = a.hd >> 1, h = o / a.hd, m = (o - h * a.hd) >> 1;
+  const RowDesc rd = a.rows[col];
+  const float c = a.cos_t[(size_t)rd.pos * half + m], s = a.sin_t[(size_t)rd.pos * half + m];
+  const float r0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+  const float r1 = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+  if (sg.epi == EPI_ROPE_Q) {
+    float* y = sg.y + (size_t)col * sg.ldy + h * a.hd + m;
+    y[0] = r0;
+    y[half] = r1;
+  } else {  // EPI_ROPE_K: into the K cache (qwen2.rs:497)
+    const SeqDesc sd = a.seqs[rd.seq];
+    float* kc = sd.k + ((size_t)a.layer * sd.cap + rd.pos) * a.kvd + h * a.hd + m;
+    kc[0] = r0;
+    kc[half] = r1;
+  }
+}
+
+// Applies the segment's epilogue to the CTA's results val[b * nrows + r]
+// (rows row_base.., columns col0..). Called by all threads of the CTA.
+__device__ void cta_epilogue(const GemvArgs& a, const GemvSeg& sg, const float* val, float* scratch, int row_base,
+                             int nrows, int col0, int ncols, const float* inv) {
+  const uint32_t n_out = sg.w.n_out;
+  if (epi_is_pair(sg.epi)) {
+    const int np = nrows >> 1;
+    for (int t = threadIdx.x; t < np * ncols; t += blockDim.x) {
+      const int b = t / np, pr = t - b * np;
+      const uint32_t o = (uint32_t)(row_base + 2 * pr);
+      if (o < n_out)
+        epi_pair(a, sg, o, (uint32_t)(col0 + b), val[b * nrows + 2 * pr] * inv[b], val[b * nrows + 2 * pr + 1] * inv[b]);
+    }
+    return;
+  }
+  for (int t = threadIdx.x; t < nrows * ncols; t += blockDim.x) {
+    const int b = t / nrows, r = t - b * nrows;
+    const uint32_t o = (uint32_t)(row_base + r);
+    float xn = 0.f;
+    if (o < n_out) xn = epi_single(a, sg, o, (uint32_t)(col0 + b), val[t] * inv[b]);
+    if (sg.epi == EPI_RESID) scratch[t] = xn * xn;
+  }
+  if (sg.epi != EPI_RESID) return;
+  __syncthreads();
+  if ((int)threadIdx.x < ncols) {  // per-column partial sum of x^2 over this CTA's rows, in row order
+    const int b = threadIdx.x;
+    float s2 = 0.f;
+    for (int r = 0; r < nrows; r++) s2 += scratch[b * nrows + r];
+    a.out_parts[(size_t)(col0 + b) * gridDim.y + blockIdx.y] = s2;
+  }
 }
 
 // ------------------------------------------------------ batch-1 GEMV ----
@@ -527,8 +614,12 @@ __global__ void __launch_bounds__(B1_WARPS * 32, 2) gemv1_kernel(const __grid_co
   if (a.nseg > 2 && cta >= a.seg[2].cta_begin) sg = a.seg[2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = B1_WARPS / nslice, grp = warp / nslice, slice = warp - grp * nslice;
-  const int row0 = (int)(cta - sg.cta_begin) * (groups * B1_R) + grp * B1_R;
+  const int row_base = (int)(cta - sg.cta_begin) * (groups * B1_R);
+  const int row0 = row_base + grp * B1_R;
   __shared__ float red[B1_WARPS][B1_R];
+  __shared__ float val[B1_WARPS * B1_R];
+  __shared__ float scratch[B1_WARPS * B1_R];
+  __shared__ float inv[1];
   float acc[B1_R];
 #pragma unroll
   for (int r = 0; r < B1_R; r++) acc[r] = 0.f;
@@ -537,27 +628,32 @@ __global__ void __launch_bounds__(B1_WARPS * 32, 2) gemv1_kernel(const __grid_co
       q4k_b1<B1_R>(sg.w, a.xp4, row0, slice, nslice, acc);
     } else if (sg.w.type == 14) {
       q6k_b1<B1_R>(sg.w, a.xp6, row0, slice, nslice, acc);
-    } else if (slice == 0) {
-      gemv_rows<0, B1_R, 1>(sg, a.x, a.ldx, row0, 0, 1);  // Q8_0 / Q5_0: generic units, unsplit
+    } else if (slice == 0) {  // Q8_0 / Q5_0: generic units, unsplit
+      float acc2[B1_R][1];
+      gemv_rows<0, B1_R, 1>(sg, a.x, a.ldx, row0, 0, 1, acc2);
+#pragma unroll
+      for (int r = 0; r < B1_R; r++) acc[r] = lane == 0 ? acc2[r][0] : 0.f;
     }
   }
-  if (sg.w.type != 12 && sg.w.type != 14) return;
 #pragma unroll
   for (int r = 0; r < B1_R; r++) {
     const float v = warp_sum(acc[r]);
     if (lane == 0) red[warp][r] = v;
   }
-  __syncthreads();
-  if (slice == 0 && lane < B1_R) {
-    const uint32_t o = (uint32_t)(row0 + lane);
-    if (row0 < (int)sg.w.n_out && o < sg.w.n_out) {
-      float v = 0.f;
-      for (int k = 0; k < nslice; k++) v += red[warp + k][lane];
-      if (sg.bias) v = v + sg.bias[o];
-      if (sg.add) v = sg.y[o] + v;
-      sg.y[o] = v;
-    }
+  if (warp == 0) {
+    const float sc = input_scale(a, 0);
+    if (lane == 0) inv[0] = sc;
   }
+  __syncthreads();
+  const int nrows = groups * B1_R;
+  if ((int)threadIdx.x < nrows) {
+    const int g = threadIdx.x / B1_R, r = threadIdx.x - g * B1_R;
+    float v = 0.f;
+    for (int k = 0; k < nslice; k++) v += red[g * nslice + k][r];
+    val[threadIdx.x] = v;
+  }
+  __syncthreads();
+  cta_epilogue(a, sg, val, scratch, row_base, nrows, 0, 1, inv);
 }
 
 // grid.x = column tiles of BT (fastest, so CTAs sharing weights run together),
@@ -568,17 +664,41 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(const __grid_cons
   GemvSeg sg = a.seg[0];
   if (a.nseg > 1 && cta >= a.seg[1].cta_begin) sg = a.seg[1];
   if (a.nseg > 2 && cta >= a.seg[2].cta_begin) sg = a.seg[2];
-  const int warp = threadIdx.x >> 5;
-  const int row0 = (int)(cta - sg.cta_begin) * (GEMV_WARPS * R) + warp * R;
-  if (row0 >= (int)sg.w.n_out) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_base = (int)(cta - sg.cta_begin) * (GEMV_WARPS * R);
+  const int row0 = row_base + warp * R;
   const int col0 = blockIdx.x * BT;
   const int ncols = min(BT, (int)a.batch - col0);
-  switch (sg.w.type) {
-    case 12: gemv_rows<12, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
-    case 14: gemv_rows<14, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
-    case 8: gemv_rows<8, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
-    case 6: gemv_rows<6, R, BT>(sg, a.x, a.ldx, row0, col0, ncols); break;
+  __shared__ float val[BT * GEMV_WARPS * R];
+  __shared__ float scratch[BT * GEMV_WARPS * R];
+  __shared__ float inv[BT];
+  float acc[R][BT];
+  if (row0 < (int)sg.w.n_out) {
+    switch (sg.w.type) {
+      case 12: gemv_rows<12, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
+      case 14: gemv_rows<14, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
+      case 8: gemv_rows<8, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
+      default: gemv_rows<6, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int b = 0; b < BT; b++) acc[r][b] = 0.f;
   }
+  const int nrows = GEMV_WARPS * R;
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int b = 0; b < BT; b++) val[b * nrows + warp * R + r] = acc[r][b];
+  }
+  for (int b = warp; b < ncols; b += GEMV_WARPS) {
+    const float sc = input_scale(a, (uint32_t)(col0 + b));
+    if (lane == 0) inv[b] = sc;
+  }
+  __syncthreads();
+  cta_epilogue(a, sg, val, scratch, row_base, nrows, col0, ncols, inv);
 }
 
 // Writes rows of natural-layout activations in both permuted layouts.
@@ -586,6 +706,30 @@ __global__ void xpack_kernel(const float* x, uint32_t ldx, uint32_t K, float* p4
   const uint32_t r = blockIdx.y;
   for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < K; e += gridDim.x * blockDim.x)
     store_act(nullptr, 0, p4, p6, ldp, r, e, x[(size_t)r * ldx + e]);
+}
+
+// Embedding lookup (qwen2.rs:468-472) fused with the first layer's RMSNorm
+// input: x = row tok of the table (exact dequant), xn = x * nw in the natural
+// and permuted layouts, parts[r] = sum(x^2) (one partial per row).
+__global__ void embed_norm_kernel(DWDesc w, const uint32_t* tokens, float* x, uint32_t ldx, const float* nw, float* xn,
+                                  float* xn4, float* xn6, uint32_t ldxn, float* parts) {
+  const uint32_t r = blockIdx.x, tok = tokens[r], n = w.n_in;
+  float ss = 0.f;
+  for (uint32_t e = threadIdx.x; e < n; e += blockDim.x) {
+    const float v = dequant_elem(w, tok, e);
+    x[(size_t)r * ldx + e] = v;
+    store_act(xn, ldxn, xn4, xn6, xperm_len(n), r, e, v * nw[e]);
+    ss += v * v;
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) parts[r] = v;
+  }
 }
 
 // ------------------------------------------------------------ launch ----
@@ -618,8 +762,9 @@ uint32_t gemv_plan(GemvArgs& a) {
   return c;
 }
 
-cudaError_t launch_gemv(GemvArgs a, cudaStream_t st) {
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* grid_y) {
   const uint32_t ny = gemv_plan(a);
+  if (grid_y) *grid_y = ny;
   const dim3 blk(GEMV_WARPS * 32);
   if (a.batch == 1) gemv1_kernel<<<dim3(1, ny), B1_WARPS * 32, 0, st>>>(a, b1_slices(a));
   else if (a.batch == 2) gemv_kernel<2, 2><<<dim3(1, ny), blk, 0, st>>>(a);
@@ -638,6 +783,14 @@ cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st) {
   size_t n = (size_t)w.n_out * w.n_in;
   if (!n) return cudaSuccess;
   dequant_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_norm(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
+                              const float* nw, float* xn, float* xn4, float* xn6, uint32_t ldxn, float* parts,
+                              cudaStream_t st) {
+  if (!rows) return cudaSuccess;
+  embed_norm_kernel<<<rows, 512, 0, st>>>(w, tokens, x, ldx, nw, xn, xn4, xn6, ldxn, parts);
   return cudaGetLastError();
 }
 
@@ -694,7 +847,7 @@ cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st) {
     e = launch_xpack(a.x, a.ldx, K, 1, xp, xp + NOALLOC_MAX_K, st);
     if (e != cudaSuccess) return e;
   }
-  return launch_gemv(a, st);
+  return launch_gemv(a, st, nullptr);
 }
 
 }  // namespace sm

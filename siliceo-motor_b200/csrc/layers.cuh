@@ -9,21 +9,6 @@
 
 namespace sm {
 
-// One row of a forward pass (a token): which sequence it belongs to and its
-// absolute position.
-struct RowDesc {
-  uint32_t seq;
-  uint32_t pos;
-};
-
-// A sequence's KV storage: k/v are [n_layers][cap][kv_dim] f32.
-struct SeqDesc {
-  float* k;
-  float* v;
-  uint32_t cap;
-  uint32_t pad;
-};
-
 struct SampleParams {
   float temperature;
   int32_t top_k;  // < 0: None
@@ -34,8 +19,11 @@ struct SampleParams {
 constexpr int SAMPLER_MAX_TOP_K = 1024;
 
 uint32_t gemv_plan(GemvArgs& a);
-cudaError_t launch_gemv(GemvArgs a, cudaStream_t st);
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* grid_y = nullptr);
 cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st);
+cudaError_t launch_embed_norm(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
+                              const float* nw, float* xn, float* xn4, float* xn6, uint32_t ldxn, float* parts,
+                              cudaStream_t st);
 cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
                          cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
