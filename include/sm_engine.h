@@ -204,13 +204,14 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
 /* sm_gemv for callers that cannot allocate device memory: hosts that hand out
  * all device memory from their own pool, and latency-critical paths that may
  * not call cudaMalloc (it can synchronize the device). No counterpart in the
- * reference. It allocates nothing: batch 1 packs x into a fixed 256 KB device
- * array of the library instead of scratch that sm_gemv allocates on first
- * use, so n_in is limited to 32768 (larger n_in returns SM_ERR_ARG). Every
- * call on a device shares that array, so calls that overlap on the GPU race;
- * nothing in it needs clearing between calls. The first call on a device
- * looks the array's address up (once per device, with the weight's device
- * current); make that first call before any stream capture. */
+ * reference. It allocates nothing: the K-split of the batch-1 kernel keeps
+ * its partial sums and arrival counters in a fixed 260 KB device array of the
+ * library instead of the scratch sm_dweight_upload allocates for sm_gemv; a
+ * split that does not fit runs unsplit. Every call on a device shares that
+ * array, so calls that overlap on the GPU race; each call leaves the counters
+ * at zero, so nothing needs clearing between calls. The first call on a
+ * device looks the array's address up (once per device, with the weight's
+ * device current); make that first call before any stream capture. */
 int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream);
 
 /* ------------------------------------------------------------------------

@@ -6,61 +6,63 @@
 namespace sm {
 
 // ---------------------------------------------------------------------------
-// HBM layout of one quantized weight [n_out x n_in] (row-major, a row = one
-// output). Every byte of the GGUF encoding is kept; only its order changes so
-// that the 32 lanes of a warp read 512 contiguous bytes per load. A row is a
-// sequence of groups of up to 8 consecutive 256-weight blocks (nbg blocks in
-// the last group); lane L = 4*bi + u works on block bi of a group.
-//   Q4_K group: [nbg headers x 16 B: d, dmin, 12 scale bytes]
-//               [qs round 0: 4*nbg lanes x 16 B][qs round 1: 4*nbg lanes x 16 B]
-//               lane 4bi+j holds qs bytes 32j..32j+15 (round 0) and
-//               32j+16..32j+31 (round 1) of block bi.   1152 B per 8 blocks.
-//   Q6_K group: [ql a: 4*nbg x 16 B][ql b: 4*nbg x 16 B][qh: 4*nbg x 16 B]
-//               [scales: nbg x 16 B][d: nbg x 2 B, padded to 16 B]
-//               lane 4bi+2n+c holds ql[64n+16c..] (a), ql[64n+32+16c..] (b) and
-//               qh[32n+16c..] of block bi.                 1680 B per 8 blocks.
-//   Q8_0: body = 32 B of qs per block, aux = fp16 d per block.
+// HBM layout of one quantized weight [n_out x n_in] (a row = one output).
+// Every byte of the GGUF encoding is kept; only its order changes.
+//
+// Q4_K / Q6_K are stored in tiles of 16 rows (the last tile zero-padded): a
+// tile holds its 256-weight blocks in order, and block b of a tile is one
+// contiguous unit of all 16 rows. Inside a unit the bytes sit where lane
+// (g, t) = (lane >> 2, lane & 3) of a warp wants them when it owns rows g and
+// g + 8 of the tile as the A operand of mma.m16n8k16: every 16-byte load of
+// the warp reads 512 contiguous bytes.
+//   Q4_K unit, 2304 B:
+//     [16 rows x 16 B header: d, dmin, 12 scale bytes]
+//     [qs: 4 loads x 32 lanes x 16 B]  load L, lane (g, t): row g + 8*(L >> 1),
+//       bytes 32j + 8t .. 32j + 8t + 7 of qs for j = 2*(L & 1) and j + 1.
+//     (Byte q of qs holds weight 64j + (q & 31) in its low nibble and weight
+//     64j + 32 + (q & 31) in its high nibble, j = q >> 5: dequant.rs:98-124.)
+//   Q6_K unit, 3360 B:
+//     [16 rows x 16 int8 scales][16 rows x fp16 d][q: 6 loads x 32 lanes x 16 B]
+//     Lane (g, t) owns, per row, weight 16s + 4t + k of every 16-weight
+//     sub-block s (k = 0..3) as the 6-bit value v = q + 32, in 12 words:
+//     loads 0-1 (row g; 3-4 for row g + 8) = ql words i = 0..7, byte k of
+//     word i = low 4 bits of v(s = i, k) | low 4 bits of v(s = i + 8, k) << 4;
+//     load 2 (5) = qh words m = 0..3, holding the top 2 bits of the values of
+//     ql words 2m and 2m + 1 at bit (q6t_field(k, nib) + 8 * (i & 1)) & 31.
+//   Q8_0: body = 32 B of qs per block, aux = fp16 d per block (row-major).
 //   Q5_0: body = 16 B of qs per block, aux = 8 B per block (qh u32 | d fp16 | 0).
-// The GGUF block formats are dequant.rs:66-206 (Q6_K keeps d last in GGUF).
 // ---------------------------------------------------------------------------
 #ifdef __CUDACC__
 #define SM_HD __host__ __device__ __forceinline__
 #else
 #define SM_HD inline
 #endif
-SM_HD uint32_t q4k_group_bytes(uint32_t nbg) { return 144u * nbg; }
-SM_HD uint32_t q6k_group_bytes(uint32_t nbg) { return 208u * nbg + (2u * nbg + 15u) / 16u * 16u; }
-SM_HD uint32_t q4k_row_bytes(uint32_t nb) { return nb / 8u * q4k_group_bytes(8) + q4k_group_bytes(nb % 8u); }
-SM_HD uint32_t q6k_row_bytes(uint32_t nb) {
-  return nb / 8u * q6k_group_bytes(8) + (nb % 8u ? q6k_group_bytes(nb % 8u) : 0u);
+constexpr uint32_t Q4T_UNIT = 2304, Q6T_UNIT = 3360, Q6T_QOFF = 288;
+SM_HD bool tiled_type(uint32_t t) { return t == 12 || t == 14; }
+SM_HD uint32_t tile_unit_bytes(uint32_t t) { return t == 12 ? Q4T_UNIT : Q6T_UNIT; }
+// Byte offset, inside a Q4_K unit, of qs byte q (0..127) of tile row rr (0..15).
+SM_HD uint32_t q4t_qs_off(uint32_t rr, uint32_t q) {
+  const uint32_t j = q >> 5, t = (q >> 3) & 3u, e = q & 7u;
+  const uint32_t L = 2u * (rr >> 3) + (j >> 1), lane = 4u * (rr & 7u) + t;
+  return 256u + 512u * L + 16u * lane + 8u * (j & 1u) + e;
 }
-// Byte offsets inside a row for block b (of nb).
-struct KqPos {
-  uint32_t base, nbg, bi;
-};
-SM_HD KqPos kq_pos(uint32_t b, uint32_t nb, uint32_t group_bytes8) {
-  KqPos p;
-  p.base = (b >> 3) * group_bytes8;
-  p.nbg = nb - (b & ~7u) < 8u ? nb - (b & ~7u) : 8u;
-  p.bi = b & 7u;
-  return p;
+// Byte offsets, inside a Q6_K unit, of ql word i (0..7) and qh word m (0..3)
+// of lane t for tile row rr.
+SM_HD uint32_t q6t_w_off(uint32_t rr, uint32_t t, uint32_t i) {
+  return Q6T_QOFF + 512u * (3u * (rr >> 3) + (i >> 2)) + 16u * (4u * (rr & 7u) + t) + 4u * (i & 3u);
 }
-SM_HD uint32_t q4k_hdr_off(const KqPos& p) { return p.base + 16u * p.bi; }
-SM_HD uint32_t q4k_qs_off(const KqPos& p, uint32_t j, uint32_t round) {
-  return p.base + 16u * p.nbg + 16u * (round * 4u * p.nbg + 4u * p.bi + j);
+SM_HD uint32_t q6t_h_off(uint32_t rr, uint32_t t, uint32_t m) {
+  return Q6T_QOFF + 512u * (3u * (rr >> 3) + 2u) + 16u * (4u * (rr & 7u) + t) + 4u * m;
 }
-// part 0: ql a, 1: ql b, 2: qh
-SM_HD uint32_t q6k_q_off(const KqPos& p, uint32_t n, uint32_t c, uint32_t part) {
-  return p.base + 16u * (part * 4u * p.nbg + 4u * p.bi + 2u * n + c);
-}
-SM_HD uint32_t q6k_sc_off(const KqPos& p) { return p.base + 192u * p.nbg + 16u * p.bi; }
-SM_HD uint32_t q6k_d_off(const KqPos& p) { return p.base + 208u * p.nbg + 2u * p.bi; }
+// Bit position of the top 2 bits of byte k, nibble nib of an even ql word in
+// its qh word (odd words: the same positions in the qh word rotated right by 8).
+SM_HD uint32_t q6t_field(uint32_t k, uint32_t nib) { return (nib ? 8u : 4u) + 2u * (k & 1u) + 16u * (k >> 1); }
 
 struct DWDesc {
   const uint8_t* body;
   const uint8_t* aux;
   uint32_t type, n_out, n_in;
-  uint32_t body_stride;  // bytes per row
+  uint32_t body_stride;  // bytes per row; Q4_K / Q6_K: bytes per 16-row tile
   uint32_t aux_stride;   // bytes per row
 };
 
@@ -108,25 +110,20 @@ struct GemvArgs {
   const float* x;  // x[b * ldx + d]
   uint32_t ldx;
   uint32_t batch;
-  // Batch 1 reads the activations in the lane order of its K-quant kernels
-  // (xperm_q4k / xperm_q6k below); both copies are written by the kernel
-  // that produced x.
-  const float* xp4;
-  const float* xp6;
   // Input RMSNorm (qwen2.rs:647-660) folded into the GEMV: x holds x*w of the
   // un-normalized residual, and the dot products of column b are scaled by
   // 1/sqrt(sum(in_parts[b*in_np .. +in_np]) / in_n + in_eps) when in_parts is set.
   const float* in_parts;
   uint32_t in_np, in_n;
   float in_eps;
-  // EPI_RESID outputs: xn = x * nw, and per-CTA partial sums of x^2
-  // (out_parts[b * gridDim.y + cta]).
+  // EPI_RESID outputs: xn = x * nw, and partial sums of x^2 over groups of
+  // rows (out_parts[b * n_parts + group]; launch_gemv returns n_parts).
   const float* nw;
-  float *xn, *xn4, *xn6;
+  float* xn;
   uint32_t ldxn;
   float* out_parts;
-  // EPI_SILU outputs
-  float *h, *h4, *h6;
+  // EPI_SILU output
+  float* h;
   uint32_t ldh;
   // RoPE and KV-cache epilogues
   const RowDesc* rows;
@@ -134,47 +131,12 @@ struct GemvArgs {
   const float* cos_t;
   const float* sin_t;
   uint32_t layer, hd, kvd;
+  // Scratch of the tensor-core batch-1 GEMV when it splits K: per-slice
+  // partial dot products and per-group arrival counters (zero between launches).
+  float* ks_part;
+  uint32_t* ks_cnt;
+  uint32_t ks_part_cap, ks_cnt_cap;
 };
-
-// ---------------------------------------------------------------------------
-// Lane-interleaved activation layouts of the batch-1 GEMV. A warp step covers
-// 8 consecutive 256-weight blocks (2048 activations); lane L = 4*bi + u owns 64
-// activations of block bi and reads them as 16 float4 loads k = 0..15. The
-// float4 of (step t, k, lane) is stored at t*2048 + k*128 + 4*lane, so every
-// load instruction of the warp reads 512 contiguous bytes. Rows are padded to
-// whole steps: xperm_len(K) floats.
-//   Q4_K lane (bi, j):    float4 k = activations 64j + 4k .. +3 of the block
-//   Q6_K lane (bi, n, c): float4 k = 4g + i -> 128n + 16c + 32g + 4i .. +3
-// Inside each float4 the four activations e..e+3 are stored as (e, e+2, e+1,
-// e+3): the kernels turn bytes (0, 2) and (1, 3) of a weight word into one
-// half2 each, and the float4's halves are then their f32x2 partners.
-// ---------------------------------------------------------------------------
-#ifdef __CUDACC__
-__host__ __device__ __forceinline__
-#else
-inline
-#endif
-uint32_t xperm_len(uint32_t K) { return (K + 2047u) / 2048u * 2048u; }
-
-#ifdef __CUDACC__
-__device__ __forceinline__ uint32_t xperm_q4k(uint32_t e) {
-  const uint32_t b = e >> 8, o = e & 255, t = b >> 3, bi = b & 7;
-  const uint32_t j = o >> 6, r = o & 63;
-  return t * 2048u + (r >> 2) * 128u + (4u * bi + j) * 4u + (((r & 1u) << 1) | ((r >> 1) & 1u));
-}
-__device__ __forceinline__ uint32_t xperm_q6k(uint32_t e) {
-  const uint32_t b = e >> 8, o = e & 255, t = b >> 3, bi = b & 7;
-  const uint32_t n = o >> 7, r1 = o & 127, g = r1 >> 5, r2 = r1 & 31, c = r2 >> 4, i = (r2 & 15) >> 2;
-  return t * 2048u + (4u * g + i) * 128u + (4u * bi + 2u * n + c) * 4u + (((r2 & 1u) << 1) | ((r2 >> 1) & 1u));
-}
-// Writes activation e of row `row` in the natural layout and both permuted ones.
-__device__ __forceinline__ void store_act(float* nat, uint32_t ldn, float* p4, float* p6, uint32_t ldp, uint32_t row,
-                                          uint32_t e, float v) {
-  if (nat) nat[(size_t)row * ldn + e] = v;
-  if (p4) p4[(size_t)row * ldp + xperm_q4k(e)] = v;
-  if (p6) p6[(size_t)row * ldp + xperm_q6k(e)] = v;
-}
-#endif
 
 #ifdef __CUDACC__
 // fp16 bit pattern -> f32 as the reference decodes it (dequant.rs:12-33):

@@ -56,42 +56,64 @@ int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_
     return SM_ERR_UNSUPPORTED;
   }
   const uint64_t nb = n_in / bs, row_src = nb * tb;
+  const bool tiled = tiled_type(type);
+  const uint64_t n_tiles = (n_out + 15) / 16, n_store = tiled ? n_tiles * 16 : n_out;
   uint64_t body_stride = 0, aux_stride = 0;
   switch (type) {
-    case QT_Q4K: body_stride = q4k_row_bytes((uint32_t)nb); break;
-    case QT_Q6K: body_stride = q6k_row_bytes((uint32_t)nb); break;
+    case QT_Q4K: body_stride = nb * Q4T_UNIT; break;  // per 16-row tile
+    case QT_Q6K: body_stride = nb * Q6T_UNIT; break;
     case QT_Q8_0: body_stride = nb * 32; aux_stride = nb * 2; break;
     case QT_Q5_0: body_stride = nb * 16; aux_stride = nb * 8; break;
   }
+  if (body_stride > 0xFFFFFFFFull) {
+    set_error("weight row too long");
+    return SM_ERR_UNSUPPORTED;
+  }
   aux_stride = (aux_stride + 15) / 16 * 16;
-  const uint64_t body_bytes = body_stride * n_out, aux_bytes = aux_stride * n_out;
+  const uint64_t body_bytes = tiled ? body_stride * n_tiles : body_stride * n_out, aux_bytes = aux_stride * n_out;
   std::vector<uint8_t> body(body_bytes, 0), aux(aux_bytes, 0);
-  for (uint64_t o = 0; o < n_out; o++) {
+  uint8_t v6[256];
+  for (uint64_t o = 0; o < n_store; o++) {
+    if (o >= n_out) break;  // padding rows of the last tile stay zero (d = 0)
     const uint8_t* r = src + o * row_src;
+    const uint32_t rr = (uint32_t)(o & 15);
+    uint8_t* tile = body.data() + (o >> 4) * body_stride;
     uint8_t* bd = body.data() + o * body_stride;
     uint8_t* ax = aux.data() + o * aux_stride;
     switch (type) {
-      case QT_Q4K:  // groups of 8 blocks, lane-interleaved qs (device.cuh)
+      case QT_Q4K:  // 16-row tiles (device.cuh)
         for (uint32_t b = 0; b < nb; b++) {
-          const uint8_t* blk = r + (size_t)b * 144;
-          const KqPos ps = kq_pos(b, (uint32_t)nb, q4k_group_bytes(8));
-          std::memcpy(bd + q4k_hdr_off(ps), blk, 16);
-          for (uint32_t j = 0; j < 4; j++)
-            for (uint32_t rd = 0; rd < 2; rd++) std::memcpy(bd + q4k_qs_off(ps, j, rd), blk + 16 + 32 * j + 16 * rd, 16);
+          const uint8_t* blk = r + (size_t)b * 144;  // d | dmin | scales 12 | qs 128
+          uint8_t* u = tile + (size_t)b * Q4T_UNIT;
+          std::memcpy(u + 16 * rr, blk, 16);
+          for (uint32_t q = 0; q < 128; q++) u[q4t_qs_off(rr, q)] = blk[16 + q];
         }
         break;
       case QT_Q6K:
         for (uint32_t b = 0; b < nb; b++) {
-          const uint8_t* blk = r + (size_t)b * 210;  // ql 128 | qh 64 | scales 16 | d 2
-          const KqPos ps = kq_pos(b, (uint32_t)nb, q6k_group_bytes(8));
-          for (uint32_t n = 0; n < 2; n++)
-            for (uint32_t c = 0; c < 2; c++) {
-              std::memcpy(bd + q6k_q_off(ps, n, c, 0), blk + 64 * n + 16 * c, 16);
-              std::memcpy(bd + q6k_q_off(ps, n, c, 1), blk + 64 * n + 32 + 16 * c, 16);
-              std::memcpy(bd + q6k_q_off(ps, n, c, 2), blk + 128 + 32 * n + 16 * c, 16);
-            }
-          std::memcpy(bd + q6k_sc_off(ps), blk + 192, 16);
-          std::memcpy(bd + q6k_d_off(ps), blk + 208, 2);
+          const uint8_t* blk = r + (size_t)b * 210;  // ql 128 | qh 64 | scales 16 | d 2 (dequant.rs:178-206)
+          uint8_t* u = tile + (size_t)b * Q6T_UNIT;
+          for (uint32_t l = 0; l < 256; l++) {  // 6-bit value q + 32 of weight l
+            const uint32_t n = l >> 7, k = (l & 127) >> 5, ll = l & 31;
+            const uint32_t qlb = blk[64 * n + ll + 32 * (k & 1)];
+            const uint32_t lo = (k >> 1) ? (qlb >> 4) : (qlb & 0x0F);
+            const uint32_t hi = (blk[128 + 32 * n + ll] >> (2 * k)) & 3;
+            v6[l] = (uint8_t)(lo | (hi << 4));
+          }
+          uint32_t W[4][8] = {}, Hq[4][4] = {};
+          for (uint32_t sb = 0; sb < 16; sb++)
+            for (uint32_t t = 0; t < 4; t++)
+              for (uint32_t k = 0; k < 4; k++) {
+                const uint32_t v = v6[16 * sb + 4 * t + k], i = sb & 7, nib = sb >> 3;
+                W[t][i] |= (v & 0x0F) << (8 * k + 4 * nib);
+                Hq[t][i >> 1] |= (v >> 4) << ((q6t_field(k, nib) + 8 * (i & 1)) & 31);
+              }
+          for (uint32_t t = 0; t < 4; t++) {
+            for (uint32_t i = 0; i < 8; i++) std::memcpy(u + q6t_w_off(rr, t, i), &W[t][i], 4);
+            for (uint32_t m = 0; m < 4; m++) std::memcpy(u + q6t_h_off(rr, t, m), &Hq[t][m], 4);
+          }
+          std::memcpy(u + 16 * rr, blk + 192, 16);
+          std::memcpy(u + 256 + 2 * rr, blk + 208, 2);
         }
         break;
       case QT_Q8_0:
@@ -130,6 +152,16 @@ int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_
   out->d.body_stride = (uint32_t)body_stride;
   out->d.aux_stride = (uint32_t)aux_stride;
   return SM_OK;
+}
+
+GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, uint32_t epi) {
+  GemvSeg s{};
+  s.w = w.d;
+  s.y = y;
+  s.ldy = ldy;
+  s.bias = bias;
+  s.epi = epi;
+  return s;
 }
 
 void free_weight(DW& w) {
@@ -189,9 +221,11 @@ struct sm_model {
   // workspace
   float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
         *u = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr;
-  // permuted copies of the GEMV inputs for batch 1 (xperm_q4k / xperm_q6k)
-  float *xn4 = nullptr, *xn6 = nullptr, *att4 = nullptr, *att6 = nullptr, *g4 = nullptr, *g6 = nullptr;
-  // per-CTA partial sums of x^2 written by residual GEMVs, read by the next GEMV
+  // K-split scratch of the batch-1 tensor-core GEMVs (counters zeroed at load)
+  float* ks_part = nullptr;
+  uint32_t* ks_cnt = nullptr;
+  uint32_t ks_part_cap = 0, ks_cnt_cap = 0;
+  // partial sums of x^2 written by residual GEMVs, read by the next GEMV
   float *parts_a = nullptr, *parts_b = nullptr;
   uint32_t parts_cap = 0;
   uint8_t* mask_dev = nullptr;
@@ -453,11 +487,47 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
       (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)))
     return rc;
   {
-    const size_t pH = (size_t)R * xperm_len((uint32_t)H), pF = (size_t)R * xperm_len((uint32_t)F);
-    if ((rc = dev_alloc(m, (void**)&m->xn4, pH * 4)) || (rc = dev_alloc(m, (void**)&m->xn6, pH * 4)) ||
-        (rc = dev_alloc(m, (void**)&m->att4, pH * 4)) || (rc = dev_alloc(m, (void**)&m->att6, pH * 4)) ||
-        (rc = dev_alloc(m, (void**)&m->g4, pF * 4)) || (rc = dev_alloc(m, (void**)&m->g6, pF * 4)))
+    // K-split scratch: the most any batch-1 GEMV of this model asks for
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device));
+    uint64_t need_part = 0;
+    uint32_t need_cnt = 0;
+    for (const Layer& L : m->layers) {
+      GemvArgs probe[4] = {};
+      probe[0].nseg = 3;
+      probe[0].seg[0] = seg(L.wq, nullptr, 0, nullptr, EPI_STORE);
+      probe[0].seg[1] = seg(L.wk, nullptr, 0, nullptr, EPI_STORE);
+      probe[0].seg[2] = seg(L.wv, nullptr, 0, nullptr, EPI_STORE);
+      probe[1].seg[0] = seg(L.wo, nullptr, 0, nullptr, EPI_STORE);
+      probe[2].seg[0] = seg(L.wgu, nullptr, 0, nullptr, EPI_STORE);
+      probe[3].seg[0] = seg(L.wdown, nullptr, 0, nullptr, EPI_STORE);
+      for (int i = 0; i < 4; i++) {
+        if (!probe[i].nseg) probe[i].nseg = 1;
+        probe[i].batch = 1;
+        uint64_t pp = 0;
+        uint32_t pc = 0;
+        gemv_tc_scratch_need(probe[i], (uint32_t)sms, &pp, &pc);
+        need_part = std::max(need_part, pp);
+        need_cnt = std::max(need_cnt, pc);
+      }
+    }
+    {
+      GemvArgs hp{};
+      hp.nseg = 1;
+      hp.batch = 1;
+      hp.seg[0] = seg(m->output, nullptr, 0, nullptr, EPI_STORE);
+      uint64_t pp = 0;
+      uint32_t pc = 0;
+      gemv_tc_scratch_need(hp, (uint32_t)sms, &pp, &pc);
+      need_part = std::max(need_part, pp);
+      need_cnt = std::max(need_cnt, pc);
+    }
+    m->ks_part_cap = (uint32_t)std::max<uint64_t>(need_part, 16);
+    m->ks_cnt_cap = std::max<uint32_t>(need_cnt, 16);
+    if ((rc = dev_alloc(m, (void**)&m->ks_part, (size_t)m->ks_part_cap * 4)) ||
+        (rc = dev_alloc(m, (void**)&m->ks_cnt, (size_t)m->ks_cnt_cap * 4)))
       return rc;
+    CK(cudaMemset(m->ks_cnt, 0, (size_t)m->ks_cnt_cap * 4));
     m->parts_cap = (uint32_t)(H / 4 + 64);
     if ((rc = dev_alloc(m, (void**)&m->parts_a, (size_t)R * m->parts_cap * 4)) ||
         (rc = dev_alloc(m, (void**)&m->parts_b, (size_t)R * m->parts_cap * 4)))
@@ -498,16 +568,6 @@ void destroy_model(sm_model* m) {
   delete m;
 }
 
-GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, uint32_t epi) {
-  GemvSeg s{};
-  s.w = w.d;
-  s.y = y;
-  s.ldy = ldy;
-  s.bias = bias;
-  s.epi = epi;
-  return s;
-}
-
 // The layer stack for `nrows` rows described in din (tokens, rows, seqs),
 // then final norm + output head for the nsel rows listed in din.sel.
 // qwen2.rs:460-561 with the kernels of gemv.cu / layers.cu.
@@ -519,14 +579,6 @@ GemvSeg seg(const DW& w, float* y, uint32_t ldy, const float* bias, uint32_t epi
 cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
   const sm_config& c = m->c;
   const uint32_t H = (uint32_t)c.n_embd, F = (uint32_t)c.n_ff, kvd = m->kvd, hd = (uint32_t)c.head_dim;
-  // batch 1 reads permuted activations; larger batches the natural layout
-  const bool b1 = nrows == 1;
-  float* xn4 = b1 ? m->xn4 : nullptr;
-  float* xn6 = b1 ? m->xn6 : nullptr;
-  float* att4 = b1 ? m->att4 : nullptr;
-  float* att6 = b1 ? m->att6 : nullptr;
-  float* g4 = b1 ? m->g4 : nullptr;
-  float* g6 = b1 ? m->g6 : nullptr;
   cudaError_t e;
 #define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
   GemvArgs base{};
@@ -539,14 +591,17 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   base.sin_t = m->sin_t;
   base.hd = hd;
   base.kvd = kvd;
-  RK(launch_embed_norm(m->tok_embd.d, m->din.tok, nrows, m->x, H, m->layers[0].attn_norm, m->xn, xn4, xn6, H,
-                       m->parts_a, st));
+  base.ks_part = m->ks_part;
+  base.ks_cnt = m->ks_cnt;
+  base.ks_part_cap = m->ks_part_cap;
+  base.ks_cnt_cap = m->ks_cnt_cap;
+  RK(launch_embed_norm(m->tok_embd.d, m->din.tok, nrows, m->x, H, m->layers[0].attn_norm, m->xn, H, m->parts_a, st));
   uint32_t np_a = 1, np_b = 0;
   for (uint32_t li = 0; li < c.n_layers; li++) {
     const Layer& L = m->layers[li];
     GemvArgs a = base;
     a.layer = li;
-    a.x = m->xn; a.ldx = H; a.xp4 = xn4; a.xp6 = xn6;
+    a.x = m->xn; a.ldx = H;
     a.in_parts = m->parts_a; a.in_np = np_a;
     a.nseg = 3;
     a.seg[0] = seg(L.wq, m->q, H, L.bq, EPI_ROPE_Q);
@@ -554,29 +609,29 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     a.seg[2] = seg(L.wv, nullptr, 0, L.bv, EPI_V);
     RK(launch_gemv(a, st));
     RK(launch_attention(m->q, H, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads, (uint32_t)c.n_kv_heads, hd,
-                        m->part_o, m->part_ml, m->max_splits, m->att, H, att4, att6, st));
+                        m->part_o, m->part_ml, m->max_splits, m->att, H, st));
     GemvArgs o = base;
     o.layer = li;
-    o.x = m->att; o.ldx = H; o.xp4 = att4; o.xp6 = att6;
+    o.x = m->att; o.ldx = H;
     o.nseg = 1;
     o.seg[0] = seg(L.wo, m->x, H, nullptr, EPI_RESID);
-    o.nw = L.ffn_norm; o.xn = m->xn; o.xn4 = xn4; o.xn6 = xn6; o.ldxn = H; o.out_parts = m->parts_b;
+    o.nw = L.ffn_norm; o.xn = m->xn; o.ldxn = H; o.out_parts = m->parts_b;
     RK(launch_gemv(o, st, &np_b));
     GemvArgs gu = base;
     gu.layer = li;
-    gu.x = m->xn; gu.ldx = H; gu.xp4 = xn4; gu.xp6 = xn6;
+    gu.x = m->xn; gu.ldx = H;
     gu.in_parts = m->parts_b; gu.in_np = np_b;
     gu.nseg = 1;
     gu.seg[0] = seg(L.wgu, nullptr, 0, nullptr, EPI_SILU);
-    gu.h = m->g; gu.h4 = g4; gu.h6 = g6; gu.ldh = F;
+    gu.h = m->g; gu.ldh = F;
     RK(launch_gemv(gu, st));
     GemvArgs dn = base;
     dn.layer = li;
-    dn.x = m->g; dn.ldx = F; dn.xp4 = g4; dn.xp6 = g6;
+    dn.x = m->g; dn.ldx = F;
     dn.nseg = 1;
     dn.seg[0] = seg(L.wdown, m->x, H, nullptr, EPI_RESID);
     dn.nw = li + 1 < c.n_layers ? m->layers[li + 1].attn_norm : m->output_norm;
-    dn.xn = m->xn; dn.xn4 = xn4; dn.xn6 = xn6; dn.ldxn = H; dn.out_parts = m->parts_a;
+    dn.xn = m->xn; dn.ldxn = H; dn.out_parts = m->parts_a;
     RK(launch_gemv(dn, st, &np_a));
   }
   if (nsel) {
@@ -584,14 +639,12 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     hd_.batch = nsel;
     hd_.nseg = 1;
     hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, EPI_STORE);
-    hd_.x = m->xn; hd_.ldx = H; hd_.xp4 = m->xn4; hd_.xp6 = m->xn6;
+    hd_.x = m->xn; hd_.ldx = H;
     if (nsel == nrows) {  // every row: the last down GEMV prepared the final norm's input
       hd_.in_parts = m->parts_a;
       hd_.in_np = np_a;
     } else {  // a selection (prefill): normalize the selected rows here (qwen2.rs:555-560)
-      const bool h1 = nsel == 1;
-      RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, h1 ? m->xn4 : nullptr, h1 ? m->xn6 : nullptr,
-                        nsel, H, c.rms_eps, st));
+      RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
     }
     RK(launch_gemv(hd_, st));
   }
@@ -755,7 +808,8 @@ static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* 
   }
   auto* m = new sm_model();
   m->device = opts ? opts->device : 0;
-  if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+  if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      gemv_tc_prepare() != cudaSuccess) {
     cudaGetLastError();
     set_error("cannot use CUDA device " + std::to_string(m->device));
     delete m;
@@ -1100,7 +1154,10 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
 struct sm_dweight {
   DW w;
   int device;
-  float* xp = nullptr;  // permuted activations for batch 1 (both layouts), allocated on first use
+  // K-split scratch of its batch-1 tensor-core GEMV (counters zeroed)
+  float* ks_part = nullptr;
+  uint32_t* ks_cnt = nullptr;
+  uint32_t ks_part_cap = 0, ks_cnt_cap = 0;
 };
 
 int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t n_in, sm_dweight** out) {
@@ -1111,12 +1168,34 @@ int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t
   w->device = dev;
   int rc = upload_weight(type, (const uint8_t*)bytes, n_out, n_in, &w->w);
   if (rc) { delete w; return rc; }
+  int sms = 0;
+  GemvArgs probe{};
+  probe.nseg = 1;
+  probe.batch = 1;
+  probe.seg[0] = seg(w->w, nullptr, 0, nullptr, EPI_STORE);
+  uint64_t need_part = 0;
+  uint32_t need_cnt = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+    gemv_tc_scratch_need(probe, (uint32_t)sms, &need_part, &need_cnt);
+  if (need_part && need_part <= 0xFFFFFFFFull) {
+    if (cudaMalloc((void**)&w->ks_part, need_part * 4) != cudaSuccess ||
+        cudaMalloc((void**)&w->ks_cnt, (size_t)need_cnt * 4) != cudaSuccess ||
+        cudaMemset(w->ks_cnt, 0, (size_t)need_cnt * 4) != cudaSuccess) {
+      cudaGetLastError();
+      sm_dweight_free(w);
+      set_error("cudaMalloc failed for the GEMV scratch");
+      return SM_ERR_OOM;
+    }
+    w->ks_part_cap = (uint32_t)need_part;
+    w->ks_cnt_cap = need_cnt;
+  }
   *out = w;
   return SM_OK;
 }
 int sm_dweight_free(sm_dweight* w) {
   if (!w) return SM_OK;
-  if (w->xp) cudaFree(w->xp);
+  if (w->ks_part) cudaFree(w->ks_part);
+  if (w->ks_cnt) cudaFree(w->ks_cnt);
   free_weight(w->w);
   delete w;
   return SM_OK;
@@ -1141,13 +1220,10 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
   a.batch = (uint32_t)batch;
   a.nseg = 1;
   a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, EPI_STORE);
-  if (batch == 1) {
-    const uint32_t lp = xperm_len(w->w.d.n_in);
-    if (!w->xp) CK(cudaMalloc((void**)&w->xp, 2 * (size_t)lp * 4));
-    a.xp4 = w->xp;
-    a.xp6 = w->xp + lp;
-    CK(launch_xpack(x_dev, w->w.d.n_in, w->w.d.n_in, 1, w->xp, w->xp + lp, (cudaStream_t)stream));
-  }
+  a.ks_part = w->ks_part;
+  a.ks_cnt = w->ks_cnt;
+  a.ks_part_cap = w->ks_part_cap;
+  a.ks_cnt_cap = w->ks_cnt_cap;
   CK(launch_gemv(a, (cudaStream_t)stream));
   return SM_OK;
 }
@@ -1158,11 +1234,6 @@ int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint6
   if (!w || !x_dev || !y_dev) { set_error("null argument"); return SM_ERR_ARG; }
   if (batch < 1 || batch > 32) { set_error("sm_gemv_noalloc: batch must be 1..32"); return SM_ERR_ARG; }
   if (((uintptr_t)x_dev & 15) || (w->w.d.n_in & 3)) { set_error("sm_gemv_noalloc: x must be 16-byte aligned"); return SM_ERR_ARG; }
-  if (w->w.d.n_in > gemv_noalloc_max_k()) {
-    set_error("sm_gemv_noalloc: n_in " + std::to_string(w->w.d.n_in) + " exceeds the fixed scratch limit of " +
-              std::to_string(gemv_noalloc_max_k()) + " inputs");
-    return SM_ERR_ARG;
-  }
   int dev = -1;
   CK(cudaGetDevice(&dev));
   if (dev != w->device) {

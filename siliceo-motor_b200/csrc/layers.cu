@@ -11,7 +11,7 @@ namespace sm {
 // out = x * (1/sqrt(sum(x^2)/n + eps)) * w  (qwen2.rs:647-660, 748-756).
 // rows: optional row selection (row r of out reads row rows[r] of x).
 __global__ void rmsnorm_kernel(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out,
-                               uint32_t ldo, float* p4, float* p6, uint32_t n, float eps) {
+                               uint32_t ldo, uint32_t n, float eps) {
   const uint32_t r = blockIdx.x;
   const float* xr = x + (size_t)(sel ? sel[r] : r) * ldx;
   float ss = 0.f;
@@ -27,9 +27,8 @@ __global__ void rmsnorm_kernel(const float* x, uint32_t ldx, const uint32_t* sel
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(red[0] / (float)n + eps);
-  const uint32_t ldp = xperm_len(n);
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
-    store_act(out, ldo, p4, p6, ldp, r, i, __fmul_rn(__fmul_rn(xr[i], inv), w[i]));
+    out[(size_t)r * ldo + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
 // --------------------------------------------------- RoPE + KV append ----
@@ -209,7 +208,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
 }
 
 __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const RowDesc* rows, uint32_t Hq,
-                                    uint32_t hd, uint32_t max_splits, float* out, uint32_t ldo, float* p4, float* p6) {
+                                    uint32_t hd, uint32_t max_splits, float* out, uint32_t ldo) {
   const uint32_t r = blockIdx.x / Hq, h = blockIdx.x - r * Hq;
   const uint32_t L = rows[r].pos + 1;
   const uint32_t tiles = (L + ATT_T - 1) / ATT_T;
@@ -224,18 +223,17 @@ __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, c
   for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
     float acc = 0.f;
     for (uint32_t s = 0; s < ns; s++) acc = fmaf(po[(size_t)s * hd + d], expf(ml[2 * s] - M), acc);
-    store_act(out, ldo, p4, p6, xperm_len(Hq * hd), r, h * hd + d, acc / den);
+    out[(size_t)r * ldo + h * hd + d] = acc / den;
   }
 }
 
 // -------------------------------------------------------------- SwiGLU ----
 // gate = silu(gate) * up, silu(x) = x / (1 + exp(-x)) (qwen2.rs:743-745, 546-548).
-__global__ void silu_mul_kernel(float* gate, const float* up, uint32_t F, size_t n, float* p4, float* p6) {
-  const uint32_t ldp = xperm_len(F);
+__global__ void silu_mul_kernel(float* gate, const float* up, uint32_t F, size_t n) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float gv = gate[i];
     const uint32_t r = (uint32_t)(i / F), e = (uint32_t)(i - (size_t)r * F);
-    store_act(gate, F, p4, p6, ldp, r, e, __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), up[i]));
+    gate[(size_t)r * F + e] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), up[i]);
   }
 }
 
@@ -471,9 +469,9 @@ __global__ void record_tokens_kernel(const uint32_t* tok, uint32_t rows, uint32_
 
 // --------------------------------------------------------------- launch ----
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
-                           float* p4, float* p6, uint32_t rows, uint32_t n, float eps, cudaStream_t st) {
+                           uint32_t rows, uint32_t n, float eps, cudaStream_t st) {
   if (!rows) return cudaSuccess;
-  rmsnorm_kernel<<<rows, n >= 4096 ? 1024 : 512, 0, st>>>(x, ldx, sel, w, out, ldo, p4, p6, n, eps);
+  rmsnorm_kernel<<<rows, n >= 4096 ? 1024 : 512, 0, st>>>(x, ldx, sel, w, out, ldo, n, eps);
   return cudaGetLastError();
 }
 
@@ -491,7 +489,7 @@ size_t attn_smem_bytes(uint32_t G, uint32_t hd) {
 
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
-                             uint32_t max_splits, float* out, uint32_t ldo, float* p4, float* p6, cudaStream_t st) {
+                             uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st) {
   if (!nrows) return cudaSuccess;
   const uint32_t G = Hq / Hkv;
   const size_t sm = attn_smem_bytes(G, hd);
@@ -500,14 +498,14 @@ cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, 
                                                                             scale, part_o, part_ml, max_splits);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo, p4, p6);
+  attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo);
   return cudaGetLastError();
 }
 
-cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, float* p4, float* p6, cudaStream_t st) {
+cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, cudaStream_t st) {
   if (!n) return cudaSuccess;
   const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 16);
-  silu_mul_kernel<<<blocks, 256, 0, st>>>(gate, up, F, n, p4, p6);
+  silu_mul_kernel<<<blocks, 256, 0, st>>>(gate, up, F, n);
   return cudaGetLastError();
 }
 

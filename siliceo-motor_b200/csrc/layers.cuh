@@ -19,30 +19,33 @@ struct SampleParams {
 constexpr int SAMPLER_MAX_TOP_K = 1024;
 
 uint32_t gemv_plan(GemvArgs& a);
-cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* grid_y = nullptr);
+// n_parts: the number of out_parts entries per column an EPI_RESID launch writes.
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts = nullptr);
 cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st);
 cudaError_t launch_embed_norm(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
-                              const float* nw, float* xn, float* xn4, float* xn6, uint32_t ldxn, float* parts,
-                              cudaStream_t st);
+                              const float* nw, float* xn, uint32_t ldxn, float* parts, cudaStream_t st);
 cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
                          cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
-                           float* p4, float* p6, uint32_t rows, uint32_t n, float eps, cudaStream_t st);
-cudaError_t launch_xpack(const float* x, uint32_t ldx, uint32_t K, uint32_t rows, float* p4, float* p6, cudaStream_t st);
+                           uint32_t rows, uint32_t n, float eps, cudaStream_t st);
 cudaError_t launch_rope_kv(float* q, const float* k, const float* v, uint32_t ldq, uint32_t ldkv, const RowDesc* rows,
                            const SeqDesc* seqs, uint32_t nrows, uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd,
                            const float* cos_t, const float* sin_t, cudaStream_t st);
 size_t attn_smem_bytes(uint32_t G, uint32_t hd);
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
-                             uint32_t max_splits, float* out, uint32_t ldo, float* p4, float* p6, cudaStream_t st);
-cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, float* p4, float* p6, cudaStream_t st);
+                             uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st);
+cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, cudaStream_t st);
 cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const uint8_t* mask,
                           const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
                           RowDesc* advance, cudaStream_t st);
 
-uint32_t gemv_noalloc_max_k();
 cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st);
+// Batch-1 Q4_K/Q6_K GEMVs run on the tensor cores (gemv_tc.cu); launch_gemv
+// dispatches to that kernel. Per-device set-up, and the K-split scratch
+// (floats, counters) a launch of this shape may use on a GPU with `sms` SMs:
+cudaError_t gemv_tc_prepare();
+void gemv_tc_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt);
 cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
                                  uint32_t cap_steps, cudaStream_t st);
 

@@ -451,7 +451,7 @@ class DWeight:
         _check(lib().sm_gemv(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), batch, C.c_void_p(stream)))
 
     def gemv_noalloc(self, x_ptr: int, y_ptr: int, batch: int, stream: int = 0) -> None:
-        """sm_gemv without allocating: scratch is a fixed library array (n_in <= 32768)."""
+        """sm_gemv without allocating: its K-split scratch is a fixed library array."""
         _check(lib().sm_gemv_noalloc(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), batch, C.c_void_p(stream)))
 
     def free(self) -> None:

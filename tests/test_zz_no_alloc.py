@@ -1,11 +1,13 @@
 """sm_gemv_noalloc: the GEMV for callers that cannot allocate device memory
 (their host hands out all device memory itself, or the call sits on a path
-where cudaMalloc's device-wide synchronization is not allowed). Its batch-1
-scratch is a fixed array inside the library; this checks that its output
-equals sm_gemv's within the GEMV tolerance, on two calls in a row with
-different inputs, and that it refuses rows longer than that array. Collected
-last on purpose (file name), so that a run stopping at the first failure has
-run every other test first."""
+where cudaMalloc's device-wide synchronization is not allowed). The scratch of
+its batch-1 K-split (partial sums and arrival counters) is a fixed array inside
+the library; this checks that its output equals sm_gemv's within the GEMV
+tolerance, on two calls in a row with different inputs (the second finds the
+counters the first left), for a row of 129 blocks split 129 ways and a
+16-row-tile count that splits K in two. Collected last on purpose (file
+name), so that a run stopping at the first failure has run every other test
+first."""
 import numpy as np
 import pytest
 
@@ -40,11 +42,17 @@ def test_noalloc_matches_gemv_twice(qt, n_out, n_in):
     w.free()
 
 
-def test_noalloc_rejects_rows_beyond_the_scratch():
-    n_in = 32768 + 256
-    w = smotor.DWeight(smotor.Q4_K, smotor.quantize(smotor.Q4_K, np.zeros(8 * n_in, np.float32)), 8, n_in)
-    x = torch.zeros(n_in, device="cuda")
-    y = torch.zeros(8, device="cuda")
-    with pytest.raises(smotor.EngineError, match="scratch"):
+@pytest.mark.parametrize("qt,n_out,n_in", [(smotor.Q4_K, 64, 32768 + 256), (smotor.Q4_K, 8192, 18944)])
+def test_noalloc_long_rows_and_large_splits(qt, n_out, n_in):
+    rng = np.random.default_rng(n_out + n_in)
+    w = smotor.DWeight(qt, smotor.quantize(qt, rng.normal(0, 1, n_out * n_in).astype(np.float32)), n_out, n_in)
+    for call in range(2):
+        x = torch.from_numpy(rng.normal(0, 1, n_in).astype(np.float32)).cuda()
+        y_ref = torch.full((n_out,), float("nan"), device="cuda")
+        y = torch.full((n_out,), float("nan"), device="cuda")
+        w.gemv(x.data_ptr(), y_ref.data_ptr(), 1)
         w.gemv_noalloc(x.data_ptr(), y.data_ptr(), 1)
+        torch.cuda.synchronize()
+        assert not torch.isnan(y).any()
+        assert rel(y, y_ref) <= GEMV_TOL, (n_out, n_in, call)
     w.free()
