@@ -136,6 +136,9 @@ struct GemvArgs {
   float* ks_part;
   uint32_t* ks_cnt;
   uint32_t ks_part_cap, ks_cnt_cap;
+  // Set non-zero by a kernel whose bounded wait gave up (the launch's results
+  // are then not valid); may be null.
+  uint32_t* err;
 };
 
 #ifdef __CUDACC__

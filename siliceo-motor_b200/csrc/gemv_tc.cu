@@ -5,9 +5,11 @@
 // multiplied costs almost nothing. On the CUDA cores it does not (the f16->f32
 // conversions run on the quarter-rate XU pipe), so here the weights go
 // straight into mma.sync.m16n8k16 (f16 x f16 -> f32) as the A operand:
-//   * a quantized value q (0..15, or -32..31 for Q6_K) is exact in f16 and is
-//     made with one LOP3 (the nibble into the mantissa of 1024) and one HSUB2
-//     or HFMA2, two weights at a time;
+//   * a quantized value q (0..15, or the 6-bit q + 32 of Q6_K) goes into the
+//     mantissa of an f16 with a zero exponent field: a subnormal q * 2^-24
+//     (or 16q * 2^-24 for a high nibble), exact, made with one AND (Q4_K) or
+//     two LOP3s (Q6_K) per two weights; the power of two and Q6_K's -32
+//     (as -32 * sum(x) over the sub-block) are applied with the scales;
 //   * x is split into hi + lo f16 halves after scaling each 256-wide block by
 //     a power of two (hi = x rounded to 11 bits, lo = the exact remainder), so
 //     the products carry ~22 bits of x, as much as the f32 reference keeps
@@ -18,9 +20,10 @@
 //     sub-block) and the GGUF scales are applied once per block:
 //       Q4_K: y += d*sc_s*sum_s(q*x) - dmin*m_s*sum_s(x)   (dequant.rs:98-124)
 //       Q6_K: y += d*sc_s*sum_s((q-32)*x)                  (dequant.rs:178-206)
-// The weights stream from HBM once (tile layout, device.cuh) with a one-block
-// register prefetch and L2 prefetches further ahead; x is converted once per
-// CTA into shared memory, already in each lane's B-fragment order.
+// The weights stream from HBM once (tile layout, device.cuh): every warp runs
+// its own ring of shared-memory slots filled by bulk asynchronous copies (one
+// per 16-row block unit, completion on an mbarrier); x is converted once per
+// unit into shared memory, already in each lane's B-fragment order.
 //
 // Work: a unit is (8 tiles of 16 rows, K-slice). Warp w of a CTA owns tile
 // w of the unit. When there are too few tiles to fill the GPU, K is split and
@@ -37,45 +40,79 @@
 
 namespace sm {
 
-constexpr int TC_WARPS = 8, TC_THREADS = TC_WARPS * 32;
-constexpr uint32_t TC_FRAG = 4096;             // expanded B fragments of one block, one type
-constexpr uint32_t TC_XS = 64;                 // per block: 4 lanes' (X_t, X_t+4, 1/scale, 0)
-constexpr uint32_t TC_SMEM_MAX = 200u * 1024u;
-constexpr uint32_t TC_PREFETCH = 4;            // L2 prefetch distance, in blocks
+constexpr int TC_WARPS = 16, TC_THREADS = TC_WARPS * 32;
+constexpr uint32_t TC_FRAG = 1024;             // B fragments of one block, one type: [2][32 lanes][16 B]
+// per block: [4 x (X32_t, X32_t+4, 1/scale, 0)][4 x (X16_t, X16_t+4, X16_t+8, X16_t+12)]
+// (X32 / X16: sums of x over 32- / 16-wide sub-blocks, for lane t's epilogue)
+constexpr uint32_t TC_XS = 128;
+constexpr uint32_t TC_SMEM_MAX = 225u * 1024u;
+// Ring slots per warp: 16 warps x 2-3 slots of one block unit each keep HBM
+// saturated; deeper rings (more requests in flight) lose bandwidth, and so do
+// L2 prefetches ahead of the ring (both measured on B200).
+constexpr uint32_t TC_MAX_STAGES = 3;
+constexpr uint32_t TC_SPIN_MAX = 1u << 22;     // bound on every mbarrier wait (then: error flag)
 
 struct TcPlan {
   uint32_t tiles, groups, ksplit, slice, units, grid, smem, t4, t6;
+  uint32_t stages, stage_bytes;  // per-warp cp.async ring of weight units
 };
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+// One bulk copy global -> shared (16-byte aligned, size a multiple of 16) that
+// completes `bytes` of transaction count on mbarrier b.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(b))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for phase `parity` of b to complete, at most TC_SPIN_MAX polls; a wait
+// that gives up records it in *err and returns (the data is then not used for
+// a result the caller keeps: the host reads the flag).
+__device__ __forceinline__ void mbar_wait(uint64_t* b, uint32_t parity, uint32_t* err) {
+  for (uint32_t n = 0; n < TC_SPIN_MAX; n++)
+    if (mbar_try(b, parity)) return;
+  if (err) atomicOr(err, 1u);
+}
 
-// Low nibbles of bytes (0, 2) as the exact half2 (q0, q2).
-__device__ __forceinline__ uint32_t nib_lo(uint32_t w) {
-  return h2u(__hsub2(u2h((w & 0x000F000Fu) | 0x64006400u), __floats2half2_rn(1024.f, 1024.f)));
-}
-// High nibbles of bytes (0, 2): (1024 + 16q) / 16 - 64, exact.
-__device__ __forceinline__ uint32_t nib_hi(uint32_t w) {
-  return h2u(__hfma2(u2h((w & 0x00F000F0u) | 0x64006400u), __floats2half2_rn(0.0625f, 0.0625f),
-                     __floats2half2_rn(-64.f, -64.f)));
-}
-// Q6_K: 6-bit values (low nibble + 2 bits of h at 4-5 / 20-21) minus 32.
-__device__ __forceinline__ uint32_t q6_lo(uint32_t w, uint32_t h) {
-  return h2u(__hsub2(u2h((w & 0x000F000Fu) | 0x64006400u | (h & 0x00300030u)), __floats2half2_rn(1056.f, 1056.f)));
-}
-// Q6_K: high nibble + 2 bits of h at 8-9 / 24-25, as (1024 + 16v) / 16 - 96.
-__device__ __forceinline__ uint32_t q6_hi(uint32_t w, uint32_t h) {
-  return h2u(__hfma2(u2h((w & 0x00F000F0u) | 0x64006400u | (h & 0x03000300u)), __floats2half2_rn(0.0625f, 0.0625f),
-                     __floats2half2_rn(-96.f, -96.f)));
-}
+// Low nibbles of bytes (0, 2) as the half2 (q0, q2) * 2^-24 (exact subnormals).
+__device__ __forceinline__ uint32_t nib_lo(uint32_t w) { return w & 0x000F000Fu; }
+// High nibbles of bytes (0, 2): (q0, q2) * 2^-20.
+__device__ __forceinline__ uint32_t nib_hi(uint32_t w) { return w & 0x00F000F0u; }
+// Q6_K: 6-bit values v = q + 32 (low nibble + 2 bits of h at 4-5 / 20-21) * 2^-24.
+__device__ __forceinline__ uint32_t q6_lo(uint32_t w, uint32_t h) { return (w & 0x000F000Fu) | (h & 0x00300030u); }
+// Q6_K: high nibble + 2 bits of h at 8-9 / 24-25: v * 2^-20.
+__device__ __forceinline__ uint32_t q6_hi(uint32_t w, uint32_t h) { return (w & 0x00F000F0u) | (h & 0x03000300u); }
+
+// B operand of a chunk of sub-block s for this lane: its fragment words when
+// s is in its column (s & 3 == u), else zero; mk[s & 3] is 1.0 or 0.0 (half2).
+__device__ __forceinline__ uint32_t bmask(uint32_t w, uint32_t m) { return h2u(__hmul2(u2h(w), u2h(m))); }
 
 // x (already scaled) -> (hi, lo): hi keeps 11 significant bits (round half
 // away from zero on the magnitude), lo = x - hi exactly.
@@ -86,9 +123,10 @@ __device__ __forceinline__ uint32_t hl_pair(float a, float b, bool lo) {
 }
 
 // Converts block bl (global block b) of x into shared memory: per type the
-// expanded B fragments [8 chunk pairs][32 lanes][4 words] (zero where the
-// chunk's sub-block is not the lane's column), and per lane t of the Q4_K
-// epilogue (X_t, X_t+4, 1/scale). One warp per block.
+// lane's B fragments [2][32 lanes][4 words] for the sub-blocks of its column
+// (u = lane >> 3: u, u + 4 for Q4_K; u, u + 4, u + 8, u + 12 for Q6_K; the
+// MMA loops zero them for the other sub-blocks), and the x sums and the
+// block's 1/scale for the epilogues. One warp per block.
 __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* f4, uint4* f6, float4* xs, bool t4,
                                            bool t6) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, u = g >> 1;
@@ -123,9 +161,8 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
       w[i] = make_uint4(hl_pair(a.x * scl, a.z * scl, lo), hl_pair(a.y * scl, a.w * scl, lo),
                         hl_pair(c.x * scl, c.z * scl, lo), hl_pair(c.y * scl, c.w * scl, lo));
     }
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int p = 0; p < 8; p++) f4[p * 32 + lane] = p == u ? w[0] : (p == u + 4 ? w[1] : z);
+    f4[lane] = w[0];       // sub-block u: chunk halves c = 0 (x, y), 1 (z, w)
+    f4[32 + lane] = w[1];  // sub-block u + 4
     // sums of x over sub-blocks u and u + 4 (unscaled), over the 4 lanes t
     float s0 = sum4(v4[0]) + sum4(v4[1]), s1 = sum4(v4[2]) + sum4(v4[3]);
     s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
@@ -137,61 +174,71 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
     xs[lane] = make_float4(0.f, 0.f, inv, 0.f);
   }
   if (t6) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
+    float q[4];  // sums over the 16-wide sub-blocks u + 4i, over the 4 lanes t
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      q[i] = sum4(v6[i]);
+      q[i] += __shfl_xor_sync(0xffffffffu, q[i], 1);
+      q[i] += __shfl_xor_sync(0xffffffffu, q[i], 2);
+    }
+    if (!lo && t == 0) xs[4 + u] = make_float4(q[0], q[1], q[2], q[3]);
     uint2 w[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
       const float4 a = v6[i];
       w[i] = make_uint2(hl_pair(a.x * scl, a.z * scl, lo), hl_pair(a.y * scl, a.w * scl, lo));
     }
-    // chunk s = u + 4i sits in pair s >> 1, words 2*(s & 1) and 2*(s & 1) + 1
-#pragma unroll
-    for (int p = 0; p < 8; p++) {
-      uint4 v = z;
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-        if (((u + 4 * i) >> 1) == p) v = (u & 1) ? make_uint4(0, 0, w[i].x, w[i].y) : make_uint4(w[i].x, w[i].y, 0, 0);
-      f6[p * 32 + lane] = v;
-    }
+    f6[lane] = make_uint4(w[0].x, w[0].y, w[1].x, w[1].y);       // sub-blocks u, u + 4
+    f6[32 + lane] = make_uint4(w[2].x, w[2].y, w[3].x, w[3].y);  // sub-blocks u + 8, u + 12
   }
 }
 
 // ------------------------------------------------------------- Q4_K ----
-// The register pipeline carries the quant bytes; the small per-row headers are
-// read when the block is computed (the L2 prefetch has brought them in).
+// A block of a tile is computed from its unit in shared memory (st).
 struct Q4Buf {
   uint4 q[4];  // loads 0..3 of the lane (rows g, g+8)
 };
-__device__ __forceinline__ void q4_load(Q4Buf& B, const uint8_t* unit, int lane) {
-  const uint8_t* qs = unit + 256 + 16 * lane;
+__device__ __forceinline__ void q4_load(Q4Buf& B, const uint8_t* st, int lane) {
+  const uint4* qs = reinterpret_cast<const uint4*>(st + 256) + lane;
 #pragma unroll
-  for (int L = 0; L < 4; L++) B.q[L] = ld_stream(qs + 512 * L);
+  for (int L = 0; L < 4; L++) B.q[L] = qs[32 * L];
 }
+// P0 / P1: the MMA sums of sub-blocks t and t + 4, times 2^-24 (t even: low
+// nibbles) or 2^-20 (t odd: high nibbles) and the block's x scale.
 __device__ __forceinline__ float q4_row(const uint4& hd, int t, float P0, float P1, const float4& xs) {
-  const float d = h2f_ref(hd.x & 0xFFFFu) * xs.z, dmin = h2f_ref(hd.x >> 16);
+  const float d = h2f_ref(hd.x & 0xFFFFu) * (xs.z * ((t & 1) ? 1048576.f : 16777216.f)), dmin = h2f_ref(hd.x >> 16);
   const int s0 = 8 * t;  // get_scale_min_k4 of sub-blocks t and t + 4 (dequant.rs:41-49)
   const uint32_t sa = (hd.y >> s0) & 63u, ma = (hd.z >> s0) & 63u;
   const uint32_t sb = ((hd.w >> s0) & 0xFu) | (((hd.y >> (s0 + 6)) & 3u) << 4);
   const uint32_t mb = ((hd.w >> (s0 + 4)) & 0xFu) | (((hd.z >> (s0 + 6)) & 3u) << 4);
   return d * ((float)sa * P0 + (float)sb * P1) - dmin * ((float)ma * xs.x + (float)mb * xs.y);
 }
-__device__ __forceinline__ void q4_block(const Q4Buf& B, const uint8_t* unit, const uint4* __restrict__ f4,
-                                         const float4* __restrict__ xs, int lane, float& rg, float& rh) {
-  const uint4 hg = ldg_u4(unit + 16 * (lane >> 2)), hh = ldg_u4(unit + 16 * ((lane >> 2) + 8));
+__device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* __restrict__ f4,
+                                         const float4* __restrict__ xs, const uint32_t (&mk)[4], int lane, float& rg,
+                                         float& rh) {
+  Q4Buf B;
+  q4_load(B, st, lane);
+  const uint4 hg = reinterpret_cast<const uint4*>(st)[lane >> 2], hh = reinterpret_cast<const uint4*>(st)[(lane >> 2) + 8];
+  const uint4 F[2] = {f4[lane], f4[32 + lane]};
+  // acc[s >> 2]: sub-blocks 0-3 / 4-7, the two chains alternate
   float acc[2][4] = {};
 #pragma unroll
-  for (int s = 0; s < 8; s++) {
-    const uint4 bf = f4[s * 32 + lane];
-    const int j = s >> 1;
-    const uint4 Lg = j < 2 ? B.q[0] : B.q[1], Lh = j < 2 ? B.q[2] : B.q[3];
-    const uint32_t ga = (j & 1) ? Lg.z : Lg.x, gb = (j & 1) ? Lg.w : Lg.y;
-    const uint32_t ha = (j & 1) ? Lh.z : Lh.x, hb = (j & 1) ? Lh.w : Lh.y;
-    if (s & 1) {
-      mma16816(acc[s >> 2], nib_hi(ga), nib_hi(ha), nib_hi(ga >> 8), nib_hi(ha >> 8), bf.x, bf.y);
-      mma16816(acc[s >> 2], nib_hi(gb), nib_hi(hb), nib_hi(gb >> 8), nib_hi(hb >> 8), bf.z, bf.w);
-    } else {
-      mma16816(acc[s >> 2], nib_lo(ga), nib_lo(ha), nib_lo(ga >> 8), nib_lo(ha >> 8), bf.x, bf.y);
-      mma16816(acc[s >> 2], nib_lo(gb), nib_lo(hb), nib_lo(gb >> 8), nib_lo(hb >> 8), bf.z, bf.w);
+  for (int s4 = 0; s4 < 4; s4++) {
+#pragma unroll
+    for (int hi = 0; hi < 2; hi++) {
+      const int s = s4 + 4 * hi, j = s >> 1;
+      const uint32_t m = mk[s4];
+      const uint4 Lg = j < 2 ? B.q[0] : B.q[1], Lh = j < 2 ? B.q[2] : B.q[3];
+      const uint32_t ga = (j & 1) ? Lg.z : Lg.x, gb = (j & 1) ? Lg.w : Lg.y;
+      const uint32_t ha = (j & 1) ? Lh.z : Lh.x, hb = (j & 1) ? Lh.w : Lh.y;
+      const uint32_t b0 = bmask(F[hi].x, m), b1 = bmask(F[hi].y, m), b2 = bmask(F[hi].z, m), b3 = bmask(F[hi].w, m);
+      if (s & 1) {
+        mma16816(acc[hi], nib_hi(ga), nib_hi(ha), nib_hi(ga >> 8), nib_hi(ha >> 8), b0, b1);
+        mma16816(acc[hi], nib_hi(gb), nib_hi(hb), nib_hi(gb >> 8), nib_hi(hb >> 8), b2, b3);
+      } else {
+        mma16816(acc[hi], nib_lo(ga), nib_lo(ha), nib_lo(ga >> 8), nib_lo(ha >> 8), b0, b1);
+        mma16816(acc[hi], nib_lo(gb), nib_lo(hb), nib_lo(gb >> 8), nib_lo(hb >> 8), b2, b3);
+      }
     }
   }
   const int t = lane & 3;
@@ -204,27 +251,34 @@ __device__ __forceinline__ void q4_block(const Q4Buf& B, const uint8_t* unit, co
 struct Q6Buf {
   uint4 q[6];  // ql 0-3, ql 4-7, qh of row g; the same of row g + 8
 };
-__device__ __forceinline__ void q6_load(Q6Buf& B, const uint8_t* unit, int lane) {
-  const uint8_t* q = unit + Q6T_QOFF + 16 * lane;
+__device__ __forceinline__ void q6_load(Q6Buf& B, const uint8_t* st, int lane) {
+  const uint4* q = reinterpret_cast<const uint4*>(st + Q6T_QOFF) + lane;
 #pragma unroll
-  for (int L = 0; L < 6; L++) B.q[L] = ld_stream(q + 512 * L);
+  for (int L = 0; L < 6; L++) B.q[L] = q[32 * L];
 }
-// Scales of sub-blocks t + 4a (a = 0..3) of one row half: word w of the row's
-// 16 scale bytes holds sub-blocks 4w .. 4w+3.
-__device__ __forceinline__ float q6_half(uint32_t w0, uint32_t w1, int t, const float (&acc)[2][4], int c) {
+// Pass p of a Q6_K row: sub-blocks s = 8p + t and 8p + t + 4 (scale bytes t of
+// words w0, w1), MMA sums D * 2^-24 (p = 0) or 2^-20 (p = 1) times the x
+// scale (F undoes both), minus 32 * sum(x) for the +32 of the stored values.
+__device__ __forceinline__ float q6_half(uint32_t w0, uint32_t w1, int t, const float (&acc)[2][4], int c, float F,
+                                         float X0, float X1) {
   const int sh = 8 * t;
   const float s0 = (float)(int8_t)((w0 >> sh) & 0xFFu), s1 = (float)(int8_t)((w1 >> sh) & 0xFFu);
-  return s0 * (acc[0][c] + acc[0][c + 1]) + s1 * (acc[1][c] + acc[1][c + 1]);
+  return s0 * fmaf(F, acc[0][c] + acc[0][c + 1], -32.f * X0) + s1 * fmaf(F, acc[1][c] + acc[1][c + 1], -32.f * X1);
 }
-__device__ __forceinline__ float q6_d(uint32_t dbits, float inv) {
+__device__ __forceinline__ float q6_d(uint32_t dbits) {
   const float d = h2f_ref(dbits);
-  return isfinite(d) ? d * inv : 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
+  return isfinite(d) ? d : 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
 }
 // Two passes: sub-blocks 0-7 (low nibbles of the 8 ql words), then 8-15 (high
 // nibbles), each into two accumulators that are scaled before the next pass.
-__device__ __forceinline__ void q6_block(const Q6Buf& B, const uint8_t* unit, const uint4* __restrict__ f6,
-                                         const float4* __restrict__ xs, int lane, float& rg, float& rh) {
+__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* __restrict__ f6,
+                                         const float4* __restrict__ xs, const uint32_t (&mk)[4], int lane, float& rg,
+                                         float& rh) {
   const int g = lane >> 2, t = lane & 3;
+  Q6Buf B;
+  q6_load(B, unit, lane);
+  const float4 x16 = xs[4 + t];
+  const uint4 F[2] = {f6[lane], f6[32 + lane]};
   const uint32_t gw[8] = {B.q[0].x, B.q[0].y, B.q[0].z, B.q[0].w, B.q[1].x, B.q[1].y, B.q[1].z, B.q[1].w};
   const uint32_t hw[8] = {B.q[3].x, B.q[3].y, B.q[3].z, B.q[3].w, B.q[4].x, B.q[4].y, B.q[4].z, B.q[4].w};
   const uint32_t gq[4] = {B.q[2].x, B.q[2].y, B.q[2].z, B.q[2].w};
@@ -234,65 +288,69 @@ __device__ __forceinline__ void q6_block(const Q6Buf& B, const uint8_t* unit, co
   for (int pass = 0; pass < 2; pass++) {
     float acc[2][4] = {};
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      const uint4 bf = f6[(4 * pass + (i >> 1)) * 32 + lane];  // chunks 8*pass + i, + 1
+    for (int i = 0; i < 4; i += 2) {
 #pragma unroll
-      for (int e = 0; e < 2; e++) {
-        const int k = i + e;
+      for (int e = 0; e < 4; e++) {  // words i, i + 4, i + 1, i + 5: the two accumulators alternate
+        const int k = i + (e >> 1) + 4 * (e & 1);
+        const int sb = 8 * pass + k, sig = sb >> 2;  // sub-block; its fragment: F[sig >> 1], words 2*(sig & 1) ..
+        const uint4 Fs = F[sig >> 1];
+        const uint32_t m = mk[sb & 3];
         const uint32_t wg = gw[k], wh = hw[k];
-        const uint32_t qg = e ? __funnelshift_r(gq[k >> 1], gq[k >> 1], 8) : gq[k >> 1];
-        const uint32_t qh = e ? __funnelshift_r(hq[k >> 1], hq[k >> 1], 8) : hq[k >> 1];
-        const uint32_t b0 = e ? bf.z : bf.x, b1 = e ? bf.w : bf.y;
+        const uint32_t qg = (k & 1) ? __funnelshift_r(gq[k >> 1], gq[k >> 1], 8) : gq[k >> 1];
+        const uint32_t qh = (k & 1) ? __funnelshift_r(hq[k >> 1], hq[k >> 1], 8) : hq[k >> 1];
+        const uint32_t b0 = bmask((sig & 1) ? Fs.z : Fs.x, m), b1 = bmask((sig & 1) ? Fs.w : Fs.y, m);
         if (pass == 0)
           mma16816(acc[k >> 2], q6_lo(wg, qg), q6_lo(wh, qh), q6_lo(wg >> 8, qg >> 2), q6_lo(wh >> 8, qh >> 2), b0, b1);
         else
           mma16816(acc[k >> 2], q6_hi(wg, qg), q6_hi(wh, qh), q6_hi(wg >> 8, qg >> 2), q6_hi(wh >> 8, qh >> 2), b0, b1);
       }
     }
-    const uint2 sg = __ldg(reinterpret_cast<const uint2*>(unit + 16 * g + 8 * pass));
-    const uint2 sh = __ldg(reinterpret_cast<const uint2*>(unit + 16 * (g + 8) + 8 * pass));
-    pg += q6_half(sg.x, sg.y, t, acc, 0);
-    ph += q6_half(sh.x, sh.y, t, acc, 2);
+    const uint2 sg = *reinterpret_cast<const uint2*>(unit + 16 * g + 8 * pass);
+    const uint2 sh = *reinterpret_cast<const uint2*>(unit + 16 * (g + 8) + 8 * pass);
+    const float F = xs[t].z * (pass ? 1048576.f : 16777216.f);
+    const float X0 = pass ? x16.z : x16.x, X1 = pass ? x16.w : x16.y;
+    pg += q6_half(sg.x, sg.y, t, acc, 0, F, X0, X1);
+    ph += q6_half(sh.x, sh.y, t, acc, 2, F, X0, X1);
   }
-  const float inv = xs[t].z;
-  rg += q6_d(__ldg(reinterpret_cast<const unsigned short*>(unit + 256) + g), inv) * pg;
-  rh += q6_d(__ldg(reinterpret_cast<const unsigned short*>(unit + 256) + g + 8), inv) * ph;
+  rg += q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g]) * pg;
+  rh += q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g + 8]) * ph;
 }
 
 // One warp: tile rows g, g+8 over blocks b0 .. b0+nblk-1 (x fragments of
-// block b0 + i at slot i). Returns the partial dot products in rg, rh
-// (summed over the lane's sub-blocks only).
-template <int QT>
-__device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t nb,
-                                        const uint4* f, const float4* xs, float& rg, float& rh) {
+// block b0 + i at slot i). The block units stream through the warp's ring of
+// S shared-memory slots: lane 0 starts one bulk copy per unit, S - 1 units
+// ahead of the one being computed, each completing on the slot's mbarrier
+// (use n of the ring waits for parity (n / S) & 1; nuse counts the warp's
+// uses across units). Returns the partial dot products in rg, rh (summed
+// over the lane's sub-blocks only).
+template <int QT, int S>
+__device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t nb, uint8_t* ring,
+                                        uint32_t stage_bytes, uint64_t* bars, uint32_t& nuse, uint32_t* err,
+                                        const uint4* f, const float4* xs, const uint32_t (&mk)[4], float& rg,
+                                        float& rh) {
   const int lane = threadIdx.x & 31;
   constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT;
-  using Buf = typename std::conditional<QT == 12, Q4Buf, Q6Buf>::type;
-  auto load = [&](Buf& B, uint32_t i) {
-    const uint8_t* unit = tile + (size_t)(b0 + i) * UB;
-    const uint32_t pf = b0 + i + TC_PREFETCH;
-    if (pf < nb && (uint32_t)lane * 128u < UB) prefetch_l2(tile + (size_t)pf * UB + 128u * lane);
-    if constexpr (QT == 12) q4_load(B, unit, lane);
-    else q6_load(B, unit, lane);
+  auto issue = [&](uint32_t i) {
+    if (i >= nblk) return;
+    if (lane == 0) {
+      const uint32_t st = (nuse + i) % S;
+      fence_proxy_async();  // this slot's previous reads (ordered by __syncwarp) before the async write
+      mbar_expect_tx(bars + st, UB);
+      bulk_g2s(ring + st * stage_bytes, tile + (size_t)(b0 + i) * UB, UB, bars + st);
+    }
   };
-  auto run = [&](const Buf& B, uint32_t i) {
-    const uint8_t* unit = tile + (size_t)(b0 + i) * UB;
-    if constexpr (QT == 12) q4_block(B, unit, f + (size_t)i * 256, xs + 4 * i, lane, rg, rh);
-    else q6_block(B, unit, f + (size_t)i * 256, xs + 4 * i, lane, rg, rh);
-  };
-  if (!nblk) return;
-  // first TC_PREFETCH blocks go to L2 ahead of the register pipeline
-  for (uint32_t i = 1; i < TC_PREFETCH && i < nblk; i++)
-    if ((uint32_t)lane * 128u < UB) prefetch_l2(tile + (size_t)(b0 + i) * UB + 128u * lane);
-  Buf A, B;
-  load(A, 0);
-  for (uint32_t i = 0; i < nblk; i += 2) {
-    if (i + 1 < nblk) load(B, i + 1);
-    run(A, i);
-    if (i + 1 >= nblk) break;
-    if (i + 2 < nblk) load(A, i + 2);
-    run(B, i + 1);
+#pragma unroll
+  for (int k = 0; k < S - 1; k++) issue((uint32_t)k);
+  for (uint32_t i = 0; i < nblk; i++) {
+    issue(i + S - 1);
+    const uint32_t n = nuse + i, st = n % S;
+    mbar_wait(bars + st, (n / S) & 1u, err);
+    const uint8_t* sp = ring + st * stage_bytes;
+    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * 64, xs + 8 * i, mk, lane, rg, rh);
+    else q6_block(sp, f + (size_t)i * 64, xs + 8 * i, mk, lane, rg, rh);
+    __syncwarp();  // every lane is done with the slot before it is refilled
   }
+  nuse += nblk;
 }
 
 // Epilogue of one tile: vg / vh are the full dot products of rows g, g + 8
@@ -328,11 +386,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   extern __shared__ __align__(16) uint8_t tc_smem[];
   __shared__ float s_in;
   __shared__ uint32_t s_last;
+  __shared__ __align__(8) uint64_t s_bars[TC_WARPS * TC_MAX_STAGES];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint4* f4 = reinterpret_cast<uint4*>(tc_smem);
-  uint4* f6 = f4 + (p.t4 ? p.slice * 256 : 0);
-  float4* xs = reinterpret_cast<float4*>(f6 + (p.t6 ? p.slice * 256 : 0));
+  uint4* f6 = f4 + (p.t4 ? p.slice * 64 : 0);
+  float4* xs = reinterpret_cast<float4*>(f6 + (p.t6 ? p.slice * 64 : 0));
+  uint8_t* ring = reinterpret_cast<uint8_t*>(xs + 8 * p.slice) + (size_t)warp * p.stages * p.stage_bytes;
   const uint32_t nb = a.seg[0].w.n_in >> 8;
+  uint64_t* bars = s_bars + warp * TC_MAX_STAGES;
+  if (lane == 0) {
+    for (uint32_t k = 0; k < p.stages; k++) mbar_init(bars + k, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  uint32_t nuse = 0;
+  // 1.0 (half2) in the column of this lane's sub-blocks, 0 elsewhere
+  uint32_t mk[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) mk[k] = (lane >> 3) == k ? 0x3C003C00u : 0u;
   if (warp == 0) {
     const float v = input_scale(a, 0);
     if (lane == 0) s_in = v;
@@ -342,7 +413,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
     __syncthreads();  // the previous unit is done with the x fragments
     for (uint32_t i = warp; i < nblk; i += TC_WARPS)
-      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * 256, f6 + i * 256, xs + 4 * i, p.t4, p.t6);
+      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * 64, f6 + i * 64, xs + 8 * i, p.t4, p.t6);
     __syncthreads();
     const uint32_t tile = rg * TC_WARPS + warp;
     float vg = 0.f, vh = 0.f;
@@ -352,8 +423,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
       const DWDesc& w = a.seg[si].w;
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
-      if (w.type == 12) tc_tile<12>(tb, b0, nblk, nb, f4, xs, vg, vh);
-      else tc_tile<14>(tb, b0, nblk, nb, f6, xs, vg, vh);
+#define TC_TILE(QT, S, F) tc_tile<QT, S>(tb, b0, nblk, nb, ring, p.stage_bytes, bars, nuse, a.err, F, xs, mk, vg, vh)
+      if (w.type == 12) {
+        if (p.stages == 3) TC_TILE(12, 3, f4);
+        else TC_TILE(12, 2, f4);
+      } else {
+        if (p.stages == 3) TC_TILE(14, 3, f6);
+        else TC_TILE(14, 2, f6);
+      }
+#undef TC_TILE
     }
     vg += __shfl_xor_sync(0xffffffffu, vg, 1);
     vh += __shfl_xor_sync(0xffffffffu, vh, 1);
@@ -437,24 +515,41 @@ static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
   }
   const uint32_t nb = a.seg[0].w.n_in >> 8;
   const uint32_t per_blk = (t4 ? TC_FRAG : 0) + (t6 ? TC_FRAG : 0) + TC_XS;
-  const uint32_t slice_max = TC_SMEM_MAX / per_blk;
+  const uint32_t stage_bytes = t6 ? Q6T_UNIT : Q4T_UNIT;
+  // x fragments of up to 32 blocks per slice; the rest of shared memory is ring
+  const uint32_t slice_max = std::max(1u, std::min(32u, (TC_SMEM_MAX - TC_WARPS * 2 * stage_bytes) / per_blk));
   const uint32_t groups = (tiles + TC_WARPS - 1) / TC_WARPS;
-  uint32_t ks = std::max((nb + slice_max - 1) / slice_max, std::min(nb, std::max(1u, sms / groups)));
   auto fits = [&](uint32_t k) {
     return k == 1 || (a.ks_part && a.ks_cnt && (uint64_t)k * tiles * 16u <= a.ks_part_cap && groups <= a.ks_cnt_cap);
   };
-  if (!fits(ks)) ks = 1;
+  // the split with the least work on the busiest SM: rounds of units x (blocks
+  // per unit + about half a block of per-unit cost: x conversion, epilogue)
+  uint32_t ks = 0;
+  uint64_t best = ~0ull;
+  for (uint32_t k = 1; k <= std::min(nb, 64u); k++) {
+    const uint32_t sl = (nb + k - 1) / k;
+    const uint32_t kk = (nb + sl - 1) / sl;
+    if (sl > slice_max || !fits(kk)) continue;
+    const uint64_t rounds = ((uint64_t)groups * kk + sms - 1) / sms;
+    if (rounds * (2 * sl + 1) < best) {
+      best = rounds * (2 * sl + 1);
+      ks = kk;
+    }
+  }
+  if (!ks) return false;
   const uint32_t slice = (nb + ks - 1) / ks;
-  if (slice > slice_max) return false;
-  ks = (nb + slice - 1) / slice;
-  if (!fits(ks)) return false;
+  const uint32_t stages = std::min(TC_MAX_STAGES, (TC_SMEM_MAX - slice * per_blk) / (TC_WARPS * stage_bytes));
+  if (stages < 2) return false;
+  const uint32_t ring = TC_WARPS * stages * stage_bytes;
   p->tiles = tiles;
   p->groups = groups;
   p->ksplit = ks;
   p->slice = slice;
   p->units = groups * ks;
   p->grid = std::min(p->units, sms);
-  p->smem = slice * per_blk;
+  p->smem = slice * per_blk + ring;
+  p->stages = stages;
+  p->stage_bytes = stage_bytes;
   p->t4 = t4;
   p->t6 = t6;
   return true;
