@@ -37,6 +37,7 @@
 
 #include "device.cuh"
 #include "gemv_common.cuh"
+#include "pdl.cuh"
 
 namespace sm {
 
@@ -67,6 +68,18 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+template <int OFF>
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a), "n"(OFF));
+  return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(a), "n"(OFF));
+  return v;
+}
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
@@ -110,9 +123,11 @@ __device__ __forceinline__ uint32_t q6_lo(uint32_t w, uint32_t h) { return (w & 
 // Q6_K: high nibble + 2 bits of h at 8-9 / 24-25: v * 2^-20.
 __device__ __forceinline__ uint32_t q6_hi(uint32_t w, uint32_t h) { return (w & 0x00F000F0u) | (h & 0x03000300u); }
 
-// B operand of a chunk of sub-block s for this lane: its fragment words when
-// s is in its column (s & 3 == u), else zero; mk[s & 3] is 1.0 or 0.0 (half2).
-__device__ __forceinline__ uint32_t bmask(uint32_t w, uint32_t m) { return h2u(__hmul2(u2h(w), u2h(m))); }
+// B operand of the chunks of sub-block s: the lane's fragment words when s is
+// in its column (s & 3 == u), else zero. fb[k] is the shared address the lane
+// reads for sub-blocks s with s & 3 == k: its fragment slot of the current
+// block, or a zero page (the fragments of the lane's sub-blocks u + 4 sigma
+// sit sigma * 512 bytes apart; the zero page is 1 KB).
 
 // x (already scaled) -> (hi, lo): hi keeps 11 significant bits (round half
 // away from zero on the magnitude), lo = x - hi exactly.
@@ -213,13 +228,11 @@ __device__ __forceinline__ float q4_row(const uint4& hd, int t, float P0, float 
   const uint32_t mb = ((hd.w >> (s0 + 4)) & 0xFu) | (((hd.z >> (s0 + 6)) & 3u) << 4);
   return d * ((float)sa * P0 + (float)sb * P1) - dmin * ((float)ma * xs.x + (float)mb * xs.y);
 }
-__device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* __restrict__ f4,
-                                         const float4* __restrict__ xs, const uint32_t (&mk)[4], int lane, float& rg,
-                                         float& rh) {
+__device__ __forceinline__ void q4_block(const uint8_t* st, const uint32_t (&fb)[4], const float4* __restrict__ xs,
+                                         int lane, float& rg, float& rh) {
   Q4Buf B;
   q4_load(B, st, lane);
   const uint4 hg = reinterpret_cast<const uint4*>(st)[lane >> 2], hh = reinterpret_cast<const uint4*>(st)[(lane >> 2) + 8];
-  const uint4 F[2] = {f4[lane], f4[32 + lane]};
   // acc[s >> 2]: sub-blocks 0-3 / 4-7, the two chains alternate
   float acc[2][4] = {};
 #pragma unroll
@@ -227,11 +240,11 @@ __device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* __restr
 #pragma unroll
     for (int hi = 0; hi < 2; hi++) {
       const int s = s4 + 4 * hi, j = s >> 1;
-      const uint32_t m = mk[s4];
+      const uint4 bf = hi ? lds128<512>(fb[s4]) : lds128<0>(fb[s4]);
       const uint4 Lg = j < 2 ? B.q[0] : B.q[1], Lh = j < 2 ? B.q[2] : B.q[3];
       const uint32_t ga = (j & 1) ? Lg.z : Lg.x, gb = (j & 1) ? Lg.w : Lg.y;
       const uint32_t ha = (j & 1) ? Lh.z : Lh.x, hb = (j & 1) ? Lh.w : Lh.y;
-      const uint32_t b0 = bmask(F[hi].x, m), b1 = bmask(F[hi].y, m), b2 = bmask(F[hi].z, m), b3 = bmask(F[hi].w, m);
+      const uint32_t b0 = bf.x, b1 = bf.y, b2 = bf.z, b3 = bf.w;
       if (s & 1) {
         mma16816(acc[hi], nib_hi(ga), nib_hi(ha), nib_hi(ga >> 8), nib_hi(ha >> 8), b0, b1);
         mma16816(acc[hi], nib_hi(gb), nib_hi(hb), nib_hi(gb >> 8), nib_hi(hb >> 8), b2, b3);
@@ -271,14 +284,12 @@ __device__ __forceinline__ float q6_d(uint32_t dbits) {
 }
 // Two passes: sub-blocks 0-7 (low nibbles of the 8 ql words), then 8-15 (high
 // nibbles), each into two accumulators that are scaled before the next pass.
-__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* __restrict__ f6,
-                                         const float4* __restrict__ xs, const uint32_t (&mk)[4], int lane, float& rg,
-                                         float& rh) {
+__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint32_t (&fb)[4], const float4* __restrict__ xs,
+                                         int lane, float& rg, float& rh) {
   const int g = lane >> 2, t = lane & 3;
   Q6Buf B;
   q6_load(B, unit, lane);
   const float4 x16 = xs[4 + t];
-  const uint4 F[2] = {f6[lane], f6[32 + lane]};
   const uint32_t gw[8] = {B.q[0].x, B.q[0].y, B.q[0].z, B.q[0].w, B.q[1].x, B.q[1].y, B.q[1].z, B.q[1].w};
   const uint32_t hw[8] = {B.q[3].x, B.q[3].y, B.q[3].z, B.q[3].w, B.q[4].x, B.q[4].y, B.q[4].z, B.q[4].w};
   const uint32_t gq[4] = {B.q[2].x, B.q[2].y, B.q[2].z, B.q[2].w};
@@ -292,13 +303,13 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* __res
 #pragma unroll
       for (int e = 0; e < 4; e++) {  // words i, i + 4, i + 1, i + 5: the two accumulators alternate
         const int k = i + (e >> 1) + 4 * (e & 1);
-        const int sb = 8 * pass + k, sig = sb >> 2;  // sub-block; its fragment: F[sig >> 1], words 2*(sig & 1) ..
-        const uint4 Fs = F[sig >> 1];
-        const uint32_t m = mk[sb & 3];
+        const int sb = 8 * pass + k, sig = sb >> 2;  // sub-block; its fragment: slot sig >> 1, words 2*(sig & 1) ..
+        const uint2 bf = sig == 0 ? lds64<0>(fb[sb & 3]) : sig == 1 ? lds64<8>(fb[sb & 3])
+                       : sig == 2 ? lds64<512>(fb[sb & 3]) : lds64<520>(fb[sb & 3]);
         const uint32_t wg = gw[k], wh = hw[k];
         const uint32_t qg = (k & 1) ? __funnelshift_r(gq[k >> 1], gq[k >> 1], 8) : gq[k >> 1];
         const uint32_t qh = (k & 1) ? __funnelshift_r(hq[k >> 1], hq[k >> 1], 8) : hq[k >> 1];
-        const uint32_t b0 = bmask((sig & 1) ? Fs.z : Fs.x, m), b1 = bmask((sig & 1) ? Fs.w : Fs.y, m);
+        const uint32_t b0 = bf.x, b1 = bf.y;
         if (pass == 0)
           mma16816(acc[k >> 2], q6_lo(wg, qg), q6_lo(wh, qh), q6_lo(wg >> 8, qg >> 2), q6_lo(wh >> 8, qh >> 2), b0, b1);
         else
@@ -323,34 +334,57 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* __res
 // (use n of the ring waits for parity (n / S) & 1; nuse counts the warp's
 // uses across units). Returns the partial dot products in rg, rh (summed
 // over the lane's sub-blocks only).
+// Lane 0: the bulk copy of one block unit (UB bytes) into ring slot st.
+__device__ __forceinline__ void tc_issue(const uint8_t* unit, uint32_t UB, uint8_t* ring, uint32_t stage_bytes,
+                                         uint64_t* bars, uint32_t st) {
+  fence_proxy_async();  // this slot's previous reads (ordered by __syncwarp) before the async write
+  mbar_expect_tx(bars + st, UB);
+  bulk_g2s(ring + st * stage_bytes, unit, UB, bars + st);
+}
+
+// The first `pre` copies may have been started by the caller already (ahead
+// of the previous kernel, pdl.cuh).
 template <int QT, int S>
-__device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t nb, uint8_t* ring,
+__device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t pre, uint8_t* ring,
                                         uint32_t stage_bytes, uint64_t* bars, uint32_t& nuse, uint32_t* err,
-                                        const uint4* f, const float4* xs, const uint32_t (&mk)[4], float& rg,
-                                        float& rh) {
+                                        const uint4* f, const float4* xs, uint32_t zero_page, float& rg, float& rh) {
   const int lane = threadIdx.x & 31;
   constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT;
+  // ring slot of the next copy to start (ip) and of the next block to compute (cp, phase cph)
+  uint32_t ip = nuse % S, cp = ip, cph = (nuse / S) & 1u;
+  for (uint32_t k = 0; k < pre; k++) ip = ip + 1 == S ? 0 : ip + 1;
   auto issue = [&](uint32_t i) {
     if (i >= nblk) return;
-    if (lane == 0) {
-      const uint32_t st = (nuse + i) % S;
-      fence_proxy_async();  // this slot's previous reads (ordered by __syncwarp) before the async write
-      mbar_expect_tx(bars + st, UB);
-      bulk_g2s(ring + st * stage_bytes, tile + (size_t)(b0 + i) * UB, UB, bars + st);
-    }
+    if (lane == 0) tc_issue(tile + (size_t)(b0 + i) * UB, UB, ring, stage_bytes, bars, ip);
+    ip = ip + 1 == S ? 0 : ip + 1;
   };
+  for (uint32_t k = pre; k + 1 < S; k++) issue(k);
+  uint32_t fb[4], dk[4];
 #pragma unroll
-  for (int k = 0; k < S - 1; k++) issue((uint32_t)k);
+  for (int k = 0; k < 4; k++) {
+    fb[k] = (lane >> 3) == k ? smem_u32(f + lane) : zero_page;
+    dk[k] = (lane >> 3) == k ? 1024u : 0u;  // fragments of one block, one type
+  }
   for (uint32_t i = 0; i < nblk; i++) {
     issue(i + S - 1);
-    const uint32_t n = nuse + i, st = n % S;
-    mbar_wait(bars + st, (n / S) & 1u, err);
-    const uint8_t* sp = ring + st * stage_bytes;
-    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * 64, xs + 8 * i, mk, lane, rg, rh);
-    else q6_block(sp, f + (size_t)i * 64, xs + 8 * i, mk, lane, rg, rh);
+    mbar_wait(bars + cp, cph, err);
+    const uint8_t* sp = ring + cp * stage_bytes;
+    if (++cp == S) { cp = 0; cph ^= 1u; }
+    if constexpr (QT == 12) q4_block(sp, fb, xs + 8 * i, lane, rg, rh);
+    else q6_block(sp, fb, xs + 8 * i, lane, rg, rh);
+#pragma unroll
+    for (int k = 0; k < 4; k++) fb[k] += dk[k];  // next block's fragment slot (the zero page stays)
     __syncwarp();  // every lane is done with the slot before it is refilled
   }
   nuse += nblk;
+}
+
+// Segment of a tile (cta_begin holds each segment's first tile).
+__device__ __forceinline__ uint32_t tc_seg(const GemvArgs& a, uint32_t tile) {
+  uint32_t si = 0;
+  if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
+  if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
+  return si;
 }
 
 // Epilogue of one tile: vg / vh are the full dot products of rows g, g + 8
@@ -400,10 +434,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   }
   __syncwarp();
   uint32_t nuse = 0;
-  // 1.0 (half2) in the column of this lane's sub-blocks, 0 elsewhere
-  uint32_t mk[4];
-#pragma unroll
-  for (int k = 0; k < 4; k++) mk[k] = (lane >> 3) == k ? 0x3C003C00u : 0u;
+  __shared__ __align__(16) uint4 s_zero[64];  // 1 KB zero page for the B operands of other columns
+  for (uint32_t i = threadIdx.x; i < 64; i += blockDim.x) s_zero[i] = make_uint4(0, 0, 0, 0);
+  const uint32_t zero_page = smem_u32(s_zero);
+  // The weights do not depend on the previous kernel: start the first unit's
+  // copies before waiting for it.
+  pdl_trigger();
+  uint32_t pre = 0;
+  if (blockIdx.x < p.units) {
+    const uint32_t rg = blockIdx.x / p.ksplit, ks = blockIdx.x - rg * p.ksplit;
+    const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0), tile = rg * TC_WARPS + warp;
+    if (tile < p.tiles) {
+      const uint32_t si = tc_seg(a, tile);
+      const DWDesc& w = a.seg[si].w;
+      const uint32_t UB = tile_unit_bytes(w.type);
+      const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
+      pre = min(p.stages - 1, nblk);
+      if (lane == 0)
+        for (uint32_t k = 0; k < pre; k++) tc_issue(tb + (size_t)(b0 + k) * UB, UB, ring, p.stage_bytes, bars, k);
+    }
+  }
+  pdl_wait();
   if (warp == 0) {
     const float v = input_scale(a, 0);
     if (lane == 0) s_in = v;
@@ -423,7 +474,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
       const DWDesc& w = a.seg[si].w;
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
-#define TC_TILE(QT, S, F) tc_tile<QT, S>(tb, b0, nblk, nb, ring, p.stage_bytes, bars, nuse, a.err, F, xs, mk, vg, vh)
+#define TC_TILE(QT, S, F) \
+  tc_tile<QT, S>(tb, b0, nblk, pre, ring, p.stage_bytes, bars, nuse, a.err, F, xs, zero_page, vg, vh)
       if (w.type == 12) {
         if (p.stages == 3) TC_TILE(12, 3, f4);
         else TC_TILE(12, 2, f4);
@@ -433,6 +485,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       }
 #undef TC_TILE
     }
+    pre = 0;
     vg += __shfl_xor_sync(0xffffffffu, vg, 1);
     vh += __shfl_xor_sync(0xffffffffu, vh, 1);
     vg += __shfl_xor_sync(0xffffffffu, vg, 2);
@@ -564,8 +617,7 @@ cudaError_t launch_gemv_tc(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   TcPlan p;
   if (!tc_plan(a, sms, &p)) return cudaErrorNotSupported;
   if (n_parts) *n_parts = p.tiles;
-  gemv_tc_kernel<<<p.grid, TC_THREADS, p.smem, st>>>(a, p);
-  return cudaGetLastError();
+  return launch_pdl(gemv_tc_kernel, dim3(p.grid), dim3(TC_THREADS), p.smem, st, a, p);
 }
 
 // Scratch a K-split of this launch shape may use (floats of partials, counters).

@@ -4,6 +4,7 @@
 
 #include "device.cuh"
 #include "layers.cuh"
+#include "pdl.cuh"
 
 namespace sm {
 
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
                                                                  uint32_t Hkv, uint32_t hd, float scale, float* part_o,
                                                                  float* part_ml, uint32_t max_splits) {
   extern __shared__ __align__(16) float smem[];
+  pdl_trigger();
   const uint32_t r = blockIdx.x / Hkv, g = blockIdx.x - r * Hkv, sp = blockIdx.y;
   const RowDesc rd = rows[r];
   const uint32_t L = rd.pos + 1;
@@ -100,6 +102,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
   const uint32_t te = min(tiles, tb + tps);
   const uint32_t G = Hq / Hkv, kvd = Hkv * hd, hs = hd + 4, hd4 = hd / 4;
   const SeqDesc sd = seqs[rd.seq];
+  {  // positions before rd.pos were written by earlier steps: start them towards L2
+    const size_t kb = (size_t)layer * sd.cap * kvd + (size_t)g * hd;
+    const uint32_t p_end = min(te * ATT_T, rd.pos), lines = (hd * 4 + 127) / 128;
+    const uint32_t nrow = p_end > tb * ATT_T ? p_end - tb * ATT_T : 0;
+    for (uint32_t i = threadIdx.x; i < nrow * lines; i += blockDim.x) {
+      const size_t off = kb + (size_t)(tb * ATT_T + i / lines) * kvd + (i % lines) * 32;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(sd.k + off));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(sd.v + off));
+    }
+  }
+  pdl_wait();  // q and this position's K / V come from the QKV GEMV
   float* qs = smem;                  // [G][hd]
   float* kt = qs + G * hd;           // [ATT_T][hd+4]
   float* vt = kt + ATT_T * hs;       // [ATT_T][hd+4]
@@ -207,22 +220,51 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
   }
 }
 
+// Merges the splits of (row r, head h): out = sum_s o_s e_s / sum_s l_s e_s with
+// e_s = exp(m_s - max m), sums in split order. The (m, l) pairs are staged in
+// shared memory by one parallel load; the partial outputs are read eight
+// splits at a time.
 __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const RowDesc* rows, uint32_t Hq,
                                     uint32_t hd, uint32_t max_splits, float* out, uint32_t ldo) {
+  __shared__ float sm_m[64], sm_e[64];
+  pdl_trigger();
   const uint32_t r = blockIdx.x / Hq, h = blockIdx.x - r * Hq;
-  const uint32_t L = rows[r].pos + 1;
+  const uint32_t L = rows[r].pos + 1;  // rows are set before the step's first kernel
   const uint32_t tiles = (L + ATT_T - 1) / ATT_T;
   const uint32_t tps = (tiles + max_splits - 1) / max_splits;
-  const uint32_t ns = (tiles + tps - 1) / tps;
+  const uint32_t ns = (tiles + tps - 1) / tps;  // <= max_splits <= 64
+  pdl_wait();  // the partials come from attn_split_kernel
   const float* ml = part_ml + ((size_t)r * Hq + h) * max_splits * 2;
+  for (uint32_t s = threadIdx.x; s < ns; s += blockDim.x) {
+    sm_m[s] = ml[2 * s];
+    sm_e[s] = ml[2 * s + 1];
+  }
+  __syncthreads();
   float M = -INFINITY;
-  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, ml[2 * s]);
+  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, sm_m[s]);
   float den = 0.f;
-  for (uint32_t s = 0; s < ns; s++) den += ml[2 * s + 1] * expf(ml[2 * s] - M);
+  for (uint32_t s = 0; s < ns; s++) den += sm_e[s] * expf(sm_m[s] - M);
+  __syncthreads();
+  for (uint32_t s = threadIdx.x; s < ns; s += blockDim.x) sm_e[s] = expf(sm_m[s] - M);
+  __syncthreads();
   const float* po = part_o + ((size_t)r * Hq + h) * max_splits * hd;
   for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
     float acc = 0.f;
-    for (uint32_t s = 0; s < ns; s++) acc = fmaf(po[(size_t)s * hd + d], expf(ml[2 * s] - M), acc);
+    uint32_t s = 0;
+    for (; s + 8 <= ns; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = po[(size_t)(s + u) * hd + d];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = fmaf(v[u], sm_e[s + u], acc);
+    }
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (s + u < ns) v[u] = po[(size_t)(s + u) * hd + d];
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (s + u < ns) acc = fmaf(v[u], sm_e[s + u], acc);
     out[(size_t)r * ldo + h * hd + d] = acc / den;
   }
 }
@@ -275,6 +317,8 @@ __device__ __forceinline__ Best better(Best a, Best b) {  // larger value, then 
 __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits, uint32_t V, const uint8_t* mask,
                                                              const SampleParams* params, uint64_t* rng,
                                                              uint32_t* out_tok, uint32_t* next_tok, RowDesc* advance) {
+  pdl_trigger();
+  pdl_wait();  // the logits come from the output-head GEMV
   const uint32_t r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* lr = logits + (size_t)r * V;
   const uint8_t* mr = mask ? mask + (size_t)r * V : nullptr;
@@ -494,12 +538,11 @@ cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, 
   const uint32_t G = Hq / Hkv;
   const size_t sm = attn_smem_bytes(G, hd);
   const float scale = 1.0f / sqrtf((float)hd);  // qwen2.rs:505
-  attn_split_kernel<<<dim3(nrows * Hkv, max_splits), ATT_THREADS, sm, st>>>(q, ldq, rows, seqs, layer, Hq, Hkv, hd,
-                                                                            scale, part_o, part_ml, max_splits);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(attn_split_kernel, dim3(nrows * Hkv, max_splits), dim3(ATT_THREADS), sm, st, q, ldq,
+                             rows, seqs, layer, Hq, Hkv, hd, scale, part_o, part_ml, max_splits);
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo);
-  return cudaGetLastError();
+  return launch_pdl(attn_combine_kernel, dim3(nrows * Hq), dim3(hd), 0, st, part_o, part_ml, rows, Hq, hd, max_splits,
+                    out, ldo);
 }
 
 cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, cudaStream_t st) {
@@ -513,8 +556,8 @@ cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const 
                           const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
                           RowDesc* advance, cudaStream_t st) {
   if (!rows) return cudaSuccess;
-  sample_kernel<<<rows, SMP_THREADS, 0, st>>>(logits, V, mask, params, rng, out_tok, next_tok, advance);
-  return cudaGetLastError();
+  return launch_pdl(sample_kernel, dim3(rows), dim3(SMP_THREADS), 0, st, logits, V, mask, params, rng, out_tok, next_tok,
+                    advance);
 }
 
 cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
