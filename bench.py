@@ -249,6 +249,49 @@ def run_gemv(args, rank, world, local_rank, barrier, allmax):
     }), flush=True)
 
 
+# The dominant kernel of a decode step: the tensor-core batch-1 GEMV, on the
+# step's largest launch shape (the interleaved gate/up projection of the 7B
+# shape, Q4_K). Its DRAM traffic per launch comes from the ncu capture
+# summarised in profiles/ (the bench cannot run ncu itself).
+DOMINANT = (37888, 3584, "Q4_K")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+
+
+def kernel_roofline(steps, warmup):
+    """Average duration of the dominant kernel over `steps` standalone launches:
+    CUDA events on the launching stream, the L2 flushed before each launch by a
+    512 MB read that is enqueued first (so the GPU never waits for the host)."""
+    import torch
+    import smotor
+    M, K, tname = DOMINANT
+    st = torch.cuda.current_stream()
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    rng = np.random.default_rng(7)
+    qt = getattr(smotor, tname)
+    w = smotor.DWeight(qt, smotor.quantize(qt, rng.normal(0, 0.02, M * K).astype(np.float32)), M, K)
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(M, device="cuda")
+    times = []
+    for it in range(warmup + steps):
+        flush.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        w.gemv(x.data_ptr(), y.data_ptr(), 1, st.cuda_stream)
+        e1.record(st)
+        e1.synchronize()
+        if it >= warmup:
+            times.append(e0.elapsed_time(e1))
+    nbytes = w.nbytes() + 4 * (K + M)
+    w.free()
+    del flush
+    us = 1e3 * sum(times) / len(times)
+    traffic = None
+    if os.path.exists(TRAFFIC_FILE):
+        with open(TRAFFIC_FILE) as f:
+            traffic = json.load(f).get("gemv_tc %dx%d %s batch 1" % DOMINANT)
+    return nbytes, us, traffic
+
+
 def run_ours(args, rank, world, local_rank, barrier, allmax):
     import torch
     import smotor
@@ -304,8 +347,10 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     # KV bytes read by attention over the timed steps: positions 0..pos per layer, K and V, f32
     kv_positions = sum(sum(p + i + 1 for i in range(args.steps)) for p in pos0)
     alg_bytes = args.steps * wbytes + 2 * L * kvd * 4 * kv_positions
-    achieved = alg_bytes / (ms / 1e3) / 1e9
+    step_achieved = alg_bytes / (ms / 1e3) / 1e9
     peak, peak_kind = peaks()
+    kbytes, kus, ktraffic = kernel_roofline(max(args.steps, 10), 3)
+    achieved = kbytes / (kus / 1e6) / 1e9
     value = world * batch * args.steps / (ms / 1e3)
     line = {
         "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -316,13 +361,17 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
                    "l2": "inputs larger than L2 (%.2f GB of weights streamed per step)" % (wbytes / 1e9),
                    "timed": "sm_decode_run: K device-resident graph replays between CUDA events on the engine stream"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_source": peak_kind,
-                     "bytes_per_step": alg_bytes / args.steps,
-                     "kernel": "whole decode step (dequant-fused GEMVs + attention); per-kernel shares in profiles/"},
+                     "traffic": ktraffic, "peak_source": peak_kind,
+                     "kernel": "gemv_tc (batch-1 tensor-core GEMV) on %dx%d %s: %.1f us per launch, %d algorithmic "
+                               "bytes per launch; standalone launches, L2 flushed" % (DOMINANT + (kus, kbytes)),
+                     "step": {"achieved": step_achieved, "frac": step_achieved / peak,
+                              "bytes_per_step": alg_bytes / args.steps,
+                              "note": "weights + KV read per decode step / step time"}},
         "e2e": {"value": world * batch * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": "sm_forward_sample" if batch == 1 else "sm_decode_batch"},
-        "gpu_launches": world * args.steps * (3 + 10 * L + 1),
+        # per step: embed+norm; per layer QKV, attention split, combine, O, gate/up, down; head, sampler, record
+        "gpu_launches": world * args.steps * (6 * L + 4),
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -336,7 +385,7 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=list(WORKLOADS) + ["gemv"])
+    ap.add_argument("--workload", default="cfg2", choices=list(WORKLOADS) + ["gemv", "dominant"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="gemv workload: one MxK:TYPE:batch case, e.g. 3584x18944:Q4_K:1")
     args = ap.parse_args()
@@ -366,7 +415,14 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             return float(t.item())
     try:
-        (run_gemv if args.workload == "gemv" else run_ours)(args, rank, world, local_rank, barrier, allmax)
+        if args.workload == "dominant":  # the roofline kernel alone (what profiles/ captures with ncu)
+            import torch
+            torch.cuda.set_device(local_rank)
+            nbytes, us, traffic = kernel_roofline(args.steps, args.warmup)
+            print(json.dumps({"kernel": "gemv_tc %dx%d %s batch 1" % DOMINANT, "us": us, "bytes": nbytes,
+                              "gbs": nbytes / us / 1e3, "traffic": traffic}), flush=True)
+        else:
+            (run_gemv if args.workload == "gemv" else run_ours)(args, rank, world, local_rank, barrier, allmax)
     finally:
         if world > 1:
             import torch.distributed as dist
