@@ -96,18 +96,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                "l"(src), "r"(bytes), "r"(smem_u32(b))
                : "memory");
 }
+// One wait of at most ~TC_SUSPEND_NS: the warp is parked by the hardware
+// (not spinning) until the phase completes or the time hint runs out.
+constexpr uint32_t TC_SUSPEND_NS = 1000;
 __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
       : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
+      : "r"(smem_u32(b)), "r"(parity), "n"(TC_SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
-// Waits for phase `parity` of b to complete, at most TC_SPIN_MAX polls; a wait
-// that gives up records it in *err and returns (the data is then not used for
-// a result the caller keeps: the host reads the flag).
+// Waits for phase `parity` of b to complete, at most TC_SPIN_MAX tries (a few
+// seconds); a wait that gives up records it in *err and returns (the data is
+// then not used for a result the caller keeps: the host reads the flag).
 __device__ __forceinline__ void mbar_wait(uint64_t* b, uint32_t parity, uint32_t* err) {
   for (uint32_t n = 0; n < TC_SPIN_MAX; n++)
     if (mbar_try(b, parity)) return;
