@@ -11,6 +11,8 @@ achieved HBM bandwidth against the measured peak in `roofline`.
 N > 1 (torchrun): every rank decodes its own replica (the single-sequence
 decode path has no partition, so this is weak scaling with no collective);
 the timed region is bracketed by barriers and the max over ranks is used.
+--workload cfg4 / cfg4b16 split the 70B shape over the job's N GPUs instead
+(tensor parallelism, strong scaling: one model, N GPUs).
 """
 import argparse
 import fcntl
@@ -34,7 +36,12 @@ WORKLOADS = {
     "cfg0": (0, 1, 128, "greedy", "Qwen2.5-0.5B-shape Q4_K_M (Q5_0/Q8_0 fallbacks), batch 1, 128-token prompt"),
     "cfg3": (3, 32, 2048, "topk40_topp0.9",
              "Llama-3-8B-shape Q4_K_M, 32 sequences, 1024 shared + 1024 own prompt tokens, T=1 top-k 40 top-p 0.9"),
+    # tensor parallel over every rank of the job (one model split N ways)
+    "cfg4": (4, 1, 1024, "greedy", "Llama-3-70B-shape Q4_K_M, tensor parallel, batch 1, 1024-token prompt, greedy"),
+    "cfg4b16": (4, 16, 1024, "greedy",
+                "Llama-3-70B-shape Q4_K_M, tensor parallel, 16 sequences of 1024-token prompts, greedy"),
 }
+TP_WORKLOADS = {"cfg4", "cfg4b16"}
 HBM_FALLBACK_GBS = 6650.0
 GEMV_SHAPES = [(896, 4864), (3584, 18944), (4096, 14336), (8192, 28672)]  # BASELINE config 1 (M x K)
 
@@ -257,13 +264,13 @@ DOMINANT = (37888, 3584, "Q4_K")
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "roofline_traffic.json")
 
 
-def kernel_roofline(steps, warmup):
+def kernel_roofline(steps, warmup, shape=DOMINANT):
     """Average duration of the dominant kernel over `steps` standalone launches:
     CUDA events on the launching stream, the L2 flushed before each launch by a
     512 MB read that is enqueued first (so the GPU never waits for the host)."""
     import torch
     import smotor
-    M, K, tname = DOMINANT
+    M, K, tname = shape
     st = torch.cuda.current_stream()
     flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
     rng = np.random.default_rng(7)
@@ -288,7 +295,7 @@ def kernel_roofline(steps, warmup):
     traffic = None
     if os.path.exists(TRAFFIC_FILE):
         with open(TRAFFIC_FILE) as f:
-            traffic = json.load(f).get("gemv_tc %dx%d %s batch 1" % DOMINANT)
+            traffic = json.load(f).get("gemv_tc %dx%d %s batch 1" % shape)
     return nbytes, us, traffic
 
 
@@ -300,7 +307,10 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     torch.cuda.set_device(local_rank)
     path = model_file(preset, local_rank, barrier)
     extra = args.warmup + 2 * args.steps + 8
-    model = smotor.Model.load(path, device=local_rank, max_batch=max(32, batch), max_context=prompt_len + extra + 64)
+    split = args.workload in TP_WORKLOADS and world > 1
+    tp = smotor.TensorParallel.from_process_group(flags=smotor.TP_NCCL if args.tp_nccl else 0) if split else None
+    model = smotor.Model.load(path, device=local_rank, max_batch=max(32, batch), max_context=prompt_len + extra + 64,
+                              tp=tp)
     cfg = model.config
     V, L, kvd = cfg.vocab_size, cfg.n_layers, cfg.n_kv_heads * cfg.head_dim
     caches, toks = setup_sequences(model, V, batch, prompt_len, kind, extra)
@@ -325,6 +335,8 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     barrier()
     clk = clocks.stop(set(range(max(world, 1)))) if clocks else None
     ms = allmax(ev0.elapsed_time(ev1))
+    # bytes the whole job streams per step: every rank's shard (tensor parallel) or one replica's weights
+    wbytes_job = int(allsum(model.weight_bytes())) if split else model.weight_bytes() * world
     toks = out[-1].tolist()
     # end to end through the per-token public API (host tokens in and out)
     barrier()
@@ -340,41 +352,55 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     torch.cuda.synchronize()
     e2e_s = allmax(time.perf_counter() - t0)
     barrier()
+    h2d, d2h = model.step_io_bytes()
+    model.free()  # every rank at the same point (tensor parallel: the group's teardown barrier)
     if rank != 0:
         return
-    h2d, d2h = model.step_io_bytes()
-    wbytes = model.weight_bytes()
     # KV bytes read by attention over the timed steps: positions 0..pos per layer, K and V, f32
+    # (the whole model's KV heads: one replica's per rank, or all ranks' shards together)
     kv_positions = sum(sum(p + i + 1 for i in range(args.steps)) for p in pos0)
-    alg_bytes = args.steps * wbytes + 2 * L * kvd * 4 * kv_positions
-    step_achieved = alg_bytes / (ms / 1e3) / 1e9
+    kv_bytes = 2 * L * kvd * 4 * kv_positions * (1 if split else world)
+    alg_bytes = args.steps * wbytes_job + kv_bytes
     peak, peak_kind = peaks()
-    kbytes, kus, ktraffic = kernel_roofline(max(args.steps, 10), 3)
+    step_achieved = alg_bytes / (ms / 1e3) / 1e9
+    step_peak = peak * world
+    if split:  # dominant launch of a rank: its gate/up shard
+        shape = (2 * cfg.n_ff // world, cfg.n_embd, "Q4_K")
+    else:
+        shape = DOMINANT
+    kbytes, kus, ktraffic = kernel_roofline(max(args.steps, 10), 3, shape)
     achieved = kbytes / (kus / 1e6) / 1e9
-    value = world * batch * args.steps / (ms / 1e3)
+    tokens = batch * args.steps * (1 if split else world)
+    value = tokens / (ms / 1e3)
+    L_ = L
     line = {
         "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if split else "weak",
         "vs_baseline": None, "dtype": "f32 (Q4_K_M weights)", "data": "synthetic (seeded N(0,0.02) GGUF, random ids)",
         "config": {"workload": args.workload, "description": desc, "batch": batch, "prompt_len": prompt_len,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (%.2f GB of weights streamed per step)" % (wbytes / 1e9),
+                   "parallelism": (f"tensor parallel x{world} ({'NCCL' if args.tp_nccl else 'peer-memory'} "
+                                   f"exchanges)") if split else (f"replicas x{world}" if world > 1 else "single GPU"),
+                   "l2": "inputs larger than L2 (%.2f GB of weights streamed per step per GPU)"
+                         % (wbytes_job / world / 1e9),
                    "timed": "sm_decode_run: K device-resident graph replays between CUDA events on the engine stream"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": ktraffic, "peak_source": peak_kind,
                      "kernel": "gemv_tc (batch-1 tensor-core GEMV) on %dx%d %s: %.1f us per launch, %d algorithmic "
-                               "bytes per launch; standalone launches, L2 flushed" % (DOMINANT + (kus, kbytes)),
-                     "step": {"achieved": step_achieved, "frac": step_achieved / peak,
-                              "bytes_per_step": alg_bytes / args.steps,
-                              "note": "weights + KV read per decode step / step time"}},
-        "e2e": {"value": world * batch * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                               "bytes per launch; standalone launches, L2 flushed" % (shape + (kus, kbytes)),
+                     "step": {"achieved": step_achieved, "frac": step_achieved / step_peak,
+                              "bytes_per_step": alg_bytes / args.steps, "peak": step_peak,
+                              "note": "weights + KV the whole job reads per decode step / step time, against "
+                                      "%d x the per-GPU peak" % world}},
+        "e2e": {"value": tokens / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": "sm_forward_sample" if batch == 1 else "sm_decode_batch"},
-        # per step: embed+norm; per layer QKV, attention split, combine, O, gate/up, down; head, sampler, record
-        "gpu_launches": world * args.steps * (6 * L + 4),
+        # per step and rank: embed+norm; per layer QKV, attention split, combine, O, gate/up, down; head,
+        # sampler, record; tensor parallel adds 2 all-reduce kernels per layer and the logit gather
+        "gpu_launches": world * args.steps * ((8 * L_ + 5) if split else (6 * L_ + 4)),
         "clocks": clk,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and args.workload not in TP_WORKLOADS:
         line["cpu_baseline"] = cpu_baseline(path)
     print(json.dumps(line), flush=True)
 
@@ -388,6 +414,8 @@ def main():
     ap.add_argument("--workload", default="cfg2", choices=list(WORKLOADS) + ["gemv", "dominant"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="gemv workload: one MxK:TYPE:batch case, e.g. 3584x18944:Q4_K:1")
+    ap.add_argument("--tp-nccl", action="store_true", help="tensor parallel: NCCL collectives instead of the "
+                                                            "engine's peer-memory exchange kernels")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = env_int("WORLD_SIZE", 1)
@@ -395,6 +423,8 @@ def main():
     local_rank = env_int("LOCAL_RANK", 0)
     barrier = lambda: None  # noqa: E731
     allmax = lambda v: v  # noqa: E731
+    global allsum
+    allsum = lambda v: v  # noqa: E731
     if args.impl == "reference":  # rank 0 alone times the CPU path; other ranks exit
         run_reference(args, rank, world, local_rank, barrier)
         return
@@ -413,6 +443,11 @@ def main():
         def allmax(v):
             t = torch.tensor([float(v)], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        def allsum(v):
+            t = torch.tensor([float(v)], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
             return float(t.item())
     try:
         if args.workload == "dominant":  # the roofline kernel alone (what profiles/ captures with ncu)

@@ -27,12 +27,15 @@ typedef enum {
   SM_ERR_CUDA = 5,        /* CUDA runtime error (message has the CUDA text) */
   SM_ERR_OOM = 6,         /* device or host allocation failed */
   SM_ERR_CAPACITY = 7,    /* sequence would exceed the cache capacity */
-  SM_ERR_STATE = 8        /* operation not valid for the object's state */
+  SM_ERR_STATE = 8,       /* operation not valid for the object's state */
+  SM_ERR_PEER = 9         /* a tensor-parallel peer failed or did not arrive in time;
+                             the model's group is unusable from then on */
 } sm_status;
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* sm_last_error(void);
-/* ABI version: increments on any incompatible change. */
+/* ABI version: increments on any incompatible change (2: tensor-parallel
+ * fields of sm_load_opts). */
 int sm_abi_version(void);
 
 /* ------------------------------------------------------------------------
@@ -55,14 +58,56 @@ typedef struct {
   int32_t device;        /* CUDA device ordinal */
   uint32_t max_batch;    /* largest decode batch (default 32) */
   uint32_t max_context;  /* largest position + 1 any cache may reach (default 32768) */
-  uint32_t tp_rank;      /* reserved: tensor-parallel rank (0) */
-  uint32_t tp_size;      /* reserved: tensor-parallel size (0 or 1) */
+  uint32_t tp_rank;      /* tensor-parallel rank, below tp_size */
+  uint32_t tp_size;      /* tensor-parallel size: 0 or 1 = none, else 2..8 (one process per GPU) */
+  uint32_t tp_flags;     /* SM_TP_* */
+  uint32_t tp_wait_ms;   /* bound on one wait for a peer (0 = 10000); group formation waits 6x this */
+  const void* tp_group;  /* SM_TP_ID_BYTES from sm_tp_group_id (made once, on one rank) */
 } sm_load_opts;
+
+/* Tensor parallelism (Megatron split; one process per GPU of one node).
+ * Every rank loads the same GGUF with its own tp_rank, the same tp_size and
+ * the same group id, and then makes the same calls with the same arguments
+ * (tokens, samplers, RNG states) in the same order. Each rank keeps the
+ * attention heads [rank*Hq/N, (rank+1)*Hq/N) (and their KV heads), FFN
+ * columns [rank*F/N, ...), the matching input columns of attn_output and
+ * ffn_down, and a 1/N slice of the output head's rows. After the O and down
+ * projections the partial sums are all-reduced in rank order (every rank
+ * gets bit-identical activations), and the logit slices are all-gathered
+ * before sampling, so every rank returns the same tokens and logits.
+ * Exchanges run over peer memory (CUDA IPC over NVLink) with kernels of the
+ * engine; SM_TP_NCCL uses NCCL all-reduce / all-gather instead. A peer that
+ * does not arrive within tp_wait_ms fails the call with SM_ERR_PEER.
+ * Per-rank views: sm_model_weight_bytes counts this rank's shard,
+ * sm_cache_read_kv returns this rank's KV heads. */
+#define SM_TP_ID_BYTES 128
+#define SM_TP_NCCL 1u
+/* Makes a group id (an NCCL unique id) to share with every rank. */
+int sm_tp_group_id(void* id_out);
+/* Which part of a model rank `rank` of `size` holds (no device needed). The
+ * loader additionally needs the split inputs of attn_output (q_heads x
+ * head_dim) and ffn_down (ff) to be whole quant blocks. */
+typedef struct {
+  uint64_t q_head0, q_heads;   /* query heads [q_head0, q_head0 + q_heads) */
+  uint64_t kv_head0, kv_heads; /* KV heads */
+  uint64_t ff0, ff;            /* FFN columns (ffn_gate/ffn_up rows, ffn_down inputs) */
+  uint64_t vocab0, vocab;      /* output-head rows */
+} sm_tp_shard;
+int sm_tp_plan(const sm_config* cfg, uint32_t rank, uint32_t size, sm_tp_shard* out);
+/* Marks the model's group failed without touching the GPU: for a host that
+ * learned (from its own heartbeat or store) that a peer left. Later compute
+ * calls return SM_ERR_PEER at once, and sm_model_free skips its final
+ * barrier with the peers. No effect on a model without tensor parallelism. */
+int sm_model_tp_abort(sm_model* m);
 
 /* Model::load / GpuQwen2::load. opts may be NULL (defaults). */
 int sm_model_load(const char* gguf_path, const sm_load_opts* opts, sm_model** out);
 /* Same, from a GGUF image in host memory (the buffer may be freed after). */
 int sm_model_load_memory(const void* gguf, uint64_t len, const sm_load_opts* opts, sm_model** out);
+/* Releases the handle (the model lives on while caches of it exist). With
+ * tensor parallelism every rank frees its handle at the same point of its
+ * program: the call waits (bounded by tp_wait_ms) for the other ranks, and
+ * the model makes no exchanges afterwards. */
 int sm_model_free(sm_model* m);
 /* Device::config */
 int sm_model_config(const sm_model* m, sm_config* out);

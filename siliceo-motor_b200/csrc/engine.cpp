@@ -20,6 +20,7 @@
 #include "common.hpp"
 #include "gguf.hpp"
 #include "layers.cuh"
+#include "tp.hpp"
 
 using namespace sm;
 
@@ -194,6 +195,7 @@ struct StepIn {
 struct StepOut {
   uint32_t* tok;  // [rows]
   uint64_t* rng;  // [rows]
+  uint32_t* err;  // error word of the bounded waits (GEMV copy rings, tensor-parallel peers)
 };
 
 }  // namespace
@@ -209,7 +211,13 @@ struct sm_model {
   int device = 0;
   cudaStream_t stream = nullptr;
   sm_config c{};
-  uint32_t kvd = 0;
+  uint32_t kvd = 0;  // this rank's KV width (kv heads x head_dim)
+  // Tensor parallelism (sh.world == 1: none): the shard plan, the group, and
+  // this rank's attention width (q heads x head_dim) and FFN width.
+  TpShard sh;
+  TpGroup* tp = nullptr;
+  uint32_t qd = 0, fl = 0;
+  bool failed = false;  // a bounded wait gave up: results are invalid from then on
   DW tok_embd, output;
   bool tied = false;
   float* output_norm = nullptr;
@@ -271,11 +279,12 @@ void layout_in(void* base, uint32_t R, StepIn& s) {
   carve(p, s.rng, R);
   carve(p, s.sel, R);
 }
-size_t step_out_bytes(uint32_t R) { return 2 * 256 + (size_t)R * (sizeof(uint32_t) + sizeof(uint64_t)); }
+size_t step_out_bytes(uint32_t R) { return 3 * 256 + (size_t)R * (sizeof(uint32_t) + sizeof(uint64_t)) + 4; }
 void layout_out(void* base, uint32_t R, StepOut& s) {
   uint8_t* p = (uint8_t*)base;
   carve(p, s.tok, R);
   carve(p, s.rng, R);
+  carve(p, s.err, 1);
 }
 
 int dev_alloc(sm_model* m, void** p, size_t bytes) {
@@ -317,7 +326,8 @@ int upload_2d(const GgufReader& g, const std::string& name, uint64_t n_in, uint6
   return rc;
 }
 
-// Uploads a 2-D tensor with its rows reordered: physical row p is logical row map[p].
+// Uploads rows of a 2-D tensor [n_out x n_in], reordered and possibly a
+// subset: physical row p is logical row map[p].
 int upload_2d_rows(const GgufReader& g, const std::string& name, uint64_t n_in, uint64_t n_out,
                    const std::vector<uint32_t>& map, DW* w) {
   const GgufTensor* t = g.tensor(name);
@@ -325,26 +335,58 @@ int upload_2d_rows(const GgufReader& g, const std::string& name, uint64_t n_in, 
   if (t->dims.size() != 2 || t->dims[0] != n_in || t->dims[1] != n_out) { set_error(name + ": unexpected shape"); return SM_ERR_FORMAT; }
   const uint8_t* src = g.data(*t);
   if (!src) { set_error(name + ": truncated tensor data"); return SM_ERR_FORMAT; }
-  const uint64_t rb = qtype_row_bytes(t->type, n_in);
-  std::vector<uint8_t> buf(rb * n_out);
-  for (uint64_t p = 0; p < n_out; p++) std::memcpy(buf.data() + p * rb, src + (uint64_t)map[p] * rb, rb);
-  int rc = upload_weight(t->type, buf.data(), n_out, n_in, w);
+  const uint64_t rb = qtype_row_bytes(t->type, n_in), n_loc = map.size();
+  std::vector<uint8_t> buf(rb * n_loc);
+  for (uint64_t p = 0; p < n_loc; p++) std::memcpy(buf.data() + p * rb, src + (uint64_t)map[p] * rb, rb);
+  int rc = upload_weight(t->type, buf.data(), n_loc, n_in, w);
   if (rc) set_error(name + ": " + get_error());
   return rc;
 }
 
-// RoPE-pair row order for a [n_heads * hd] projection (see Layer).
-std::vector<uint32_t> rope_pair_map(uint64_t n_heads, uint64_t hd) {
+// RoPE-pair row order for heads [h0, h0 + n_heads) of a projection (see Layer).
+std::vector<uint32_t> rope_pair_map(uint64_t n_heads, uint64_t hd, uint64_t h0 = 0) {
   std::vector<uint32_t> map(n_heads * hd);
   const uint64_t half = hd / 2;
   for (uint64_t h = 0; h < n_heads; h++)
     for (uint64_t mm = 0; mm < half; mm++)
-      for (uint64_t sdx = 0; sdx < 2; sdx++) map[h * hd + 2 * mm + sdx] = (uint32_t)(h * hd + mm + sdx * half);
+      for (uint64_t sdx = 0; sdx < 2; sdx++)
+        map[h * hd + 2 * mm + sdx] = (uint32_t)((h0 + h) * hd + mm + sdx * half);
   return map;
 }
 
-// ffn_gate and ffn_up interleaved row by row into one weight (see Layer).
-int upload_gate_up(const GgufReader& g, const std::string& pg, const std::string& pu, uint64_t n_in, uint64_t n_ff, DW* w) {
+std::vector<uint32_t> range_map(uint64_t first, uint64_t n) {
+  std::vector<uint32_t> map(n);
+  for (uint64_t i = 0; i < n; i++) map[i] = (uint32_t)(first + i);
+  return map;
+}
+
+// Uploads input columns [c0, c0 + nc) of every row of a 2-D tensor (the row
+// split of tensor parallelism): whole quant blocks of each row.
+int upload_2d_cols(const GgufReader& g, const std::string& name, uint64_t n_in, uint64_t n_out, uint64_t c0,
+                   uint64_t nc, DW* w) {
+  const GgufTensor* t = g.tensor(name);
+  if (!t) { set_error("tensor not found: " + name); return SM_ERR_FORMAT; }
+  if (t->dims.size() != 2 || t->dims[0] != n_in || t->dims[1] != n_out) { set_error(name + ": unexpected shape"); return SM_ERR_FORMAT; }
+  const uint8_t* src = g.data(*t);
+  if (!src) { set_error(name + ": truncated tensor data"); return SM_ERR_FORMAT; }
+  uint32_t bs = 1, tb = 4;
+  if (!qtype_layout(t->type, &bs, &tb) || c0 % bs || nc % bs || c0 + nc > n_in) {
+    set_error(name + ": the tensor-parallel split of its " + std::to_string(n_in) +
+              " input columns does not fall on quant block boundaries");
+    return SM_ERR_UNSUPPORTED;
+  }
+  const uint64_t rb = qtype_row_bytes(t->type, n_in), lb = nc / bs * tb, o0 = c0 / bs * tb;
+  std::vector<uint8_t> buf(lb * n_out);
+  for (uint64_t r = 0; r < n_out; r++) std::memcpy(buf.data() + r * lb, src + r * rb + o0, lb);
+  int rc = upload_weight(t->type, buf.data(), n_out, nc, w);
+  if (rc) set_error(name + ": " + get_error());
+  return rc;
+}
+
+// Rows [f0, f0 + fl) of ffn_gate and ffn_up interleaved row by row into one
+// weight (see Layer).
+int upload_gate_up(const GgufReader& g, const std::string& pg, const std::string& pu, uint64_t n_in, uint64_t n_ff,
+                   uint64_t f0, uint64_t fl, DW* w) {
   const GgufTensor* tg = g.tensor(pg);
   const GgufTensor* tu = g.tensor(pu);
   if (!tg || !tu) { set_error("tensor not found: " + (tg ? pu : pg)); return SM_ERR_FORMAT; }
@@ -355,12 +397,12 @@ int upload_gate_up(const GgufReader& g, const std::string& pg, const std::string
   const uint8_t* su = g.data(*tu);
   if (!sg_ || !su) { set_error(pg + ": truncated tensor data"); return SM_ERR_FORMAT; }
   const uint64_t rb = qtype_row_bytes(tg->type, n_in);
-  std::vector<uint8_t> buf(rb * 2 * n_ff);
-  for (uint64_t r = 0; r < n_ff; r++) {
-    std::memcpy(buf.data() + (2 * r) * rb, sg_ + r * rb, rb);
-    std::memcpy(buf.data() + (2 * r + 1) * rb, su + r * rb, rb);
+  std::vector<uint8_t> buf(rb * 2 * fl);
+  for (uint64_t r = 0; r < fl; r++) {
+    std::memcpy(buf.data() + (2 * r) * rb, sg_ + (f0 + r) * rb, rb);
+    std::memcpy(buf.data() + (2 * r + 1) * rb, su + (f0 + r) * rb, rb);
   }
-  int rc = upload_weight(tg->type, buf.data(), 2 * n_ff, n_in, w);
+  int rc = upload_weight(tg->type, buf.data(), 2 * fl, n_in, w);
   if (rc) set_error(pg + ": " + get_error());
   return rc;
 }
@@ -408,48 +450,70 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   const GgufTensor* te = g.tensor("token_embd.weight");
   if (!te || te->dims.size() != 2) { set_error("tensor not found: token_embd.weight"); return SM_ERR_FORMAT; }
   c.vocab_size = te->dims[1];
-  const uint64_t H = c.n_embd, hd = c.head_dim, kvd = c.n_kv_heads * hd, G = c.n_heads / c.n_kv_heads;
+  const uint64_t H = c.n_embd, hd = c.head_dim, G = c.n_heads / c.n_kv_heads, kvd_full = c.n_kv_heads * hd;
+  // Tensor-parallel shard of this rank (world 1: the whole model).
+  const uint32_t world = opts && opts->tp_size > 1 ? opts->tp_size : 1, rank = world > 1 ? opts->tp_rank : 0;
+  if (world > 1 && !opts->tp_group) { set_error("tensor parallelism needs the group id (tp_group)"); return SM_ERR_ARG; }
+  if (world > 1 && rank >= world) { set_error("tp_rank must be below tp_size"); return SM_ERR_ARG; }
+  {
+    const std::string why = tp_plan(c.n_heads, c.n_kv_heads, hd, c.n_ff, c.vocab_size, 0, 0, rank, world, &m->sh);
+    if (!why.empty()) { set_error(why); return SM_ERR_UNSUPPORTED; }
+  }
+  const TpShard& sh = m->sh;
+  const uint64_t qd = sh.q_heads * hd, kvd = sh.kv_heads * hd, fl = sh.ff;
   m->kvd = (uint32_t)kvd;
-  if (c.n_heads * hd != H || hd % 4 || hd > 128 || G > 8 || (G * hd) > 1024 || H % 4 || c.n_ff % 4) {
+  m->qd = (uint32_t)qd;
+  m->fl = (uint32_t)fl;
+  if (c.n_heads * hd != H || hd % 4 || hd > 128 || G > 8 || (G * hd) > 1024 || H % 4 || c.n_ff % 4 || fl % 4) {
     set_error("shape not supported by the attention kernels (head_dim <= 128, heads/kv_heads <= 8)");
     return SM_ERR_UNSUPPORTED;
   }
   if ((rc = upload_2d(g, "token_embd.weight", H, c.vocab_size, &m->tok_embd))) return rc;
-  if (g.tensor("output.weight")) {
+  const char* head_name = g.tensor("output.weight") ? "output.weight" : "token_embd.weight";  // tied: qwen2.rs:115-118
+  if (world > 1) {  // this rank's rows of the vocab-split head
+    if ((rc = upload_2d_rows(g, head_name, H, c.vocab_size, range_map(sh.vocab0, sh.vocab), &m->output))) return rc;
+  } else if (g.tensor("output.weight")) {
     if ((rc = upload_2d(g, "output.weight", H, c.vocab_size, &m->output))) return rc;
   } else {
-    m->output = m->tok_embd;  // tied embeddings (qwen2.rs:115-118)
+    m->output = m->tok_embd;
     m->tied = true;
   }
   if ((rc = upload_f32(m, g, "output_norm.weight", H, &m->output_norm))) return rc;
   m->weight_bytes = m->output.enc_bytes;
-  const std::vector<uint32_t> qmap = rope_pair_map(c.n_heads, hd), kmap = rope_pair_map(c.n_kv_heads, hd);
+  // This rank's heads (q rows in RoPE-pair order), KV heads and FFN columns.
+  const std::vector<uint32_t> qmap = rope_pair_map(sh.q_heads, hd, rank * sh.q_heads),
+                              kmap = rope_pair_map(sh.kv_heads, hd, rank * sh.kv_heads),
+                              vmap = range_map(rank * kvd, kvd);
   for (uint64_t i = 0; i < c.n_layers; i++) {
     Layer L;
     const std::string p = "blk." + std::to_string(i) + ".";
-    auto opt_bias = [&](const char* n, uint64_t len, const std::vector<uint32_t>* map, float** out) -> int {
+    auto opt_bias = [&](const char* n, uint64_t len, const std::vector<uint32_t>& map, float** out) -> int {
       if (!g.tensor(p + n)) return SM_OK;  // opt_bias (qwen2.rs:687-697)
       const GgufTensor* t = g.tensor(p + n);
       if (t->type != QT_F32 || t->n_elements() != len) { set_error(p + n + ": expected F32"); return SM_ERR_UNSUPPORTED; }
       const float* src = reinterpret_cast<const float*>(g.data(*t));
       if (!src) { set_error(p + n + ": truncated tensor data"); return SM_ERR_FORMAT; }
-      std::vector<float> b(len);
-      for (uint64_t k = 0; k < len; k++) b[k] = src[map ? (*map)[k] : k];
-      int rc2 = dev_alloc(m, (void**)out, len * 4);
+      std::vector<float> b(map.size());
+      for (size_t k = 0; k < map.size(); k++) b[k] = src[map[k]];
+      int rc2 = dev_alloc(m, (void**)out, b.size() * 4);
       if (rc2) return rc2;
-      CK(cudaMemcpy(*out, b.data(), len * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(*out, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
       return SM_OK;
     };
-    if ((rc = opt_bias("attn_q.bias", H, &qmap, &L.bq)) || (rc = opt_bias("attn_k.bias", kvd, &kmap, &L.bk)) ||
-        (rc = opt_bias("attn_v.bias", kvd, nullptr, &L.bv)) ||
+    const bool split = world > 1;
+    if ((rc = opt_bias("attn_q.bias", H, qmap, &L.bq)) || (rc = opt_bias("attn_k.bias", kvd_full, kmap, &L.bk)) ||
+        (rc = opt_bias("attn_v.bias", kvd_full, vmap, &L.bv)) ||
         (rc = upload_f32(m, g, p + "attn_norm.weight", H, &L.attn_norm)) ||
         (rc = upload_f32(m, g, p + "ffn_norm.weight", H, &L.ffn_norm)) ||
         (rc = upload_2d_rows(g, p + "attn_q.weight", H, H, qmap, &L.wq)) ||
-        (rc = upload_2d_rows(g, p + "attn_k.weight", H, kvd, kmap, &L.wk)) ||
-        (rc = upload_2d(g, p + "attn_v.weight", H, kvd, &L.wv)) ||
-        (rc = upload_2d(g, p + "attn_output.weight", H, H, &L.wo)) ||
-        (rc = upload_gate_up(g, p + "ffn_gate.weight", p + "ffn_up.weight", H, c.n_ff, &L.wgu)) ||
-        (rc = upload_2d(g, p + "ffn_down.weight", c.n_ff, H, &L.wdown))) {
+        (rc = upload_2d_rows(g, p + "attn_k.weight", H, kvd_full, kmap, &L.wk)) ||
+        (rc = split ? upload_2d_rows(g, p + "attn_v.weight", H, kvd_full, vmap, &L.wv)
+                    : upload_2d(g, p + "attn_v.weight", H, kvd, &L.wv)) ||
+        (rc = split ? upload_2d_cols(g, p + "attn_output.weight", H, H, rank * qd, qd, &L.wo)
+                    : upload_2d(g, p + "attn_output.weight", H, H, &L.wo)) ||
+        (rc = upload_gate_up(g, p + "ffn_gate.weight", p + "ffn_up.weight", H, c.n_ff, rank * fl, fl, &L.wgu)) ||
+        (rc = split ? upload_2d_cols(g, p + "ffn_down.weight", c.n_ff, H, rank * fl, fl, &L.wdown)
+                    : upload_2d(g, p + "ffn_down.weight", c.n_ff, H, &L.wdown))) {
       m->layers.push_back(L);  // so that free releases what was uploaded
       return rc;
     }
@@ -476,14 +540,14 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   // workspace
   const uint32_t R = std::max<uint32_t>(32, opts && opts->max_batch ? opts->max_batch : 32);
   m->rows_max = R;
-  const size_t F = c.n_ff, V = c.vocab_size;
+  const size_t F = fl, V = c.vocab_size;
   if ((rc = dev_alloc(m, (void**)&m->x, R * H * 4)) || (rc = dev_alloc(m, (void**)&m->xn, R * H * 4)) ||
-      (rc = dev_alloc(m, (void**)&m->q, R * H * 4)) || (rc = dev_alloc(m, (void**)&m->k, R * kvd * 4)) ||
-      (rc = dev_alloc(m, (void**)&m->v, R * kvd * 4)) || (rc = dev_alloc(m, (void**)&m->att, R * H * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->q, R * qd * 4)) || (rc = dev_alloc(m, (void**)&m->k, R * kvd * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->v, R * kvd * 4)) || (rc = dev_alloc(m, (void**)&m->att, R * qd * 4)) ||
       (rc = dev_alloc(m, (void**)&m->g, R * F * 4)) || (rc = dev_alloc(m, (void**)&m->u, R * F * 4)) ||
       (rc = dev_alloc(m, (void**)&m->logits, R * V * 4)) ||
-      (rc = dev_alloc(m, (void**)&m->part_o, (size_t)R * c.n_heads * m->max_splits * hd * 4)) ||
-      (rc = dev_alloc(m, (void**)&m->part_ml, (size_t)R * c.n_heads * m->max_splits * 2 * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->part_o, (size_t)R * sh.q_heads * m->max_splits * hd * 4)) ||
+      (rc = dev_alloc(m, (void**)&m->part_ml, (size_t)R * sh.q_heads * m->max_splits * 2 * 4)) ||
       (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)))
     return rc;
   {
@@ -546,6 +610,15 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   layout_out(m->out_dev, R, m->dout);
   layout_out(m->out_host, R, m->hout);
   for (uint32_t i = 0; i < R; i++) m->hin.sel[i] = i;
+  CK(cudaMemset(m->out_dev, 0, m->out_bytes));
+  if (world > 1) {
+    // Formed last, so that ranks whose loading takes longer do not run
+    // into the peers' wait bound: the group forms once every rank is ready.
+    CK(cudaDeviceSynchronize());
+    rc = tp_group_create(opts->tp_group, rank, world, opts->tp_flags, opts->tp_wait_ms, (size_t)R * H,
+                         std::max<size_t>(64, (size_t)R * sh.vocab_stride), &m->tp);
+    if (rc) return rc;
+  }
   return SM_OK;
 }
 
@@ -555,6 +628,8 @@ void destroy_model(sm_model* m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : m->run_graphs) cudaGraphExecDestroy(kv.second);
+  tp_group_destroy(m->tp);
+  m->tp = nullptr;
   free_weight(m->tok_embd);
   if (!m->tied) free_weight(m->output);
   for (auto& L : m->layers) {
@@ -576,11 +651,30 @@ void destroy_model(sm_model* m) {
 // (qwen2.rs:460-561). Per layer: QKV GEMV (input RMSNorm, bias, RoPE, KV
 // append in its epilogue), attention, O GEMV (+ residual, next norm's input),
 // gate/up GEMV (+ SwiGLU), down GEMV (+ residual, next norm's input).
+//
+// With tensor parallelism the O and down GEMVs store this rank's partial sums
+// into the exchange arena and tp_reduce_resid_kernel adds the sum over ranks
+// to the residual (and prepares the next norm's input); the output head
+// computes this rank's vocab slice and tp_gather_kernel assembles the logits.
+// A pass makes an even number (2 per layer) of all-reduces, so the arena
+// halves alternate from one all-reduce to the next across passes too.
 cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
   const sm_config& c = m->c;
-  const uint32_t H = (uint32_t)c.n_embd, F = (uint32_t)c.n_ff, kvd = m->kvd, hd = (uint32_t)c.head_dim;
+  const uint32_t H = (uint32_t)c.n_embd, F = m->fl, kvd = m->kvd, hd = (uint32_t)c.head_dim, qd = m->qd;
+  const uint32_t Hq = (uint32_t)m->sh.q_heads, Hkv = (uint32_t)m->sh.kv_heads;
+  TpGroup* tp = m->tp;
+  uint32_t parity = 0;
   cudaError_t e;
 #define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
+  // all-reduce of the partial sums in the arena half `parity`, + residual
+  auto reduce_resid = [&](const float* nw, float* parts) -> cudaError_t {
+    TpCall call;
+    cudaError_t e2 = tp_allreduce_prepare(tp, parity, (size_t)nrows * H, st, &call);
+    if (e2 != cudaSuccess) return e2;
+    call.peers.err = m->dout.err;
+    parity ^= 1u;
+    return launch_tp_reduce_resid(call.peers, call.src, call.nsrc, nrows, H, m->x, H, nw, m->xn, H, parts, st);
+  };
   GemvArgs base{};
   base.batch = nrows;
   base.in_n = H;
@@ -595,6 +689,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   base.ks_cnt = m->ks_cnt;
   base.ks_part_cap = m->ks_part_cap;
   base.ks_cnt_cap = m->ks_cnt_cap;
+  base.err = m->dout.err;
   RK(launch_embed_norm(m->tok_embd.d, m->din.tok, nrows, m->x, H, m->layers[0].attn_norm, m->xn, H, m->parts_a, st));
   uint32_t np_a = 1, np_b = 0;
   for (uint32_t li = 0; li < c.n_layers; li++) {
@@ -604,19 +699,26 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     a.x = m->xn; a.ldx = H;
     a.in_parts = m->parts_a; a.in_np = np_a;
     a.nseg = 3;
-    a.seg[0] = seg(L.wq, m->q, H, L.bq, EPI_ROPE_Q);
+    a.seg[0] = seg(L.wq, m->q, qd, L.bq, EPI_ROPE_Q);
     a.seg[1] = seg(L.wk, nullptr, 0, L.bk, EPI_ROPE_K);
     a.seg[2] = seg(L.wv, nullptr, 0, L.bv, EPI_V);
     RK(launch_gemv(a, st));
-    RK(launch_attention(m->q, H, m->din.rows, m->din.seqs, nrows, li, (uint32_t)c.n_heads, (uint32_t)c.n_kv_heads, hd,
-                        m->part_o, m->part_ml, m->max_splits, m->att, H, st));
+    RK(launch_attention(m->q, qd, m->din.rows, m->din.seqs, nrows, li, Hq, Hkv, hd, m->part_o, m->part_ml,
+                        m->max_splits, m->att, qd, st));
     GemvArgs o = base;
     o.layer = li;
-    o.x = m->att; o.ldx = H;
+    o.x = m->att; o.ldx = qd;
     o.nseg = 1;
-    o.seg[0] = seg(L.wo, m->x, H, nullptr, EPI_RESID);
-    o.nw = L.ffn_norm; o.xn = m->xn; o.ldxn = H; o.out_parts = m->parts_b;
-    RK(launch_gemv(o, st, &np_b));
+    if (tp) {
+      o.seg[0] = seg(L.wo, tp_send_buffer(tp, parity), H, nullptr, EPI_STORE);
+      RK(launch_gemv(o, st));
+      RK(reduce_resid(L.ffn_norm, m->parts_b));
+      np_b = TP_BLOCKS;
+    } else {
+      o.seg[0] = seg(L.wo, m->x, H, nullptr, EPI_RESID);
+      o.nw = L.ffn_norm; o.xn = m->xn; o.ldxn = H; o.out_parts = m->parts_b;
+      RK(launch_gemv(o, st, &np_b));
+    }
     GemvArgs gu = base;
     gu.layer = li;
     gu.x = m->xn; gu.ldx = H;
@@ -629,16 +731,26 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     dn.layer = li;
     dn.x = m->g; dn.ldx = F;
     dn.nseg = 1;
-    dn.seg[0] = seg(L.wdown, m->x, H, nullptr, EPI_RESID);
-    dn.nw = li + 1 < c.n_layers ? m->layers[li + 1].attn_norm : m->output_norm;
-    dn.xn = m->xn; dn.ldxn = H; dn.out_parts = m->parts_a;
-    RK(launch_gemv(dn, st, &np_a));
+    const float* next_norm = li + 1 < c.n_layers ? m->layers[li + 1].attn_norm : m->output_norm;
+    if (tp) {
+      dn.seg[0] = seg(L.wdown, tp_send_buffer(tp, parity), H, nullptr, EPI_STORE);
+      RK(launch_gemv(dn, st));
+      RK(reduce_resid(next_norm, m->parts_a));
+      np_a = TP_BLOCKS;
+    } else {
+      dn.seg[0] = seg(L.wdown, m->x, H, nullptr, EPI_RESID);
+      dn.nw = next_norm;
+      dn.xn = m->xn; dn.ldxn = H; dn.out_parts = m->parts_a;
+      RK(launch_gemv(dn, st, &np_a));
+    }
   }
   if (nsel) {
     GemvArgs hd_ = base;
     hd_.batch = nsel;
     hd_.nseg = 1;
-    hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, EPI_STORE);
+    const uint32_t vs = (uint32_t)m->sh.vocab_stride;
+    hd_.seg[0] = tp ? seg(m->output, tp_gather_buffer(tp), vs, nullptr, EPI_STORE)
+                    : seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, EPI_STORE);
     hd_.x = m->xn; hd_.ldx = H;
     if (nsel == nrows) {  // every row: the last down GEMV prepared the final norm's input
       hd_.in_parts = m->parts_a;
@@ -647,6 +759,13 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
       RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
     }
     RK(launch_gemv(hd_, st));
+    if (tp) {  // this rank's slice [vocab0, vocab0 + vocab) -> the full logits of every rank
+      TpCall call;
+      RK(tp_gather_prepare(tp, (size_t)nsel * vs, st, &call));
+      call.peers.err = m->dout.err;
+      RK(launch_tp_gather(call.peers, call.src, call.nsrc, nsel, vs, (uint32_t)c.vocab_size, m->logits,
+                          (uint32_t)c.vocab_size, st));
+    }
   }
 #undef RK
   return cudaSuccess;
@@ -784,6 +903,34 @@ int guard_model(const sm_model* m) {
   return SM_OK;
 }
 
+// Compute entry points refuse a model whose bounded waits gave up earlier
+// (its activations, KV or tensor-parallel exchange state are not valid).
+int guard_live(const sm_model* m) {
+  if (!m) { set_error("null model"); return SM_ERR_ARG; }
+  if (m->failed) {
+    set_error(m->tp ? "the model's tensor-parallel group failed earlier (a peer timed out); load it again"
+                    : "the model failed earlier (a bounded wait gave up); load it again");
+    return m->tp ? SM_ERR_PEER : SM_ERR_STATE;
+  }
+  return SM_OK;
+}
+
+// After the stream is synchronized: fails the call (and marks the model
+// failed) if a bounded wait gave up during it. fetch: copy the error word
+// first (paths whose step block did not bring it back).
+int check_waits(sm_model* m, bool fetch) {
+  if (fetch) CK(cudaMemcpy(m->hout.err, m->dout.err, 4, cudaMemcpyDeviceToHost));
+  const uint32_t e = *m->hout.err;
+  if (!e) return SM_OK;
+  m->failed = true;
+  if (e & TP_ERR_WAIT) {
+    set_error("a tensor-parallel peer did not arrive within the wait bound (tp_wait_ms); the group is unusable");
+    return SM_ERR_PEER;
+  }
+  set_error("a bounded wait in a GEMV gave up (a weight copy did not complete); results are invalid");
+  return SM_ERR_CUDA;
+}
+
 void model_release(sm_model* m) {
   if (m && m->refs.fetch_sub(1) == 1) destroy_model(m);
 }
@@ -794,7 +941,33 @@ void model_release(sm_model* m) {
 extern "C" {
 
 const char* sm_last_error(void) { return get_error().c_str(); }
-int sm_abi_version(void) { return 1; }
+int sm_abi_version(void) { return 2; }
+int sm_tp_group_id(void* id_out) {
+  if (!id_out) { set_error("null id"); return SM_ERR_ARG; }
+  return tp_unique_id(id_out);
+}
+int sm_model_tp_abort(sm_model* m) {
+  if (guard_model(m)) return SM_ERR_ARG;
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->tp) m->failed = true;
+  return SM_OK;
+}
+int sm_tp_plan(const sm_config* c, uint32_t rank, uint32_t size, sm_tp_shard* out) {
+  if (!c || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  TpShard s;
+  const std::string why =
+      tp_plan(c->n_heads, c->n_kv_heads, c->head_dim, c->n_ff, c->vocab_size, 0, 0, rank, size ? size : 1, &s);
+  if (!why.empty()) { set_error(why); return rank >= (size ? size : 1) ? SM_ERR_ARG : SM_ERR_UNSUPPORTED; }
+  out->q_head0 = (uint64_t)rank * s.q_heads;
+  out->q_heads = s.q_heads;
+  out->kv_head0 = (uint64_t)rank * s.kv_heads;
+  out->kv_heads = s.kv_heads;
+  out->ff0 = (uint64_t)rank * s.ff;
+  out->ff = s.ff;
+  out->vocab0 = s.vocab0;
+  out->vocab = s.vocab;
+  return SM_OK;
+}
 uint64_t sm_rng_seed(uint64_t seed) { return seed + 0x9E3779B97F4A7C15ull; }
 
 static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* opts, sm_model** out) {
@@ -834,6 +1007,15 @@ int sm_model_load_memory(const void* buf, uint64_t len, const sm_load_opts* opts
 }
 
 int sm_model_free(sm_model* m) {
+  if (m && m->tp) {
+    // Every rank frees its handle at the same point of the program: meet
+    // there, then make no further exchanges (caches may outlive the handle).
+    std::lock_guard<std::mutex> lk(m->mu);
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    if (!m->failed) tp_group_barrier(m->tp);
+    m->failed = true;
+  }
   model_release(m);
   return SM_OK;
 }
@@ -1002,6 +1184,7 @@ int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_o
 // ------------------------------------------------------------ forward ----
 int sm_forward_cached(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n, float* logits_out) {
   if (guard_model(m) || !c || !toks || c->m != m) { set_error("sm_forward_cached: bad arguments"); return SM_ERR_ARG; }
+  if (int g = guard_live(m)) return g;
   std::lock_guard<std::mutex> lk(m->mu);
   cudaSetDevice(m->device);
   int rc = forward_tokens(m, c, toks, n);
@@ -1010,7 +1193,7 @@ int sm_forward_cached(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n
     CK(cudaMemcpyAsync(logits_out, m->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
   }
   CK(cudaStreamSynchronize(m->stream));
-  return SM_OK;
+  return check_waits(m, true);
 }
 
 int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n, const sm_sampler* s,
@@ -1021,6 +1204,7 @@ int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n
   }
   int rc = check_sampler(s);
   if (rc) return rc;
+  if ((rc = guard_live(m))) return rc;
   std::lock_guard<std::mutex> lk(m->mu);
   cudaSetDevice(m->device);
   if (n == 1 && !mask) {  // the decode step: graph replay
@@ -1040,6 +1224,7 @@ int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n
     m->hin.sel[0] = 0;
     CK(cudaGraphLaunch(ex, m->stream));
     CK(cudaStreamSynchronize(m->stream));
+    if ((rc = check_waits(m, false))) return rc;
     c->len += 1;
     *out_token = m->hout.tok[0];
     *rng_state = m->hout.rng[0];
@@ -1053,6 +1238,7 @@ int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n
   CK(cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, m->stream));
   if ((rc = sample_rows(m, 1, mask, false))) return rc;
   CK(cudaStreamSynchronize(m->stream));
+  if ((rc = check_waits(m, false))) return rc;
   *out_token = m->hout.tok[0];
   *rng_state = m->hout.rng[0];
   return SM_OK;
@@ -1065,6 +1251,7 @@ int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint
     return SM_ERR_ARG;
   }
   if (n > m->rows_max) { set_error("sm_decode_batch: batch larger than the model's max_batch"); return SM_ERR_ARG; }
+  if (int g = guard_live(m)) return g;
   for (uint64_t i = 0; i < n; i++) {
     int rc = check_sampler(samplers ? &samplers[i] : nullptr);
     if (rc) return rc;
@@ -1091,6 +1278,7 @@ int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint
   }
   CK(cudaGraphLaunch(ex, m->stream));
   CK(cudaStreamSynchronize(m->stream));
+  if ((rc = check_waits(m, false))) return rc;
   for (uint64_t i = 0; i < n; i++) {
     caches[i]->len += 1;
     out_tokens[i] = m->hout.tok[i];
@@ -1106,6 +1294,7 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
     return SM_ERR_ARG;
   }
   if (n > m->rows_max) { set_error("sm_decode_run: batch larger than the model's max_batch"); return SM_ERR_ARG; }
+  if (int g = guard_live(m)) return g;
   if (n_steps == 0) return SM_OK;
   for (uint64_t i = 0; i < n; i++) {
     int rc = check_sampler(samplers ? &samplers[i] : nullptr);
@@ -1143,6 +1332,7 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
   if (ev_end) CK(cudaEventRecord((cudaEvent_t)ev_end, m->stream));
   CK(cudaMemcpyAsync(m->hout.rng, m->din.rng, n * sizeof(uint64_t), cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
+  if ((rc = check_waits(m, true))) return rc;
   for (uint64_t i = 0; i < n; i++) {
     caches[i]->len += n_steps;
     rng_states[i] = m->hout.rng[i];

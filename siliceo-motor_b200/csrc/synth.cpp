@@ -24,6 +24,7 @@
 
 namespace sm {
 bool quantize_row(uint32_t t, const float* x, uint64_t n, uint8_t* out);
+void normal_fill(uint64_t key, uint64_t e0, uint64_t n, float stdv, float* x);  // synth_normal.cpp
 
 namespace {
 
@@ -76,19 +77,6 @@ std::vector<TSpec> layout(const sm_synth_spec& s) {
     v.push_back({p + "ffn_down.weight", F, H, pick(i % 2 == 0 ? QT_Q6K : QT_Q4K, F, ov), K_NORMAL, false});
   }
   return v;
-}
-
-// Fills x[0..n) with elements [e0, e0+n) of the tensor's N(0, std) stream.
-void normal_fill(uint64_t key, uint64_t e0, uint64_t n, float stdv, float* x) {
-  for (uint64_t k = 0; k < n; k++) {
-    uint64_t e = e0 + k;
-    uint64_t h = mix64(key + (e >> 1) * 0x9E3779B97F4A7C15ull);
-    float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
-    float u2 = ((float)((h >> 16) & 0xFFFFFFu) + 0.5f) * (1.0f / 16777216.0f);
-    float r = sqrtf(-2.0f * logf(u1));
-    float th = 6.283185307179586f * u2;
-    x[k] = stdv * ((e & 1) ? r * sinf(th) : r * cosf(th));
-  }
 }
 
 struct Sink {

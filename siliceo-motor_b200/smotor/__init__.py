@@ -45,7 +45,19 @@ class sm_config(C.Structure):
 
 class sm_load_opts(C.Structure):
     _fields_ = [("device", C.c_int32), ("max_batch", C.c_uint32), ("max_context", C.c_uint32),
-                ("tp_rank", C.c_uint32), ("tp_size", C.c_uint32)]
+                ("tp_rank", C.c_uint32), ("tp_size", C.c_uint32), ("tp_flags", C.c_uint32),
+                ("tp_wait_ms", C.c_uint32), ("tp_group", C.c_void_p)]
+
+
+class sm_tp_shard(C.Structure):
+    _fields_ = [("q_head0", C.c_uint64), ("q_heads", C.c_uint64), ("kv_head0", C.c_uint64),
+                ("kv_heads", C.c_uint64), ("ff0", C.c_uint64), ("ff", C.c_uint64),
+                ("vocab0", C.c_uint64), ("vocab", C.c_uint64)]
+
+
+TP_ID_BYTES = 128
+TP_NCCL = 1  # SM_TP_NCCL: NCCL collectives instead of the engine's peer-memory kernels
+ERR_PEER = 9  # SM_ERR_PEER
 
 
 class sm_sampler(C.Structure):
@@ -90,6 +102,9 @@ P, U64, U32, I32, PU32, PU64 = C.c_void_p, C.c_uint64, C.c_uint32, C.c_int32, C.
 SIGNATURES = {
     "sm_last_error": (C.c_char_p, []),
     "sm_abi_version": (C.c_int, []),
+    "sm_tp_group_id": (C.c_int, [P]),
+    "sm_model_tp_abort": (C.c_int, [P]),
+    "sm_tp_plan": (C.c_int, [C.POINTER(sm_config), U32, U32, C.POINTER(sm_tp_shard)]),
     "sm_model_load": (C.c_int, [C.c_char_p, C.POINTER(sm_load_opts), C.POINTER(P)]),
     "sm_model_load_memory": (C.c_int, [P, U64, C.POINTER(sm_load_opts), C.POINTER(P)]),
     "sm_model_free": (C.c_int, [P]),
@@ -219,7 +234,9 @@ class Cache:
         return Cache(out.value, self.model)
 
     def read_kv(self, layer: int, pos: int):
-        kvd = self.model.config.n_kv_heads * self.model.config.head_dim
+        """K and V of one position: the model's KV heads, or with tensor
+        parallelism this rank's (sm_tp_plan)."""
+        kvd = self.model.kv_width()
         k = np.empty(kvd, np.float32)
         v = np.empty(kvd, np.float32)
         _check(lib().sm_cache_read_kv(self.h, layer, pos, _p(k, C.c_float), _p(v, C.c_float)))
@@ -237,8 +254,54 @@ class Cache:
             pass
 
 
+def tp_group_id() -> bytes:
+    """A new tensor-parallel group id (an NCCL unique id): made on one rank
+    and shared with every rank of the group."""
+    buf = (C.c_uint8 * TP_ID_BYTES)()
+    _check(lib().sm_tp_group_id(C.cast(buf, C.c_void_p)))
+    return bytes(buf)
+
+
+def tp_plan(config: sm_config, rank: int, size: int) -> sm_tp_shard:
+    """The part of the model rank `rank` of a `size`-way group holds."""
+    out = sm_tp_shard()
+    _check(lib().sm_tp_plan(C.byref(config), rank, size, C.byref(out)))
+    return out
+
+
+def config_of(n_layers, n_embd, n_ff, n_heads, n_kv_heads, vocab, rope_theta=1e6, rms_eps=1e-6) -> sm_config:
+    return sm_config(n_layers, n_embd, n_ff, n_heads, n_kv_heads, n_embd // n_heads, rope_theta, rms_eps, vocab)
+
+
+@dataclass
+class TensorParallel:
+    """This process's place in a tensor-parallel group (sm_load_opts.tp_*)."""
+    rank: int
+    size: int
+    group_id: bytes
+    flags: int = 0
+    wait_ms: int = 0
+
+    def __post_init__(self):
+        if len(self.group_id) != TP_ID_BYTES:
+            raise ValueError(f"group_id must be {TP_ID_BYTES} bytes")
+        self._id = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(self.group_id)
+
+    @classmethod
+    def from_process_group(cls, flags: int = 0, wait_ms: int = 0, group=None) -> "TensorParallel":
+        """One rank per process of a torch.distributed group: rank 0 makes the
+        id and broadcasts it (any backend)."""
+        import torch.distributed as dist
+        rank, size = dist.get_rank(group), dist.get_world_size(group)
+        obj = [tp_group_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return cls(rank, size, obj[0], flags, wait_ms)
+
+
 class Model:
     """A qwen2/llama GGUF model resident in HBM."""
+
+    tp: Optional[TensorParallel] = None
 
     def __init__(self, handle: int):
         self.h = C.c_void_p(handle)
@@ -247,23 +310,46 @@ class Model:
         self.config = cfg
 
     @staticmethod
-    def _opts(device: int, max_batch: int, max_context: int) -> sm_load_opts:
-        return sm_load_opts(device, max_batch, max_context, 0, 0)
+    def _opts(device: int, max_batch: int, max_context: int, tp=None) -> sm_load_opts:
+        o = sm_load_opts(device, max_batch, max_context, 0, 0, 0, 0, None)
+        if tp is not None:
+            o.tp_rank, o.tp_size = tp.rank, tp.size
+            o.tp_flags, o.tp_wait_ms = tp.flags, tp.wait_ms
+            o.tp_group = C.cast(tp._id, C.c_void_p)
+        return o
 
     @classmethod
-    def load(cls, path: str, device: int = 0, max_batch: int = 32, max_context: int = 32768) -> "Model":
+    def load(cls, path: str, device: int = 0, max_batch: int = 32, max_context: int = 32768,
+             tp: Optional["TensorParallel"] = None) -> "Model":
+        """tp: this process's rank of a tensor-parallel group (every rank
+        loads the same file with its own rank and the same group id)."""
         out = C.c_void_p()
-        o = cls._opts(device, max_batch, max_context)
+        o = cls._opts(device, max_batch, max_context, tp)
         _check(lib().sm_model_load(path.encode(), C.byref(o), C.byref(out)))
-        return cls(out.value)
+        m = cls(out.value)
+        m.tp = tp
+        return m
 
     @classmethod
     def load_memory(cls, buf: int, length: int, device: int = 0, max_batch: int = 32,
-                    max_context: int = 32768) -> "Model":
+                    max_context: int = 32768, tp: Optional["TensorParallel"] = None) -> "Model":
         out = C.c_void_p()
-        o = cls._opts(device, max_batch, max_context)
+        o = cls._opts(device, max_batch, max_context, tp)
         _check(lib().sm_model_load_memory(C.c_void_p(buf), length, C.byref(o), C.byref(out)))
-        return cls(out.value)
+        m = cls(out.value)
+        m.tp = tp
+        return m
+
+    def kv_width(self) -> int:
+        """Floats per position of this rank's K (and V) cache."""
+        c = self.config
+        heads = tp_plan(c, self.tp.rank, self.tp.size).kv_heads if self.tp is not None else c.n_kv_heads
+        return heads * c.head_dim
+
+    def tp_abort(self) -> None:
+        """Mark the tensor-parallel group failed (a peer left): later calls
+        raise EngineError(ERR_PEER) without launching, free skips the barrier."""
+        _check(lib().sm_model_tp_abort(self.h))
 
     def weight_bytes(self) -> int:
         v = C.c_uint64()

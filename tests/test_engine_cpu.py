@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(L, n), n
         assert n in smotor.SIGNATURES, f"binding lacks {n}"
-    assert L.sm_abi_version() == 1
+    assert L.sm_abi_version() == 2
 
 
 def test_rng_seed_matches_reference_rng():
