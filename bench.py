@@ -395,9 +395,10 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
         "e2e": {"value": tokens / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": "sm_forward_sample" if batch == 1 else "sm_decode_batch"},
-        # per step and rank: embed+norm; per layer QKV, attention split, combine, O, gate/up, down; head,
-        # sampler, record; tensor parallel adds 2 all-reduce kernels per layer and the logit gather
-        "gpu_launches": world * args.steps * ((8 * L_ + 5) if split else (6 * L_ + 4)),
+        # per step and rank: embed+norm; per layer QKV (batched: one launch per weight type, 2), attention
+        # split, combine, O, gate/up, down; head, sampler, record; tensor parallel adds 2 all-reduce
+        # kernels per layer and the logit gather
+        "gpu_launches": world * args.steps * (L_ * (6 + (batch > 1) + 2 * split) + 4 + split),
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline and args.workload not in TP_WORKLOADS:

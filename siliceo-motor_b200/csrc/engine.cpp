@@ -10,10 +10,12 @@
 #include <atomic>
 #include <chrono>
 #include <cmath>
+#include <initializer_list>
 #include <map>
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/sm_engine.h"
@@ -58,7 +60,7 @@ int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_
   }
   const uint64_t nb = n_in / bs, row_src = nb * tb;
   const bool tiled = tiled_type(type);
-  const uint64_t n_tiles = (n_out + 15) / 16, n_store = tiled ? n_tiles * 16 : n_out;
+  const uint64_t n_tiles = (n_out + 15) / 16;
   uint64_t body_stride = 0, aux_stride = 0;
   switch (type) {
     case QT_Q4K: body_stride = nb * Q4T_UNIT; break;  // per 16-row tile
@@ -73,64 +75,78 @@ int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_
   aux_stride = (aux_stride + 15) / 16 * 16;
   const uint64_t body_bytes = tiled ? body_stride * n_tiles : body_stride * n_out, aux_bytes = aux_stride * n_out;
   std::vector<uint8_t> body(body_bytes, 0), aux(aux_bytes, 0);
-  uint8_t v6[256];
-  for (uint64_t o = 0; o < n_store; o++) {
-    if (o >= n_out) break;  // padding rows of the last tile stay zero (d = 0)
-    const uint8_t* r = src + o * row_src;
-    const uint32_t rr = (uint32_t)(o & 15);
-    uint8_t* tile = body.data() + (o >> 4) * body_stride;
-    uint8_t* bd = body.data() + o * body_stride;
-    uint8_t* ax = aux.data() + o * aux_stride;
-    switch (type) {
-      case QT_Q4K:  // 16-row tiles (device.cuh)
-        for (uint32_t b = 0; b < nb; b++) {
-          const uint8_t* blk = r + (size_t)b * 144;  // d | dmin | scales 12 | qs 128
-          uint8_t* u = tile + (size_t)b * Q4T_UNIT;
-          std::memcpy(u + 16 * rr, blk, 16);
-          for (uint32_t q = 0; q < 128; q++) u[q4t_qs_off(rr, q)] = blk[16 + q];
-        }
-        break;
-      case QT_Q6K:
-        for (uint32_t b = 0; b < nb; b++) {
-          const uint8_t* blk = r + (size_t)b * 210;  // ql 128 | qh 64 | scales 16 | d 2 (dequant.rs:178-206)
-          uint8_t* u = tile + (size_t)b * Q6T_UNIT;
-          for (uint32_t l = 0; l < 256; l++) {  // 6-bit value q + 32 of weight l
-            const uint32_t n = l >> 7, k = (l & 127) >> 5, ll = l & 31;
-            const uint32_t qlb = blk[64 * n + ll + 32 * (k & 1)];
-            const uint32_t lo = (k >> 1) ? (qlb >> 4) : (qlb & 0x0F);
-            const uint32_t hi = (blk[128 + 32 * n + ll] >> (2 * k)) & 3;
-            v6[l] = (uint8_t)(lo | (hi << 4));
+  // Rows are repacked independently (a tile's rows write disjoint bytes), in
+  // parallel over ranges of whole tiles; padding rows of the last tile stay
+  // zero (d = 0).
+  auto repack = [&](uint64_t o_begin, uint64_t o_end) {
+    uint8_t v6[256];
+    for (uint64_t o = o_begin; o < o_end; o++) {
+      const uint8_t* r = src + o * row_src;
+      const uint32_t rr = (uint32_t)(o & 15);
+      uint8_t* tile = body.data() + (o >> 4) * body_stride;
+      uint8_t* bd = body.data() + o * body_stride;
+      uint8_t* ax = aux.data() + o * aux_stride;
+      switch (type) {
+        case QT_Q4K:  // 16-row tiles (device.cuh)
+          for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* blk = r + (size_t)b * 144;  // d | dmin | scales 12 | qs 128
+            uint8_t* u = tile + (size_t)b * Q4T_UNIT;
+            std::memcpy(u + 16 * rr, blk, 16);
+            for (uint32_t q = 0; q < 128; q++) u[q4t_qs_off(rr, q)] = blk[16 + q];
           }
-          uint32_t W[4][8] = {}, Hq[4][4] = {};
-          for (uint32_t sb = 0; sb < 16; sb++)
-            for (uint32_t t = 0; t < 4; t++)
-              for (uint32_t k = 0; k < 4; k++) {
-                const uint32_t v = v6[16 * sb + 4 * t + k], i = sb & 7, nib = sb >> 3;
-                W[t][i] |= (v & 0x0F) << (8 * k + 4 * nib);
-                Hq[t][i >> 1] |= (v >> 4) << ((q6t_field(k, nib) + 8 * (i & 1)) & 31);
-              }
-          for (uint32_t t = 0; t < 4; t++) {
-            for (uint32_t i = 0; i < 8; i++) std::memcpy(u + q6t_w_off(rr, t, i), &W[t][i], 4);
-            for (uint32_t m = 0; m < 4; m++) std::memcpy(u + q6t_h_off(rr, t, m), &Hq[t][m], 4);
+          break;
+        case QT_Q6K:
+          for (uint32_t b = 0; b < nb; b++) {
+            const uint8_t* blk = r + (size_t)b * 210;  // ql 128 | qh 64 | scales 16 | d 2 (dequant.rs:178-206)
+            uint8_t* u = tile + (size_t)b * Q6T_UNIT;
+            for (uint32_t l = 0; l < 256; l++) {  // 6-bit value q + 32 of weight l
+              const uint32_t n = l >> 7, k = (l & 127) >> 5, ll = l & 31;
+              const uint32_t qlb = blk[64 * n + ll + 32 * (k & 1)];
+              const uint32_t lo = (k >> 1) ? (qlb >> 4) : (qlb & 0x0F);
+              const uint32_t hi = (blk[128 + 32 * n + ll] >> (2 * k)) & 3;
+              v6[l] = (uint8_t)(lo | (hi << 4));
+            }
+            uint32_t W[4][8] = {}, Hq[4][4] = {};
+            for (uint32_t sb = 0; sb < 16; sb++)
+              for (uint32_t t = 0; t < 4; t++)
+                for (uint32_t k = 0; k < 4; k++) {
+                  const uint32_t v = v6[16 * sb + 4 * t + k], i = sb & 7, nib = sb >> 3;
+                  W[t][i] |= (v & 0x0F) << (8 * k + 4 * nib);
+                  Hq[t][i >> 1] |= (v >> 4) << ((q6t_field(k, nib) + 8 * (i & 1)) & 31);
+                }
+            for (uint32_t t = 0; t < 4; t++) {
+              for (uint32_t i = 0; i < 8; i++) std::memcpy(u + q6t_w_off(rr, t, i), &W[t][i], 4);
+              for (uint32_t m = 0; m < 4; m++) std::memcpy(u + q6t_h_off(rr, t, m), &Hq[t][m], 4);
+            }
+            std::memcpy(u + 16 * rr, blk + 192, 16);
+            std::memcpy(u + 256 + 2 * rr, blk + 208, 2);
           }
-          std::memcpy(u + 16 * rr, blk + 192, 16);
-          std::memcpy(u + 256 + 2 * rr, blk + 208, 2);
-        }
-        break;
-      case QT_Q8_0:
-        for (uint64_t b = 0; b < nb; b++) {
-          std::memcpy(ax + b * 2, r + b * 34, 2);
-          std::memcpy(bd + b * 32, r + b * 34 + 2, 32);
-        }
-        break;
-      case QT_Q5_0:
-        for (uint64_t b = 0; b < nb; b++) {
-          std::memcpy(ax + b * 8 + 4, r + b * 22, 2);  // d
-          std::memcpy(ax + b * 8, r + b * 22 + 2, 4);  // qh
-          std::memcpy(bd + b * 16, r + b * 22 + 6, 16);
-        }
-        break;
+          break;
+        case QT_Q8_0:
+          for (uint64_t b = 0; b < nb; b++) {
+            std::memcpy(ax + b * 2, r + b * 34, 2);
+            std::memcpy(bd + b * 32, r + b * 34 + 2, 32);
+          }
+          break;
+        case QT_Q5_0:
+          for (uint64_t b = 0; b < nb; b++) {
+            std::memcpy(ax + b * 8 + 4, r + b * 22, 2);  // d
+            std::memcpy(ax + b * 8, r + b * 22 + 2, 4);  // qh
+            std::memcpy(bd + b * 16, r + b * 22 + 6, 16);
+          }
+          break;
+      }
     }
+  };
+  {
+    const uint64_t work = n_out * nb;
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const uint64_t nt = std::min<uint64_t>(hw, std::max<uint64_t>(1, work / (1u << 16)));
+    std::vector<std::thread> pool;
+    for (uint64_t k = 1; k < nt; k++)
+      pool.emplace_back(repack, std::min(n_out, 16 * (n_tiles * k / nt)), std::min(n_out, 16 * (n_tiles * (k + 1) / nt)));
+    repack(0, std::min(n_out, 16 * (n_tiles / nt)));
+    for (auto& t : pool) t.join();
   }
   void* mem = nullptr;
   const uint64_t total = body_bytes + aux_bytes + 256;
@@ -556,36 +572,36 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device));
     uint64_t need_part = 0;
     uint32_t need_cnt = 0;
-    for (const Layer& L : m->layers) {
-      GemvArgs probe[4] = {};
-      probe[0].nseg = 3;
-      probe[0].seg[0] = seg(L.wq, nullptr, 0, nullptr, EPI_STORE);
-      probe[0].seg[1] = seg(L.wk, nullptr, 0, nullptr, EPI_STORE);
-      probe[0].seg[2] = seg(L.wv, nullptr, 0, nullptr, EPI_STORE);
-      probe[1].seg[0] = seg(L.wo, nullptr, 0, nullptr, EPI_STORE);
-      probe[2].seg[0] = seg(L.wgu, nullptr, 0, nullptr, EPI_STORE);
-      probe[3].seg[0] = seg(L.wdown, nullptr, 0, nullptr, EPI_STORE);
-      for (int i = 0; i < 4; i++) {
-        if (!probe[i].nseg) probe[i].nseg = 1;
-        probe[i].batch = 1;
-        uint64_t pp = 0;
-        uint32_t pc = 0;
-        gemv_tc_scratch_need(probe[i], (uint32_t)sms, &pp, &pc);
+    // a launch of these segments: batch 1 (gemv_tc) and batches up to R
+    // (gemv_tcb, one launch per weight type)
+    auto need = [&](std::initializer_list<const DW*> ws) {
+      GemvArgs a{};
+      for (const DW* w : ws) a.seg[a.nseg++] = seg(*w, nullptr, 0, nullptr, EPI_STORE);
+      uint64_t pp = 0;
+      uint32_t pc = 0;
+      a.batch = 1;
+      gemv_tc_scratch_need(a, (uint32_t)sms, &pp, &pc);
+      need_part = std::max(need_part, pp);
+      need_cnt = std::max(need_cnt, pc);
+      for (uint32_t qt : {(uint32_t)QT_Q4K, (uint32_t)QT_Q6K}) {
+        GemvArgs b{};
+        for (const DW* w : ws)
+          if (w->d.type == qt) b.seg[b.nseg++] = seg(*w, nullptr, 0, nullptr, EPI_STORE);
+        if (!b.nseg) continue;
+        b.batch = R;
+        b.ldx = b.seg[0].w.n_in;
+        gemv_tcb_scratch_need(b, (uint32_t)sms, &pp, &pc);
         need_part = std::max(need_part, pp);
         need_cnt = std::max(need_cnt, pc);
       }
+    };
+    for (const Layer& L : m->layers) {
+      need({&L.wq, &L.wk, &L.wv});
+      need({&L.wo});
+      need({&L.wgu});
+      need({&L.wdown});
     }
-    {
-      GemvArgs hp{};
-      hp.nseg = 1;
-      hp.batch = 1;
-      hp.seg[0] = seg(m->output, nullptr, 0, nullptr, EPI_STORE);
-      uint64_t pp = 0;
-      uint32_t pc = 0;
-      gemv_tc_scratch_need(hp, (uint32_t)sms, &pp, &pc);
-      need_part = std::max(need_part, pp);
-      need_cnt = std::max(need_cnt, pc);
-    }
+    need({&m->output});
     m->ks_part_cap = (uint32_t)std::max<uint64_t>(need_part, 16);
     m->ks_cnt_cap = std::max<uint32_t>(need_cnt, 16);
     if ((rc = dev_alloc(m, (void**)&m->ks_part, (size_t)m->ks_part_cap * 4)) ||
@@ -982,7 +998,7 @@ static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* 
   auto* m = new sm_model();
   m->device = opts ? opts->device : 0;
   if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      gemv_tc_prepare() != cudaSuccess) {
+      gemv_tc_prepare() != cudaSuccess || gemv_tcb_prepare() != cudaSuccess) {
     cudaGetLastError();
     set_error("cannot use CUDA device " + std::to_string(m->device));
     delete m;
@@ -1365,8 +1381,16 @@ int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t
   probe.seg[0] = seg(w->w, nullptr, 0, nullptr, EPI_STORE);
   uint64_t need_part = 0;
   uint32_t need_cnt = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
     gemv_tc_scratch_need(probe, (uint32_t)sms, &need_part, &need_cnt);
+    probe.batch = 32;  // the batched kernel's largest split
+    probe.ldx = w->w.d.n_in;
+    uint64_t pp = 0;
+    uint32_t pc = 0;
+    gemv_tcb_scratch_need(probe, (uint32_t)sms, &pp, &pc);
+    need_part = std::max(need_part, pp);
+    need_cnt = std::max(need_cnt, pc);
+  }
   if (need_part && need_part <= 0xFFFFFFFFull) {
     if (cudaMalloc((void**)&w->ks_part, need_part * 4) != cudaSuccess ||
         cudaMalloc((void**)&w->ks_cnt, (size_t)need_cnt * 4) != cudaSuccess ||

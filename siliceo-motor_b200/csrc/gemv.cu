@@ -462,11 +462,42 @@ uint32_t gemv_plan(GemvArgs& a) {
 
 bool gemv_tc_ok(const GemvArgs& a);
 cudaError_t launch_gemv_tc(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
+bool gemv_tcb_ok(const GemvArgs& a);
+cudaError_t launch_gemv_tcb(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
+
+// Segments of one launch regrouped by weight type (the batched tensor-core
+// kernel takes one type per launch); false if any segment is not tiled.
+static bool split_by_type(const GemvArgs& a, GemvArgs* out, uint32_t* n) {
+  *n = 0;
+  for (uint32_t i = 0; i < a.nseg; i++) {
+    if (!tiled_type(a.seg[i].w.type)) return false;
+    uint32_t k = 0;
+    while (k < *n && out[k].seg[0].w.type != a.seg[i].w.type) k++;
+    if (k == *n) {
+      out[k] = a;
+      out[k].nseg = 0;
+      (*n)++;
+    }
+    out[k].seg[out[k].nseg++] = a.seg[i];
+  }
+  return true;
+}
 
 cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   if (gemv_tc_ok(a)) {
     const cudaError_t e = launch_gemv_tc(a, st, n_parts);
     if (e != cudaErrorNotSupported) return e;
+  }
+  GemvArgs parts[3];
+  uint32_t np = 0;
+  if (a.batch >= 2 && split_by_type(a, parts, &np) && (np == 1 || !n_parts)) {
+    bool ok = true;
+    for (uint32_t i = 0; i < np && ok; i++) ok = gemv_tcb_ok(parts[i]);
+    if (ok) {
+      cudaError_t e = cudaSuccess;
+      for (uint32_t i = 0; i < np && e == cudaSuccess; i++) e = launch_gemv_tcb(parts[i], st, n_parts);
+      if (e != cudaErrorNotSupported) return e;
+    }
   }
   const uint32_t ny = gemv_plan(a);
   if (n_parts) *n_parts = ny;

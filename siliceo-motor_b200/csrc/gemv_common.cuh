@@ -14,6 +14,12 @@ __device__ __forceinline__ float h2f_ref(uint32_t h) {
   const float v = __half2float(__ushort_as_half((unsigned short)h));
   return ((h & 0x7C00u) == 0x7C00u) ? __uint_as_float(((h & 0x8000u) << 16) | 0x7F800000u) : v;
 }
+// Q6_K block scale: a non-finite d makes the block zero (dequant.rs:183-186;
+// the reference GPU kernel skips such a block, kernels/src/lib.rs:845).
+__device__ __forceinline__ float q6_d(uint32_t dbits) {
+  const float d = h2f_ref(dbits);
+  return isfinite(d) ? d : 0.f;
+}
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 // v = two halves (off + a, off + b), exact: returns (a, b) in f32.
 __device__ __forceinline__ float2 hpair(uint32_t v, __half2 off) {

@@ -38,6 +38,7 @@
 #include "device.cuh"
 #include "gemv_common.cuh"
 #include "pdl.cuh"
+#include "tc_common.cuh"
 
 namespace sm {
 
@@ -51,94 +52,17 @@ constexpr uint32_t TC_SMEM_MAX = 225u * 1024u;
 // saturated; deeper rings (more requests in flight) lose bandwidth, and so do
 // L2 prefetches ahead of the ring (both measured on B200).
 constexpr uint32_t TC_MAX_STAGES = 3;
-constexpr uint32_t TC_SPIN_MAX = 1u << 22;     // bound on every mbarrier wait (then: error flag)
 
 struct TcPlan {
   uint32_t tiles, groups, ksplit, slice, units, grid, smem, t4, t6;
   uint32_t stages, stage_bytes;  // per-warp cp.async ring of weight units
 };
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-template <int OFF>
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a), "n"(OFF));
-  return v;
-}
-template <int OFF>
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(a), "n"(OFF));
-  return v;
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-// One bulk copy global -> shared (16-byte aligned, size a multiple of 16) that
-// completes `bytes` of transaction count on mbarrier b.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(b))
-               : "memory");
-}
-// One wait of at most ~TC_SUSPEND_NS: the warp is parked by the hardware
-// (not spinning) until the phase completes or the time hint runs out.
-constexpr uint32_t TC_SUSPEND_NS = 1000;
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity), "n"(TC_SUSPEND_NS)
-      : "memory");
-  return ok != 0;
-}
-// Waits for phase `parity` of b to complete, at most TC_SPIN_MAX tries (a few
-// seconds); a wait that gives up records it in *err and returns (the data is
-// then not used for a result the caller keeps: the host reads the flag).
-__device__ __forceinline__ void mbar_wait(uint64_t* b, uint32_t parity, uint32_t* err) {
-  for (uint32_t n = 0; n < TC_SPIN_MAX; n++)
-    if (mbar_try(b, parity)) return;
-  if (err) atomicOr(err, 1u);
-}
-
-// Low nibbles of bytes (0, 2) as the half2 (q0, q2) * 2^-24 (exact subnormals).
-__device__ __forceinline__ uint32_t nib_lo(uint32_t w) { return w & 0x000F000Fu; }
-// High nibbles of bytes (0, 2): (q0, q2) * 2^-20.
-__device__ __forceinline__ uint32_t nib_hi(uint32_t w) { return w & 0x00F000F0u; }
-// Q6_K: 6-bit values v = q + 32 (low nibble + 2 bits of h at 4-5 / 20-21) * 2^-24.
-__device__ __forceinline__ uint32_t q6_lo(uint32_t w, uint32_t h) { return (w & 0x000F000Fu) | (h & 0x00300030u); }
-// Q6_K: high nibble + 2 bits of h at 8-9 / 24-25: v * 2^-20.
-__device__ __forceinline__ uint32_t q6_hi(uint32_t w, uint32_t h) { return (w & 0x00F000F0u) | (h & 0x03000300u); }
-
 // B operand of the chunks of sub-block s: the lane's fragment words when s is
 // in its column (s & 3 == u), else zero. fb[k] is the shared address the lane
 // reads for sub-blocks s with s & 3 == k: its fragment slot of the current
 // block, or a zero page (the fragments of the lane's sub-blocks u + 4 sigma
 // sit sigma * 512 bytes apart; the zero page is 1 KB).
-
-// x (already scaled) -> (hi, lo): hi keeps 11 significant bits (round half
-// away from zero on the magnitude), lo = x - hi exactly.
-__device__ __forceinline__ float hi11(float v) { return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u); }
-__device__ __forceinline__ uint32_t hl_pair(float a, float b, bool lo) {
-  const float ah = hi11(a), bh = hi11(b);
-  return lo ? h2u(__floats2half2_rn(a - ah, b - bh)) : h2u(__floats2half2_rn(ah, bh));
-}
 
 // Converts block bl (global block b) of x into shared memory: per type the
 // lane's B fragments [2][32 lanes][4 words] for the sub-blocks of its column
@@ -281,10 +205,6 @@ __device__ __forceinline__ float q6_half(uint32_t w0, uint32_t w1, int t, const 
   const float s0 = (float)(int8_t)((w0 >> sh) & 0xFFu), s1 = (float)(int8_t)((w1 >> sh) & 0xFFu);
   return s0 * fmaf(F, acc[0][c] + acc[0][c + 1], -32.f * X0) + s1 * fmaf(F, acc[1][c] + acc[1][c + 1], -32.f * X1);
 }
-__device__ __forceinline__ float q6_d(uint32_t dbits) {
-  const float d = h2f_ref(dbits);
-  return isfinite(d) ? d : 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
-}
 // Two passes: sub-blocks 0-7 (low nibbles of the 8 ql words), then 8-15 (high
 // nibbles), each into two accumulators that are scaled before the next pass.
 __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint32_t (&fb)[4], const float4* __restrict__ xs,
@@ -337,14 +257,6 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint32_t (&f
 // (use n of the ring waits for parity (n / S) & 1; nuse counts the warp's
 // uses across units). Returns the partial dot products in rg, rh (summed
 // over the lane's sub-blocks only).
-// Lane 0: the bulk copy of one block unit (UB bytes) into ring slot st.
-__device__ __forceinline__ void tc_issue(const uint8_t* unit, uint32_t UB, uint8_t* ring, uint32_t stage_bytes,
-                                         uint64_t* bars, uint32_t st) {
-  fence_proxy_async();  // this slot's previous reads (ordered by __syncwarp) before the async write
-  mbar_expect_tx(bars + st, UB);
-  bulk_g2s(ring + st * stage_bytes, unit, UB, bars + st);
-}
-
 // The first `pre` copies may have been started by the caller already (ahead
 // of the previous kernel, pdl.cuh).
 template <int QT, int S>

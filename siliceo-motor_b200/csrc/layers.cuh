@@ -46,6 +46,10 @@ cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st);
 // (floats, counters) a launch of this shape may use on a GPU with `sms` SMs:
 cudaError_t gemv_tc_prepare();
 void gemv_tc_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt);
+// The same for the batched (2..32 columns, one weight type) tensor-core GEMV
+// of gemv_tcb.cu (a.batch columns).
+cudaError_t gemv_tcb_prepare();
+void gemv_tcb_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt);
 cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
                                  uint32_t cap_steps, cudaStream_t st);
 

@@ -52,7 +52,7 @@ def test_dequant_bit_exact(qt, special):
     assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
 
 
-def gemv_check(qt, n_out, n_in, batches, seed, std=1.0):
+def gemv_check(qt, n_out, n_in, batches, seed, std=1.0, outliers=False):
     rng = np.random.default_rng(seed)
     wf = rng.normal(0, std, n_out * n_in).astype(np.float32)
     raw = smotor.quantize(qt, wf)
@@ -62,6 +62,9 @@ def gemv_check(qt, n_out, n_in, batches, seed, std=1.0):
     assert w.nbytes() == len(raw)
     bmax = max(batches)
     x = rng.normal(0, 1, (bmax, n_in)).astype(np.float32)
+    if outliers:  # a few large channels, as activations have: per-block scaling of x must cope
+        x[:, ::97] *= 300.0
+        x[1::2] *= 1e-3  # and columns of very different magnitude
     y_ref = x.astype(np.float64) @ wdq.T
     xd = torch.from_numpy(x).cuda()
     for b in batches:
@@ -69,7 +72,8 @@ def gemv_check(qt, n_out, n_in, batches, seed, std=1.0):
         w.gemv(xd.data_ptr(), y.data_ptr(), b)
         torch.cuda.synchronize()
         got = y.cpu().numpy().astype(np.float64)
-        err = np.abs(got - y_ref[:b]).max() / np.abs(y_ref[:b]).max()
+        # normwise per column: a column of small values is held to its own scale
+        err = (np.abs(got - y_ref[:b]).max(axis=1) / np.abs(y_ref[:b]).max(axis=1)).max()
         assert err <= GEMV_TOL, (qt, n_out, n_in, b, err)
 
 
@@ -90,6 +94,20 @@ def test_gemv_fallback_types_and_odd_batches(qt, batch):
 def test_gemv_kquants_odd_batches_and_ragged_rows(batch):
     gemv_check(smotor.Q4_K, 100, 512, [batch], seed=3)
     gemv_check(smotor.Q6_K, 36, 768, [batch], seed=4)
+
+
+@pytest.mark.parametrize("qt", [smotor.Q4_K, smotor.Q6_K])
+@pytest.mark.parametrize("n_out,n_in", [(512, 8192), (4096, 256), (272, 2304)])
+def test_gemv_batched_tensor_core_sweep(qt, n_out, n_in):
+    # every n-tile count (1, 2, 4, 8 groups of 4 columns) and partial groups;
+    # K split many ways (512 x 8192), unsplit (4096 x 256), a ragged last tile
+    gemv_check(qt, n_out, n_in, [2, 4, 5, 8, 9, 16, 17, 24, 31, 32], seed=n_out + n_in)
+
+
+@pytest.mark.parametrize("qt", [smotor.Q4_K, smotor.Q6_K])
+def test_gemv_batched_outlier_channels(qt):
+    gemv_check(qt, 1024, 4096, [2, 8, 32], seed=9, outliers=True)
+    gemv_check(qt, 1024, 4096, [1], seed=9, outliers=True)
 
 
 def test_gemv_rejects_bad_arguments():
