@@ -91,6 +91,7 @@ enum GemvEpi : uint32_t {
   EPI_ROPE_K = 4,  // same, store into the K cache
   EPI_V = 5,       // store into the V cache
   EPI_SILU = 6,    // pair (gate m, up m): h[m] = silu(gate) * up (natural and permuted)
+  EPI_PUSH = 7,    // tensor parallel: send (v, epoch) to every rank's receive area (TpPush)
 };
 __host__ __device__ inline bool epi_is_pair(uint32_t e) { return e == EPI_ROPE_Q || e == EPI_ROPE_K || e == EPI_SILU; }
 
@@ -102,6 +103,20 @@ struct GemvSeg {
   uint32_t ldy;
   uint32_t epi;        // GemvEpi
   uint32_t cta_begin;  // first CTA index of this segment
+};
+
+// Where an EPI_PUSH GEMV sends its outputs (tensor parallelism, tp.hpp):
+// element o of column b goes, as the 8-byte packet (v bits | epoch << 32), to
+// dst[k][parity * parity_stride + rank * src_stride + b * ld + o] of every
+// rank k (mapped peer memory; k == rank is local). The epoch is that of the
+// consumer block owning global element base + o: epoch[(base + o) / per] + 1,
+// and parity = epoch & 1.
+constexpr uint32_t TP_MAX_RANKS = 8;
+struct TpPush {
+  uint64_t* dst[TP_MAX_RANKS];
+  uint64_t parity_stride, src_stride;
+  const uint32_t* epoch;
+  uint32_t world, rank, ld, per, base;
 };
 
 struct GemvArgs {
@@ -139,6 +154,7 @@ struct GemvArgs {
   // Set non-zero by a kernel whose bounded wait gave up (the launch's results
   // are then not valid); may be null.
   uint32_t* err;
+  TpPush push;  // EPI_PUSH
 };
 
 #ifdef __CUDACC__

@@ -631,8 +631,8 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
     // Formed last, so that ranks whose loading takes longer do not run
     // into the peers' wait bound: the group forms once every rank is ready.
     CK(cudaDeviceSynchronize());
-    rc = tp_group_create(opts->tp_group, rank, world, opts->tp_flags, opts->tp_wait_ms, (size_t)R * H,
-                         std::max<size_t>(64, (size_t)R * sh.vocab_stride), &m->tp);
+    rc = tp_group_create(opts->tp_group, rank, world, opts->tp_flags, opts->tp_wait_ms, R, (uint32_t)H,
+                         (uint32_t)sh.vocab_stride, &m->tp);
     if (rc) return rc;
   }
   return SM_OK;
@@ -668,28 +668,32 @@ void destroy_model(sm_model* m) {
 // append in its epilogue), attention, O GEMV (+ residual, next norm's input),
 // gate/up GEMV (+ SwiGLU), down GEMV (+ residual, next norm's input).
 //
-// With tensor parallelism the O and down GEMVs store this rank's partial sums
-// into the exchange arena and tp_reduce_resid_kernel adds the sum over ranks
+// With tensor parallelism the O and down GEMVs push this rank's partial sums
+// to every rank (EPI_PUSH) and tp_reduce_resid_kernel adds the sum over ranks
 // to the residual (and prepares the next norm's input); the output head
-// computes this rank's vocab slice and tp_gather_kernel assembles the logits.
-// A pass makes an even number (2 per layer) of all-reduces, so the arena
-// halves alternate from one all-reduce to the next across passes too.
+// pushes this rank's vocab slice and tp_gather_kernel assembles the logits.
 cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
   const sm_config& c = m->c;
   const uint32_t H = (uint32_t)c.n_embd, F = m->fl, kvd = m->kvd, hd = (uint32_t)c.head_dim, qd = m->qd;
   const uint32_t Hq = (uint32_t)m->sh.q_heads, Hkv = (uint32_t)m->sh.kv_heads;
   TpGroup* tp = m->tp;
-  uint32_t parity = 0;
   cudaError_t e;
 #define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
-  // all-reduce of the partial sums in the arena half `parity`, + residual
-  auto reduce_resid = [&](const float* nw, float* parts) -> cudaError_t {
-    TpCall call;
-    cudaError_t e2 = tp_allreduce_prepare(tp, parity, (size_t)nrows * H, st, &call);
-    if (e2 != cudaSuccess) return e2;
-    call.peers.err = m->dout.err;
-    parity ^= 1u;
-    return launch_tp_reduce_resid(call.peers, call.src, call.nsrc, nrows, H, m->x, H, nw, m->xn, H, parts, st);
+  // A row-split GEMV (O or down) whose rank partials are all-reduced into the
+  // residual, which also yields the next norm's input.
+  auto split_gemv = [&](GemvArgs g, const DW& w, const float* nw, float* parts, uint32_t* np) -> cudaError_t {
+    const TpExchange ex = tp_allreduce(tp, m->dout.err);
+    if (ex.send) {
+      g.seg[0] = seg(w, ex.send, H, nullptr, EPI_STORE);
+    } else {
+      g.seg[0] = seg(w, nullptr, H, nullptr, EPI_PUSH);
+      g.push = ex.push;
+    }
+    cudaError_t e2 = launch_gemv(g, st);
+    if (e2 == cudaSuccess && ex.send) e2 = tp_allreduce_issue(tp, nrows, st);
+    if (e2 == cudaSuccess) e2 = launch_tp_reduce_resid(ex.recv, nrows, H, m->x, H, nw, m->xn, H, parts, st);
+    *np = TP_BLOCKS;
+    return e2;
   };
   GemvArgs base{};
   base.batch = nrows;
@@ -726,10 +730,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     o.x = m->att; o.ldx = qd;
     o.nseg = 1;
     if (tp) {
-      o.seg[0] = seg(L.wo, tp_send_buffer(tp, parity), H, nullptr, EPI_STORE);
-      RK(launch_gemv(o, st));
-      RK(reduce_resid(L.ffn_norm, m->parts_b));
-      np_b = TP_BLOCKS;
+      RK(split_gemv(o, L.wo, L.ffn_norm, m->parts_b, &np_b));
     } else {
       o.seg[0] = seg(L.wo, m->x, H, nullptr, EPI_RESID);
       o.nw = L.ffn_norm; o.xn = m->xn; o.ldxn = H; o.out_parts = m->parts_b;
@@ -749,10 +750,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     dn.nseg = 1;
     const float* next_norm = li + 1 < c.n_layers ? m->layers[li + 1].attn_norm : m->output_norm;
     if (tp) {
-      dn.seg[0] = seg(L.wdown, tp_send_buffer(tp, parity), H, nullptr, EPI_STORE);
-      RK(launch_gemv(dn, st));
-      RK(reduce_resid(next_norm, m->parts_a));
-      np_a = TP_BLOCKS;
+      RK(split_gemv(dn, L.wdown, next_norm, m->parts_a, &np_a));
     } else {
       dn.seg[0] = seg(L.wdown, m->x, H, nullptr, EPI_RESID);
       dn.nw = next_norm;
@@ -765,8 +763,18 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     hd_.batch = nsel;
     hd_.nseg = 1;
     const uint32_t vs = (uint32_t)m->sh.vocab_stride;
-    hd_.seg[0] = tp ? seg(m->output, tp_gather_buffer(tp), vs, nullptr, EPI_STORE)
-                    : seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, EPI_STORE);
+    TpExchange gx{};
+    if (tp) {  // this rank's slice [vocab0, vocab0 + vocab) goes to every rank
+      gx = tp_gather(tp, nsel, m->sh.vocab0, m->dout.err);
+      if (gx.send) {
+        hd_.seg[0] = seg(m->output, gx.send, vs, nullptr, EPI_STORE);
+      } else {
+        hd_.seg[0] = seg(m->output, nullptr, vs, nullptr, EPI_PUSH);
+        hd_.push = gx.push;
+      }
+    } else {
+      hd_.seg[0] = seg(m->output, m->logits, (uint32_t)c.vocab_size, nullptr, EPI_STORE);
+    }
     hd_.x = m->xn; hd_.ldx = H;
     if (nsel == nrows) {  // every row: the last down GEMV prepared the final norm's input
       hd_.in_parts = m->parts_a;
@@ -775,12 +783,9 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
       RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
     }
     RK(launch_gemv(hd_, st));
-    if (tp) {  // this rank's slice [vocab0, vocab0 + vocab) -> the full logits of every rank
-      TpCall call;
-      RK(tp_gather_prepare(tp, (size_t)nsel * vs, st, &call));
-      call.peers.err = m->dout.err;
-      RK(launch_tp_gather(call.peers, call.src, call.nsrc, nsel, vs, (uint32_t)c.vocab_size, m->logits,
-                          (uint32_t)c.vocab_size, st));
+    if (tp) {  // the full logits on every rank
+      if (gx.send) RK(tp_gather_issue(tp, nsel, st));
+      RK(launch_tp_gather(gx.recv, nsel, vs, (uint32_t)c.vocab_size, m->logits, (uint32_t)c.vocab_size, st));
     }
   }
 #undef RK

@@ -61,6 +61,15 @@ __device__ __forceinline__ float epi_single(const GemvArgs& a, const GemvSeg& sg
       a.xn[(size_t)col * a.ldxn + o] = xn * a.nw[o];
       return xn;
     }
+    case EPI_PUSH: {  // tensor parallel: this rank's partial sum to every rank (tp.cu)
+      const TpPush& P = a.push;
+      const uint32_t e = __ldcg(P.epoch + (P.base + o) / P.per) + 1u;
+      const uint64_t pk = ((uint64_t)e << 32) | __float_as_uint(v);
+      const uint64_t off = (e & 1u) * P.parity_stride + P.rank * P.src_stride + (uint64_t)col * P.ld + o;
+      for (uint32_t k = 0; k < P.world; k++)
+        asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(P.dst[k] + off), "l"(pk) : "memory");
+      return 0.f;
+    }
     case EPI_V: {  // v row into the cache at the row's position (qwen2.rs:498)
       const RowDesc rd = a.rows[col];
       const SeqDesc sd = a.seqs[rd.seq];

@@ -1,6 +1,8 @@
-// Exchange kernels of tensor-parallel decode (see tp.hpp): the all-reduce
+// Consumer kernels of tensor-parallel decode (see tp.hpp): the all-reduce
 // that follows the row-split O and down GEMVs, fused with the residual add
 // and the next RMSNorm's input, and the all-gather of the vocab-split logits.
+// The producing GEMVs push their outputs as packets (EPI_PUSH); these kernels
+// wait for the packets in their own memory and combine them.
 //
 // Replaces, for the partitioned 70B configuration, the per-block NCCL
 // all-reduce of a Megatron split: the reference runs one process on one
@@ -15,69 +17,40 @@ namespace {
 
 constexpr uint32_t TP_THREADS = 128;
 
-struct TpSrc {
-  const float* p[TP_MAX];
-};
-
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_packet(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Peer data: never served from a stale L1 line of an earlier exchange.
-__device__ __forceinline__ float4 ld_peer4(const float* p) { return __ldcv(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ float ld_peer(const float* p) { return __ldcv(p); }
 
-// Block-level barrier of one exchange. Thread r < world publishes this
-// block's epoch into rank r's flag slot [block][rank] and waits (bounded)
-// until rank r has published the same epoch into ours. All ranks run the
-// same sequence of exchanges with the same grid, so a block's epoch is the
-// same on every rank. Returns false (and sets the error word) if a peer did
-// not arrive within wait_ns.
-__device__ bool tp_block_sync(const TpPeers& p) {
-  __shared__ uint32_t s_ep, s_ok;
-  const uint32_t b = blockIdx.x;
-  if (threadIdx.x == 0) {
-    const uint32_t e = p.epoch[b] + 1u;
-    p.epoch[b] = e;
-    s_ep = e;
-    s_ok = 1u;
-  }
-  __syncthreads();
-  if (!p.sync) return true;
-  const uint32_t ep = s_ep;
-  // After one timed-out wait the group is broken: the exchanges that follow
-  // in the same pass give up at once instead of each waiting out the bound.
-  const bool broken = (*reinterpret_cast<volatile uint32_t*>(p.err) & TP_ERR_WAIT) != 0u;
-  if (broken) {
-    if (threadIdx.x == 0) s_ok = 0u;
-  } else if (threadIdx.x < p.world) {
-    const uint32_t r = threadIdx.x;
-    __threadfence_system();  // this rank's send data before the signal
-    st_release_sys(p.flag[r] + b * TP_MAX + p.rank, ep);
-    const uint32_t* f = p.flag[p.rank] + b * TP_MAX + r;
-    const uint64_t t0 = global_ns();
-    // A peer is at most one exchange ahead (it waits for this rank's signal
-    // of the next one), so "arrived" is epoch >= ep, compared modulo 2^32.
-    while ((int32_t)(ld_acquire_sys(f) - ep) < 0) {
-      if (global_ns() - t0 > p.wait_ns) {
-        atomicOr(p.err, TP_ERR_WAIT);
-        s_ok = 0u;
-        break;
-      }
-      __nanosleep(100);
+// The value of packet *p once it carries epoch e. A sender is at most one
+// exchange ahead (it waits for this rank's packets of the next exchange), and
+// the two halves of an area alternate, so the packet holds epoch e, e - 2
+// (not yet written) or 0 (never written). The wait is bounded; after one
+// timed-out wait the group is broken and later waits give up at once.
+__device__ __forceinline__ float tp_wait_packet(const uint64_t* p, uint32_t e, const TpRecv& r, bool& ok) {
+  uint64_t v = ld_packet(p);
+  if ((uint32_t)(v >> 32) == e) return __uint_as_float((uint32_t)v);
+  const uint64_t t0 = global_ns();
+  while (ok) {
+    if (*reinterpret_cast<volatile uint32_t*>(r.err) & TP_ERR_WAIT) {
+      ok = false;
+      break;
+    }
+    __nanosleep(32);
+    v = ld_packet(p);
+    if ((uint32_t)(v >> 32) == e) return __uint_as_float((uint32_t)v);
+    if (global_ns() - t0 > r.wait_ns) {
+      atomicOr(r.err, TP_ERR_WAIT);
+      ok = false;
     }
   }
-  __syncthreads();
-  return s_ok != 0u;
+  return 0.f;
 }
 
 // Deterministic block sum (fixed shuffle tree, then warps in order).
@@ -95,84 +68,90 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
+// This block's epoch of the exchange (packets mode), and its update once the
+// block is done.
+__device__ __forceinline__ uint32_t tp_epoch(const TpRecv& r) {
+  __shared__ uint32_t s_e;
+  if (threadIdx.x == 0) s_e = r.pk ? r.epoch[blockIdx.x] + 1u : 0u;
+  __syncthreads();
+  return s_e;
+}
+__device__ __forceinline__ void tp_epoch_done(const TpRecv& r, uint32_t e) {
+  __syncthreads();
+  if (threadIdx.x == 0 && r.pk) r.epoch[blockIdx.x] = e;
+}
+
 __global__ void __launch_bounds__(TP_THREADS, 16)
-    tp_reduce_resid_kernel(const __grid_constant__ TpPeers p, const __grid_constant__ TpSrc s, uint32_t nsrc,
-                           uint32_t rows, uint32_t n, float* x, uint32_t ldx, const float* nw, float* xn,
-                           uint32_t ldxn, float* parts) {
+    tp_reduce_resid_kernel(const __grid_constant__ TpRecv r, uint32_t rows, uint32_t n, float* x, uint32_t ldx,
+                           const float* nw, float* xn, uint32_t ldxn, float* parts) {
   pdl_trigger();  // the next GEMV may start its weight copies
-  pdl_wait();     // the GEMV that wrote this rank's partial sums has finished
-  if (!tp_block_sync(p)) return;
+  pdl_wait();     // this rank's producer GEMV has finished (its pushes are out)
+  const uint32_t e = tp_epoch(r);
   __shared__ float red[TP_THREADS / 32];
-  const uint32_t per = (n + TP_BLOCKS - 1) / TP_BLOCKS;
-  const uint32_t e0 = blockIdx.x * per, e1 = min(n, e0 + per);
-  for (uint32_t r = 0; r < rows; r++) {
+  bool ok = true;
+  const uint32_t nsrc = r.pk ? r.world : 1u;
+  const uint32_t o0 = blockIdx.x * r.per, o1 = min(n, o0 + r.per);
+  const uint64_t* half = r.pk ? r.pk + (e & 1u) * r.parity_stride : nullptr;
+  for (uint32_t row = 0; row < rows; row++) {
     float ss = 0.f;
-    for (uint32_t e = e0 + threadIdx.x; e < e1; e += TP_THREADS) {
-      const size_t off = (size_t)r * n + e;
-      float v[TP_MAX];
+    for (uint32_t o = o0 + threadIdx.x; o < o1; o += TP_THREADS) {
+      const size_t off = (size_t)row * r.ld + o;
+      float acc = 0.f;
+      if (half) {
+        float v[TP_MAX];
 #pragma unroll
-      for (uint32_t k = 0; k < TP_MAX; k++)
-        if (k < nsrc) v[k] = ld_peer(s.p[k] + off);
-      float acc = v[0];
+        for (uint32_t k = 0; k < TP_MAX; k++)
+          if (k < nsrc) v[k] = tp_wait_packet(half + k * r.src_stride + off, e, r, ok);
+        acc = v[0];
 #pragma unroll
-      for (uint32_t k = 1; k < TP_MAX; k++)
-        if (k < nsrc) acc = __fadd_rn(acc, v[k]);
-      float* xp = x + (size_t)r * ldx + e;
+        for (uint32_t k = 1; k < TP_MAX; k++)
+          if (k < nsrc) acc = __fadd_rn(acc, v[k]);  // rank order: the same bits on every rank
+      } else {
+        acc = r.plain[off];
+      }
+      float* xp = x + (size_t)row * ldx + o;
       const float xv = __fadd_rn(*xp, acc);
       *xp = xv;
-      xn[(size_t)r * ldxn + e] = __fmul_rn(xv, nw[e]);
+      xn[(size_t)row * ldxn + o] = __fmul_rn(xv, nw[o]);
       ss = __fmaf_rn(xv, xv, ss);
     }
     const float t = block_sum(ss, red);
-    if (threadIdx.x == 0) parts[(size_t)r * TP_BLOCKS + blockIdx.x] = t;
+    if (threadIdx.x == 0) parts[(size_t)row * TP_BLOCKS + blockIdx.x] = t;
   }
+  tp_epoch_done(r, e);
 }
 
 __global__ void __launch_bounds__(TP_THREADS, 16)
-    tp_gather_kernel(const __grid_constant__ TpPeers p, const __grid_constant__ TpSrc s, uint32_t nsrc, uint32_t rows,
-                     uint32_t nl, uint32_t n_total, float* out, uint32_t ldo) {
+    tp_gather_kernel(const __grid_constant__ TpRecv r, uint32_t rows, uint32_t nl, uint32_t n_total, float* out,
+                     uint32_t ldo) {
   pdl_trigger();
-  pdl_wait();  // the head GEMV that wrote this rank's slice has finished
-  if (!tp_block_sync(p)) return;
-  // Groups of 4 consecutive elements of one (row, source) slice.
-  const uint32_t g_per = (nl + 3) / 4, per_row = g_per * nsrc, total = rows * per_row;
-  for (uint32_t i = blockIdx.x * TP_THREADS + threadIdx.x; i < total; i += TP_BLOCKS * TP_THREADS) {
-    const uint32_t r = i / per_row, rem = i - r * per_row, k = rem / g_per, j0 = 4u * (rem - k * g_per);
-    const uint32_t base = k * nl;
-    if (base >= n_total) continue;
-    const uint32_t cnt = min(nl, n_total - base);
-    const float* src = s.p[k] + (size_t)r * nl;
-    float* dst = out + (size_t)r * ldo + base;
-    float v[4];
-#pragma unroll
-    for (uint32_t q = 0; q < 4; q++) v[q] = (j0 + q < cnt) ? ld_peer(src + j0 + q) : 0.f;
-#pragma unroll
-    for (uint32_t q = 0; q < 4; q++)
-      if (j0 + q < cnt) dst[j0 + q] = v[q];
-  }
-}
-
-TpSrc to_src(const float* const* src, uint32_t nsrc) {
-  TpSrc s{};
-  for (uint32_t k = 0; k < nsrc && k < TP_MAX; k++) s.p[k] = src[k];
-  return s;
+  pdl_wait();  // this rank's head GEMV has finished
+  const uint32_t e = tp_epoch(r);
+  bool ok = true;
+  const uint32_t v0 = blockIdx.x * r.per, v1 = min(n_total, v0 + r.per);
+  for (uint32_t row = 0; row < rows; row++)
+    for (uint32_t v = v0 + threadIdx.x; v < v1; v += TP_THREADS) {
+      const uint32_t k = v / nl, j = v - k * nl;
+      const size_t off = k * r.src_stride + (size_t)row * r.ld + j;
+      out[(size_t)row * ldo + v] = r.pk ? tp_wait_packet(r.pk + off, e, r, ok) : r.plain[off];
+    }
+  tp_epoch_done(r, e);
 }
 
 }  // namespace
 
-cudaError_t launch_tp_reduce_resid(const TpPeers& p, const float* const* src, uint32_t nsrc, uint32_t rows, uint32_t n,
-                                   float* x, uint32_t ldx, const float* nw, float* xn, uint32_t ldxn, float* parts,
-                                   cudaStream_t st) {
-  if (nsrc == 0 || nsrc > TP_MAX) return cudaErrorInvalidValue;
-  return launch_pdl(tp_reduce_resid_kernel, dim3(TP_BLOCKS), dim3(TP_THREADS), 0, st, p, to_src(src, nsrc), nsrc, rows,
-                    n, x, ldx, nw, xn, ldxn, parts);
+cudaError_t launch_tp_reduce_resid(const TpRecv& rv, uint32_t rows, uint32_t n, float* x, uint32_t ldx, const float* nw,
+                                   float* xn, uint32_t ldxn, float* parts, cudaStream_t st) {
+  if (rv.world == 0 || rv.world > TP_MAX || !rv.err || (!rv.pk && !rv.plain) || !rv.per) return cudaErrorInvalidValue;
+  return launch_pdl(tp_reduce_resid_kernel, dim3(TP_BLOCKS), dim3(TP_THREADS), 0, st, rv, rows, n, x, ldx, nw, xn,
+                    ldxn, parts);
 }
 
-cudaError_t launch_tp_gather(const TpPeers& p, const float* const* src, uint32_t nsrc, uint32_t rows, uint32_t nl,
-                             uint32_t n_total, float* out, uint32_t ldo, cudaStream_t st) {
-  if (nsrc == 0 || nsrc > TP_MAX) return cudaErrorInvalidValue;
-  return launch_pdl(tp_gather_kernel, dim3(TP_BLOCKS), dim3(TP_THREADS), 0, st, p, to_src(src, nsrc), nsrc, rows, nl,
-                    n_total, out, ldo);
+cudaError_t launch_tp_gather(const TpRecv& rv, uint32_t rows, uint32_t nl, uint32_t n_total, float* out, uint32_t ldo,
+                             cudaStream_t st) {
+  if (rv.world == 0 || rv.world > TP_MAX || !rv.err || (!rv.pk && !rv.plain) || nl == 0 || !rv.per)
+    return cudaErrorInvalidValue;
+  return launch_pdl(tp_gather_kernel, dim3(TP_BLOCKS), dim3(TP_THREADS), 0, st, rv, rows, nl, n_total, out, ldo);
 }
 
 }  // namespace sm

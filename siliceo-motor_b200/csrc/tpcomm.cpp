@@ -70,14 +70,18 @@ using Clock = std::chrono::steady_clock;
 
 }  // namespace
 
+// This rank's arena (one allocation, mapped by every peer):
+//   epochs: all-reduce [TP_BLOCKS] | gather [TP_BLOCKS]
+//   all-reduce packets [2 halves][world sources][rows][n]
+//   gather packets [world sources][rows][nl]
+//   NCCL mode: send f32 [rows][n] | receive f32 [rows][n] | gather send f32 [rows][nl] | gather receive [world][rows][nl]
 struct TpGroup {
-  uint32_t rank = 0, world = 1, flags = 0;
+  uint32_t rank = 0, world = 1, flags = 0, rows = 0, n = 0, nl = 0;
   uint64_t wait_ns = 0;
   ncclComm_t comm = nullptr;
-  uint8_t* arena = nullptr;  // this rank's arena
+  uint8_t* arena = nullptr;
   uint8_t* peer[TP_MAX] = {};
-  size_t off_flag = 0, off_epoch = 0, off_send[2] = {0, 0}, off_gather = 0, off_recv = 0, off_grecv = 0;
-  size_t send_floats = 0, gather_floats = 0;
+  size_t off_ep_ar = 0, off_ep_g = 0, off_ar = 0, off_g = 0, off_send = 0, off_recv = 0, off_gsend = 0, off_grecv = 0;
   bool opened[TP_MAX] = {};
 };
 
@@ -174,7 +178,8 @@ void tp_group_barrier(TpGroup* g) {
   cudaStream_t st = nullptr;
   if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess) {
     const auto deadline = Clock::now() + std::chrono::nanoseconds(g->wait_ns);
-    float* b = reinterpret_cast<float*>(g->arena + g->off_gather);
+    // a scratch float of the arena that no exchange uses any more
+    float* b = reinterpret_cast<float*>(g->arena + (tp_uses_nccl(g) ? g->off_send : g->off_ar));
     ncclResult_t r = a.all_reduce(b, b, 1, ncclFloat, ncclSum, g->comm, st);
     if (nccl_settle(g, r, deadline, "teardown barrier") == SM_OK) stream_settle(g, st, deadline, "teardown barrier");
     cudaStreamDestroy(st);
@@ -196,15 +201,22 @@ void tp_group_destroy(TpGroup* g) {
   delete g;
 }
 
-int tp_group_create(const void* id, uint32_t rank, uint32_t world, uint32_t flags, uint32_t wait_ms,
-                    size_t arena_floats, size_t gather_floats, TpGroup** out) {
+
+int tp_group_create(const void* id, uint32_t rank, uint32_t world, uint32_t flags, uint32_t wait_ms, uint32_t rows,
+                    uint32_t n, uint32_t nl, TpGroup** out) {
   const NcclApi& a = nccl();
   if (!a.h) { set_error(a.why); return SM_ERR_UNSUPPORTED; }
-  if (!id || world < 2 || world > TP_MAX || rank >= world) { set_error("tensor-parallel group: bad rank/size/id"); return SM_ERR_ARG; }
+  if (!id || world < 2 || world > TP_MAX || rank >= world || !rows || !n || !nl) {
+    set_error("tensor-parallel group: bad rank/size/id");
+    return SM_ERR_ARG;
+  }
   auto* g = new TpGroup();
   g->rank = rank;
   g->world = world;
   g->flags = flags;
+  g->rows = rows;
+  g->n = n;
+  g->nl = nl;
   g->wait_ns = (uint64_t)(wait_ms ? wait_ms : 10000u) * 1000000ull;
   const auto deadline = Clock::now() + std::chrono::milliseconds(wait_ms ? wait_ms : 10000u) * 6;
   int rc = SM_OK;
@@ -228,19 +240,19 @@ int tp_group_create(const void* id, uint32_t rank, uint32_t world, uint32_t flag
     return fail(SM_ERR_PEER);
   }
   if ((rc = nccl_settle(g, r, deadline, "communicator set-up"))) return fail(rc);
-  // 2. arena: flags | epochs | send parity 0 | send parity 1 | gather | NCCL receive buffers
+  // 2. arena (zeroed: every epoch 0, no packet carries an exchange's epoch)
   const bool use_nccl = flags & SM_TP_NCCL;
+  const size_t rn = (size_t)rows * n, rl = (size_t)rows * nl;
   size_t off = 0;
-  g->off_flag = off; off += up256(TP_BLOCKS * TP_MAX * 4);
-  g->off_epoch = off; off += up256(TP_BLOCKS * 4);
-  g->send_floats = arena_floats;
-  g->gather_floats = gather_floats;
-  g->off_send[0] = off; off += up256(arena_floats * 4);
-  g->off_send[1] = off; off += up256(arena_floats * 4);
-  g->off_gather = off; off += up256(gather_floats * 4);
+  g->off_ep_ar = off; off += up256(TP_BLOCKS * 4);
+  g->off_ep_g = off; off += up256(TP_BLOCKS * 4);
+  g->off_ar = off; off += up256(2 * world * rn * 8);
+  g->off_g = off; off += up256(world * rl * 8);
   if (use_nccl) {
-    g->off_recv = off; off += up256(arena_floats * 4);
-    g->off_grecv = off; off += up256(gather_floats * 4 * world);
+    g->off_send = off; off += up256(rn * 4);
+    g->off_recv = off; off += up256(rn * 4);
+    g->off_gsend = off; off += up256(rl * 4);
+    g->off_grecv = off; off += up256(world * rl * 4);
   }
   if (cudaMalloc(&g->arena, off) != cudaSuccess) {
     cudaGetLastError();
@@ -290,16 +302,17 @@ int tp_group_create(const void* id, uint32_t rank, uint32_t world, uint32_t flag
     g->peer[k] = (uint8_t*)p;
     g->opened[k] = true;
   }
-  // 4. warm the collectives up outside any graph capture, and make sure every
-  //    rank has mapped its peers before any exchange signals into them.
+  // 4. warm the collectives up outside any graph capture; this also makes
+  //    every rank map its peers before any of them pushes.
   {
-    float* b = reinterpret_cast<float*>(g->arena + g->off_send[0]);
+    float* b = reinterpret_cast<float*>(g->arena + (use_nccl ? g->off_send : g->off_ar));
     r = a.all_reduce(b, b, 64, ncclFloat, ncclSum, g->comm, st);
     if ((rc = nccl_settle(g, r, deadline, "warm-up all-reduce")) || (rc = stream_settle(g, st, deadline, "warm-up all-reduce")))
       return fail(rc);
     if (use_nccl) {
-      float* gb = reinterpret_cast<float*>(g->arena + g->off_grecv);
-      r = a.all_gather(reinterpret_cast<float*>(g->arena + g->off_gather), gb, 64, ncclFloat, g->comm, st);
+      r = a.all_gather(reinterpret_cast<float*>(g->arena + g->off_gsend),
+                       reinterpret_cast<float*>(g->arena + g->off_grecv), std::min<size_t>(rl, 64), ncclFloat, g->comm,
+                       st);
       if ((rc = nccl_settle(g, r, deadline, "warm-up all-gather")) || (rc = stream_settle(g, st, deadline, "warm-up all-gather")))
         return fail(rc);
     }
@@ -314,58 +327,88 @@ int tp_group_create(const void* id, uint32_t rank, uint32_t world, uint32_t flag
   return SM_OK;
 }
 
-float* tp_send_buffer(TpGroup* g, uint32_t parity) { return reinterpret_cast<float*>(g->arena + g->off_send[parity & 1]); }
-float* tp_gather_buffer(TpGroup* g) { return reinterpret_cast<float*>(g->arena + g->off_gather); }
 bool tp_uses_nccl(const TpGroup* g) { return g->flags & SM_TP_NCCL; }
 
-static TpPeers peers_of(TpGroup* g, bool sync) {
-  TpPeers p{};
-  for (uint32_t k = 0; k < g->world; k++) p.flag[k] = reinterpret_cast<uint32_t*>(g->peer[k] + g->off_flag);
-  p.epoch = reinterpret_cast<uint32_t*>(g->arena + g->off_epoch);
-  p.err = nullptr;
-  p.wait_ns = g->wait_ns;
-  p.rank = g->rank;
-  p.world = g->world;
-  p.sync = sync ? 1u : 0u;
-  return p;
+namespace {
+TpRecv recv_base(TpGroup* g, uint32_t* err) {
+  TpRecv r{};
+  r.err = err;
+  r.wait_ns = g->wait_ns;
+  r.world = g->world;
+  return r;
 }
 
-cudaError_t tp_allreduce_prepare(TpGroup* g, uint32_t parity, size_t count, cudaStream_t st, TpCall* call) {
-  *call = TpCall{};
+cudaError_t nccl_issue(TpGroup* g, ncclResult_t r) {
+  if (r == ncclInProgress &&
+      nccl_settle(g, r, Clock::now() + std::chrono::nanoseconds(g->wait_ns), "collective") != SM_OK)
+    return cudaErrorLaunchFailure;
+  return (r == ncclSuccess || r == ncclInProgress) ? cudaSuccess : cudaErrorLaunchFailure;
+}
+}  // namespace
+
+TpExchange tp_allreduce(TpGroup* g, uint32_t* err) {
+  TpExchange x{};
+  x.recv = recv_base(g, err);
+  x.recv.ld = g->n;
+  x.recv.per = (g->n + TP_BLOCKS - 1) / TP_BLOCKS;
   if (tp_uses_nccl(g)) {
-    float* recv = reinterpret_cast<float*>(g->arena + g->off_recv);
-    ncclResult_t r = nccl().all_reduce(tp_send_buffer(g, parity), recv, count, ncclFloat, ncclSum, g->comm, st);
-    if (r == ncclInProgress && nccl_settle(g, r, Clock::now() + std::chrono::nanoseconds(g->wait_ns), "all-reduce"))
-      return cudaErrorLaunchFailure;
-    if (r != ncclSuccess && r != ncclInProgress) return cudaErrorLaunchFailure;
-    call->peers = peers_of(g, false);
-    call->src[0] = recv;
-    call->nsrc = 1;
-    return cudaSuccess;
+    x.send = reinterpret_cast<float*>(g->arena + g->off_send);
+    x.recv.plain = reinterpret_cast<const float*>(g->arena + g->off_recv);
+    return x;
   }
-  call->peers = peers_of(g, true);
-  for (uint32_t k = 0; k < g->world; k++) call->src[k] = reinterpret_cast<const float*>(g->peer[k] + g->off_send[parity & 1]);
-  call->nsrc = g->world;
-  return cudaSuccess;
+  const uint64_t rn = (uint64_t)g->rows * g->n;
+  for (uint32_t k = 0; k < g->world; k++) x.push.dst[k] = reinterpret_cast<uint64_t*>(g->peer[k] + g->off_ar);
+  x.push.parity_stride = g->world * rn;
+  x.push.src_stride = rn;
+  x.push.epoch = reinterpret_cast<const uint32_t*>(g->arena + g->off_ep_ar);
+  x.push.world = g->world;
+  x.push.rank = g->rank;
+  x.push.ld = g->n;
+  x.push.per = x.recv.per;
+  x.push.base = 0;
+  x.recv.pk = reinterpret_cast<const uint64_t*>(g->arena + g->off_ar);
+  x.recv.parity_stride = x.push.parity_stride;
+  x.recv.src_stride = rn;
+  x.recv.epoch = reinterpret_cast<uint32_t*>(g->arena + g->off_ep_ar);
+  return x;
 }
 
-cudaError_t tp_gather_prepare(TpGroup* g, size_t count_per_rank, cudaStream_t st, TpCall* call) {
-  *call = TpCall{};
+TpExchange tp_gather(TpGroup* g, uint32_t rows, uint64_t vocab0, uint32_t* err) {
+  TpExchange x{};
+  x.recv = recv_base(g, err);
+  x.recv.ld = g->nl;
+  const uint64_t total = (uint64_t)g->nl * g->world;
+  x.recv.per = (uint32_t)((total + TP_BLOCKS - 1) / TP_BLOCKS);
   if (tp_uses_nccl(g)) {
-    float* recv = reinterpret_cast<float*>(g->arena + g->off_grecv);
-    ncclResult_t r = nccl().all_gather(tp_gather_buffer(g), recv, count_per_rank, ncclFloat, g->comm, st);
-    if (r == ncclInProgress && nccl_settle(g, r, Clock::now() + std::chrono::nanoseconds(g->wait_ns), "all-gather"))
-      return cudaErrorLaunchFailure;
-    if (r != ncclSuccess && r != ncclInProgress) return cudaErrorLaunchFailure;
-    call->peers = peers_of(g, false);
-    for (uint32_t k = 0; k < g->world; k++) call->src[k] = recv + k * count_per_rank;
-    call->nsrc = g->world;
-    return cudaSuccess;
+    x.send = reinterpret_cast<float*>(g->arena + g->off_gsend);
+    x.recv.plain = reinterpret_cast<const float*>(g->arena + g->off_grecv);
+    x.recv.src_stride = (uint64_t)rows * g->nl;  // all-gather output: [rank][rows][nl]
+    return x;
   }
-  call->peers = peers_of(g, true);
-  for (uint32_t k = 0; k < g->world; k++) call->src[k] = reinterpret_cast<const float*>(g->peer[k] + g->off_gather);
-  call->nsrc = g->world;
-  return cudaSuccess;
+  const uint64_t rl = (uint64_t)g->rows * g->nl;
+  for (uint32_t k = 0; k < g->world; k++) x.push.dst[k] = reinterpret_cast<uint64_t*>(g->peer[k] + g->off_g);
+  x.push.parity_stride = 0;
+  x.push.src_stride = rl;
+  x.push.epoch = reinterpret_cast<const uint32_t*>(g->arena + g->off_ep_g);
+  x.push.world = g->world;
+  x.push.rank = g->rank;
+  x.push.ld = g->nl;
+  x.push.per = x.recv.per;
+  x.push.base = (uint32_t)vocab0;
+  x.recv.pk = reinterpret_cast<const uint64_t*>(g->arena + g->off_g);
+  x.recv.src_stride = rl;
+  x.recv.epoch = reinterpret_cast<uint32_t*>(g->arena + g->off_ep_g);
+  return x;
+}
+
+cudaError_t tp_allreduce_issue(TpGroup* g, uint32_t rows, cudaStream_t st) {
+  return nccl_issue(g, nccl().all_reduce(g->arena + g->off_send, g->arena + g->off_recv, (size_t)rows * g->n, ncclFloat,
+                                         ncclSum, g->comm, st));
+}
+
+cudaError_t tp_gather_issue(TpGroup* g, uint32_t rows, cudaStream_t st) {
+  return nccl_issue(g, nccl().all_gather(g->arena + g->off_gsend, g->arena + g->off_grecv, (size_t)rows * g->nl,
+                                         ncclFloat, g->comm, st));
 }
 
 }  // namespace sm
