@@ -11,24 +11,29 @@ namespace sm {
 //
 // Q4_K / Q6_K are stored in tiles of 16 rows (the last tile zero-padded): a
 // tile holds its 256-weight blocks in order, and block b of a tile is one
-// contiguous unit of all 16 rows. Inside a unit the bytes sit where lane
-// (g, t) = (lane >> 2, lane & 3) of a warp wants them when it owns rows g and
-// g + 8 of the tile as the A operand of mma.m16n8k16: every 16-byte load of
-// the warp reads 512 contiguous bytes.
+// contiguous unit of all 16 rows (one bulk copy into shared memory). Inside a
+// unit the quants are regrouped so that lane (g, t) = (lane >> 2, lane & 3)
+// of a warp that owns rows g and g + 8 finds the A operands of
+// mma.m16n8k32 (u8) for its rows in a few 16-byte loads: every 32-bit word
+// holds four consecutive weights of one sub-block (Q4_K: their nibbles;
+// Q6_K: low nibbles and the 2-bit high parts split over words), and the
+// 16-byte chunks are rotated per row so that the lanes' loads hit distinct
+// shared-memory banks.
 //   Q4_K unit, 2304 B:
 //     [16 rows x 16 B header: d, dmin, 12 scale bytes]
-//     [qs: 4 loads x 32 lanes x 16 B]  load L, lane (g, t): row g + 8*(L >> 1),
-//       bytes 32j + 8t .. 32j + 8t + 7 of qs for j = 2*(L & 1) and j + 1.
+//     [16 rows x 128 B of qs]: word (j, c, p) = qs bytes 32j + 8c + 4p .. + 3
+//       (j, c = 0..3, p = 0..1) at q4t_word_off(rr, j, c, p).
 //     (Byte q of qs holds weight 64j + (q & 31) in its low nibble and weight
 //     64j + 32 + (q & 31) in its high nibble, j = q >> 5: dequant.rs:98-124.)
 //   Q6_K unit, 3360 B:
-//     [16 rows x 16 int8 scales][16 rows x fp16 d][q: 6 loads x 32 lanes x 16 B]
-//     Lane (g, t) owns, per row, weight 16s + 4t + k of every 16-weight
-//     sub-block s (k = 0..3) as the 6-bit value v = q + 32, in 12 words:
-//     loads 0-1 (row g; 3-4 for row g + 8) = ql words i = 0..7, byte k of
-//     word i = low 4 bits of v(s = i, k) | low 4 bits of v(s = i + 8, k) << 4;
-//     load 2 (5) = qh words m = 0..3, holding the top 2 bits of the values of
-//     ql words 2m and 2m + 1 at bit (q6t_field(k, nib) + 8 * (i & 1)) & 31.
+//     [16 rows x 16 int8 scales][16 rows x fp16 d][16 rows x 192 B]
+//     Weight 8c + 4p + b (b = 0..3) of sub-block s = 4G + sigma (16 weights
+//     per sub-block, G = 0..3, c, p = 0..1) as the 6-bit value v = q + 32
+//     (dequant.rs:178-206) is byte b of three words (G, c, p) of its row:
+//       W0: low nibble of v(sigma = 0) | low nibble of v(sigma = 2) << 4
+//       W1: low nibble of v(sigma = 1) | low nibble of v(sigma = 3) << 4
+//       H:  high 2 bits of v(1) | v(3) << 2 | v(0) << 4 | v(2) << 6
+//     at q6t_word_off(rr, array 0/1/2, G, c, p).
 //   Q8_0: body = 32 B of qs per block, aux = fp16 d per block (row-major).
 //   Q5_0: body = 16 B of qs per block, aux = 8 B per block (qh u32 | d fp16 | 0).
 // ---------------------------------------------------------------------------
@@ -40,23 +45,34 @@ namespace sm {
 constexpr uint32_t Q4T_UNIT = 2304, Q6T_UNIT = 3360, Q6T_QOFF = 288;
 SM_HD bool tiled_type(uint32_t t) { return t == 12 || t == 14; }
 SM_HD uint32_t tile_unit_bytes(uint32_t t) { return t == 12 ? Q4T_UNIT : Q6T_UNIT; }
-// Byte offset, inside a Q4_K unit, of qs byte q (0..127) of tile row rr (0..15).
+// Q4_K: byte offset in a unit of qs word (j, c, p) of tile row rr: row rr's
+// 128 bytes are 8 chunks of 16 B, logical chunk 4p + j stored at position
+// (4p + j) ^ (rr & 7), word c of the chunk.
+SM_HD uint32_t q4t_word_off(uint32_t rr, uint32_t j, uint32_t c, uint32_t p) {
+  return 256u + 128u * rr + 16u * ((4u * p + j) ^ (rr & 7u)) + 4u * c;
+}
+// Q4_K: byte offset of qs byte q (0..127) of tile row rr.
 SM_HD uint32_t q4t_qs_off(uint32_t rr, uint32_t q) {
-  const uint32_t j = q >> 5, t = (q >> 3) & 3u, e = q & 7u;
-  const uint32_t L = 2u * (rr >> 3) + (j >> 1), lane = 4u * (rr & 7u) + t;
-  return 256u + 512u * L + 16u * lane + 8u * (j & 1u) + e;
+  const uint32_t w = q & 31u;
+  return q4t_word_off(rr, q >> 5, w >> 3, (w >> 2) & 1u) + (w & 3u);
 }
-// Byte offsets, inside a Q6_K unit, of ql word i (0..7) and qh word m (0..3)
-// of lane t for tile row rr.
-SM_HD uint32_t q6t_w_off(uint32_t rr, uint32_t t, uint32_t i) {
-  return Q6T_QOFF + 512u * (3u * (rr >> 3) + (i >> 2)) + 16u * (4u * (rr & 7u) + t) + 4u * (i & 3u);
+// Q6_K: byte offset in a unit of word (G, c) of array a (0: W0, 1: W1, 2: H)
+// for parity p of tile row rr. A row's 192 bytes are 12 chunks of 16 B,
+// logical chunk 6p + 2a + (G >> 1) (words 2(G & 1) + c of it), stored at
+// position (logical + 3 * ((rr & 7) >> 1)) mod 12.
+SM_HD uint32_t q6t_word_off(uint32_t rr, uint32_t a, uint32_t G, uint32_t c, uint32_t p) {
+  const uint32_t chunk = (6u * p + 2u * a + (G >> 1) + 3u * ((rr & 7u) >> 1)) % 12u;
+  return Q6T_QOFF + 192u * rr + 16u * chunk + 4u * (2u * (G & 1u) + c);
 }
-SM_HD uint32_t q6t_h_off(uint32_t rr, uint32_t t, uint32_t m) {
-  return Q6T_QOFF + 512u * (3u * (rr >> 3) + 2u) + 16u * (4u * (rr & 7u) + t) + 4u * m;
+// Q6_K: the 6-bit value v = q + 32 of weight l (0..255) of tile row rr.
+SM_HD uint32_t q6t_value(const uint8_t* unit, uint32_t rr, uint32_t l) {
+  const uint32_t s = l >> 4, w = l & 15u, G = s >> 2, sg = s & 3u, c = w >> 3, p = (w >> 2) & 1u, b = w & 3u;
+  const uint32_t wv = unit[q6t_word_off(rr, sg & 1u, G, c, p) + b];
+  const uint32_t h = unit[q6t_word_off(rr, 2, G, c, p) + b];
+  const uint32_t lo = (sg >> 1) ? (wv >> 4) : (wv & 15u);
+  const uint32_t hs = sg == 0 ? 4u : sg == 1 ? 0u : sg == 2 ? 6u : 2u;
+  return lo | (((h >> hs) & 3u) << 4);
 }
-// Bit position of the top 2 bits of byte k, nibble nib of an even ql word in
-// its qh word (odd words: the same positions in the qh word rotated right by 8).
-SM_HD uint32_t q6t_field(uint32_t k, uint32_t nib) { return (nib ? 8u : 4u) + 2u * (k & 1u) + 16u * (k >> 1); }
 
 struct DWDesc {
   const uint8_t* body;

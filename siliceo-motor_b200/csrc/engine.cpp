@@ -106,17 +106,12 @@ int upload_weight(uint32_t type, const uint8_t* src, uint64_t n_out, uint64_t n_
               const uint32_t hi = (blk[128 + 32 * n + ll] >> (2 * k)) & 3;
               v6[l] = (uint8_t)(lo | (hi << 4));
             }
-            uint32_t W[4][8] = {}, Hq[4][4] = {};
-            for (uint32_t sb = 0; sb < 16; sb++)
-              for (uint32_t t = 0; t < 4; t++)
-                for (uint32_t k = 0; k < 4; k++) {
-                  const uint32_t v = v6[16 * sb + 4 * t + k], i = sb & 7, nib = sb >> 3;
-                  W[t][i] |= (v & 0x0F) << (8 * k + 4 * nib);
-                  Hq[t][i >> 1] |= (v >> 4) << ((q6t_field(k, nib) + 8 * (i & 1)) & 31);
-                }
-            for (uint32_t t = 0; t < 4; t++) {
-              for (uint32_t i = 0; i < 8; i++) std::memcpy(u + q6t_w_off(rr, t, i), &W[t][i], 4);
-              for (uint32_t m = 0; m < 4; m++) std::memcpy(u + q6t_h_off(rr, t, m), &Hq[t][m], 4);
+            for (uint32_t l = 0; l < 256; l++) {  // into the words of device.cuh (the unit starts zeroed)
+              const uint32_t sb = l >> 4, w = l & 15, G = sb >> 2, sg = sb & 3, c = w >> 3, pp = (w >> 2) & 1,
+                             bb = w & 3, v = v6[l];
+              u[q6t_word_off(rr, sg & 1, G, c, pp) + bb] |= (uint8_t)((v & 15) << (4 * (sg >> 1)));
+              const uint32_t hs = sg == 0 ? 4 : sg == 1 ? 0 : sg == 2 ? 6 : 2;
+              u[q6t_word_off(rr, 2, G, c, pp) + bb] |= (uint8_t)((v >> 4) << hs);
             }
             std::memcpy(u + 16 * rr, blk + 192, 16);
             std::memcpy(u + 256 + 2 * rr, blk + 208, 2);

@@ -51,15 +51,11 @@ __device__ float dequant_elem(const DWDesc& w, uint32_t o, uint32_t e) {
       return __fsub_rn(__fmul_rn(d1, (float)q), m1);
     }
     case 14: {  // Q6_K, dequant.rs:178-206
-      const uint32_t blk = e >> 8, l = e & 255, rr = o & 15, sb = l >> 4, t = (l >> 2) & 3, k = l & 3;
-      const uint32_t i = sb & 7, nib = sb >> 3;
+      const uint32_t blk = e >> 8, l = e & 255, rr = o & 15, sb = l >> 4;
       const uint8_t* u = w.body + (size_t)(o >> 4) * w.body_stride + (size_t)blk * Q6T_UNIT;
       float d = fp16_ref(rd16(u + 256 + 2 * rr));
       if (!isfinite(d)) return 0.0f;
-      const uint32_t lo = (u[q6t_w_off(rr, t, i) + k] >> (4 * nib)) & 0x0F;
-      const uint32_t hw = *reinterpret_cast<const uint32_t*>(u + q6t_h_off(rr, t, i >> 1));
-      const uint32_t hi = (hw >> ((q6t_field(k, nib) + 8 * (i & 1)) & 31)) & 3;
-      int32_t q = (int32_t)(lo | (hi << 4)) - 32;
+      int32_t q = (int32_t)q6t_value(u, rr, l) - 32;
       float sc = (float)(int8_t)u[16 * rr + sb];
       return __fmul_rn(__fmul_rn(d, sc), (float)q);
     }
@@ -101,118 +97,6 @@ __global__ void embed_kernel(DWDesc w, const uint32_t* tokens, float* x, uint32_
 // -------------------------------------------------------------- GEMV ----
 // Each unit function adds, for R rows and up to BT columns, one lane's share
 // of a row: acc[r][b] += sum over the unit's weights of W*x.
-
-// Q4_K / Q6_K unit = lane t's 64 weights of one block of a row in the tile
-// layout (device.cuh); tp[r] is the row's tile, rrs[r] its row in the tile.
-// Q4_K: 8 weights of each of the 8 sub-blocks (offsets 8t .. 8t + 7).
-template <int R, int BT>
-__device__ __forceinline__ void unit_q4k(const uint8_t* const* tp, const uint32_t* rrs, int u, const float* x,
-                                         uint32_t ldx, int ncols, float (&acc)[R][BT]) {
-  const int blk = u >> 2, t = u & 3;
-  uint4 hd[R], qa[R], qb[R];
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    const uint8_t* ub = tp[r] + (size_t)blk * Q4T_UNIT;
-    const uint32_t rr = rrs[r], q0 = 256u + 1024u * (rr >> 3) + 16u * (4u * (rr & 7u) + (uint32_t)t);
-    hd[r] = ldg_u4(ub + 16 * rr);
-    qa[r] = ld_stream(ub + q0);
-    qb[r] = ld_stream(ub + q0 + 512);
-  }
-  float ds[R][8], dm[R][8];
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    const float d = fp16_ref(hd[r].x & 0xFFFFu), dmin = fp16_ref(hd[r].x >> 16);
-#pragma unroll
-    for (int sb = 0; sb < 8; sb++) {  // get_scale_min_k4, dequant.rs:41-49
-      uint32_t sc, m;
-      if (sb < 4) {
-        sc = (hd[r].y >> (8 * sb)) & 63u;
-        m = (hd[r].z >> (8 * sb)) & 63u;
-      } else {
-        const int s0 = 8 * (sb - 4);
-        sc = ((hd[r].w >> s0) & 0xFu) | (((hd[r].y >> (s0 + 6)) & 3u) << 4);
-        m = ((hd[r].w >> (s0 + 4)) & 0xFu) | (((hd[r].z >> (s0 + 6)) & 3u) << 4);
-      }
-      ds[r][sb] = d * (float)sc;
-      dm[r][sb] = dmin * (float)m;
-    }
-  }
-#pragma unroll
-  for (int b = 0; b < BT; b++) {
-    if (b >= ncols) break;
-    const float* xb = x + (size_t)b * ldx + blk * 256 + 8 * t;
-#pragma unroll
-    for (int sb = 0; sb < 8; sb++) {
-      const float4 x0 = ldg4(xb + 32 * sb), x1 = ldg4(xb + 32 * sb + 4);
-      const float xs = sum4(x0) + sum4(x1);
-      const int j = sb >> 1, nib = sb & 1;
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        const uint4 q = j < 2 ? qa[r] : qb[r];
-        const uint32_t wa = (j & 1) ? q.z : q.x, wb = (j & 1) ? q.w : q.y;
-        const uint32_t la = (wa >> (4 * nib)) & 0x0F0F0F0Fu, lb = (wb >> (4 * nib)) & 0x0F0F0F0Fu;
-        float s0 = byte_f<0>(la, 8388608.f) * x0.x;
-        float s1 = byte_f<1>(la, 8388608.f) * x0.y;
-        s0 = fmaf(byte_f<2>(la, 8388608.f), x0.z, s0);
-        s1 = fmaf(byte_f<3>(la, 8388608.f), x0.w, s1);
-        s0 = fmaf(byte_f<0>(lb, 8388608.f), x1.x, s0);
-        s1 = fmaf(byte_f<1>(lb, 8388608.f), x1.y, s1);
-        s0 = fmaf(byte_f<2>(lb, 8388608.f), x1.z, s0);
-        s1 = fmaf(byte_f<3>(lb, 8388608.f), x1.w, s1);
-        acc[r][b] += ds[r][sb] * (s0 + s1) - dm[r][sb] * xs;
-      }
-    }
-  }
-}
-
-// Q6_K: 4 weights of each of the 16 sub-blocks (offsets 4t .. 4t + 3).
-template <int R, int BT>
-__device__ __forceinline__ void unit_q6k(const uint8_t* const* tp, const uint32_t* rrs, int u, const float* x,
-                                         uint32_t ldx, int ncols, float (&acc)[R][BT]) {
-  const int blk = u >> 2, t = u & 3;
-  uint4 w0[R], w1[R], hh[R];
-  float ds[R][16];
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    const uint8_t* ub = tp[r] + (size_t)blk * Q6T_UNIT;
-    const uint32_t rr = rrs[r], q0 = q6t_w_off(rr, (uint32_t)t, 0);
-    w0[r] = ld_stream(ub + q0);
-    w1[r] = ld_stream(ub + q0 + 512);
-    hh[r] = ld_stream(ub + q0 + 1024);
-    const uint4 sc = ldg_u4(ub + 16 * rr);
-    float d = fp16_ref(__ldg(reinterpret_cast<const unsigned short*>(ub + 256 + 2 * rr)));
-    if (!isfinite(d)) d = 0.f;  // the reference skips such a block (kernels/src/lib.rs:845)
-    const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-    for (int sb = 0; sb < 16; sb++) ds[r][sb] = d * (float)(int8_t)((scw[sb >> 2] >> (8 * (sb & 3))) & 0xFFu);
-  }
-#pragma unroll
-  for (int b = 0; b < BT; b++) {
-    if (b >= ncols) break;
-    const float* xb = x + (size_t)b * ldx + blk * 256 + 4 * t;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const float4 xa = ldg4(xb + 16 * i), xc = ldg4(xb + 16 * (i + 8));
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        const uint32_t wv = (i < 4 ? (&w0[r].x)[i] : (&w1[r].x)[i - 4]);
-        const uint32_t hw = (&hh[r].x)[i >> 1];
-        const uint32_t hq = (i & 1) ? __funnelshift_r(hw, hw, 8) : hw;
-        const uint32_t va = (wv & 0x0F0F0F0Fu) | (hq & 0x00300030u) | ((hq << 6) & 0x30003000u);
-        const uint32_t vb = ((wv >> 4) & 0x0F0F0F0Fu) | ((hq >> 4) & 0x00300030u) | ((hq << 2) & 0x30003000u);
-        float sa = byte_f<0>(va, 8388640.f) * xa.x;
-        sa = fmaf(byte_f<1>(va, 8388640.f), xa.y, sa);
-        sa = fmaf(byte_f<2>(va, 8388640.f), xa.z, sa);
-        sa = fmaf(byte_f<3>(va, 8388640.f), xa.w, sa);
-        float sb2 = byte_f<0>(vb, 8388640.f) * xc.x;
-        sb2 = fmaf(byte_f<1>(vb, 8388640.f), xc.y, sb2);
-        sb2 = fmaf(byte_f<2>(vb, 8388640.f), xc.z, sb2);
-        sb2 = fmaf(byte_f<3>(vb, 8388640.f), xc.w, sb2);
-        acc[r][b] += ds[r][i] * sa + ds[r][i + 8] * sb2;
-      }
-    }
-  }
-}
 
 // Q8_0 unit = 16 int8 weights (half a block) + d.
 template <int R, int BT>
@@ -313,13 +197,10 @@ __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uin
   const int lane = threadIdx.x & 31;
   const uint8_t* rowp[R];
   const uint8_t* auxp[R];
-  uint32_t rrs[R];
-  const bool tiled = tiled_type(QT ? (uint32_t)QT : w.type);
 #pragma unroll
   for (int r = 0; r < R; r++) {
     const uint32_t o = min((uint32_t)(row0 + r), w.n_out - 1);
-    rowp[r] = tiled ? w.body + (size_t)(o >> 4) * w.body_stride : w.body + (size_t)o * w.body_stride;
-    rrs[r] = o & 15u;
+    rowp[r] = w.body + (size_t)o * w.body_stride;
     auxp[r] = w.aux + (size_t)o * w.aux_stride;
   }
 #pragma unroll
@@ -328,13 +209,7 @@ __device__ __forceinline__ void gemv_rows(const GemvSeg& sg, const float* x, uin
     for (int b = 0; b < BT; b++) acc[r][b] = 0.f;
   const float* xc = x + (size_t)col0 * ldx;
   const uint32_t qt = QT ? (uint32_t)QT : w.type;
-  if (qt == 12) {
-    const int nu = (int)(w.n_in >> 8) * 4;
-    for (int u = lane; u < nu; u += 32) unit_q4k<R, BT>(rowp, rrs, u, xc, ldx, ncols, acc);
-  } else if (qt == 14) {
-    const int nu = (int)(w.n_in >> 8) * 4;
-    for (int u = lane; u < nu; u += 32) unit_q6k<R, BT>(rowp, rrs, u, xc, ldx, ncols, acc);
-  } else if (qt == 8) {
+  if (qt == 8) {
     const int nu = (int)(w.n_in >> 5) * 2;
     for (int u = lane; u < nu; u += 32) unit_q80<R, BT>(rowp, auxp, u, xc, ldx, ncols, acc);
   } else {
@@ -398,8 +273,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(const __grid_cons
   float acc[R][BT];
   if (row0 < (int)sg.w.n_out) {
     switch (sg.w.type) {
-      case 12: gemv_rows<12, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
-      case 14: gemv_rows<14, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
       case 8: gemv_rows<8, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
       default: gemv_rows<6, R, BT>(sg, a.x, a.ldx, row0, col0, ncols, acc); break;
     }
@@ -460,45 +333,15 @@ uint32_t gemv_plan(GemvArgs& a) {
   return c;
 }
 
-bool gemv_tc_ok(const GemvArgs& a);
 cudaError_t launch_gemv_tc(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
-bool gemv_tcb_ok(const GemvArgs& a);
 cudaError_t launch_gemv_tcb(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
 
-// Segments of one launch regrouped by weight type (the batched tensor-core
-// kernel takes one type per launch); false if any segment is not tiled.
-static bool split_by_type(const GemvArgs& a, GemvArgs* out, uint32_t* n) {
-  *n = 0;
-  for (uint32_t i = 0; i < a.nseg; i++) {
-    if (!tiled_type(a.seg[i].w.type)) return false;
-    uint32_t k = 0;
-    while (k < *n && out[k].seg[0].w.type != a.seg[i].w.type) k++;
-    if (k == *n) {
-      out[k] = a;
-      out[k].nseg = 0;
-      (*n)++;
-    }
-    out[k].seg[out[k].nseg++] = a.seg[i];
-  }
-  return true;
-}
-
-cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
-  if (gemv_tc_ok(a)) {
-    const cudaError_t e = launch_gemv_tc(a, st, n_parts);
-    if (e != cudaErrorNotSupported) return e;
-  }
-  GemvArgs parts[3];
-  uint32_t np = 0;
-  if (a.batch >= 2 && split_by_type(a, parts, &np) && (np == 1 || !n_parts)) {
-    bool ok = true;
-    for (uint32_t i = 0; i < np && ok; i++) ok = gemv_tcb_ok(parts[i]);
-    if (ok) {
-      cudaError_t e = cudaSuccess;
-      for (uint32_t i = 0; i < np && e == cudaSuccess; i++) e = launch_gemv_tcb(parts[i], st, n_parts);
-      if (e != cudaErrorNotSupported) return e;
-    }
-  }
+// Q4_K / Q6_K segments run on the tensor-core kernels (batch 1: gemv_tc.cu,
+// mixed types in one launch; batches: gemv_tcb.cu, one launch per type), the
+// Q5_0 / Q8_0 fallback types on gemv_kernel; a launch whose segments mix the
+// two families is split. n_parts (EPI_RESID) needs a single-segment launch.
+static cudaError_t launch_generic(const GemvArgs& a0, cudaStream_t st, uint32_t* n_parts) {
+  GemvArgs a = a0;
   const uint32_t ny = gemv_plan(a);
   if (n_parts) *n_parts = ny;
   const dim3 blk(GEMV_WARPS * 32);
@@ -506,6 +349,33 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   else if (a.batch <= 4) gemv_kernel<2, 4><<<dim3(1, ny), blk, 0, st>>>(a);
   else gemv_kernel<2, 8><<<dim3((a.batch + 7) / 8, ny), blk, 0, st>>>(a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
+  // segments by family: tiled types grouped per type (QT_Q4K, QT_Q6K), the rest together
+  GemvArgs q4 = a, q6 = a, other = a;
+  q4.nseg = q6.nseg = other.nseg = 0;
+  for (uint32_t i = 0; i < a.nseg; i++) {
+    GemvArgs& d = a.seg[i].w.type == 12 ? q4 : a.seg[i].w.type == 14 ? q6 : other;
+    d.seg[d.nseg++] = a.seg[i];
+  }
+  const uint32_t launches = (q4.nseg > 0) + (q6.nseg > 0) + (other.nseg > 0);
+  if (n_parts && (launches != 1 || a.nseg != 1)) return cudaErrorInvalidValue;
+  cudaError_t e = cudaSuccess;
+  if (a.batch == 1 && q4.nseg && q6.nseg) {  // one batch-1 launch for both tiled types
+    GemvArgs t = a;
+    t.nseg = 0;
+    for (uint32_t i = 0; i < a.nseg; i++)
+      if (tiled_type(a.seg[i].w.type)) t.seg[t.nseg++] = a.seg[i];
+    e = launch_gemv_tc(t, st, n_parts);
+  } else {
+    for (GemvArgs* g : {&q4, &q6}) {
+      if (!g->nseg || e != cudaSuccess) continue;
+      e = g->batch == 1 ? launch_gemv_tc(*g, st, n_parts) : launch_gemv_tcb(*g, st, n_parts);
+    }
+  }
+  if (e == cudaSuccess && other.nseg) e = launch_generic(other, st, n_parts);
+  return e;
 }
 
 cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st) {

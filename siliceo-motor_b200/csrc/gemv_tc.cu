@@ -1,31 +1,30 @@
-// Batch-1 GEMV of Q4_K / Q6_K weights on the tensor cores.
+// Batch-1 GEMV of Q4_K / Q6_K weights on the tensor cores (int8 MMA).
 //
 // A decode step is one matrix-vector product per weight, so the work is bound
 // by HBM bandwidth only if turning a 4/6-bit weight into something that can be
-// multiplied costs almost nothing. On the CUDA cores it does not (the f16->f32
-// conversions run on the quarter-rate XU pipe), so here the weights go
-// straight into mma.sync.m16n8k16 (f16 x f16 -> f32) as the A operand:
-//   * a quantized value q (0..15, or the 6-bit q + 32 of Q6_K) goes into the
-//     mantissa of an f16 with a zero exponent field: a subnormal q * 2^-24
-//     (or 16q * 2^-24 for a high nibble), exact, made with one AND (Q4_K) or
-//     two LOP3s (Q6_K) per two weights; the power of two and Q6_K's -32
-//     (as -32 * sum(x) over the sub-block) are applied with the scales;
-//   * x is split into hi + lo f16 halves after scaling each 256-wide block by
-//     a power of two (hi = x rounded to 11 bits, lo = the exact remainder), so
-//     the products carry ~22 bits of x, as much as the f32 reference keeps
-//     within rounding of its own sum;
-//   * the 8 columns of the MMA are (sub-block mod 4, hi/lo): each k16 chunk of
-//     weights belongs to one sub-block and meets x only in that sub-block's
-//     two columns, so the accumulators hold one dot product per (row,
-//     sub-block) and the GGUF scales are applied once per block:
-//       Q4_K: y += d*sc_s*sum_s(q*x) - dmin*m_s*sum_s(x)   (dequant.rs:98-124)
-//       Q6_K: y += d*sc_s*sum_s((q-32)*x)                  (dequant.rs:178-206)
+// multiplied costs almost nothing. Here the weights go into
+// mma.sync.m16n8k32 (u8 x s8 -> s32) as the A operand with one AND per four
+// weights (Q4_K: a low nibble is q, a high nibble 16q; Q6_K: two LOP3s and
+// shifts join the 4-bit and 2-bit parts of q + 32), and products are exact:
+//   * x is cut per 32- (Q4_K) or 16-wide (Q6_K) sub-block into a power-of-two
+//     scaled integer of 22 bits and three signed 8-bit limbs (x~ = l0 2^16 +
+//     l1 2^8 + l2), as precise as the f32 x of the reference;
+//   * one MMA covers 8 weights of each of 4 sub-blocks (k = 8 sigma + i), and
+//     its 8 columns are (sub-block sigma, limb l0 | l1) -- a second MMA with the
+//     same A carries l2 -- so lane t's accumulators hold the integer sums of
+//     sub-block sigma = t for its two rows; four (Q4_K) or two (Q6_K) MMAs
+//     complete a sub-block group, and the GGUF scales are applied once per
+//     (row, sub-block) in f32 (dequant.rs:98-126, 178-206):
+//       Q4_K: y += d*sc_s*u_s*S_s - dmin*m_s*X_s
+//       Q6_K: y += d*sc_s*(u_s*S_s - 32*X_s)
+//     with S_s the limb-combined integer sum, u_s = 1 / (x's scale of the
+//     sub-block) (/16 for a high nibble) and X_s = sum of x over s.
 // The weights stream from HBM once (tile layout, device.cuh): every warp runs
 // its own ring of shared-memory slots filled by bulk asynchronous copies (one
 // per 16-row block unit, completion on an mbarrier); x is converted once per
 // unit into shared memory, already in each lane's B-fragment order.
 //
-// Work: a unit is (8 tiles of 16 rows, K-slice). Warp w of a CTA owns tile
+// Work: a unit is (16 tiles of 16 rows, K-slice). Warp w of a CTA owns tile
 // w of the unit. When there are too few tiles to fill the GPU, K is split and
 // the CTA that finishes a group last sums the slices in order (deterministic)
 // and runs the epilogue. Epilogues are the fused ones of gemv_common.cuh.
@@ -43,10 +42,10 @@
 namespace sm {
 
 constexpr int TC_WARPS = 16, TC_THREADS = TC_WARPS * 32;
-constexpr uint32_t TC_FRAG = 1024;             // B fragments of one block, one type: [2][32 lanes][16 B]
-// per block: [4 x (X32_t, X32_t+4, 1/scale, 0)][4 x (X16_t, X16_t+4, X16_t+8, X16_t+12)]
-// (X32 / X16: sums of x over 32- / 16-wide sub-blocks, for lane t's epilogue)
-constexpr uint32_t TC_XS = 128;
+// B fragments of one block, one type: [8 MMA positions][32 lanes][4 words]
+constexpr uint32_t TC_FRAG = 4096;
+// per block: (u_s, X_s) of the 8 Q4_K sub-blocks, then of the 16 Q6_K ones
+constexpr uint32_t TC_XS = 256;
 constexpr uint32_t TC_SMEM_MAX = 225u * 1024u;
 // Ring slots per warp: 16 warps x 2-3 slots of one block unit each keep HBM
 // saturated; deeper rings (more requests in flight) lose bandwidth, and so do
@@ -58,196 +57,187 @@ struct TcPlan {
   uint32_t stages, stage_bytes;  // per-warp cp.async ring of weight units
 };
 
-// B operand of the chunks of sub-block s: the lane's fragment words when s is
-// in its column (s & 3 == u), else zero. fb[k] is the shared address the lane
-// reads for sub-blocks s with s & 3 == k: its fragment slot of the current
-// block, or a zero page (the fragments of the lane's sub-blocks u + 4 sigma
-// sit sigma * 512 bytes apart; the zero page is 1 KB).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int c) { return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w; }
 
-// Converts block bl (global block b) of x into shared memory: per type the
-// lane's B fragments [2][32 lanes][4 words] for the sub-blocks of its column
-// (u = lane >> 3: u, u + 4 for Q4_K; u, u + 4, u + 8, u + 12 for Q6_K; the
-// MMA loops zero them for the other sub-blocks), and the x sums and the
-// block's 1/scale for the epilogues. One warp per block.
-__device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* f4, uint4* f6, float4* xs, bool t4,
+// Power-of-two scale for a sub-block whose largest |x| is mx: the scaled
+// integers stay below 2^22 (three 8-bit limbs); returns 2^e, and 2^-e in inv.
+__device__ __forceinline__ float limb_scale(float mx, float& inv) {
+  const int E = (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127;
+  const int e = mx > 0.f ? max(-100, min(100, 21 - E)) : 0;
+  inv = __uint_as_float((uint32_t)(127 - e) << 23);
+  return __uint_as_float((uint32_t)(127 + e) << 23);
+}
+// Four x values (scaled by f) as limb words: byte b of l[k] is limb k of value b.
+__device__ __forceinline__ void limbs4(const float4& v, float f, uint32_t (&l)[3]) {
+  const float vv[4] = {v.x, v.y, v.z, v.w};
+  l[0] = l[1] = l[2] = 0;
+#pragma unroll
+  for (int b = 0; b < 4; b++) {
+    const int xi = __float2int_rn(vv[b] * f);  // |xi| < 2^22
+    const int l2 = ((xi + 128) & 255) - 128, r = (xi - l2) >> 8;
+    const int l1 = ((r + 128) & 255) - 128, l0 = (r - l1) >> 8;
+    l[0] |= (uint32_t)(l0 & 255) << (8 * b);
+    l[1] |= (uint32_t)(l1 & 255) << (8 * b);
+    l[2] |= (uint32_t)(l2 & 255) << (8 * b);
+  }
+}
+
+// Converts one block of x (256 values at xb) into shared memory, one warp per
+// block: per type the B fragments of its 8 MMA positions (f4, f6: [position]
+// [lane] uint4 = b0, b1 of the l0/l1 MMA, b0, b1 of the l2 MMA), and per
+// sub-block (u_s, X_s) (xs: 8 for Q4_K, then 16 for Q6_K). Column n = g of
+// lane (g, t) is (sub-block sigma = g >> 1, limb g & 1); its b0 (k = 4t ..
+// 4t + 3) holds sub-block t >> 1 and b1 (k = 4t + 16 ..) sub-block 2 + (t >> 1),
+// so a lane's word is non-zero only where that matches sigma.
+__device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* f4, uint4* f6, float2* xs, bool t4,
                                            bool t6) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, u = g >> 1;
-  const bool lo = g & 1;
-  float4 v4[4], v6[4];
-  float mx = 0.f;
-  if (t4) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, sn = g >> 1, lim = g & 1;
+  const bool active = (t >> 1) == (sn & 1);
+  const float4 v0 = ldg4(xb + 8 * lane), v1 = ldg4(xb + 8 * lane + 4);
+  const float mx = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
+                         fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
+  const float sm = sum4(v0) + sum4(v1);
+  auto frag = [&](uint4* f, int nsub, int wsub, float scl_own) {
+    // positions P = (sub-block group G, chunk c): 8 weights of each of 4 sub-blocks
+    const int nc = wsub / 8;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {  // runs of sub-blocks u, u+4 (i >> 1), halves c = i & 1
-      v4[i] = ldg4(xb + 32 * (u + 4 * (i >> 1)) + 8 * t + 4 * (i & 1));
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v4[i].x), fabsf(v4[i].y)), fmaxf(fabsf(v4[i].z), fabsf(v4[i].w))));
+    for (int P = 0; P < 8; P++) {
+      const int G = P / nc, c = P % nc, s = 4 * G + sn;
+      const float f_s = __shfl_sync(0xffffffffu, scl_own, (s * wsub) / 8);  // the scale of sub-block s
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (active) {
+        const float4 v = ldg4(xb + s * wsub + 8 * c + 4 * (t & 1));
+        uint32_t l[3];
+        limbs4(v, f_s, l);
+        const uint32_t A = lim ? l[1] : l[0], B = lim ? 0u : l[2];
+        w = (sn >> 1) ? make_uint4(0, A, 0, B) : make_uint4(A, 0, B, 0);
+      }
+      f[P * 32 + lane] = w;
     }
+    (void)nsub;
+  };
+  if (t4) {  // 32-wide sub-blocks: lanes 4s .. 4s + 3
+    float m = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    float su = sm + __shfl_xor_sync(0xffffffffu, sm, 1);
+    su += __shfl_xor_sync(0xffffffffu, su, 2);
+    float inv;
+    const float scl = limb_scale(m, inv);
+    if ((lane & 3) == 0) xs[lane >> 2] = make_float2(inv * (((lane >> 2) & 1) ? 0.0625f : 1.f), su);
+    frag(f4, 8, 32, scl);
   }
-  if (t6) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) {  // sub-block u + 4i, offsets 4t..4t+3
-      v6[i] = ldg4(xb + 16 * (u + 4 * i) + 4 * t);
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v6[i].x), fabsf(v6[i].y)), fmaxf(fabsf(v6[i].z), fabsf(v6[i].w))));
-    }
+  if (t6) {  // 16-wide sub-blocks: lanes 2s, 2s + 1
+    const float m = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    const float su = sm + __shfl_xor_sync(0xffffffffu, sm, 1);
+    float inv;
+    const float scl = limb_scale(m, inv);
+    if ((lane & 1) == 0) xs[8 + (lane >> 1)] = make_float2(inv, su);
+    frag(f6, 16, 16, scl);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  // scale = 2^(141 - E) puts max|x| in [2^14, 2^15): hi stays below the f16 maximum.
-  const uint32_t E = (__float_as_uint(mx) >> 23) & 0xFFu;
-  const float scl = E >= 15u ? __uint_as_float((268u - E) << 23) : 1.0f;
-  const float inv = E >= 15u ? __uint_as_float((E - 14u) << 23) : 1.0f;
-  if (t4) {
-    uint4 w[2];
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const float4 a = v4[2 * i], c = v4[2 * i + 1];
-      w[i] = make_uint4(hl_pair(a.x * scl, a.z * scl, lo), hl_pair(a.y * scl, a.w * scl, lo),
-                        hl_pair(c.x * scl, c.z * scl, lo), hl_pair(c.y * scl, c.w * scl, lo));
-    }
-    f4[lane] = w[0];       // sub-block u: chunk halves c = 0 (x, y), 1 (z, w)
-    f4[32 + lane] = w[1];  // sub-block u + 4
-    // sums of x over sub-blocks u and u + 4 (unscaled), over the 4 lanes t
-    float s0 = sum4(v4[0]) + sum4(v4[1]), s1 = sum4(v4[2]) + sum4(v4[3]);
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-    if (!lo && t == 0) xs[u] = make_float4(s0, s1, inv, 0.f);
-  } else if (lane < 4) {
-    xs[lane] = make_float4(0.f, 0.f, inv, 0.f);
-  }
-  if (t6) {
-    float q[4];  // sums over the 16-wide sub-blocks u + 4i, over the 4 lanes t
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      q[i] = sum4(v6[i]);
-      q[i] += __shfl_xor_sync(0xffffffffu, q[i], 1);
-      q[i] += __shfl_xor_sync(0xffffffffu, q[i], 2);
-    }
-    if (!lo && t == 0) xs[4 + u] = make_float4(q[0], q[1], q[2], q[3]);
-    uint2 w[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float4 a = v6[i];
-      w[i] = make_uint2(hl_pair(a.x * scl, a.z * scl, lo), hl_pair(a.y * scl, a.w * scl, lo));
-    }
-    f6[lane] = make_uint4(w[0].x, w[0].y, w[1].x, w[1].y);       // sub-blocks u, u + 4
-    f6[32 + lane] = make_uint4(w[2].x, w[2].y, w[3].x, w[3].y);  // sub-blocks u + 8, u + 12
-  }
+}
+
+// Integer sums of lane t's sub-block for rows g (d0) and g + 8 (d1), as floats.
+__device__ __forceinline__ void limb_sums(const int (&A)[4], const int (&B)[4], float& d0, float& d1) {
+  d0 = fmaf((float)A[0], 65536.f, (float)(A[1] * 256 + B[0]));
+  d1 = fmaf((float)A[2], 65536.f, (float)(A[3] * 256 + B[2]));
 }
 
 // ------------------------------------------------------------- Q4_K ----
-// A block of a tile is computed from its unit in shared memory (st).
-struct Q4Buf {
-  uint4 q[4];  // loads 0..3 of the lane (rows g, g+8)
-};
-__device__ __forceinline__ void q4_load(Q4Buf& B, const uint8_t* st, int lane) {
-  const uint4* qs = reinterpret_cast<const uint4*>(st + 256) + lane;
-#pragma unroll
-  for (int L = 0; L < 4; L++) B.q[L] = qs[32 * L];
-}
-// P0 / P1: the MMA sums of sub-blocks t and t + 4, times 2^-24 (t even: low
-// nibbles) or 2^-20 (t odd: high nibbles) and the block's x scale.
-__device__ __forceinline__ float q4_row(const uint4& hd, int t, float P0, float P1, const float4& xs) {
-  const float d = h2f_ref(hd.x & 0xFFFFu) * (xs.z * ((t & 1) ? 1048576.f : 16777216.f)), dmin = h2f_ref(hd.x >> 16);
-  const int s0 = 8 * t;  // get_scale_min_k4 of sub-blocks t and t + 4 (dequant.rs:41-49)
-  const uint32_t sa = (hd.y >> s0) & 63u, ma = (hd.z >> s0) & 63u;
-  const uint32_t sb = ((hd.w >> s0) & 0xFu) | (((hd.y >> (s0 + 6)) & 3u) << 4);
-  const uint32_t mb = ((hd.w >> (s0 + 4)) & 0xFu) | (((hd.z >> (s0 + 6)) & 3u) << 4);
-  return d * ((float)sa * P0 + (float)sb * P1) - dmin * ((float)ma * xs.x + (float)mb * xs.y);
-}
-__device__ __forceinline__ void q4_block(const uint8_t* st, const uint32_t (&fb)[4], const float4* __restrict__ xs,
-                                         int lane, float& rg, float& rh) {
-  Q4Buf B;
-  q4_load(B, st, lane);
-  const uint4 hg = reinterpret_cast<const uint4*>(st)[lane >> 2], hh = reinterpret_cast<const uint4*>(st)[(lane >> 2) + 8];
-  // acc[s >> 2]: sub-blocks 0-3 / 4-7, the two chains alternate
-  float acc[2][4] = {};
-#pragma unroll
-  for (int s4 = 0; s4 < 4; s4++) {
-#pragma unroll
-    for (int hi = 0; hi < 2; hi++) {
-      const int s = s4 + 4 * hi, j = s >> 1;
-      const uint4 bf = hi ? lds128<512>(fb[s4]) : lds128<0>(fb[s4]);
-      const uint4 Lg = j < 2 ? B.q[0] : B.q[1], Lh = j < 2 ? B.q[2] : B.q[3];
-      const uint32_t ga = (j & 1) ? Lg.z : Lg.x, gb = (j & 1) ? Lg.w : Lg.y;
-      const uint32_t ha = (j & 1) ? Lh.z : Lh.x, hb = (j & 1) ? Lh.w : Lh.y;
-      const uint32_t b0 = bf.x, b1 = bf.y, b2 = bf.z, b3 = bf.w;
-      if (s & 1) {
-        mma16816(acc[hi], nib_hi(ga), nib_hi(ha), nib_hi(ga >> 8), nib_hi(ha >> 8), b0, b1);
-        mma16816(acc[hi], nib_hi(gb), nib_hi(hb), nib_hi(gb >> 8), nib_hi(hb >> 8), b2, b3);
-      } else {
-        mma16816(acc[hi], nib_lo(ga), nib_lo(ha), nib_lo(ga >> 8), nib_lo(ha >> 8), b0, b1);
-        mma16816(acc[hi], nib_lo(gb), nib_lo(hb), nib_lo(gb >> 8), nib_lo(hb >> 8), b2, b3);
-      }
-    }
+// get_scale_min_k4 of sub-block s = 4G + t (dequant.rs:41-49) from a row header.
+__device__ __forceinline__ void q4_sc_m(const uint4& h, int G, int t, float& sc, float& m) {
+  const int sh = 8 * t;
+  if (G == 0) {
+    sc = (float)((h.y >> sh) & 63u);
+    m = (float)((h.z >> sh) & 63u);
+  } else {
+    sc = (float)(((h.w >> sh) & 0xFu) | (((h.y >> (sh + 6)) & 3u) << 4));
+    m = (float)(((h.w >> (sh + 4)) & 0xFu) | (((h.z >> (sh + 6)) & 3u) << 4));
   }
-  const int t = lane & 3;
-  const float4 x4 = xs[t];
-  rg += q4_row(hg, t, acc[0][0] + acc[0][1], acc[1][0] + acc[1][1], x4);
-  rh += q4_row(hh, t, acc[0][2] + acc[0][3], acc[1][2] + acc[1][3], x4);
+}
+__device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* f, const float2* xs, int lane, float& rg,
+                                         float& rh) {
+  const int g = lane >> 2, t = lane & 3, p = t & 1;
+  const uint32_t M = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;  // nibble of sub-blocks t >> 1, 2 + (t >> 1)
+  uint4 Wg[4], Wh[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    Wg[j] = *reinterpret_cast<const uint4*>(st + q4t_word_off(g, j, 0, p));
+    Wh[j] = *reinterpret_cast<const uint4*>(st + q4t_word_off(g + 8, j, 0, p));
+  }
+  const uint4 hg = reinterpret_cast<const uint4*>(st)[g], hh = reinterpret_cast<const uint4*>(st)[g + 8];
+  const float dg = h2f_ref(hg.x & 0xFFFFu), dmg = h2f_ref(hg.x >> 16);
+  const float dh = h2f_ref(hh.x & 0xFFFFu), dmh = h2f_ref(hh.x >> 16);
+#pragma unroll
+  for (int G = 0; G < 2; G++) {
+    int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const uint4 bf = f[(4 * G + c) * 32 + lane];
+      const uint32_t a0 = word_of(Wg[2 * G], c) & M, a2 = word_of(Wg[2 * G + 1], c) & M;
+      const uint32_t a1 = word_of(Wh[2 * G], c) & M, a3 = word_of(Wh[2 * G + 1], c) & M;
+      mma_u8s8(A, a0, a1, a2, a3, bf.x, bf.y);
+      mma_u8s8(B, a0, a1, a2, a3, bf.z, bf.w);
+    }
+    float Sg, Sh;
+    limb_sums(A, B, Sg, Sh);
+    const float2 ux = xs[4 * G + t];
+    float scg, mg, sch, mh;
+    q4_sc_m(hg, G, t, scg, mg);
+    q4_sc_m(hh, G, t, sch, mh);
+    rg += (dg * scg) * (ux.x * Sg) - (dmg * mg) * ux.y;
+    rh += (dh * sch) * (ux.x * Sh) - (dmh * mh) * ux.y;
+  }
 }
 
 // ------------------------------------------------------------- Q6_K ----
-struct Q6Buf {
-  uint4 q[6];  // ql 0-3, ql 4-7, qh of row g; the same of row g + 8
-};
-__device__ __forceinline__ void q6_load(Q6Buf& B, const uint8_t* st, int lane) {
-  const uint4* q = reinterpret_cast<const uint4*>(st + Q6T_QOFF) + lane;
-#pragma unroll
-  for (int L = 0; L < 6; L++) B.q[L] = q[32 * L];
+// A operands of sub-blocks h and 2 + h (h = t >> 1) from words W_h and H.
+__device__ __forceinline__ void q6_a(uint32_t w, uint32_t hbits, int h, uint32_t& lo, uint32_t& hi) {
+  const uint32_t hs = hbits << (4 * h);
+  lo = (w & 0x0F0F0F0Fu) | (hs & 0x30303030u);
+  hi = ((w >> 4) & 0x0F0F0F0Fu) | ((hs >> 2) & 0x30303030u);
 }
-// Pass p of a Q6_K row: sub-blocks s = 8p + t and 8p + t + 4 (scale bytes t of
-// words w0, w1), MMA sums D * 2^-24 (p = 0) or 2^-20 (p = 1) times the x
-// scale (F undoes both), minus 32 * sum(x) for the +32 of the stored values.
-__device__ __forceinline__ float q6_half(uint32_t w0, uint32_t w1, int t, const float (&acc)[2][4], int c, float F,
-                                         float X0, float X1) {
-  const int sh = 8 * t;
-  const float s0 = (float)(int8_t)((w0 >> sh) & 0xFFu), s1 = (float)(int8_t)((w1 >> sh) & 0xFFu);
-  return s0 * fmaf(F, acc[0][c] + acc[0][c + 1], -32.f * X0) + s1 * fmaf(F, acc[1][c] + acc[1][c + 1], -32.f * X1);
-}
-// Two passes: sub-blocks 0-7 (low nibbles of the 8 ql words), then 8-15 (high
-// nibbles), each into two accumulators that are scaled before the next pass.
-__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint32_t (&fb)[4], const float4* __restrict__ xs,
-                                         int lane, float& rg, float& rh) {
-  const int g = lane >> 2, t = lane & 3;
-  Q6Buf B;
-  q6_load(B, unit, lane);
-  const float4 x16 = xs[4 + t];
-  const uint32_t gw[8] = {B.q[0].x, B.q[0].y, B.q[0].z, B.q[0].w, B.q[1].x, B.q[1].y, B.q[1].z, B.q[1].w};
-  const uint32_t hw[8] = {B.q[3].x, B.q[3].y, B.q[3].z, B.q[3].w, B.q[4].x, B.q[4].y, B.q[4].z, B.q[4].w};
-  const uint32_t gq[4] = {B.q[2].x, B.q[2].y, B.q[2].z, B.q[2].w};
-  const uint32_t hq[4] = {B.q[5].x, B.q[5].y, B.q[5].z, B.q[5].w};
-  float pg = 0.f, ph = 0.f;
+__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, const float2* xs, int lane, float& rg,
+                                         float& rh) {
+  const int g = lane >> 2, t = lane & 3, p = t & 1, h = t >> 1;
+  // per row: W_h words (G, c) and H words (G, c), G = 0..3, c = 0..1
+  const uint4 wg0 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, h, 0, 0, p));
+  const uint4 wg1 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, h, 2, 0, p));
+  const uint4 hg0 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, 2, 0, 0, p));
+  const uint4 hg1 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, 2, 2, 0, p));
+  const uint4 wh0 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g + 8, h, 0, 0, p));
+  const uint4 wh1 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g + 8, h, 2, 0, p));
+  const uint4 hh0 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g + 8, 2, 0, 0, p));
+  const uint4 hh1 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g + 8, 2, 2, 0, p));
+  const uint4 scg = reinterpret_cast<const uint4*>(unit)[g], sch = reinterpret_cast<const uint4*>(unit)[g + 8];
+  const float dg = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g]);
+  const float dh = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g + 8]);
 #pragma unroll
-  for (int pass = 0; pass < 2; pass++) {
-    float acc[2][4] = {};
+  for (int G = 0; G < 4; G++) {
+    int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int i = 0; i < 4; i += 2) {
-#pragma unroll
-      for (int e = 0; e < 4; e++) {  // words i, i + 4, i + 1, i + 5: the two accumulators alternate
-        const int k = i + (e >> 1) + 4 * (e & 1);
-        const int sb = 8 * pass + k, sig = sb >> 2;  // sub-block; its fragment: slot sig >> 1, words 2*(sig & 1) ..
-        const uint2 bf = sig == 0 ? lds64<0>(fb[sb & 3]) : sig == 1 ? lds64<8>(fb[sb & 3])
-                       : sig == 2 ? lds64<512>(fb[sb & 3]) : lds64<520>(fb[sb & 3]);
-        const uint32_t wg = gw[k], wh = hw[k];
-        const uint32_t qg = (k & 1) ? __funnelshift_r(gq[k >> 1], gq[k >> 1], 8) : gq[k >> 1];
-        const uint32_t qh = (k & 1) ? __funnelshift_r(hq[k >> 1], hq[k >> 1], 8) : hq[k >> 1];
-        const uint32_t b0 = bf.x, b1 = bf.y;
-        if (pass == 0)
-          mma16816(acc[k >> 2], q6_lo(wg, qg), q6_lo(wh, qh), q6_lo(wg >> 8, qg >> 2), q6_lo(wh >> 8, qh >> 2), b0, b1);
-        else
-          mma16816(acc[k >> 2], q6_hi(wg, qg), q6_hi(wh, qh), q6_hi(wg >> 8, qg >> 2), q6_hi(wh >> 8, qh >> 2), b0, b1);
-      }
+    for (int c = 0; c < 2; c++) {
+      const int wi = 2 * (G & 1) + c;
+      const uint4 bf = f[(2 * G + c) * 32 + lane];
+      uint32_t a0, a1, a2, a3;
+      q6_a(word_of(G < 2 ? wg0 : wg1, wi), word_of(G < 2 ? hg0 : hg1, wi), h, a0, a2);
+      q6_a(word_of(G < 2 ? wh0 : wh1, wi), word_of(G < 2 ? hh0 : hh1, wi), h, a1, a3);
+      mma_u8s8(A, a0, a1, a2, a3, bf.x, bf.y);
+      mma_u8s8(B, a0, a1, a2, a3, bf.z, bf.w);
     }
-    const uint2 sg = *reinterpret_cast<const uint2*>(unit + 16 * g + 8 * pass);
-    const uint2 sh = *reinterpret_cast<const uint2*>(unit + 16 * (g + 8) + 8 * pass);
-    const float F = xs[t].z * (pass ? 1048576.f : 16777216.f);
-    const float X0 = pass ? x16.z : x16.x, X1 = pass ? x16.w : x16.y;
-    pg += q6_half(sg.x, sg.y, t, acc, 0, F, X0, X1);
-    ph += q6_half(sh.x, sh.y, t, acc, 2, F, X0, X1);
+    float Sg, Sh;
+    limb_sums(A, B, Sg, Sh);
+    const float2 ux = xs[8 + 4 * G + t];
+    const float sg = (float)(int8_t)((word_of(scg, G) >> (8 * t)) & 0xFFu);
+    const float sh = (float)(int8_t)((word_of(sch, G) >> (8 * t)) & 0xFFu);
+    rg += (dg * sg) * fmaf(ux.x, Sg, -32.f * ux.y);
+    rh += (dh * sh) * fmaf(ux.x, Sh, -32.f * ux.y);
   }
-  rg += q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g]) * pg;
-  rh += q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g + 8]) * ph;
 }
 
 // One warp: tile rows g, g+8 over blocks b0 .. b0+nblk-1 (x fragments of
@@ -262,7 +252,7 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint32_t (&f
 template <int QT, int S>
 __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t pre, uint8_t* ring,
                                         uint32_t stage_bytes, uint64_t* bars, uint32_t& nuse, uint32_t* err,
-                                        const uint4* f, const float4* xs, uint32_t zero_page, float& rg, float& rh) {
+                                        const uint4* f, const float2* xs, float& rg, float& rh) {
   const int lane = threadIdx.x & 31;
   constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT;
   // ring slot of the next copy to start (ip) and of the next block to compute (cp, phase cph)
@@ -274,21 +264,13 @@ __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32
     ip = ip + 1 == S ? 0 : ip + 1;
   };
   for (uint32_t k = pre; k + 1 < S; k++) issue(k);
-  uint32_t fb[4], dk[4];
-#pragma unroll
-  for (int k = 0; k < 4; k++) {
-    fb[k] = (lane >> 3) == k ? smem_u32(f + lane) : zero_page;
-    dk[k] = (lane >> 3) == k ? 1024u : 0u;  // fragments of one block, one type
-  }
   for (uint32_t i = 0; i < nblk; i++) {
     issue(i + S - 1);
     mbar_wait(bars + cp, cph, err);
     const uint8_t* sp = ring + cp * stage_bytes;
     if (++cp == S) { cp = 0; cph ^= 1u; }
-    if constexpr (QT == 12) q4_block(sp, fb, xs + 8 * i, lane, rg, rh);
-    else q6_block(sp, fb, xs + 8 * i, lane, rg, rh);
-#pragma unroll
-    for (int k = 0; k < 4; k++) fb[k] += dk[k];  // next block's fragment slot (the zero page stays)
+    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
+    else q6_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
     __syncwarp();  // every lane is done with the slot before it is refilled
   }
   nuse += nblk;
@@ -338,9 +320,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   __shared__ __align__(8) uint64_t s_bars[TC_WARPS * TC_MAX_STAGES];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint4* f4 = reinterpret_cast<uint4*>(tc_smem);
-  uint4* f6 = f4 + (p.t4 ? p.slice * 64 : 0);
-  float4* xs = reinterpret_cast<float4*>(f6 + (p.t6 ? p.slice * 64 : 0));
-  uint8_t* ring = reinterpret_cast<uint8_t*>(xs + 8 * p.slice) + (size_t)warp * p.stages * p.stage_bytes;
+  uint4* f6 = f4 + (p.t4 ? p.slice * (TC_FRAG / 16) : 0);
+  float2* xs = reinterpret_cast<float2*>(f6 + (p.t6 ? p.slice * (TC_FRAG / 16) : 0));
+  uint8_t* ring = reinterpret_cast<uint8_t*>(xs + 32 * p.slice) + (size_t)warp * p.stages * p.stage_bytes;
   const uint32_t nb = a.seg[0].w.n_in >> 8;
   uint64_t* bars = s_bars + warp * TC_MAX_STAGES;
   if (lane == 0) {
@@ -349,9 +331,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   }
   __syncwarp();
   uint32_t nuse = 0;
-  __shared__ __align__(16) uint4 s_zero[64];  // 1 KB zero page for the B operands of other columns
-  for (uint32_t i = threadIdx.x; i < 64; i += blockDim.x) s_zero[i] = make_uint4(0, 0, 0, 0);
-  const uint32_t zero_page = smem_u32(s_zero);
   // The weights do not depend on the previous kernel: start the first unit's
   // copies before waiting for it.
   pdl_trigger();
@@ -379,7 +358,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
     __syncthreads();  // the previous unit is done with the x fragments
     for (uint32_t i = warp; i < nblk; i += TC_WARPS)
-      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * 64, f6 + i * 64, xs + 8 * i, p.t4, p.t6);
+      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * (TC_FRAG / 16), f6 + i * (TC_FRAG / 16), xs + 32 * i, p.t4,
+                 p.t6);
     __syncthreads();
     const uint32_t tile = rg * TC_WARPS + warp;
     float vg = 0.f, vh = 0.f;
@@ -390,7 +370,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       const DWDesc& w = a.seg[si].w;
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
 #define TC_TILE(QT, S, F) \
-  tc_tile<QT, S>(tb, b0, nblk, pre, ring, p.stage_bytes, bars, nuse, a.err, F, xs, zero_page, vg, vh)
+  tc_tile<QT, S>(tb, b0, nblk, pre, ring, p.stage_bytes, bars, nuse, a.err, F, xs, vg, vh)
       if (w.type == 12) {
         if (p.stages == 3) TC_TILE(12, 3, f4);
         else TC_TILE(12, 2, f4);
@@ -433,14 +413,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------- host ----
-bool gemv_tc_ok(const GemvArgs& a) {
-  if (a.batch != 1 || !a.nseg) return false;
-  for (uint32_t i = 0; i < a.nseg; i++) {
-    const DWDesc& w = a.seg[i].w;
-    if (!tiled_type(w.type) || w.n_in != a.seg[0].w.n_in) return false;
-  }
-  return true;
-}
 
 constexpr int TC_MAX_DEVICES = 64;
 static std::mutex g_tc_mu;

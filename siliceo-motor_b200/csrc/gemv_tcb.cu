@@ -90,8 +90,9 @@ __device__ __forceinline__ void tb_scales(const float* __restrict__ x, uint32_t 
 
 // (ii) B fragments of 256-block k0: entry (s, n, lane (g, t)) holds column
 // c = 4n + g/2, hi (g even) or lo (g odd) of the scaled x at the lane's
-// positions of sub-block s in the A operand's k order (the batch-1 layout):
-// Q4_K: x[32s + 8t + {0,2},{1,3},{4,6},{5,7}] (16 B); Q6_K: x[16s + 4t + {0,2},{1,3}] (8 B).
+// positions of sub-block s in the A operand's k order (tb_q4_block,
+// tb_q6_block): Q4_K: x[32s + 4t + {0,2},{1,3}] then x[32s + 16 + 4t + ...]
+// (16 B, one pair of words per MMA); Q6_K: x[16s + 4t + {0,2},{1,3}] (8 B).
 template <int NT, int QT>
 __device__ __forceinline__ void tb_frags(const float* __restrict__ x, uint32_t ldx, uint32_t batch, uint32_t k0,
                                          const float* scl, uint8_t* frag) {
@@ -103,8 +104,8 @@ __device__ __forceinline__ void tb_frags(const float* __restrict__ x, uint32_t l
     if (QT == 12) {
       uint4 w = make_uint4(0, 0, 0, 0);
       if ((uint32_t)c < batch) {
-        const float* xp = x + (size_t)c * ldx + k0 + 32 * s + 8 * t;
-        const float4 a = ldg4(xp), b = ldg4(xp + 4);
+        const float* xp = x + (size_t)c * ldx + k0 + 32 * s + 4 * t;
+        const float4 a = ldg4(xp), b = ldg4(xp + 16);
         const float f = scl[c];
         w = make_uint4(hl_pair(a.x * f, a.z * f, lo), hl_pair(a.y * f, a.w * f, lo), hl_pair(b.x * f, b.z * f, lo),
                        hl_pair(b.y * f, b.w * f, lo));
@@ -128,9 +129,16 @@ template <int NT>
 __device__ __forceinline__ void tb_q4_block(const uint8_t* st, const uint8_t* frag, const float* sums,
                                             const float* fsc, float (&yg)[NT], float (&yh)[NT]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  uint4 q[4];
+  // qs words (j, c, p = t & 1) of rows g, g + 8; MMA m of a sub-block takes word c = 2m + (t >> 1)
+  const uint32_t c0 = t >> 1;
+  uint32_t Wg[4][2], Wh[4][2];
 #pragma unroll
-  for (int L = 0; L < 4; L++) q[L] = reinterpret_cast<const uint4*>(st + 256)[32 * L + lane];
+  for (int j = 0; j < 4; j++)
+#pragma unroll
+    for (int m = 0; m < 2; m++) {
+      Wg[j][m] = *reinterpret_cast<const uint32_t*>(st + q4t_word_off(g, j, 2 * m + c0, t & 1));
+      Wh[j][m] = *reinterpret_cast<const uint32_t*>(st + q4t_word_off(g + 8, j, 2 * m + c0, t & 1));
+    }
   const uint4 hg = reinterpret_cast<const uint4*>(st)[g], hh = reinterpret_cast<const uint4*>(st)[g + 8];
   float pg[NT], ph[NT];
 #pragma unroll
@@ -139,9 +147,7 @@ __device__ __forceinline__ void tb_q4_block(const uint8_t* st, const uint8_t* fr
 #pragma unroll
   for (int s = 0; s < 8; s++) {
     const int j = s >> 1;
-    const uint4 Lg = j < 2 ? q[0] : q[1], Lh = j < 2 ? q[2] : q[3];
-    const uint32_t ga = (j & 1) ? Lg.z : Lg.x, gb = (j & 1) ? Lg.w : Lg.y;
-    const uint32_t ha = (j & 1) ? Lh.z : Lh.x, hb = (j & 1) ? Lh.w : Lh.y;
+    const uint32_t ga = Wg[j][0], gb = Wg[j][1], ha = Wh[j][0], hb = Wh[j][1];
     uint32_t a1[4], a2[4];
     if (s & 1) {
       a1[0] = nib_hi(ga); a1[1] = nib_hi(ha); a1[2] = nib_hi(ga >> 8); a1[3] = nib_hi(ha >> 8);
@@ -191,19 +197,29 @@ __device__ __forceinline__ void tb_q4_block(const uint8_t* st, const uint8_t* fr
   }
 }
 
-// (iii) One Q6_K block: sub-blocks 0-7 from the low nibbles of the 8 ql words,
-// 8-15 from the high nibbles (x16 scale), one k16 MMA each.
+// (iii) One Q6_K block: one k16 MMA per 16-weight sub-block.
 template <int NT>
 __device__ __forceinline__ void tb_q6_block(const uint8_t* unit, const uint8_t* frag, const float* sums,
                                             const float* fsc, float (&yg)[NT], float (&yh)[NT]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  uint4 q[6];
+  // words W0, W1, H (G, c = t >> 1, p = t & 1) of rows g, g + 8 (device.cuh): lane t
+  // holds weights 4t .. 4t + 3 of every sub-block
+  const uint32_t c = t >> 1, p = t & 1;
+  uint32_t wg[3][4], wh[3][4];
 #pragma unroll
-  for (int L = 0; L < 6; L++) q[L] = reinterpret_cast<const uint4*>(unit + Q6T_QOFF)[32 * L + lane];
-  const uint32_t gw[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
-  const uint32_t hw[8] = {q[3].x, q[3].y, q[3].z, q[3].w, q[4].x, q[4].y, q[4].z, q[4].w};
-  const uint32_t gq[4] = {q[2].x, q[2].y, q[2].z, q[2].w};
-  const uint32_t hq[4] = {q[5].x, q[5].y, q[5].z, q[5].w};
+  for (int arr = 0; arr < 3; arr++)
+#pragma unroll
+    for (int G = 0; G < 4; G++) {
+      wg[arr][G] = *reinterpret_cast<const uint32_t*>(unit + q6t_word_off(g, arr, G, c, p));
+      wh[arr][G] = *reinterpret_cast<const uint32_t*>(unit + q6t_word_off(g + 8, arr, G, c, p));
+    }
+  // the 6-bit values of sub-block 4G + sg as four bytes
+  auto v6 = [](const uint32_t (&w)[3][4], int G, int sg) -> uint32_t {
+    const uint32_t n = w[sg & 1][G], h = w[2][G];
+    const uint32_t lo = (sg >> 1) ? (n >> 4) : n;
+    const uint32_t hi = sg == 0 ? h : sg == 1 ? (h << 4) : sg == 2 ? (h >> 2) : (h << 2);
+    return (lo & 0x0F0F0F0Fu) | (hi & 0x30303030u);
+  };
   const uint4 scg4 = reinterpret_cast<const uint4*>(unit)[g], sch4 = reinterpret_cast<const uint4*>(unit)[g + 8];
   const uint32_t scgw[4] = {scg4.x, scg4.y, scg4.z, scg4.w}, schw[4] = {sch4.x, sch4.y, sch4.z, sch4.w};
   const float dg = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g]);
@@ -213,19 +229,12 @@ __device__ __forceinline__ void tb_q6_block(const uint8_t* unit, const uint8_t* 
   for (int n = 0; n < NT; n++) pg[n] = ph[n] = 0.f;
 #pragma unroll
   for (int s = 0; s < 16; s++) {
-    const int pass = s >> 3, k = s & 7;
-    const uint32_t wg = gw[k], wh = hw[k];
-    const uint32_t qg = (k & 1) ? __funnelshift_r(gq[k >> 1], gq[k >> 1], 8) : gq[k >> 1];
-    const uint32_t qh = (k & 1) ? __funnelshift_r(hq[k >> 1], hq[k >> 1], 8) : hq[k >> 1];
-    uint32_t a[4];
-    if (pass == 0) {
-      a[0] = q6_lo(wg, qg); a[1] = q6_lo(wh, qh); a[2] = q6_lo(wg >> 8, qg >> 2); a[3] = q6_lo(wh >> 8, qh >> 2);
-    } else {
-      a[0] = q6_hi(wg, qg); a[1] = q6_hi(wh, qh); a[2] = q6_hi(wg >> 8, qg >> 2); a[3] = q6_hi(wh >> 8, qh >> 2);
-    }
+    const uint32_t vg = v6(wg, s >> 2, s & 3), vh = v6(wh, s >> 2, s & 3);
+    // bytes 0, 2 / 1, 3 as f16 subnormals v * 2^-24
+    const uint32_t a[4] = {vg & 0x003F003Fu, vh & 0x003F003Fu, (vg >> 8) & 0x003F003Fu, (vh >> 8) & 0x003F003Fu};
     const float sg = (float)(int8_t)((scgw[s >> 2] >> (8 * (s & 3))) & 0xFFu);
     const float sh = (float)(int8_t)((schw[s >> 2] >> (8 * (s & 3))) & 0xFFu);
-    const float sgp = pass ? 16.f * sg : sg, shp = pass ? 16.f * sh : sh;
+    const float sgp = sg, shp = sh;
     const float nqg = -32.f * dg * sg, nqh = -32.f * dh * sh;  // the stored values are q + 32
 #pragma unroll
     for (int n = 0; n < NT; n++) {
