@@ -56,7 +56,7 @@ typedef struct {
 
 typedef struct {
   int32_t device;        /* CUDA device ordinal */
-  uint32_t max_batch;    /* largest decode batch (default 32) */
+  uint32_t max_batch;    /* largest decode batch: 0 (= 32) .. 32 */
   uint32_t max_context;  /* largest position + 1 any cache may reach (default 32768) */
   uint32_t tp_rank;      /* tensor-parallel rank, below tp_size */
   uint32_t tp_size;      /* tensor-parallel size: 0 or 1 = none, else 2..8 (one process per GPU) */

@@ -549,7 +549,12 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   CK(cudaMemcpy(m->cos_t, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(m->sin_t, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
   // workspace
-  const uint32_t R = std::max<uint32_t>(32, opts && opts->max_batch ? opts->max_batch : 32);
+  // Rows of one pass (decode batch, prefill chunk): the batched GEMV takes up to 32 columns.
+  if (opts && opts->max_batch > 32) {
+    set_error("max_batch above 32 is not supported (the batched GEMV takes up to 32 columns)");
+    return SM_ERR_UNSUPPORTED;
+  }
+  const uint32_t R = 32;
   m->rows_max = R;
   const size_t F = fl, V = c.vocab_size;
   if ((rc = dev_alloc(m, (void**)&m->x, R * H * 4)) || (rc = dev_alloc(m, (void**)&m->xn, R * H * 4)) ||
