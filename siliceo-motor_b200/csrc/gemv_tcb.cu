@@ -157,7 +157,7 @@ __device__ __forceinline__ void tb_q4_block(const uint8_t* st, const uint8_t* fr
       a2[0] = nib_lo(gb); a2[1] = nib_lo(hb); a2[2] = nib_lo(gb >> 8); a2[3] = nib_lo(hb >> 8);
     }
     // get_scale_min_k4 of sub-block s for rows g, g + 8 (dequant.rs:41-49);
-    // a high nibble is 16x the low one's scale (2^-20 vs 2^-24)
+    // a high nibble's operand is 16q * 2^-24, so its sums are scaled by 1/16
     auto scale_min = [&](const uint4& h, float& sc, float& mn) {
       uint32_t a, m;
       if (s < 4) {
@@ -168,7 +168,7 @@ __device__ __forceinline__ void tb_q4_block(const uint8_t* st, const uint8_t* fr
         a = ((h.w >> s4) & 0xFu) | (((h.y >> (s4 + 6)) & 3u) << 4);
         m = ((h.w >> (s4 + 4)) & 0xFu) | (((h.z >> (s4 + 6)) & 3u) << 4);
       }
-      sc = (float)a * ((s & 1) ? 16.f : 1.f);
+      sc = (float)a * ((s & 1) ? 0.0625f : 1.f);
       mn = (float)m;
     };
     float scg, mg, sch, mh;
