@@ -103,24 +103,24 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
   const float mx = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
                          fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
   const float sm = sum4(v0) + sum4(v1);
-  auto frag = [&](uint4* f, int nsub, int wsub, float scl_own) {
-    // positions P = (sub-block group G, chunk c): 8 weights of each of 4 sub-blocks
-    const int nc = wsub / 8;
+  // Each lane cuts its own 8 values into limbs (with its sub-block's scale);
+  // the fragment words are then fetched from the owning lanes by shuffles.
+  auto frag = [&](uint4* f, int wsub, float scl_own) {
+    uint32_t L0[3], L1[3];  // limbs of values 8 lane + 0..3 and + 4..7
+    limbs4(v0, scl_own, L0);
+    limbs4(v1, scl_own, L1);
+    const int nc = wsub / 8, half = t & 1;
 #pragma unroll
     for (int P = 0; P < 8; P++) {
-      const int G = P / nc, c = P % nc, s = 4 * G + sn;
-      const float f_s = __shfl_sync(0xffffffffu, scl_own, (s * wsub) / 8);  // the scale of sub-block s
-      uint4 w = make_uint4(0, 0, 0, 0);
-      if (active) {
-        const float4 v = ldg4(xb + s * wsub + 8 * c + 4 * (t & 1));
-        uint32_t l[3];
-        limbs4(v, f_s, l);
-        const uint32_t A = lim ? l[1] : l[0], B = lim ? 0u : l[2];
-        w = (sn >> 1) ? make_uint4(0, A, 0, B) : make_uint4(A, 0, B, 0);
-      }
-      f[P * 32 + lane] = w;
+      // positions P = (sub-block group G, chunk c): 8 weights of each of 4 sub-blocks
+      const int G = P / nc, c = P % nc, src = (4 * G + sn) * wsub / 8 + c;
+      const uint32_t a00 = __shfl_sync(0xffffffffu, L0[0], src), a01 = __shfl_sync(0xffffffffu, L0[1], src);
+      const uint32_t a10 = __shfl_sync(0xffffffffu, L1[0], src), a11 = __shfl_sync(0xffffffffu, L1[1], src);
+      const uint32_t b0 = __shfl_sync(0xffffffffu, L0[2], src), b1 = __shfl_sync(0xffffffffu, L1[2], src);
+      const uint32_t A = active ? (half ? (lim ? a11 : a10) : (lim ? a01 : a00)) : 0u;
+      const uint32_t B = (active && !lim) ? (half ? b1 : b0) : 0u;
+      f[P * 32 + lane] = (sn >> 1) ? make_uint4(0, A, 0, B) : make_uint4(A, 0, B, 0);
     }
-    (void)nsub;
   };
   if (t4) {  // 32-wide sub-blocks: lanes 4s .. 4s + 3
     float m = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -130,7 +130,7 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
     float inv;
     const float scl = limb_scale(m, inv);
     if ((lane & 3) == 0) xs[lane >> 2] = make_float2(inv * (((lane >> 2) & 1) ? 0.0625f : 1.f), su);
-    frag(f4, 8, 32, scl);
+    frag(f4, 32, scl);
   }
   if (t6) {  // 16-wide sub-blocks: lanes 2s, 2s + 1
     const float m = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -138,7 +138,7 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
     float inv;
     const float scl = limb_scale(m, inv);
     if ((lane & 1) == 0) xs[8 + (lane >> 1)] = make_float2(inv, su);
-    frag(f6, 16, 16, scl);
+    frag(f6, 16, scl);
   }
 }
 
@@ -217,21 +217,24 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, co
   const uint4 scg = reinterpret_cast<const uint4*>(unit)[g], sch = reinterpret_cast<const uint4*>(unit)[g + 8];
   const float dg = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g]);
   const float dh = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g + 8]);
+  // eight independent accumulator chains (groups x limb sets) hide the MMA latency
+  int A[4][4] = {}, B[4][4] = {};
 #pragma unroll
-  for (int G = 0; G < 4; G++) {
-    int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
+  for (int c = 0; c < 2; c++)
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
+    for (int G = 0; G < 4; G++) {
       const int wi = 2 * (G & 1) + c;
       const uint4 bf = f[(2 * G + c) * 32 + lane];
       uint32_t a0, a1, a2, a3;
       q6_a(word_of(G < 2 ? wg0 : wg1, wi), word_of(G < 2 ? hg0 : hg1, wi), h, a0, a2);
       q6_a(word_of(G < 2 ? wh0 : wh1, wi), word_of(G < 2 ? hh0 : hh1, wi), h, a1, a3);
-      mma_u8s8(A, a0, a1, a2, a3, bf.x, bf.y);
-      mma_u8s8(B, a0, a1, a2, a3, bf.z, bf.w);
+      mma_u8s8(A[G], a0, a1, a2, a3, bf.x, bf.y);
+      mma_u8s8(B[G], a0, a1, a2, a3, bf.z, bf.w);
     }
+#pragma unroll
+  for (int G = 0; G < 4; G++) {
     float Sg, Sh;
-    limb_sums(A, B, Sg, Sh);
+    limb_sums(A[G], B[G], Sg, Sh);
     const float2 ux = xs[8 + 4 * G + t];
     const float sg = (float)(int8_t)((word_of(scg, G) >> (8 * t)) & 0xFFu);
     const float sh = (float)(int8_t)((word_of(sch, G) >> (8 * t)) & 0xFFu);
