@@ -47,10 +47,11 @@ constexpr uint32_t TC_FRAG = 4096;
 // per block: (u_s, X_s) of the 8 Q4_K sub-blocks, then of the 16 Q6_K ones
 constexpr uint32_t TC_XS = 256;
 constexpr uint32_t TC_SMEM_MAX = 225u * 1024u;
-// Ring slots per warp: 16 warps x 2-3 slots of one block unit each keep HBM
-// saturated; deeper rings (more requests in flight) lose bandwidth, and so do
-// L2 prefetches ahead of the ring (both measured on B200).
-constexpr uint32_t TC_MAX_STAGES = 3;
+// Ring slots per warp: 16 warps x 2-4 slots of one block unit each (as many as
+// shared memory holds; 4 measured 4% faster than 3 on Q4_K with compute in the
+// loop, while a copy-only probe lost bandwidth beyond 3; L2 prefetches ahead
+// of the ring lost bandwidth too).
+constexpr uint32_t TC_MAX_STAGES = 4;
 
 struct TcPlan {
   uint32_t tiles, groups, ksplit, slice, units, grid, smem, t4, t6;
@@ -375,10 +376,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 #define TC_TILE(QT, S, F) \
   tc_tile<QT, S>(tb, b0, nblk, pre, ring, p.stage_bytes, bars, nuse, a.err, F, xs, vg, vh)
       if (w.type == 12) {
-        if (p.stages == 3) TC_TILE(12, 3, f4);
+        if (p.stages == 4) TC_TILE(12, 4, f4);
+        else if (p.stages == 3) TC_TILE(12, 3, f4);
         else TC_TILE(12, 2, f4);
       } else {
-        if (p.stages == 3) TC_TILE(14, 3, f6);
+        if (p.stages == 4) TC_TILE(14, 4, f6);
+        else if (p.stages == 3) TC_TILE(14, 3, f6);
         else TC_TILE(14, 2, f6);
       }
 #undef TC_TILE
