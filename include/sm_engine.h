@@ -124,8 +124,12 @@ int sm_model_step_io_bytes(const sm_model* m, uint64_t* h2d, uint64_t* d2h);
 /* ------------------------------------------------------------------------
  * Sequence state. Replaces `s_models::state::SeqState` for dense models
  * (crates/s-models/src/state.rs:202-361) and the position counter GpuCache
- * (crates/s-backend-cuda/src/model.rs:97-105): K/V live in HBM, f32,
- * [layer][position][kv_dim], owned by the handle.
+ * (crates/s-backend-cuda/src/model.rs:97-105): K/V live in HBM, f32, in
+ * pages of 32 positions ([layer][32][kv_dim] of K, then the same of V) drawn
+ * from a pool of the model. A clone shares its source's pages; a page is
+ * copied before one of its holders writes it, so clones behave as the
+ * reference's deep copies while a shared prefix sits in HBM once. Positions
+ * never written read as zeros.
  * ---------------------------------------------------------------------- */
 int sm_cache_new(sm_model* m, uint64_t max_seq, sm_cache** out); /* Device::new_cache (qwen2.rs:633-637) */
 int sm_cache_free(sm_cache* c);
@@ -138,6 +142,10 @@ int sm_cache_ensure_capacity(sm_cache* c, uint64_t min_cap); /* state.rs:323-329
 int sm_cache_clone(const sm_cache* c, sm_cache** out);       /* SeqState: Clone (state.rs:64-69) */
 /* Host copy of the K and V rows (kv_dim floats each) of one position. */
 int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_out, float* v_out);
+/* Pages of the model's KV pool held by caches, and pages allocated in all
+ * (held + free), each of kv_page_bytes bytes. No reference counterpart: the
+ * reference's SeqState owns contiguous vectors. */
+int sm_model_kv_pages(const sm_model* m, uint64_t* held, uint64_t* allocated, uint64_t* kv_page_bytes);
 
 /* ------------------------------------------------------------------------
  * Forward. Device::forward_cached (crates/s-models/src/device.rs:33,

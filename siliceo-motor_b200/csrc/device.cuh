@@ -89,13 +89,20 @@ struct RowDesc {
   uint32_t pos;
 };
 
-// A sequence's KV storage: k/v are [n_layers][cap][kv_dim] f32.
+// A sequence's KV storage, in pages of KV_PAGE positions (f32, the
+// reference's SeqState precision): page t holds positions [KV_PAGE t,
+// KV_PAGE (t + 1)) of every layer, K as [layer][KV_PAGE][kv_dim] and V the
+// same voff floats further. Sequences that share a prefix share its pages.
+constexpr uint32_t KV_PAGE = 32;
 struct SeqDesc {
-  float* k;
-  float* v;
-  uint32_t cap;
-  uint32_t pad;
+  float* const* pages;  // device array: the base of page t (t < cap / KV_PAGE, rounded up)
+  uint32_t cap;         // capacity in positions
+  uint32_t voff;        // floats from a page's K half to its V half: n_layers * KV_PAGE * kv_dim
 };
+// Offset of (layer, position) inside its page, in floats (K half).
+SM_HD size_t kv_page_off(uint32_t layer, uint32_t pos, uint32_t kvd) {
+  return ((size_t)layer * KV_PAGE + (pos % KV_PAGE)) * kvd;
+}
 
 // What a GEMV does with the dot product v of (physical row o, column b).
 // Pair kinds act on physical rows (2m, 2m+1) together.

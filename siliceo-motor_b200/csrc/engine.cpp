@@ -10,6 +10,7 @@
 #include <atomic>
 #include <chrono>
 #include <cmath>
+#include <unordered_map>
 #include <initializer_list>
 #include <map>
 #include <memory>
@@ -211,11 +212,16 @@ struct StepOut {
 
 }  // namespace
 
+// A sequence state (SeqState): its KV pages (device.cuh) in position order.
+// Pages are shared between clones (reference counted by the model) and
+// copied before a shared page is written; a page that was never written is
+// absent and reads as zeros.
 struct sm_cache {
   sm_model* m = nullptr;
-  float* k = nullptr;
-  float* v = nullptr;
+  std::vector<float*> pages;    // page t's base or nullptr, t < ceil(cap / KV_PAGE)
+  float** pages_dev = nullptr;  // the same array on the device, for the kernels
   uint64_t cap = 0, len = 0;
+  bool dirty = true;            // pages_dev is behind pages
 };
 
 struct sm_model {
@@ -256,6 +262,12 @@ struct sm_model {
   StepIn din{}, hin{};
   StepOut dout{}, hout{};
   std::vector<void*> allocs;
+  // KV pages of all the model's caches: chunks of device memory cut into pages
+  // of 2 * voff floats, a free list and reference counts.
+  uint32_t kv_voff = 0;
+  std::vector<void*> page_chunks;
+  std::vector<float*> free_pages;
+  std::unordered_map<float*, uint32_t> page_refs;
   std::map<uint32_t, cudaGraphExec_t> graphs;       // one step, state from the host
   std::map<uint32_t, cudaGraphExec_t> run_graphs;   // one step, state carried on the device
   uint32_t* hist = nullptr;  // [HIST_TOKENS] tokens recorded by decode runs
@@ -473,6 +485,7 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
   const TpShard& sh = m->sh;
   const uint64_t qd = sh.q_heads * hd, kvd = sh.kv_heads * hd, fl = sh.ff;
   m->kvd = (uint32_t)kvd;
+  m->kv_voff = (uint32_t)(c.n_layers * KV_PAGE * kvd);
   m->qd = (uint32_t)qd;
   m->fl = (uint32_t)fl;
   if (c.n_heads * hd != H || hd % 4 || hd > 128 || G > 8 || (G * hd) > 1024 || H % 4 || c.n_ff % 4 || fl % 4) {
@@ -653,6 +666,7 @@ void destroy_model(sm_model* m) {
     free_weight(L.wgu); free_weight(L.wdown);
   }
   for (void* p : m->allocs) cudaFree(p);
+  for (void* p : m->page_chunks) cudaFree(p);
   if (m->in_host) cudaFreeHost(m->in_host);
   if (m->out_host) cudaFreeHost(m->out_host);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -810,6 +824,101 @@ SampleParams to_params(const sm_sampler* s) {
   return p;
 }
 
+// Page management; the caller holds m->mu.
+static int page_alloc(sm_model* m, float** out) {
+  const size_t pbytes = (size_t)m->kv_voff * 2 * 4;
+  if (m->free_pages.empty()) {
+    const size_t per_chunk = std::max<size_t>(1, (size_t(256) << 20) / pbytes);
+    void* p = nullptr;
+    if (cudaMalloc(&p, per_chunk * pbytes) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cudaMalloc failed for " + std::to_string(per_chunk) + " KV pages of " + std::to_string(pbytes) +
+                " bytes");
+      return SM_ERR_OOM;
+    }
+    m->page_chunks.push_back(p);
+    for (size_t i = per_chunk; i-- > 0;) m->free_pages.push_back((float*)p + i * (size_t)m->kv_voff * 2);
+  }
+  float* pg = m->free_pages.back();
+  m->free_pages.pop_back();
+  m->page_refs[pg] = 1;
+  // unwritten positions read as zeros, as in a freshly allocated SeqState
+  CK(cudaMemsetAsync(pg, 0, pbytes, m->stream));
+  *out = pg;
+  return SM_OK;
+}
+static void page_release(sm_model* m, float* pg) {
+  if (!pg) return;
+  auto it = m->page_refs.find(pg);
+  if (it == m->page_refs.end()) return;
+  if (--it->second == 0) {
+    m->page_refs.erase(it);
+    m->free_pages.push_back(pg);  // reused in stream order: earlier reads are enqueued before any reuse
+  }
+}
+// The device copy of the page array, after changes.
+static int cache_sync(sm_model* m, sm_cache* c) {
+  if (!c->dirty) return SM_OK;
+  CK(cudaMemcpyAsync(c->pages_dev, c->pages.data(), c->pages.size() * sizeof(float*), cudaMemcpyHostToDevice,
+                     m->stream));
+  c->dirty = false;
+  return SM_OK;
+}
+// Positions [len, upto) are about to be written: every page they touch is
+// allocated, and a page shared with another cache is copied first.
+static int cache_prepare(sm_model* m, sm_cache* c, uint64_t upto) {
+  if (upto > c->cap) {
+    set_error(std::to_string(upto) + " positions exceed the cache capacity " + std::to_string(c->cap));
+    return SM_ERR_CAPACITY;
+  }
+  const uint64_t t1 = (upto + KV_PAGE - 1) / KV_PAGE;
+  for (uint64_t t = c->len / KV_PAGE; t < t1; t++) {
+    float*& pg = c->pages[t];
+    if (!pg) {
+      if (int rc = page_alloc(m, &pg)) return rc;
+      c->dirty = true;
+    } else if (m->page_refs[pg] > 1) {  // copy on write
+      float* np = nullptr;
+      if (int rc = page_alloc(m, &np)) return rc;
+      CK(cudaMemcpyAsync(np, pg, (size_t)m->kv_voff * 2 * 4, cudaMemcpyDeviceToDevice, m->stream));
+      page_release(m, pg);
+      pg = np;
+      c->dirty = true;
+    }
+  }
+  return cache_sync(m, c);
+}
+// Drops the pages past position n.
+static void cache_drop_after(sm_model* m, sm_cache* c, uint64_t n) {
+  for (uint64_t t = (n + KV_PAGE - 1) / KV_PAGE; t < c->pages.size(); t++)
+    if (c->pages[t]) {
+      page_release(m, c->pages[t]);
+      c->pages[t] = nullptr;
+      c->dirty = true;
+    }
+}
+static int cache_resize(sm_model* m, sm_cache* c, uint64_t cap) {
+  const size_t np = (cap + KV_PAGE - 1) / KV_PAGE;
+  float** d = nullptr;
+  if (cudaMalloc((void**)&d, std::max<size_t>(np, 1) * sizeof(float*)) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaMalloc failed for a KV page table");
+    return SM_ERR_OOM;
+  }
+  if (c->pages_dev) {
+    cudaStreamSynchronize(m->stream);
+    cudaFree(c->pages_dev);
+  }
+  c->pages_dev = d;
+  c->pages.resize(np, nullptr);
+  c->cap = cap;
+  c->dirty = true;
+  return cache_sync(m, c);
+}
+static SeqDesc seq_desc(const sm_model* m, const sm_cache* c) {
+  return SeqDesc{c->pages_dev, (uint32_t)c->cap, m->kv_voff};
+}
+
 // Prefill / forward of n tokens of one cache, chunked by rows_max. The last
 // token's logits end in m->logits row 0.
 int forward_tokens(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n) {
@@ -819,6 +928,7 @@ int forward_tokens(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n) {
               std::to_string(c->cap));
     return SM_ERR_CAPACITY;
   }
+  if (int rc = cache_prepare(m, c, c->len + n)) return rc;
   for (uint64_t i = 0; i < n; i++)
     if (toks[i] >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
   cudaStream_t st = m->stream;
@@ -830,7 +940,7 @@ int forward_tokens(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n) {
       m->hin.tok[r] = toks[c0 + r];
       m->hin.rows[r] = RowDesc{0u, (uint32_t)(c->len + c0 + r)};
     }
-    m->hin.seqs[0] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.seqs[0] = seq_desc(m, c);
     m->hin.sel[0] = rows - 1;
     CK(cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, st));
     CK(run_rows(m, rows, last ? 1 : 0, st));
@@ -1067,30 +1177,6 @@ int sm_model_stream(const sm_model* m, void** stream) {
 }
 
 // ------------------------------------------------------------- caches ----
-static int alloc_kv(sm_model* m, uint64_t cap, float** k, float** v) {
-  const size_t bytes = (size_t)m->c.n_layers * cap * m->kvd * 4;
-  *k = *v = nullptr;
-  if (cudaMalloc((void**)k, bytes) != cudaSuccess || cudaMalloc((void**)v, bytes) != cudaSuccess) {
-    cudaGetLastError();
-    if (*k) cudaFree(*k);
-    *k = nullptr;
-    set_error("cudaMalloc failed for a KV cache of " + std::to_string(2 * bytes) + " bytes");
-    return SM_ERR_OOM;
-  }
-  return SM_OK;
-}
-
-// copies positions [0, len) of every layer between caches of capacities ca -> cb
-static int copy_kv(sm_model* m, float* dk, float* dv, uint64_t dcap, const float* sk, const float* sv, uint64_t scap,
-                   uint64_t len) {
-  if (!len) return SM_OK;
-  const size_t row = (size_t)m->kvd * 4;
-  CK(cudaMemcpy2DAsync(dk, dcap * row, sk, scap * row, len * row, m->c.n_layers, cudaMemcpyDeviceToDevice, m->stream));
-  CK(cudaMemcpy2DAsync(dv, dcap * row, sv, scap * row, len * row, m->c.n_layers, cudaMemcpyDeviceToDevice, m->stream));
-  CK(cudaStreamSynchronize(m->stream));
-  return SM_OK;
-}
-
 int sm_cache_new(sm_model* m, uint64_t max_seq, sm_cache** out) {
   if (guard_model(m) || !out) return SM_ERR_ARG;
   if (max_seq == 0 || max_seq > m->max_ctx) {
@@ -1101,8 +1187,7 @@ int sm_cache_new(sm_model* m, uint64_t max_seq, sm_cache** out) {
   cudaSetDevice(m->device);
   auto* c = new sm_cache();
   c->m = m;
-  c->cap = max_seq;
-  int rc = alloc_kv(m, max_seq, &c->k, &c->v);
+  int rc = cache_resize(m, c, max_seq);
   if (rc) { delete c; return rc; }
   m->refs++;
   *out = c;
@@ -1116,8 +1201,8 @@ int sm_cache_free(sm_cache* c) {
     std::lock_guard<std::mutex> lk(m->mu);
     cudaSetDevice(m->device);
     cudaStreamSynchronize(m->stream);
-    cudaFree(c->k);
-    cudaFree(c->v);
+    for (float* pg : c->pages) page_release(m, pg);
+    cudaFree(c->pages_dev);
     delete c;
   }
   model_release(m);
@@ -1137,13 +1222,21 @@ int sm_cache_capacity(const sm_cache* c, uint64_t* out) {
 int sm_cache_advance(sm_cache* c, uint64_t n) {
   if (!c) { set_error("null cache"); return SM_ERR_ARG; }
   if (c->len + n > c->cap) { set_error("sm_cache_advance: beyond capacity"); return SM_ERR_CAPACITY; }
+  sm_model* m = c->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  if (int rc = cache_prepare(m, c, c->len + n)) return rc;  // the positions exist (zeros unless written)
   c->len += n;
   return SM_OK;
 }
 int sm_cache_reset(sm_cache* c) {
   if (!c) { set_error("null cache"); return SM_ERR_ARG; }
+  sm_model* m = c->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  cache_drop_after(m, c, 0);
   c->len = 0;
-  return SM_OK;
+  return cache_sync(m, c);
 }
 int sm_cache_truncate(sm_cache* c, uint64_t len) {
   if (!c) { set_error("null cache"); return SM_ERR_ARG; }
@@ -1151,8 +1244,12 @@ int sm_cache_truncate(sm_cache* c, uint64_t len) {
     set_error("truncate: " + std::to_string(len) + " > len=" + std::to_string(c->len) + " (a state cannot grow this way)");
     return SM_ERR_STATE;
   }
+  sm_model* m = c->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  cache_drop_after(m, c, len);
   c->len = len;
-  return SM_OK;
+  return cache_sync(m, c);
 }
 int sm_cache_ensure_capacity(sm_cache* c, uint64_t min_cap) {
   if (!c) { set_error("null cache"); return SM_ERR_ARG; }
@@ -1161,17 +1258,7 @@ int sm_cache_ensure_capacity(sm_cache* c, uint64_t min_cap) {
   if (min_cap > m->max_ctx) { set_error("ensure_capacity: beyond the model's max_context"); return SM_ERR_CAPACITY; }
   std::lock_guard<std::mutex> lk(m->mu);
   cudaSetDevice(m->device);
-  float *k, *v;
-  int rc = alloc_kv(m, min_cap, &k, &v);
-  if (rc) return rc;
-  rc = copy_kv(m, k, v, min_cap, c->k, c->v, c->cap, c->len);
-  if (rc) { cudaFree(k); cudaFree(v); return rc; }
-  cudaFree(c->k);
-  cudaFree(c->v);
-  c->k = k;
-  c->v = v;
-  c->cap = min_cap;
-  return SM_OK;
+  return cache_resize(m, c, min_cap);  // the pages stay: nothing is copied
 }
 int sm_cache_clone(const sm_cache* c, sm_cache** out) {
   if (!c || !out) { set_error("null argument"); return SM_ERR_ARG; }
@@ -1180,13 +1267,24 @@ int sm_cache_clone(const sm_cache* c, sm_cache** out) {
   cudaSetDevice(m->device);
   auto* n = new sm_cache();
   n->m = m;
-  n->cap = c->cap;
+  int rc = cache_resize(m, n, c->cap);
+  if (rc) { delete n; return rc; }
   n->len = c->len;
-  int rc = alloc_kv(m, c->cap, &n->k, &n->v);
-  if (!rc) rc = copy_kv(m, n->k, n->v, n->cap, c->k, c->v, c->cap, c->len);
-  if (rc) { if (n->k) { cudaFree(n->k); cudaFree(n->v); } delete n; return rc; }
+  n->pages = c->pages;  // shared until one of them writes a page (cache_prepare)
+  for (float* pg : n->pages)
+    if (pg) m->page_refs[pg]++;
+  n->dirty = true;
+  if ((rc = cache_sync(m, n))) return rc;
   m->refs++;
   *out = n;
+  return SM_OK;
+}
+int sm_model_kv_pages(const sm_model* m, uint64_t* held, uint64_t* allocated, uint64_t* kv_page_bytes) {
+  if (!m || !held || !allocated || !kv_page_bytes) { set_error("null argument"); return SM_ERR_ARG; }
+  std::lock_guard<std::mutex> lk(const_cast<sm_model*>(m)->mu);
+  *held = m->page_refs.size();
+  *allocated = m->page_refs.size() + m->free_pages.size();
+  *kv_page_bytes = (uint64_t)m->kv_voff * 2 * 4;
   return SM_OK;
 }
 int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_out, float* v_out) {
@@ -1195,10 +1293,16 @@ int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_o
   if (layer >= m->c.n_layers || pos >= c->cap) { set_error("read_kv: index out of range"); return SM_ERR_ARG; }
   std::lock_guard<std::mutex> lk(m->mu);
   cudaSetDevice(m->device);
-  const size_t off = ((size_t)layer * c->cap + pos) * m->kvd;
   CK(cudaStreamSynchronize(m->stream));
-  CK(cudaMemcpy(k_out, c->k + off, m->kvd * 4, cudaMemcpyDeviceToHost));
-  CK(cudaMemcpy(v_out, c->v + off, m->kvd * 4, cudaMemcpyDeviceToHost));
+  const float* pg = c->pages[pos / KV_PAGE];
+  if (!pg) {
+    std::fill(k_out, k_out + m->kvd, 0.f);
+    std::fill(v_out, v_out + m->kvd, 0.f);
+    return SM_OK;
+  }
+  const size_t off = kv_page_off((uint32_t)layer, (uint32_t)pos, m->kvd);
+  CK(cudaMemcpy(k_out, pg + off, m->kvd * 4, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(v_out, pg + m->kv_voff + off, m->kvd * 4, cudaMemcpyDeviceToHost));
   return SM_OK;
 }
 
@@ -1236,10 +1340,11 @@ int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n
     if (toks[0] >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
     cudaGraphExec_t ex;
     if ((rc = decode_graph(m, 1, &ex))) return rc;
+    if ((rc = cache_prepare(m, c, c->len + 1))) return rc;
     CK(cudaStreamSynchronize(m->stream));
     m->hin.tok[0] = toks[0];
     m->hin.rows[0] = RowDesc{0u, (uint32_t)c->len};
-    m->hin.seqs[0] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.seqs[0] = seq_desc(m, c);
     m->hin.sp[0] = to_params(s);
     m->hin.rng[0] = *rng_state;
     m->hin.sel[0] = 0;
@@ -1287,12 +1392,14 @@ int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint
   cudaGraphExec_t ex;
   int rc = decode_graph(m, (uint32_t)n, &ex);
   if (rc) return rc;
+  for (uint64_t i = 0; i < n; i++)
+    if ((rc = cache_prepare(m, caches[i], caches[i]->len + 1))) return rc;
   CK(cudaStreamSynchronize(m->stream));
   for (uint64_t i = 0; i < n; i++) {
     sm_cache* c = caches[i];
     m->hin.tok[i] = toks[i];
     m->hin.rows[i] = RowDesc{(uint32_t)i, (uint32_t)c->len};
-    m->hin.seqs[i] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.seqs[i] = seq_desc(m, c);
     m->hin.sp[i] = to_params(samplers ? &samplers[i] : nullptr);
     m->hin.rng[i] = rng_states[i];
     m->hin.sel[i] = (uint32_t)i;
@@ -1331,13 +1438,15 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
   cudaGraphExec_t ex;
   int rc = run_graph(m, (uint32_t)n, &ex);
   if (rc) return rc;
+  for (uint64_t i = 0; i < n; i++)
+    if ((rc = cache_prepare(m, caches[i], caches[i]->len + n_steps))) return rc;
   const uint64_t chunk = HIST_TOKENS / n;
   CK(cudaStreamSynchronize(m->stream));
   for (uint64_t i = 0; i < n; i++) {
     sm_cache* c = caches[i];
     m->hin.tok[i] = toks[i];
     m->hin.rows[i] = RowDesc{(uint32_t)i, (uint32_t)c->len};
-    m->hin.seqs[i] = SeqDesc{c->k, c->v, (uint32_t)c->cap, 0u};
+    m->hin.seqs[i] = seq_desc(m, c);
     m->hin.sp[i] = to_params(samplers ? &samplers[i] : nullptr);
     m->hin.rng[i] = rng_states[i];
     m->hin.sel[i] = (uint32_t)i;

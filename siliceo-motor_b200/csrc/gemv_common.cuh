@@ -73,7 +73,7 @@ __device__ __forceinline__ float epi_single(const GemvArgs& a, const GemvSeg& sg
     case EPI_V: {  // v row into the cache at the row's position (qwen2.rs:498)
       const RowDesc rd = a.rows[col];
       const SeqDesc sd = a.seqs[rd.seq];
-      sd.v[((size_t)a.layer * sd.cap + rd.pos) * a.kvd + o] = v;
+      sd.pages[rd.pos / KV_PAGE][sd.voff + kv_page_off(a.layer, rd.pos, a.kvd) + o] = v;
       return 0.f;
     }
   }
@@ -103,7 +103,7 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, const GemvSeg& sg, u
     y[half] = r1;
   } else {  // EPI_ROPE_K: into the K cache (qwen2.rs:497)
     const SeqDesc sd = a.seqs[rd.seq];
-    float* kc = sd.k + ((size_t)a.layer * sd.cap + rd.pos) * a.kvd + h * a.hd + m;
+    float* kc = sd.pages[rd.pos / KV_PAGE] + kv_page_off(a.layer, rd.pos, a.kvd) + h * a.hd + m;
     kc[0] = r0;
     kc[half] = r1;
   }

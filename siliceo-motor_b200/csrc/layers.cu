@@ -32,41 +32,6 @@ __global__ void rmsnorm_kernel(const float* x, uint32_t ldx, const uint32_t* sel
     out[(size_t)r * ldo + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
-// --------------------------------------------------- RoPE + KV append ----
-// NEOX half-split rotation of pairs (i, i+hd/2) at the row's absolute
-// position (qwen2.rs:708-724) with cos/sin from a table built on the host by
-// the reference's own f32 formula; q is rotated in place, k is rotated into
-// the cache and v copied into it (qwen2.rs:494-499).
-__global__ void rope_kv_kernel(float* q, const float* k, const float* v, uint32_t ldq, uint32_t ldkv,
-                               const RowDesc* rows, const SeqDesc* seqs, uint32_t layer, uint32_t Hq, uint32_t Hkv,
-                               uint32_t hd, const float* cos_t, const float* sin_t) {
-  const uint32_t r = blockIdx.x, half = hd >> 1, kvd = Hkv * hd;
-  const RowDesc rd = rows[r];
-  const SeqDesc sd = seqs[rd.seq];
-  const float* ct = cos_t + (size_t)rd.pos * half;
-  const float* st = sin_t + (size_t)rd.pos * half;
-  float* qr = q + (size_t)r * ldq;
-  for (uint32_t idx = threadIdx.x; idx < Hq * half; idx += blockDim.x) {
-    const uint32_t h = idx / half, i = idx - h * half;
-    float* p = qr + h * hd + i;
-    const float x0 = p[0], x1 = p[half], c = ct[i], s = st[i];
-    p[0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    p[half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-  }
-  const size_t off = ((size_t)layer * sd.cap + rd.pos) * kvd;
-  float* kc = sd.k + off;
-  float* vc = sd.v + off;
-  const float* kr = k + (size_t)r * ldkv;
-  const float* vr = v + (size_t)r * ldkv;
-  for (uint32_t idx = threadIdx.x; idx < Hkv * half; idx += blockDim.x) {
-    const uint32_t g = idx / half, i = idx - g * half;
-    const float x0 = kr[g * hd + i], x1 = kr[g * hd + i + half], c = ct[i], s = st[i];
-    kc[g * hd + i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    kc[g * hd + i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-  }
-  for (uint32_t idx = threadIdx.x; idx < kvd; idx += blockDim.x) vc[idx] = vr[idx];
-}
-
 // ------------------------------------------------------------ attention ----
 // Split-K decode attention with GQA (qwen2.rs:502-533). CTA (row r, kv head
 // g, split sp) covers a run of 32-position tiles of the row's context
@@ -74,8 +39,9 @@ __global__ void rope_kv_kernel(float* q, const float* k, const float* v, uint32_
 // Both tiles of a step are staged with cp.async at once (V arrives while the
 // scores are computed); rows are padded to hd+4 floats so that the float4
 // shared-memory reads of 8 lanes hit distinct banks. Online softmax inside
-// the CTA; splits are merged by attn_combine_kernel.
+// the CTA; splits are merged by attn_combine_kernel. A tile is one KV page.
 constexpr int ATT_T = 32;     // positions per tile
+static_assert(ATT_T == (int)KV_PAGE, "an attention tile is one KV page");
 constexpr int ATT_THREADS = 128;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -103,13 +69,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
   const uint32_t G = Hq / Hkv, kvd = Hkv * hd, hs = hd + 4, hd4 = hd / 4;
   const SeqDesc sd = seqs[rd.seq];
   {  // positions before rd.pos were written by earlier steps: start them towards L2
-    const size_t kb = (size_t)layer * sd.cap * kvd + (size_t)g * hd;
     const uint32_t p_end = min(te * ATT_T, rd.pos), lines = (hd * 4 + 127) / 128;
     const uint32_t nrow = p_end > tb * ATT_T ? p_end - tb * ATT_T : 0;
     for (uint32_t i = threadIdx.x; i < nrow * lines; i += blockDim.x) {
-      const size_t off = kb + (size_t)(tb * ATT_T + i / lines) * kvd + (i % lines) * 32;
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(sd.k + off));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(sd.v + off));
+      const uint32_t pos = tb * ATT_T + i / lines;
+      const float* kp = sd.pages[pos / KV_PAGE] + kv_page_off(layer, pos, kvd) + (size_t)g * hd + (i % lines) * 32;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kp));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kp + sd.voff));
     }
   }
   pdl_wait();  // q and this position's K / V come from the QKV GEMV
@@ -128,19 +94,20 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
   float4 o[MAXO];
 #pragma unroll
   for (int i = 0; i < MAXO; i++) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  const size_t kbase = (size_t)layer * sd.cap * kvd + (size_t)g * hd;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (uint32_t t = tb; t < te; t++) {
     const uint32_t p0 = t * ATT_T, n = min((uint32_t)ATT_T, L - p0);
+    // page t: rows (layer, p0 + pp) of K at kb + pp * kvd, of V voff floats further
+    const float* kb = sd.pages[t] + (size_t)layer * KV_PAGE * kvd + (size_t)g * hd;
     __syncthreads();  // previous tile fully consumed
     for (uint32_t i = threadIdx.x; i < n * hd4; i += blockDim.x) {
       const uint32_t pp = i / hd4, d4 = i - pp * hd4;
-      cp_async16(kt + pp * hs + 4 * d4, sd.k + kbase + (size_t)(p0 + pp) * kvd + 4 * d4);
+      cp_async16(kt + pp * hs + 4 * d4, kb + (size_t)pp * kvd + 4 * d4);
     }
     cp_async_commit();
     for (uint32_t i = threadIdx.x; i < n * hd4; i += blockDim.x) {
       const uint32_t pp = i / hd4, d4 = i - pp * hd4;
-      cp_async16(vt + pp * hs + 4 * d4, sd.v + kbase + (size_t)(p0 + pp) * kvd + 4 * d4);
+      cp_async16(vt + pp * hs + 4 * d4, kb + sd.voff + (size_t)pp * kvd + 4 * d4);
     }
     cp_async_commit();
     cp_async_wait<1>();  // K landed
@@ -516,14 +483,6 @@ cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, co
                            uint32_t rows, uint32_t n, float eps, cudaStream_t st) {
   if (!rows) return cudaSuccess;
   rmsnorm_kernel<<<rows, n >= 4096 ? 1024 : 512, 0, st>>>(x, ldx, sel, w, out, ldo, n, eps);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_rope_kv(float* q, const float* k, const float* v, uint32_t ldq, uint32_t ldkv, const RowDesc* rows,
-                           const SeqDesc* seqs, uint32_t nrows, uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd,
-                           const float* cos_t, const float* sin_t, cudaStream_t st) {
-  if (!nrows) return cudaSuccess;
-  rope_kv_kernel<<<nrows, 256, 0, st>>>(q, k, v, ldq, ldkv, rows, seqs, layer, Hq, Hkv, hd, cos_t, sin_t);
   return cudaGetLastError();
 }
 

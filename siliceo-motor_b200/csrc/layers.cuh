@@ -28,9 +28,6 @@ cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows,
                          cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
                            uint32_t rows, uint32_t n, float eps, cudaStream_t st);
-cudaError_t launch_rope_kv(float* q, const float* k, const float* v, uint32_t ldq, uint32_t ldkv, const RowDesc* rows,
-                           const SeqDesc* seqs, uint32_t nrows, uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd,
-                           const float* cos_t, const float* sin_t, cudaStream_t st);
 size_t attn_smem_bytes(uint32_t G, uint32_t hd);
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,

@@ -122,6 +122,7 @@ SIGNATURES = {
     "sm_cache_ensure_capacity": (C.c_int, [P, U64]),
     "sm_cache_clone": (C.c_int, [P, C.POINTER(P)]),
     "sm_cache_read_kv": (C.c_int, [P, U64, U64, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
+    "sm_model_kv_pages": (C.c_int, [P, PU64, PU64, PU64]),
     "sm_forward_cached": (C.c_int, [P, P, PU32, U64, C.POINTER(C.c_float)]),
     "sm_rng_seed": (C.c_uint64, [U64]),
     "sm_forward_sample": (C.c_int, [P, P, PU32, U64, C.POINTER(sm_sampler), PU64, C.POINTER(C.c_uint8), PU32]),
@@ -355,6 +356,13 @@ class Model:
         v = C.c_uint64()
         _check(lib().sm_model_weight_bytes(self.h, C.byref(v)))
         return v.value
+
+    def kv_pages(self):
+        """(pages held by caches, pages allocated, bytes per page) of the
+        model's KV pool. Clones share pages until one of them writes."""
+        h, a, b = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _check(lib().sm_model_kv_pages(self.h, C.byref(h), C.byref(a), C.byref(b)))
+        return h.value, a.value, b.value
 
     def stream(self) -> int:
         v = C.c_void_p()

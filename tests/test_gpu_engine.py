@@ -219,3 +219,49 @@ def test_decode_run_matches_stepwise(models):
             assert out[k, i] == tok, (i, k)
         assert int(st[i]) == s
         assert len(runs[i]) == len(steps[i])
+
+
+def test_paged_prefix_sharing(models):
+    """Clones share KV pages; each writer copies only the page it writes into,
+    and every fork still matches the oracle's deep-copied SeqState."""
+    eng, ora = models["llama_tiny"]
+    prompt = list(range(100, 170))  # 70 positions: pages 0 and 1 full, page 2 holds 64..69
+    c = eng.new_cache(256)
+    eng.forward_cached(c, prompt, logits=False)
+    held0, _, page_bytes = eng.kv_pages()
+    assert page_bytes == 2 * eng.config.n_layers * 32 * eng.kv_width() * 4
+    forks = [c.clone() for _ in range(3)]
+    assert eng.kv_pages()[0] == held0  # nothing copied yet
+    co = ora.new_cache(256)
+    ora.forward_cached(co, prompt)
+    conts = [[7, 8], [9], [10, 11, 12, 13]]
+    first = []
+    for f, t in zip(forks, conts):
+        oc = co.clone()
+        want = ora.forward_cached(oc, t)
+        got = eng.forward_cached(f, t)
+        assert rel_err(got, want) <= LOGIT_TOL and top8(got) == top8(want)
+        first.append(got)
+    assert eng.kv_pages()[0] == held0 + 3  # one copied page (page 2) per writer
+    # the source is untouched by its forks' writes
+    for layer in (0, eng.config.n_layers - 1):
+        for pos in (0, 63, 64, 69):
+            k, v = c.read_kv(layer, pos)
+            kw, vw = co.read_kv(layer, pos)
+            assert rel_err(k, kw) <= 1e-4 and rel_err(v, vw) <= 1e-4
+        k, v = c.read_kv(layer, 70)
+        assert not k.any() and not v.any()  # never written here
+    # the source now writes its own page 2 in place (no holder shares it), and
+    # the same tokens after the same prefix give forks[0]'s bits
+    assert np.array_equal(eng.forward_cached(c, conts[0]), first[0])
+    assert eng.kv_pages()[0] == held0 + 3
+    # truncating inside a page and writing again
+    forks[2].truncate(66)
+    oc = co.clone()
+    oc.truncate(66)
+    want = ora.forward_cached(oc, [5, 6])
+    got = eng.forward_cached(forks[2], [5, 6])
+    assert rel_err(got, want) <= LOGIT_TOL and top8(got) == top8(want)
+    for f in forks:
+        f.free()
+    assert eng.kv_pages()[0] == held0  # back to the source's three pages
