@@ -330,8 +330,11 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     clocks = Clocks() if rank == 0 else None
     if clocks:
         clocks.start()
+    # a profiler started with capture off (ncu --profile-from-start off) sees only the timed steps
+    torch.cuda.profiler.start()
     out, states = model.decode_run(caches, toks, samplers, states, args.steps, ev0.cuda_event, ev1.cuda_event)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     barrier()
     clk = clocks.stop(set(range(max(world, 1)))) if clocks else None
     ms = allmax(ev0.elapsed_time(ev1))

@@ -1,12 +1,14 @@
 // Batched GEMV (2..32 columns: batched decode steps and prefill chunks) of
 // Q4_K / Q6_K weights on the tensor cores.
 //
-// The batch-1 kernel (gemv_tc.cu) spends the 8 MMA columns on sub-blocks of
-// one vector; here they hold four columns of x, each split into hi + lo f16
-// halves (MMA columns 2c / 2c+1 = hi / lo of column 4n + c of n-tile n, so a
-// lane's two accumulators of a row are one product and simply add). The A
-// operand is the same exact f16 subnormal made from the weight nibbles with
-// one AND, read from the same 16-row tile units; every k16 chunk lies in one
+// The batch-1 kernel (gemv_tc.cu) spends the 8 columns of its int8 MMAs on
+// sub-blocks of one vector; here f16 MMAs (m16n8k16) hold four columns of x,
+// each split into hi + lo f16 halves (MMA columns 2c / 2c+1 = hi / lo of
+// column 4n + c of n-tile n, so a lane's two accumulators of a row are one
+// product and simply add). The A operand is an exact f16 subnormal made from
+// the weight nibbles with one AND (w & 0x000F000F is q * 2^-24 in both
+// halves; a high nibble, w & 0x00F000F0, is 16 times that and takes a 1/16
+// factor), read from the same 16-row tile units; every k16 chunk lies in one
 // sub-block, so a sub-block's MMAs go into a fresh accumulator that is scaled
 // by the row's sub-block scale on the CUDA cores (dequant.rs:98-126, 178-206):
 //   Q4_K: y += d*F*sum_s(sc_s*acc_s) - dmin*sum_s(m_s*X_s)
@@ -52,8 +54,8 @@ struct TbSmem {
 };
 
 // (i) Column scales and sub-block sums of 256-block `blk` (K offset k0), one
-// warp per column: scl = the power of two that puts max|x| in [2^14, 2^15)
-// (as the batch-1 kernel), fscale = 2^24 / scl, sums of x over the 16-wide
+// warp per column: scl = the power of two that puts max|x| in [2^14, 2^15),
+// fscale = 2^24 / scl, sums of x over the 16-wide
 // (Q6_K) or 32-wide (Q4_K) sub-blocks in [s][t][n] order for the lane that
 // owns column 4n + t. Columns >= batch get zeros.
 template <int NT, int QT>
