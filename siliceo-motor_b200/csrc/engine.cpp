@@ -606,6 +606,9 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
         gemv_tcb_scratch_need(b, (uint32_t)sms, &pp, &pc);
         need_part = std::max(need_part, pp);
         need_cnt = std::max(need_cnt, pc);
+        gemv_umma_scratch_need(b, (uint32_t)sms, &pp, &pc);
+        need_part = std::max(need_part, pp);
+        need_cnt = std::max(need_cnt, pc);
       }
     };
     for (const Layer& L : m->layers) {
@@ -1113,7 +1116,8 @@ static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* 
   auto* m = new sm_model();
   m->device = opts ? opts->device : 0;
   if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      gemv_tc_prepare() != cudaSuccess || gemv_tcb_prepare() != cudaSuccess) {
+      gemv_tc_prepare() != cudaSuccess || gemv_tcb_prepare() != cudaSuccess ||
+      gemv_umma_prepare() != cudaSuccess) {
     cudaGetLastError();
     set_error("cannot use CUDA device " + std::to_string(m->device));
     delete m;
@@ -1502,6 +1506,9 @@ int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t
     uint64_t pp = 0;
     uint32_t pc = 0;
     gemv_tcb_scratch_need(probe, (uint32_t)sms, &pp, &pc);
+    need_part = std::max(need_part, pp);
+    need_cnt = std::max(need_cnt, pc);
+    gemv_umma_scratch_need(probe, (uint32_t)sms, &pp, &pc);
     need_part = std::max(need_part, pp);
     need_cnt = std::max(need_cnt, pc);
   }

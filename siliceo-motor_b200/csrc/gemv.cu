@@ -335,9 +335,17 @@ uint32_t gemv_plan(GemvArgs& a) {
 
 cudaError_t launch_gemv_tc(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
 cudaError_t launch_gemv_tcb(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
+cudaError_t launch_gemv_umma(GemvArgs a, cudaStream_t st, uint32_t* n_parts);
+
+// Batches of 2..32 columns of one tiled type: tcgen05 (gemv_umma.cu), else
+// the mma.sync kernel of gemv_tcb.cu when no plan of the former fits.
+static cudaError_t launch_batched(const GemvArgs& a, cudaStream_t st, uint32_t* n_parts) {
+  const cudaError_t e = launch_gemv_umma(a, st, n_parts);
+  return e == cudaErrorNotSupported ? launch_gemv_tcb(a, st, n_parts) : e;
+}
 
 // Q4_K / Q6_K segments run on the tensor-core kernels (batch 1: gemv_tc.cu,
-// mixed types in one launch; batches: gemv_tcb.cu, one launch per type), the
+// mixed types in one launch; batches: launch_batched, one launch per type), the
 // Q5_0 / Q8_0 fallback types on gemv_kernel; a launch whose segments mix the
 // two families is split. n_parts (EPI_RESID) needs a single-segment launch.
 static cudaError_t launch_generic(const GemvArgs& a0, cudaStream_t st, uint32_t* n_parts) {
@@ -371,7 +379,7 @@ cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   } else {
     for (GemvArgs* g : {&q4, &q6}) {
       if (!g->nseg || e != cudaSuccess) continue;
-      e = g->batch == 1 ? launch_gemv_tc(*g, st, n_parts) : launch_gemv_tcb(*g, st, n_parts);
+      e = g->batch == 1 ? launch_gemv_tc(*g, st, n_parts) : launch_batched(*g, st, n_parts);
     }
   }
   if (e == cudaSuccess && other.nseg) e = launch_generic(other, st, n_parts);

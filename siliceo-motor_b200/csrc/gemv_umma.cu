@@ -1,0 +1,739 @@
+// Batched GEMV (2..32 columns: batched decode steps and prefill chunks) of
+// Q4_K / Q6_K weights on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// A CTA tile is 128 output rows (eight 16-row weight tiles, device.cuh) and a
+// K-slice, computed as D[128 x N] += A[128 x 16] B[N x 16] MMAs (M = 128,
+// N = 2 x columns, K = 16) with f32 accumulators in tensor memory:
+//   * a producer warp streams the block units of the eight tiles from HBM
+//     into a ring of shared-memory stages with bulk copies;
+//   * eight row warps (one row per thread, tensor-memory lane = row) turn
+//     the quants into exact f16 integers and store them as the A operand:
+//       Q4_K: sc_s * q                     (sc <= 63, q <= 15: at most 945)
+//       Q6_K: sc_s * ql / 16 and sc_s * qh (two operands of one accumulator:
+//             their sum is sc_s * v / 16 for the stored v = q + 32 = ql +
+//             16 qh, and each stays exact in f16 where sc_s * v would not)
+//     with one LOP3 (mask | 0x6400 exponent) and one HFMA2 per two weights;
+//   * four x warps write x as the B operand: per column and 256-block a
+//     power-of-two scale, then each value as hi + lo f16 rows (22 bits);
+//   * one thread issues the MMAs, and per block one more from shared memory
+//     for the per-sub-block term: A2 = the Q4_K mins m_s or the Q6_K scales
+//     sc_s, B2 = sum of x over sub-block s (times 2^-6);
+//   * after each block the row warps read both accumulators and apply the
+//     block's d / dmin in f32 (dequant.rs:98-126, 178-206):
+//       Q4_K: y += u * (d * D - 64 * dmin * D2)
+//       Q6_K: y += u * d * (16 * D - 2048 * D2)
+//     with u = 1 / (the block's x scale of the column).
+// K orders of A and B agree: item i of a block (weights 8i .. 8i + 7) is K
+// step i / 2 (16 wide), core-matrix half i % 2, in the order 0 2 1 3 4 6 5 7
+// that one mask of a 32-bit quant word yields (weights e, e + 2 per f16x2).
+//
+// Synchronization is by mbarriers, every wait bounded: a wait that gives up
+// sets the launch's error word and a CTA-wide abort flag after which the
+// other waits return at once; the CTA then waits (bounded) for its own MMAs
+// and copies, frees its tensor memory and exits. K-splits end in the
+// deterministic last-arriver fixup of the other GEMVs; epilogues are the
+// fused ones of gemv_common.cuh.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "device.cuh"
+#include "gemv_common.cuh"
+#include "pdl.cuh"
+#include "tc_common.cuh"
+#include "umma.cuh"
+
+namespace sm {
+
+constexpr int UM_RW = 8, UM_XW = 4;  // row warps, x warps
+constexpr int UM_PROD = UM_RW + UM_XW, UM_MMAW = UM_PROD + 1, UM_WARPS = UM_MMAW + 1;
+constexpr int UM_THREADS = UM_WARPS * 32;
+constexpr uint32_t UM_ST = 4;                   // weight stages (blocks) in flight
+constexpr uint32_t UM_MAXB = 32;                // columns
+constexpr uint32_t UM_TILES = 8;                // 16-row weight tiles per CTA tile
+constexpr uint32_t UM_SMEM_MIN = 116u * 1024u;  // one CTA per SM: it holds all of tensor memory
+constexpr uint32_t UM_SMEM_MAX = 227u * 1024u;
+// tensor-memory columns: A operands of two half-blocks, D and D2 of two blocks
+constexpr uint32_t UM_TA = 0, UM_TD = 256, UM_TD2 = 384, UM_TCOLS = 512;
+
+struct UmPlan {
+  uint32_t tiles, groups, ksplit, slice, units, grid, smem;
+};
+
+// Byte offset of row `row`, core-matrix half kc (K 8kc .. 8kc + 7) in a
+// K-major 16-wide operand without swizzle (LBO 128 B, SBO 256 B).
+SM_HD uint32_t um_core(uint32_t row, uint32_t kc) { return (row >> 3) * 256u + kc * 128u + (row & 7u) * 16u; }
+
+// Shared memory: ring[UM_ST][8 tiles] | B[2 blocks] | B2[2] | A2[2] | xs[4][32] | s_in[32]
+template <int NB>
+struct UmSmem {
+  static constexpr uint32_t N = 2 * NB;         // MMA N: a hi and a lo row per column
+  static constexpr uint32_t KSTEP = N * 32;     // B bytes of one 16-wide K step
+  static constexpr uint32_t BBLK = 16 * KSTEP;  // B of one 256-block
+  static constexpr uint32_t B2 = N * 32, A2 = 128 * 32;
+  SM_HD static uint32_t off_b(uint32_t ub) { return (UM_ST * UM_TILES * ub + 1023u) / 1024u * 1024u; }
+  SM_HD static uint32_t off_b2(uint32_t ub) { return off_b(ub) + 2 * BBLK; }
+  SM_HD static uint32_t off_a2(uint32_t ub) { return off_b2(ub) + 2 * B2; }
+  SM_HD static uint32_t off_xs(uint32_t ub) { return off_a2(ub) + 2 * A2; }
+  SM_HD static uint32_t bytes(uint32_t ub) { return off_xs(ub) + 5u * UM_MAXB * 4u; }
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void named_bar(uint32_t id, uint32_t n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// Bounded wait that also gives up at once when the CTA has aborted.
+__device__ __forceinline__ bool um_wait(uint64_t* b, uint32_t parity, uint32_t* err, volatile uint32_t* abort) {
+  for (uint32_t n = 0; n < TC_SPIN_MAX; n++) {
+    if (mbar_try(b, parity)) return true;
+    if (*abort) return false;
+  }
+  *abort = 1u;
+  if (err) atomicOr(err, 1u);
+  return false;
+}
+// Bounded wait for teardown (ignores the abort flag).
+__device__ __forceinline__ void um_drain(uint64_t* b, uint32_t parity, uint32_t* err) {
+  for (uint32_t n = 0; n < TC_SPIN_MAX; n++)
+    if (mbar_try(b, parity)) return;
+  if (err) atomicOr(err, 1u);
+}
+// (w & mask) | 0x6400 in both halves: 1024 + the masked field, as f16.
+__device__ __forceinline__ __half2 um_mag(uint32_t w, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(0x64006400u));  // (a & b) | c
+  return u2h(r);
+}
+__device__ __forceinline__ uint32_t um_fma(__half2 v, __half2 m, __half2 c) { return h2u(__hfma2(v, m, c)); }
+template <int K>
+__device__ __forceinline__ void tmem_ld(uint32_t t, uint32_t (&r)[K]) {
+  if constexpr (K == 8) tmem_ld8(t, r);
+  else if constexpr (K == 16) tmem_ld16(t, r);
+  else tmem_ld32(t, r);
+}
+
+// Q4_K: get_scale_min_k4 (dequant.rs:41-49) of all eight sub-blocks.
+__device__ __forceinline__ void um_q4_scales(const uint4& h, uint32_t (&sc)[8], uint32_t (&mn)[8]) {
+#pragma unroll
+  for (int s = 0; s < 8; s++) {
+    if (s < 4) {
+      sc[s] = (h.y >> (8 * s)) & 63u;
+      mn[s] = (h.z >> (8 * s)) & 63u;
+    } else {
+      const int s4 = 8 * (s - 4);
+      sc[s] = ((h.w >> s4) & 0xFu) | (((h.y >> (s4 + 6)) & 3u) << 4);
+      mn[s] = ((h.w >> (s4 + 4)) & 0xFu) | (((h.z >> (s4 + 6)) & 3u) << 4);
+    }
+  }
+}
+
+// A operand of one half-block for the calling row: Q4_K sub-blocks 2j, 2j + 1
+// (words W[p][c] = qs bytes 32j + 8c + 4p .. + 3). Column sigma*16 + 4c + 2p
+// + b holds weights (8c + 4p + b, + 2) of sub-block 2j + sigma.
+__device__ __forceinline__ void um_q4_a(const uint4 (&W)[2], uint32_t sc0, uint32_t sc1, uint32_t (&A)[32]) {
+  const __half2 m0 = __float2half2_rn((float)sc0), c0 = __float2half2_rn(-1024.f * (float)sc0);
+  const __half2 m1 = __float2half2_rn(0.0625f * (float)sc1), c1 = __float2half2_rn(-64.f * (float)sc1);
+#pragma unroll
+  for (int p = 0; p < 2; p++) {
+    const uint32_t w4[4] = {W[p].x, W[p].y, W[p].z, W[p].w};
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const uint32_t w = w4[c], w8 = w >> 8;
+      A[4 * c + 2 * p + 0] = um_fma(um_mag(w, 0x000F000Fu), m0, c0);
+      A[4 * c + 2 * p + 1] = um_fma(um_mag(w8, 0x000F000Fu), m0, c0);
+      A[16 + 4 * c + 2 * p + 0] = um_fma(um_mag(w, 0x00F000F0u), m1, c1);
+      A[16 + 4 * c + 2 * p + 1] = um_fma(um_mag(w8, 0x00F000F0u), m1, c1);
+    }
+  }
+}
+
+// Q6_K operands of one half-block for the calling row, sub-blocks 4G + sigma:
+// w[a][p] = words (a, G, c = 0, 1, p) (a: W0, W1, H). Column sigma*8 + 4c +
+// 2p + b holds weights (8c + 4p + b, + 2); Al = sc * ql / 16, Ah = sc * qh.
+__device__ __forceinline__ void um_q6_al(const uint2 (&w)[3][2], const int32_t (&sc)[4], uint32_t (&A)[32]) {
+  __half2 m[4], c[4];
+#pragma unroll
+  for (int s = 0; s < 4; s++) {
+    const float f = (float)sc[s];
+    // sigma 0, 1: low nibble (1024 + ql); sigma 2, 3: high nibble (1024 + 16 ql)
+    m[s] = __float2half2_rn(s < 2 ? f * 0.0625f : f * 0.00390625f);
+    c[s] = __float2half2_rn(s < 2 ? -64.f * f : -4.f * f);
+  }
+#pragma unroll
+  for (int p = 0; p < 2; p++)
+#pragma unroll
+    for (int cc = 0; cc < 2; cc++) {
+      const uint32_t w0 = cc ? w[0][p].y : w[0][p].x, w1 = cc ? w[1][p].y : w[1][p].x;
+#pragma unroll
+      for (int b = 0; b < 2; b++) {
+        const uint32_t v0 = b ? w0 >> 8 : w0, v1 = b ? w1 >> 8 : w1;
+        const int col = 4 * cc + 2 * p + b;
+        A[0 * 8 + col] = um_fma(um_mag(v0, 0x000F000Fu), m[0], c[0]);
+        A[1 * 8 + col] = um_fma(um_mag(v1, 0x000F000Fu), m[1], c[1]);
+        A[2 * 8 + col] = um_fma(um_mag(v0, 0x00F000F0u), m[2], c[2]);
+        A[3 * 8 + col] = um_fma(um_mag(v1, 0x00F000F0u), m[3], c[3]);
+      }
+    }
+}
+__device__ __forceinline__ void um_q6_ah(const uint2 (&w)[3][2], const int32_t (&sc)[4], uint32_t (&A)[32]) {
+  // H: bits 0-1 sigma 1 (moved to 2-3), 2-3 sigma 3, 4-5 sigma 0, 6-7 sigma 2
+  __half2 m[4], c[4];
+  const float mul[4] = {0.0625f, 0.25f, 0.015625f, 0.25f}, add[4] = {-64.f, -256.f, -16.f, -256.f};
+#pragma unroll
+  for (int s = 0; s < 4; s++) {
+    m[s] = __float2half2_rn(mul[s] * (float)sc[s]);
+    c[s] = __float2half2_rn(add[s] * (float)sc[s]);
+  }
+#pragma unroll
+  for (int p = 0; p < 2; p++)
+#pragma unroll
+    for (int cc = 0; cc < 2; cc++) {
+      const uint32_t h = cc ? w[2][p].y : w[2][p].x;
+#pragma unroll
+      for (int b = 0; b < 2; b++) {
+        const uint32_t v = b ? h >> 8 : h, v2 = v << 2;
+        const int col = 4 * cc + 2 * p + b;
+        A[0 * 8 + col] = um_fma(um_mag(v, 0x00300030u), m[0], c[0]);
+        A[1 * 8 + col] = um_fma(um_mag(v2, 0x000C000Cu), m[1], c[1]);
+        A[2 * 8 + col] = um_fma(um_mag(v, 0x00C000C0u), m[2], c[2]);
+        A[3 * 8 + col] = um_fma(um_mag(v, 0x000C000Cu), m[3], c[3]);
+      }
+    }
+}
+
+// Epilogue of the calling row for its half of the columns (y[i]: column
+// NB / 2 * e + i, already times the input-norm scale). Every lane calls it.
+template <int NB>
+__device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, uint32_t n_parts, bool valid,
+                                            uint32_t rr, uint32_t e, const float (&y)[NB / 2]) {
+  const int lane = threadIdx.x & 31;
+  uint32_t si = 0;
+  if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
+  if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
+  const GemvSeg& sg = a.seg[si];
+  const uint32_t o = (tile - sg.cta_begin) * 16u + rr;
+  const bool any_resid = a.seg[0].epi == EPI_RESID || (a.nseg > 1 && a.seg[1].epi == EPI_RESID) ||
+                         (a.nseg > 2 && a.seg[2].epi == EPI_RESID);
+#pragma unroll
+  for (int i = 0; i < NB / 2; i++) {
+    const uint32_t col = (NB / 2) * e + i;
+    const float v = y[i], nv = __shfl_xor_sync(0xffffffffu, v, 1);
+    const bool ok = valid && col < a.batch && o < sg.w.n_out;
+    float xv = 0.f;
+    if (epi_is_pair(sg.epi)) {
+      if (ok && !(lane & 1)) epi_pair(a, sg, o, col, v, nv);
+    } else if (ok) {
+      xv = epi_single(a, sg, o, col, v);
+    }
+    if (any_resid) {  // partial sum of x^2 over the tile's 16 rows, per column
+      float s2 = xv * xv;
+      s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, 8);
+      if ((lane & 15) == 0 && valid && col < a.batch && sg.epi == EPI_RESID) a.out_parts[(size_t)col * n_parts + tile] = s2;
+    }
+  }
+}
+
+template <int NB, int QT>
+__global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_constant__ GemvArgs a,
+                                                                  const __grid_constant__ UmPlan p) {
+  using L = UmSmem<NB>;
+  constexpr uint32_t N = L::N, UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT, NH = NB / 2;
+  extern __shared__ __align__(1024) uint8_t um_smem[];
+  __shared__ __align__(8) uint64_t bar_wfull[UM_ST], bar_wempty[UM_ST], bar_bfull[2], bar_afull[2], bar_half[2],
+      bar_dfull[2], bar_xs[4], bar_fin;
+  __shared__ uint32_t s_tmem, s_last;
+  __shared__ uint32_t s_abort_word;
+  volatile uint32_t* abort = &s_abort_word;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = um_smem;
+  uint8_t* bbuf = um_smem + L::off_b(UB);
+  uint8_t* b2buf = um_smem + L::off_b2(UB);
+  uint8_t* a2buf = um_smem + L::off_a2(UB);
+  float* xs = reinterpret_cast<float*>(um_smem + L::off_xs(UB));
+  float* s_in = xs + 4 * UM_MAXB;
+  const uint32_t nb = a.seg[0].w.n_in >> 8;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t k = 0; k < UM_ST; k++) {
+      mbar_init(&bar_wfull[k], 1);
+      mbar_init(&bar_wempty[k], UM_RW * 32);
+    }
+    for (uint32_t k = 0; k < 2; k++) {
+      mbar_init(&bar_bfull[k], UM_XW * 32);
+      mbar_init(&bar_afull[k], UM_RW * 32);
+      mbar_init(&bar_half[k], 1);
+      mbar_init(&bar_dfull[k], 1);
+    }
+    for (uint32_t k = 0; k < 4; k++) mbar_init(&bar_xs[k], UM_XW * 32);
+    mbar_init(&bar_fin, 1);
+    *abort = 0u;
+    fence_mbar_init();
+  }
+  if (warp == UM_MMAW) {
+    tmem_alloc(&s_tmem, UM_TCOLS);
+    tmem_relinquish();
+  }
+  if (warp >= UM_RW && warp < UM_PROD) {  // B2 and A2 start zero (the K positions no sub-block uses stay zero)
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (uint32_t i = threadIdx.x - UM_RW * 32; i < (2 * L::B2 + 2 * L::A2) / 16; i += UM_XW * 32)
+      reinterpret_cast<uint4*>(b2buf)[i] = z;
+    fence_proxy_async();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = s_tmem;
+
+  if (warp == UM_PROD) {
+    // ------------------------------------------------ producer: weight units
+    uint32_t wc = 0;
+    if (lane == 0) {
+      for (uint32_t unit = blockIdx.x; unit < p.units && !*abort; unit += gridDim.x) {
+        const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
+        const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
+        const uint8_t* src[UM_TILES];
+        uint32_t bytes = 0;
+#pragma unroll
+        for (uint32_t tl = 0; tl < UM_TILES; tl++) {
+          const uint32_t tile = rg * UM_TILES + tl;
+          src[tl] = nullptr;
+          if (tile < p.tiles) {
+            uint32_t si = 0;
+            if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
+            if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
+            const DWDesc& w = a.seg[si].w;
+            src[tl] = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
+            bytes += UB;
+          }
+        }
+        for (uint32_t i = 0; i < nblk && !*abort; i++, wc++) {
+          const uint32_t st = wc % UM_ST, k = wc / UM_ST;
+          if (k >= 1) um_wait(&bar_wempty[st], (k - 1) & 1u, a.err, abort);
+          fence_proxy_async();
+          mbar_expect_tx(&bar_wfull[st], bytes);
+#pragma unroll
+          for (uint32_t tl = 0; tl < UM_TILES; tl++)
+            if (src[tl]) bulk_g2s(ring + (st * UM_TILES + tl) * UB, src[tl] + (size_t)(b0 + i) * UB, UB, &bar_wfull[st]);
+        }
+      }
+      // teardown: every copy issued has landed
+      for (uint32_t st = 0; st < UM_ST && st < wc; st++) {
+        const uint32_t uses = (wc - st + UM_ST - 1) / UM_ST;
+        um_drain(&bar_wfull[st], (uses - 1) & 1u, a.err);
+      }
+    }
+  } else if (warp == UM_MMAW) {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(128, N);
+      uint32_t gb = 0;
+      for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
+        const uint32_t ks = unit % p.ksplit, nblk = min(p.slice, nb - ks * p.slice);
+        for (uint32_t i = 0; i < nblk; i++, gb++) {
+          for (uint32_t h = 0; h < 2; h++) {
+            const uint32_t hb = 2 * gb + h;
+            um_wait(&bar_afull[hb & 1], (hb >> 1) & 1u, a.err, abort);
+            if (h == 0) um_wait(&bar_bfull[gb & 1], (gb >> 1) & 1u, a.err, abort);
+            if (*abort) continue;
+            tc_fence_after();
+            const uint32_t ta = tb + UM_TA + 128u * (hb & 1), td = tb + UM_TD + 64u * (gb & 1);
+            const uint32_t bs = smem_u32(bbuf + (gb & 1) * L::BBLK + h * 8 * L::KSTEP);
+#pragma unroll
+            for (uint32_t t = 0; t < 8; t++)
+              umma_ts(td, ta + 8 * t, umma_desc_k(bs + t * L::KSTEP, 128, 256), idesc, (h | t) != 0);
+            if constexpr (QT == 14) {
+#pragma unroll
+              for (uint32_t t = 0; t < 8; t++)
+                umma_ts(td, ta + 64 + 8 * t, umma_desc_k(bs + t * L::KSTEP, 128, 256), idesc, 1u);
+            }
+            if (h == 0)
+              umma_ss(tb + UM_TD2 + 64u * (gb & 1), umma_desc_k(smem_u32(a2buf + (gb & 1) * L::A2), 128, 256),
+                      umma_desc_k(smem_u32(b2buf + (gb & 1) * L::B2), 128, 256), idesc, 0u);
+            umma_commit(&bar_half[hb & 1]);
+            if (h == 1) umma_commit(&bar_dfull[gb & 1]);
+          }
+        }
+      }
+      // teardown: every MMA issued is complete
+      umma_commit(&bar_fin);
+      um_drain(&bar_fin, 0, a.err);
+    }
+  } else if (warp >= UM_RW) {
+    // -------------------------------------------- x warps: B and B2 operands
+    constexpr uint32_t LPC = 128 / NB, IPL = NB / 4;  // lanes per column, 8-value items per lane and block
+    constexpr uint32_t IPS = QT == 12 ? 4 : 2;        // items per sub-block
+    const uint32_t xt = threadIdx.x - UM_RW * 32, c = xt / LPC, u = xt % LPC;
+    pdl_wait();
+    for (uint32_t cc = warp - UM_RW; cc < a.batch; cc += UM_XW) {
+      const float v = input_scale(a, cc);
+      if (lane == 0) s_in[cc] = v;
+    }
+    uint32_t gb = 0;
+    for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
+      const uint32_t ks = unit % p.ksplit, b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
+      for (uint32_t i = 0; i < nblk; i++, gb++) {
+        if (gb >= 2) um_wait(&bar_dfull[gb & 1], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 done
+        float v[IPL][8];
+        const bool live = c < a.batch;
+        const float* xp = a.x + (size_t)c * a.ldx + (size_t)(b0 + i) * 256 + 8 * IPL * u;
+        float mx = 0.f;
+#pragma unroll
+        for (uint32_t j = 0; j < IPL; j++) {
+          float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+          if (live) {
+            lo = ldg4(xp + 8 * j);
+            hi = ldg4(xp + 8 * j + 4);
+          }
+          v[j][0] = lo.x; v[j][1] = lo.y; v[j][2] = lo.z; v[j][3] = lo.w;
+          v[j][4] = hi.x; v[j][5] = hi.y; v[j][6] = hi.z; v[j][7] = hi.w;
+#pragma unroll
+          for (int k = 0; k < 8; k++) mx = fmaxf(mx, fabsf(v[j][k]));
+        }
+#pragma unroll
+        for (uint32_t o = 1; o < LPC; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // the power of two that puts max|x| in [2^14, 2^15)
+        const uint32_t E = (__float_as_uint(mx) >> 23) & 0xFFu;
+        const float scl = E >= 15u ? __uint_as_float((268u - E) << 23) : 1.f;
+        const float inv = E >= 15u ? __uint_as_float((E - 14u) << 23) : 1.f;
+        if (u == 0) xs[(gb & 3) * UM_MAXB + c] = inv;
+        uint8_t* bb = bbuf + (gb & 1) * L::BBLK;
+        uint8_t* b2 = b2buf + (gb & 1) * L::B2;
+        float xsum[IPL / IPS > 0 ? IPL / IPS : 1];
+#pragma unroll
+        for (uint32_t s = 0; s < (IPL / IPS > 0 ? IPL / IPS : 1); s++) xsum[s] = 0.f;
+        float xpart = 0.f;
+#pragma unroll
+        for (uint32_t j = 0; j < IPL; j++) {
+          const uint32_t it = IPL * u + j, T = it >> 1, kc = it & 1;
+          const float w[8] = {v[j][0] * scl, v[j][2] * scl, v[j][1] * scl, v[j][3] * scl,
+                              v[j][4] * scl, v[j][6] * scl, v[j][5] * scl, v[j][7] * scl};
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float ah = hi11(w[2 * q]), bh = hi11(w[2 * q + 1]);
+            hw[q] = h2u(__floats2half2_rn(ah, bh));
+            lw[q] = h2u(__floats2half2_rn(w[2 * q] - ah, w[2 * q + 1] - bh));
+          }
+          *reinterpret_cast<uint4*>(bb + T * L::KSTEP + um_core(2 * c, kc)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(bb + T * L::KSTEP + um_core(2 * c + 1, kc)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          const float s8 = ((w[0] + w[1]) + (w[2] + w[3])) + ((w[4] + w[5]) + (w[6] + w[7]));
+          if constexpr (IPL >= IPS) xsum[j / IPS] += s8;
+          else xpart += s8;
+        }
+        // sub-block sums of the scaled x (times 2^-6) as hi / lo rows of B2, K position = sub-block
+        auto put_sum = [&](uint32_t s, float X) {
+          X *= 0.015625f;
+          const float Xh = hi11(X);
+          const uint32_t off = (s & 7u) * 2u;
+          *reinterpret_cast<__half*>(b2 + um_core(2 * c, s >> 3) + off) = __float2half_rn(Xh);
+          *reinterpret_cast<__half*>(b2 + um_core(2 * c + 1, s >> 3) + off) = __float2half_rn(X - Xh);
+        };
+        if constexpr (IPL >= IPS) {
+#pragma unroll
+          for (uint32_t s = 0; s < IPL / IPS; s++) put_sum((IPL * u) / IPS + s, xsum[s]);
+        } else {  // two lanes share a sub-block
+          xpart += __shfl_xor_sync(0xffffffffu, xpart, 1);
+          if (!(u & 1)) put_sum((IPL * u) / IPS, xpart);
+        }
+        fence_proxy_async();  // the operands are read by the tensor cores (async proxy)
+        mbar_arrive(&bar_bfull[gb & 1]);
+        mbar_arrive(&bar_xs[gb & 3]);
+      }
+    }
+  } else {
+    // ---------------------------------- row warps: A operands, epilogues
+    const uint32_t q = warp & 3, e = warp >> 2, m = 32 * q + lane, tl = m >> 4, rr = m & 15;
+    const uint32_t tlane = (32u * q) << 16;
+    pdl_wait();
+    uint32_t wc = 0, gb = 0;
+    float dcur = 0.f, mcur = 0.f;  // d, dmin (Q4_K) of the block being multiplied
+    // the accumulators of block g into y
+    auto drain = [&](uint32_t g, float d, float dm, float (&y)[NH]) {
+      um_wait(&bar_dfull[g & 1], (g >> 1) & 1u, a.err, abort);
+      um_wait(&bar_xs[g & 3], (g >> 2) & 1u, a.err, abort);
+      tc_fence_after();
+      uint32_t dr[NB], d2r[NB];
+      tmem_ld<NB>(tb + tlane + UM_TD + 64u * (g & 1) + NB * e, dr);
+      tmem_ld<NB>(tb + tlane + UM_TD2 + 64u * (g & 1) + NB * e, d2r);
+      tmem_wait_ld();
+      const float* uu = xs + (g & 3) * UM_MAXB + NH * e;
+#pragma unroll
+      for (uint32_t i = 0; i < NH; i++) {
+        const float D = __uint_as_float(dr[2 * i]) + __uint_as_float(dr[2 * i + 1]);
+        const float D2 = __uint_as_float(d2r[2 * i]) + __uint_as_float(d2r[2 * i + 1]);
+        if constexpr (QT == 12) y[i] = fmaf(uu[i], fmaf(d, D, -64.f * dm * D2), y[i]);
+        else y[i] = fmaf(uu[i] * d, fmaf(16.f, D, -2048.f * D2), y[i]);
+      }
+      tc_fence_before();
+    };
+    for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
+      const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
+      const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0), tile = rg * UM_TILES + tl;
+      float y[NH];
+#pragma unroll
+      for (uint32_t i = 0; i < NH; i++) y[i] = 0.f;
+      for (uint32_t i = 0; i < nblk; i++, gb++, wc++) {
+        const uint32_t st = wc % UM_ST;
+        um_wait(&bar_wfull[st], (wc / UM_ST) & 1u, a.err, abort);
+        const uint8_t* un = ring + (st * UM_TILES + tl) * UB;
+        const uint4 hd = *reinterpret_cast<const uint4*>(un + 16 * rr);
+        float dn, mn_ = 0.f;
+        uint4 W4[2][2];   // Q4_K: [half][p]
+        uint2 W6[2][3][2];  // Q6_K: [half][array][p]
+        uint32_t d6 = 0;
+        if constexpr (QT == 12) {
+#pragma unroll
+          for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int pp = 0; pp < 2; pp++)
+              W4[h][pp] = *reinterpret_cast<const uint4*>(un + q4t_word_off(rr, 2 * h + e, 0, pp));
+        } else {
+#pragma unroll
+          for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int ar = 0; ar < 3; ar++)
+#pragma unroll
+              for (int pp = 0; pp < 2; pp++)
+                W6[h][ar][pp] = *reinterpret_cast<const uint2*>(un + q6t_word_off(rr, ar, 2 * h + e, 0, pp));
+          d6 = *reinterpret_cast<const unsigned short*>(un + 256 + 2 * rr);
+        }
+        mbar_arrive(&bar_wempty[st]);  // the stage's bytes this row needs are in registers
+        uint32_t s4[8], m4[8];
+        int32_t s6[16];
+        if constexpr (QT == 12) {
+          um_q4_scales(hd, s4, m4);
+          dn = h2f_ref(hd.x & 0xFFFFu);
+          mn_ = h2f_ref(hd.x >> 16);
+        } else {
+          const uint32_t hw[4] = {hd.x, hd.y, hd.z, hd.w};
+#pragma unroll
+          for (int s = 0; s < 16; s++) s6[s] = (int32_t)(int8_t)((hw[s >> 2] >> (8 * (s & 3))) & 0xFFu);
+          dn = q6_d(d6);
+        }
+        for (uint32_t h = 0; h < 2; h++) {
+          const uint32_t hb = 2 * gb + h;
+          if (hb >= 2) um_wait(&bar_half[hb & 1], ((hb >> 1) + 1) & 1u, a.err, abort);  // half-block hb - 2 done
+          const uint32_t ta = tb + tlane + UM_TA + 128u * (hb & 1) + 32u * e;
+          if (h == 0 && e == 0) {  // per-block term operand A2 (row m)
+            uint8_t* a2 = a2buf + (gb & 1) * L::A2;
+            if constexpr (QT == 12) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int k = 0; k < 4; k++) pk[k] = h2u(__floats2half2_rn((float)m4[2 * k], (float)m4[2 * k + 1]));
+              *reinterpret_cast<uint4*>(a2 + um_core(m, 0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            } else {
+              uint32_t pk[8];
+#pragma unroll
+              for (int k = 0; k < 8; k++) pk[k] = h2u(__floats2half2_rn((float)s6[2 * k], (float)s6[2 * k + 1]));
+              *reinterpret_cast<uint4*>(a2 + um_core(m, 0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              *reinterpret_cast<uint4*>(a2 + um_core(m, 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            }
+            fence_proxy_async();
+          }
+          uint32_t A[32];
+          if constexpr (QT == 12) {
+            const uint32_t j = 2 * h + e;
+            um_q4_a(W4[h], s4[2 * j], s4[2 * j + 1], A);
+            tmem_st32(ta, A);
+          } else {
+            const uint32_t G = 2 * h + e;
+            const int32_t sc[4] = {s6[4 * G], s6[4 * G + 1], s6[4 * G + 2], s6[4 * G + 3]};
+            um_q6_al(W6[h], sc, A);
+            tmem_st32(ta, A);
+            um_q6_ah(W6[h], sc, A);
+            tmem_st32(ta + 64, A);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bar_afull[hb & 1]);
+        }
+        if (i >= 1) drain(gb - 1, dcur, mcur, y);
+        dcur = dn;
+        mcur = mn_;
+      }
+      drain(gb - 1, dcur, mcur, y);
+      // input-norm scale of each column
+#pragma unroll
+      for (uint32_t i = 0; i < NH; i++) {
+        const uint32_t col = NH * e + i;
+        y[i] *= col < a.batch ? s_in[col] : 0.f;
+      }
+      const bool valid = tile < p.tiles;
+      if (p.ksplit == 1) {
+        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, e, y);
+        continue;
+      }
+      // K-split: publish this slice; the last CTA of the group sums the slices in order
+      const size_t stride = (size_t)p.tiles * 16u * a.batch;
+      if (valid) {
+#pragma unroll
+        for (uint32_t i = 0; i < NH; i++) {
+          const uint32_t col = NH * e + i;
+          if (col < a.batch) a.ks_part[ks * stride + ((size_t)tile * 16u + rr) * a.batch + col] = y[i];
+        }
+      }
+      __threadfence();
+      named_bar(1, UM_RW * 32);
+      if (threadIdx.x == 0) s_last = atomicAdd(&a.ks_cnt[rg], 1u) == p.ksplit - 1;
+      named_bar(1, UM_RW * 32);
+      if (s_last) {
+        __threadfence();
+#pragma unroll
+        for (uint32_t i = 0; i < NH; i++) {
+          const uint32_t col = NH * e + i;
+          float s = 0.f;
+          if (valid && col < a.batch)
+            for (uint32_t k = 0; k < p.ksplit; k++)
+              s += __ldcg(a.ks_part + k * stride + ((size_t)tile * 16u + rr) * a.batch + col);
+          y[i] = s;
+        }
+        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, e, y);
+        if (threadIdx.x == 0) a.ks_cnt[rg] = 0;  // ready for the next launch
+      }
+    }
+  }
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == UM_MMAW) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tb, UM_TCOLS);
+  }
+}
+
+// ------------------------------------------------------------- host ----
+namespace {
+
+using UmKernel = void (*)(GemvArgs, UmPlan);
+
+UmKernel um_kernel(uint32_t nb8, uint32_t qt) {
+  switch (nb8 * 100 + qt) {
+    case 812: return gemv_umma_kernel<8, 12>;
+    case 814: return gemv_umma_kernel<8, 14>;
+    case 1612: return gemv_umma_kernel<16, 12>;
+    case 1614: return gemv_umma_kernel<16, 14>;
+    case 3212: return gemv_umma_kernel<32, 12>;
+    case 3214: return gemv_umma_kernel<32, 14>;
+  }
+  return nullptr;
+}
+uint32_t um_nb8(uint32_t batch) { return batch <= 8 ? 8 : batch <= 16 ? 16 : 32; }
+uint32_t um_smem_for(uint32_t nb8, uint32_t ub) {
+  const uint32_t b = nb8 == 8 ? UmSmem<8>::bytes(ub) : nb8 == 16 ? UmSmem<16>::bytes(ub) : UmSmem<32>::bytes(ub);
+  return std::max(b, UM_SMEM_MIN);
+}
+
+constexpr int UM_MAX_DEVICES = 64;
+std::mutex g_um_mu;
+int g_um_sms[UM_MAX_DEVICES] = {};
+
+cudaError_t um_setup(uint32_t* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= UM_MAX_DEVICES) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_um_mu);
+  if (!g_um_sms[dev]) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    for (uint32_t nb8 : {8u, 16u, 32u})
+      for (uint32_t qt : {12u, 14u})
+        if (e == cudaSuccess)
+          e = cudaFuncSetAttribute(um_kernel(nb8, qt), cudaFuncAttributeMaxDynamicSharedMemorySize, UM_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    g_um_sms[dev] = n;
+  }
+  *sms = (uint32_t)g_um_sms[dev];
+  return cudaSuccess;
+}
+
+// One weight type for every segment, batch 2..32, whole 256-blocks.
+bool um_ok(const GemvArgs& a) {
+  if (a.batch < 2 || a.batch > UM_MAXB || !a.nseg) return false;
+  const uint32_t qt = a.seg[0].w.type;
+  if (!tiled_type(qt)) return false;
+  for (uint32_t i = 0; i < a.nseg; i++)
+    if (a.seg[i].w.type != qt || a.seg[i].w.n_in != a.seg[0].w.n_in) return false;
+  return (a.ldx & 3u) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0;
+}
+
+// CTA tiles of 128 rows and a K-split that minimizes rounds of units x
+// (blocks per unit + 2 blocks of per-unit cost), bounded by the scratch.
+bool um_plan(GemvArgs& a, uint32_t sms, UmPlan* p) {
+  uint32_t tiles = 0;
+  for (uint32_t i = 0; i < a.nseg; i++) {
+    a.seg[i].cta_begin = tiles;
+    tiles += (a.seg[i].w.n_out + 15) / 16;
+  }
+  const uint32_t nb = a.seg[0].w.n_in >> 8, groups = (tiles + UM_TILES - 1) / UM_TILES;
+  const uint32_t ub = tile_unit_bytes(a.seg[0].w.type);
+  const uint32_t smem = um_smem_for(um_nb8(a.batch), ub);
+  if (smem > UM_SMEM_MAX || nb == 0) return false;
+  auto fits = [&](uint32_t k) {
+    return k == 1 || (a.ks_part && a.ks_cnt && (uint64_t)k * tiles * 16u * a.batch <= a.ks_part_cap &&
+                      groups <= a.ks_cnt_cap);
+  };
+  uint32_t ks = 0;
+  uint64_t best = ~0ull;
+  for (uint32_t k = 1; k <= std::min(nb, 64u); k++) {
+    const uint32_t sl = (nb + k - 1) / k, kk = (nb + sl - 1) / sl;
+    if (!fits(kk)) continue;
+    const uint64_t rounds = ((uint64_t)groups * kk + sms - 1) / sms;
+    if (rounds * (sl + 2) < best) {
+      best = rounds * (sl + 2);
+      ks = kk;
+    }
+  }
+  if (!ks) return false;
+  p->tiles = tiles;
+  p->groups = groups;
+  p->ksplit = ks;
+  p->slice = (nb + ks - 1) / ks;
+  p->units = groups * ks;
+  p->grid = std::min(p->units, sms);
+  p->smem = smem;
+  return true;
+}
+
+}  // namespace
+
+cudaError_t gemv_umma_prepare() {
+  uint32_t sms = 0;
+  return um_setup(&sms);
+}
+
+// cudaErrorNotSupported: no plan fits (use another kernel). n_parts: the
+// per-column partials an EPI_RESID launch writes (one per 16-row tile).
+cudaError_t launch_gemv_umma(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
+  if (!um_ok(a)) return cudaErrorNotSupported;
+  uint32_t sms = 0;
+  cudaError_t e = um_setup(&sms);
+  if (e != cudaSuccess) return e;
+  UmPlan p;
+  if (!um_plan(a, sms, &p)) return cudaErrorNotSupported;
+  if (n_parts) *n_parts = p.tiles;
+  return launch_pdl(um_kernel(um_nb8(a.batch), a.seg[0].w.type), dim3(p.grid), dim3(UM_THREADS), p.smem, st, a, p);
+}
+
+void gemv_umma_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt) {
+  a.ks_part = reinterpret_cast<float*>(16);
+  a.ks_cnt = reinterpret_cast<uint32_t*>(16);
+  a.ks_part_cap = 0xFFFFFFFFu;
+  a.ks_cnt_cap = 0xFFFFFFFFu;
+  *part = 0;
+  *cnt = 0;
+  UmPlan p;
+  if (!um_ok(a) || !um_plan(a, sms, &p) || p.ksplit == 1) return;
+  *part = (uint64_t)p.ksplit * p.tiles * 16u * a.batch;
+  *cnt = p.groups;
+}
+
+}  // namespace sm

@@ -47,6 +47,10 @@ void gemv_tc_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cn
 // of gemv_tcb.cu (a.batch columns).
 cudaError_t gemv_tcb_prepare();
 void gemv_tcb_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt);
+// The same for the tcgen05 batched GEMV of gemv_umma.cu, which launch_gemv
+// uses for batches of 2..32 (gemv_tcb.cu when no plan of it fits).
+cudaError_t gemv_umma_prepare();
+void gemv_umma_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt);
 cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
                                  uint32_t cap_steps, cudaStream_t st);
 
