@@ -174,6 +174,10 @@ struct GemvArgs {
   float* ks_part;
   uint32_t* ks_cnt;
   uint32_t ks_part_cap, ks_cnt_cap;
+  // Scratch of the tcgen05 batched GEMV: x converted once per launch into
+  // the shared-memory image of its B operand (may be null: another kernel runs).
+  uint8_t* xblob;
+  uint64_t xblob_cap;  // bytes
   // Set non-zero by a kernel whose bounded wait gave up (the launch's results
   // are then not valid); may be null.
   uint32_t* err;

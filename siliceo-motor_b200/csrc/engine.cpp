@@ -250,6 +250,9 @@ struct sm_model {
   float* ks_part = nullptr;
   uint32_t* ks_cnt = nullptr;
   uint32_t ks_part_cap = 0, ks_cnt_cap = 0;
+  // x images of the tcgen05 batched GEMV (one launch at a time, stream order)
+  uint8_t* xblob = nullptr;
+  uint64_t xblob_cap = 0;
   // partial sums of x^2 written by residual GEMVs, read by the next GEMV
   float *parts_a = nullptr, *parts_b = nullptr;
   uint32_t parts_cap = 0;
@@ -624,6 +627,9 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
         (rc = dev_alloc(m, (void**)&m->ks_cnt, (size_t)m->ks_cnt_cap * 4)))
       return rc;
     CK(cudaMemset(m->ks_cnt, 0, (size_t)m->ks_cnt_cap * 4));
+    for (uint32_t n_in : {(uint32_t)H, m->qd, m->fl})
+      m->xblob_cap = std::max(m->xblob_cap, gemv_umma_blob_bytes(n_in, R));
+    if ((rc = dev_alloc(m, (void**)&m->xblob, (size_t)m->xblob_cap))) return rc;
     m->parts_cap = (uint32_t)(H / 4 + 64);
     if ((rc = dev_alloc(m, (void**)&m->parts_a, (size_t)R * m->parts_cap * 4)) ||
         (rc = dev_alloc(m, (void**)&m->parts_b, (size_t)R * m->parts_cap * 4)))
@@ -726,6 +732,8 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   base.ks_cnt = m->ks_cnt;
   base.ks_part_cap = m->ks_part_cap;
   base.ks_cnt_cap = m->ks_cnt_cap;
+  base.xblob = m->xblob;
+  base.xblob_cap = m->xblob_cap;
   base.err = m->dout.err;
   RK(launch_embed_norm(m->tok_embd.d, m->din.tok, nrows, m->x, H, m->layers[0].attn_norm, m->xn, H, m->parts_a, st));
   uint32_t np_a = 1, np_b = 0;
@@ -1482,6 +1490,9 @@ struct sm_dweight {
   float* ks_part = nullptr;
   uint32_t* ks_cnt = nullptr;
   uint32_t ks_part_cap = 0, ks_cnt_cap = 0;
+  // x image of its batched tcgen05 GEMV (up to 32 columns)
+  uint8_t* xblob = nullptr;
+  uint64_t xblob_cap = 0;
 };
 
 int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t n_in, sm_dweight** out) {
@@ -1524,6 +1535,16 @@ int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t
     w->ks_part_cap = (uint32_t)need_part;
     w->ks_cnt_cap = need_cnt;
   }
+  if (tiled_type(w->w.d.type)) {
+    w->xblob_cap = gemv_umma_blob_bytes(w->w.d.n_in, 32);
+    if (cudaMalloc((void**)&w->xblob, w->xblob_cap) != cudaSuccess) {
+      cudaGetLastError();
+      w->xblob = nullptr;
+      sm_dweight_free(w);
+      set_error("cudaMalloc failed for the GEMV scratch");
+      return SM_ERR_OOM;
+    }
+  }
   *out = w;
   return SM_OK;
 }
@@ -1531,6 +1552,7 @@ int sm_dweight_free(sm_dweight* w) {
   if (!w) return SM_OK;
   if (w->ks_part) cudaFree(w->ks_part);
   if (w->ks_cnt) cudaFree(w->ks_cnt);
+  if (w->xblob) cudaFree(w->xblob);
   free_weight(w->w);
   delete w;
   return SM_OK;
@@ -1559,6 +1581,8 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
   a.ks_cnt = w->ks_cnt;
   a.ks_part_cap = w->ks_part_cap;
   a.ks_cnt_cap = w->ks_cnt_cap;
+  a.xblob = w->xblob;
+  a.xblob_cap = w->xblob_cap;
   CK(launch_gemv(a, (cudaStream_t)stream));
   return SM_OK;
 }

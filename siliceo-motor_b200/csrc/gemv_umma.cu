@@ -4,8 +4,13 @@
 // A CTA tile is 128 output rows (eight 16-row weight tiles, device.cuh) and a
 // K-slice, computed as D[128 x N] += A[128 x 16] B[N x 16] MMAs (M = 128,
 // N = 2 x columns, K = 16) with f32 accumulators in tensor memory:
-//   * a producer warp streams the block units of the eight tiles from HBM
-//     into a ring of shared-memory stages with bulk copies;
+//   * a prep kernel converts x once per launch into the shared-memory image
+//     of the B operand (per column and 256-block a power-of-two scale, each
+//     value as hi + lo f16 rows: 22 bits), plus the per-sub-block sums of x
+//     and the input-norm scales; a producer warp bulk-copies that image block
+//     by block into a ring of shared-memory slots;
+//   * a second producer warp streams the block units of the eight weight
+//     tiles from HBM into a ring of stages;
 //   * eight row warps (one row per thread, tensor-memory lane = row) turn
 //     the quants into exact f16 integers and store them as the A operand:
 //       Q4_K: sc_s * q                     (sc <= 63, q <= 15: at most 945)
@@ -13,11 +18,9 @@
 //             their sum is sc_s * v / 16 for the stored v = q + 32 = ql +
 //             16 qh, and each stays exact in f16 where sc_s * v would not)
 //     with one LOP3 (mask | 0x6400 exponent) and one HFMA2 per two weights;
-//   * four x warps write x as the B operand: per column and 256-block a
-//     power-of-two scale, then each value as hi + lo f16 rows (22 bits);
-//   * one thread issues the MMAs, and per block one more from shared memory
-//     for the per-sub-block term: A2 = the Q4_K mins m_s or the Q6_K scales
-//     sc_s, B2 = sum of x over sub-block s (times 2^-6);
+//   * one thread issues the MMAs, and per block one more with both operands
+//     in shared memory for the per-sub-block term: A2 = the Q4_K mins m_s or
+//     the Q6_K scales sc_s, B2 = sum of x over sub-block s (times 2^-6);
 //   * after each block the row warps read both accumulators and apply the
 //     block's d / dmin in f32 (dequant.rs:98-126, 178-206):
 //       Q4_K: y += u * (d * D - 64 * dmin * D2)
@@ -46,16 +49,18 @@
 
 namespace sm {
 
-constexpr int UM_RW = 8, UM_XW = 4;  // row warps, x warps
-constexpr int UM_PROD = UM_RW + UM_XW, UM_MMAW = UM_PROD + 1, UM_WARPS = UM_MMAW + 1;
+uint64_t gemv_umma_blob_bytes(uint32_t n_in, uint32_t batch);
+
+constexpr int UM_RW = 8;  // row warps
+constexpr int UM_BPW = UM_RW, UM_PROD = UM_RW + 1, UM_MMAW = UM_RW + 2, UM_WARPS = UM_RW + 3;
 constexpr int UM_THREADS = UM_WARPS * 32;
-constexpr uint32_t UM_ST = 4;                   // weight stages (blocks) in flight
 constexpr uint32_t UM_MAXB = 32;                // columns
 constexpr uint32_t UM_TILES = 8;                // 16-row weight tiles per CTA tile
 constexpr uint32_t UM_SMEM_MIN = 116u * 1024u;  // one CTA per SM: it holds all of tensor memory
-constexpr uint32_t UM_SMEM_MAX = 227u * 1024u;
+constexpr uint32_t UM_SMEM_MAX = 225u * 1024u;  // with the static part, within the 227 KB opt-in
 // tensor-memory columns: A operands of two half-blocks, D and D2 of two blocks
 constexpr uint32_t UM_TA = 0, UM_TD = 256, UM_TD2 = 384, UM_TCOLS = 512;
+constexpr uint32_t UM_XPREP_THREADS = 128;
 
 struct UmPlan {
   uint32_t tiles, groups, ksplit, slice, units, grid, smem;
@@ -65,18 +70,29 @@ struct UmPlan {
 // K-major 16-wide operand without swizzle (LBO 128 B, SBO 256 B).
 SM_HD uint32_t um_core(uint32_t row, uint32_t kc) { return (row >> 3) * 256u + kc * 128u + (row & 7u) * 16u; }
 
-// Shared memory: ring[UM_ST][8 tiles] | B[2 blocks] | B2[2] | A2[2] | xs[4][32] | s_in[32]
+// The B image of one 256-block (NB columns, padded to 8 / 16 / 32):
+// [16 K steps x N rows x 16 K f16][B2: N rows x 16][u: 32 f32]; the whole
+// launch's image is nb of them followed by the input-norm scales (32 f32).
 template <int NB>
+struct UmBlob {
+  static constexpr uint32_t N = 2 * NB;  // MMA N: a hi and a lo row per column
+  static constexpr uint32_t KSTEP = N * 32, B2 = N * 32;
+  static constexpr uint32_t OFF_B2 = 16 * KSTEP, OFF_U = OFF_B2 + B2, BLK = OFF_U + UM_MAXB * 4;
+  static constexpr uint32_t SLOTS = NB == 32 ? 3 : 4;  // shared-memory ring
+};
+// Weight stages in flight per type.
+template <int QT>
+struct UmW {
+  static constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT, STAGES = QT == 12 ? 4 : 3;
+  static constexpr uint32_t BYTES = STAGES * UM_TILES * UB;
+};
+// Shared memory: weight stages | B slots | A2[2] (128 rows x 16 K f16)
+template <int NB, int QT>
 struct UmSmem {
-  static constexpr uint32_t N = 2 * NB;         // MMA N: a hi and a lo row per column
-  static constexpr uint32_t KSTEP = N * 32;     // B bytes of one 16-wide K step
-  static constexpr uint32_t BBLK = 16 * KSTEP;  // B of one 256-block
-  static constexpr uint32_t B2 = N * 32, A2 = 128 * 32;
-  SM_HD static uint32_t off_b(uint32_t ub) { return (UM_ST * UM_TILES * ub + 1023u) / 1024u * 1024u; }
-  SM_HD static uint32_t off_b2(uint32_t ub) { return off_b(ub) + 2 * BBLK; }
-  SM_HD static uint32_t off_a2(uint32_t ub) { return off_b2(ub) + 2 * B2; }
-  SM_HD static uint32_t off_xs(uint32_t ub) { return off_a2(ub) + 2 * A2; }
-  SM_HD static uint32_t bytes(uint32_t ub) { return off_xs(ub) + 5u * UM_MAXB * 4u; }
+  static constexpr uint32_t OFF_B = (UmW<QT>::BYTES + 1023u) / 1024u * 1024u;
+  static constexpr uint32_t OFF_A2 = OFF_B + UmBlob<NB>::SLOTS * UmBlob<NB>::BLK;
+  static constexpr uint32_t A2 = 128 * 32;
+  static constexpr uint32_t BYTES = OFF_A2 + 2 * A2;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
@@ -239,38 +255,128 @@ __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, ui
   }
 }
 
+// ------------------------------------------------------- x prep kernel ----
+// One CTA per 256-block: the B image of x[:, 256 b .. 256 b + 255] for all
+// padded columns (column c: lanes c * LPC .. + LPC - 1, each IPL items of 8
+// consecutive values). CTA 0 also writes the input-norm scales.
+template <int NB, int QT>
+__global__ void __launch_bounds__(UM_XPREP_THREADS) umma_xprep_kernel(const __grid_constant__ GemvArgs a, uint32_t nb) {
+  using L = UmBlob<NB>;
+  constexpr uint32_t LPC = UM_XPREP_THREADS / NB, IPL = NB / 4;  // lanes per column, items per lane
+  constexpr uint32_t IPS = QT == 12 ? 4 : 2;                    // items per sub-block
+  constexpr uint32_t NXS = IPL / IPS > 0 ? IPL / IPS : 1;
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t blk = blockIdx.x, xt = threadIdx.x, c = xt / LPC, u = xt % LPC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* out = a.xblob + (size_t)blk * L::BLK;
+  if (blk == 0) {
+    float* s_in = reinterpret_cast<float*>(a.xblob + (size_t)nb * L::BLK);
+    for (uint32_t cc = warp; cc < a.batch; cc += UM_XPREP_THREADS / 32) {
+      const float v = input_scale(a, cc);
+      if (lane == 0) s_in[cc] = v;
+    }
+  }
+  float v[IPL][8];
+  const bool live = c < a.batch;
+  const float* xp = a.x + (size_t)c * a.ldx + (size_t)blk * 256 + 8 * IPL * u;
+  float mx = 0.f;
+#pragma unroll
+  for (uint32_t j = 0; j < IPL; j++) {
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (live) {
+      lo = ldg4(xp + 8 * j);
+      hi = ldg4(xp + 8 * j + 4);
+    }
+    v[j][0] = lo.x; v[j][1] = lo.y; v[j][2] = lo.z; v[j][3] = lo.w;
+    v[j][4] = hi.x; v[j][5] = hi.y; v[j][6] = hi.z; v[j][7] = hi.w;
+#pragma unroll
+    for (int k = 0; k < 8; k++) mx = fmaxf(mx, fabsf(v[j][k]));
+  }
+#pragma unroll
+  for (uint32_t o = 1; o < LPC; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  // the power of two that puts max|x| in [2^14, 2^15)
+  const uint32_t E = (__float_as_uint(mx) >> 23) & 0xFFu;
+  const float scl = E >= 15u ? __uint_as_float((268u - E) << 23) : 1.f;
+  const float inv = E >= 15u ? __uint_as_float((E - 14u) << 23) : 1.f;
+  if (u == 0) reinterpret_cast<float*>(out + L::OFF_U)[c] = inv;
+  float xsum[NXS];
+#pragma unroll
+  for (uint32_t s = 0; s < NXS; s++) xsum[s] = 0.f;
+  float xpart = 0.f;
+#pragma unroll
+  for (uint32_t j = 0; j < IPL; j++) {
+    const uint32_t it = IPL * u + j, T = it >> 1, kc = it & 1;
+    const float w[8] = {v[j][0] * scl, v[j][2] * scl, v[j][1] * scl, v[j][3] * scl,
+                        v[j][4] * scl, v[j][6] * scl, v[j][5] * scl, v[j][7] * scl};
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float ah = hi11(w[2 * q]), bh = hi11(w[2 * q + 1]);
+      hw[q] = h2u(__floats2half2_rn(ah, bh));
+      lw[q] = h2u(__floats2half2_rn(w[2 * q] - ah, w[2 * q + 1] - bh));
+    }
+    *reinterpret_cast<uint4*>(out + T * L::KSTEP + um_core(2 * c, kc)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(out + T * L::KSTEP + um_core(2 * c + 1, kc)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    const float s8 = ((w[0] + w[1]) + (w[2] + w[3])) + ((w[4] + w[5]) + (w[6] + w[7]));
+    if constexpr (IPL >= IPS) xsum[j / IPS] += s8;
+    else xpart += s8;
+  }
+  // B2: sub-block sums of the scaled x times 2^-6, hi / lo rows, K position = sub-block
+  uint8_t* b2 = out + L::OFF_B2;
+  if (QT == 12 && u == 0) {  // Q4_K has 8 sub-blocks: K 8..15 are zero
+    *reinterpret_cast<uint4*>(b2 + um_core(2 * c, 1)) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(b2 + um_core(2 * c + 1, 1)) = make_uint4(0, 0, 0, 0);
+  }
+  auto put_sum = [&](uint32_t s, float X) {
+    X *= 0.015625f;
+    const float Xh = hi11(X);
+    const uint32_t off = (s & 7u) * 2u;
+    *reinterpret_cast<__half*>(b2 + um_core(2 * c, s >> 3) + off) = __float2half_rn(Xh);
+    *reinterpret_cast<__half*>(b2 + um_core(2 * c + 1, s >> 3) + off) = __float2half_rn(X - Xh);
+  };
+  if constexpr (IPL >= IPS) {
+#pragma unroll
+    for (uint32_t s = 0; s < NXS; s++) put_sum((IPL * u) / IPS + s, xsum[s]);
+  } else {  // two lanes share a sub-block
+    xpart += __shfl_xor_sync(0xffffffffu, xpart, 1);
+    if (!(u & 1)) put_sum((IPL * u) / IPS, xpart);
+  }
+}
+
 template <int NB, int QT>
 __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_constant__ GemvArgs a,
                                                                   const __grid_constant__ UmPlan p) {
-  using L = UmSmem<NB>;
-  constexpr uint32_t N = L::N, UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT, NH = NB / 2;
+  using XB = UmBlob<NB>;
+  using W = UmW<QT>;
+  using L = UmSmem<NB, QT>;
+  constexpr uint32_t N = XB::N, UB = W::UB, WS = W::STAGES, BS = XB::SLOTS, NH = NB / 2;
   extern __shared__ __align__(1024) uint8_t um_smem[];
-  __shared__ __align__(8) uint64_t bar_wfull[UM_ST], bar_wempty[UM_ST], bar_bfull[2], bar_afull[2], bar_half[2],
-      bar_dfull[2], bar_xs[4], bar_fin;
+  __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[2],
+      bar_half[2], bar_dfull[2], bar_fin;
   __shared__ uint32_t s_tmem, s_last;
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring = um_smem;
-  uint8_t* bbuf = um_smem + L::off_b(UB);
-  uint8_t* b2buf = um_smem + L::off_b2(UB);
-  uint8_t* a2buf = um_smem + L::off_a2(UB);
-  float* xs = reinterpret_cast<float*>(um_smem + L::off_xs(UB));
-  float* s_in = xs + 4 * UM_MAXB;
+  uint8_t* bring = um_smem + L::OFF_B;
+  uint8_t* a2buf = um_smem + L::OFF_A2;
   const uint32_t nb = a.seg[0].w.n_in >> 8;
 
   if (threadIdx.x == 0) {
-    for (uint32_t k = 0; k < UM_ST; k++) {
+    for (uint32_t k = 0; k < WS; k++) {
       mbar_init(&bar_wfull[k], 1);
       mbar_init(&bar_wempty[k], UM_RW * 32);
     }
+    for (uint32_t k = 0; k < BS; k++) {
+      mbar_init(&bar_bfull[k], 1);
+      mbar_init(&bar_bfree[k], UM_RW * 32);
+    }
     for (uint32_t k = 0; k < 2; k++) {
-      mbar_init(&bar_bfull[k], UM_XW * 32);
       mbar_init(&bar_afull[k], UM_RW * 32);
       mbar_init(&bar_half[k], 1);
       mbar_init(&bar_dfull[k], 1);
     }
-    for (uint32_t k = 0; k < 4; k++) mbar_init(&bar_xs[k], UM_XW * 32);
     mbar_init(&bar_fin, 1);
     *abort = 0u;
     fence_mbar_init();
@@ -279,10 +385,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     tmem_alloc(&s_tmem, UM_TCOLS);
     tmem_relinquish();
   }
-  if (warp >= UM_RW && warp < UM_PROD) {  // B2 and A2 start zero (the K positions no sub-block uses stay zero)
+  if (warp < UM_RW) {  // A2 starts zero (Q4_K: K 8..15 stay zero)
     const uint4 z = make_uint4(0, 0, 0, 0);
-    for (uint32_t i = threadIdx.x - UM_RW * 32; i < (2 * L::B2 + 2 * L::A2) / 16; i += UM_XW * 32)
-      reinterpret_cast<uint4*>(b2buf)[i] = z;
+    for (uint32_t i = threadIdx.x; i < 2 * L::A2 / 16; i += UM_RW * 32) reinterpret_cast<uint4*>(a2buf)[i] = z;
     fence_proxy_async();
   }
   pdl_trigger();
@@ -291,9 +396,13 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   tc_fence_after();
   const uint32_t tb = s_tmem;
 
-  if (warp == UM_PROD) {
-    // ------------------------------------------------ producer: weight units
-    uint32_t wc = 0;
+  if (warp == UM_PROD || warp == UM_BPW) {
+    // ---------------------- producers: weight units / B images (bulk copies)
+    const bool wprod = warp == UM_PROD;
+    if (!wprod) pdl_wait();  // the B images come from the prep kernel
+    const uint32_t S = wprod ? WS : BS;
+    uint64_t* full = wprod ? bar_wfull : bar_bfull;
+    uint32_t cnt = 0;
     if (lane == 0) {
       for (uint32_t unit = blockIdx.x; unit < p.units && !*abort; unit += gridDim.x) {
         const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
@@ -304,7 +413,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
         for (uint32_t tl = 0; tl < UM_TILES; tl++) {
           const uint32_t tile = rg * UM_TILES + tl;
           src[tl] = nullptr;
-          if (tile < p.tiles) {
+          if (wprod && tile < p.tiles) {
             uint32_t si = 0;
             if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
             if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
@@ -313,21 +422,23 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             bytes += UB;
           }
         }
-        for (uint32_t i = 0; i < nblk && !*abort; i++, wc++) {
-          const uint32_t st = wc % UM_ST, k = wc / UM_ST;
-          if (k >= 1) um_wait(&bar_wempty[st], (k - 1) & 1u, a.err, abort);
+        for (uint32_t i = 0; i < nblk && !*abort; i++, cnt++) {
+          const uint32_t st = cnt % S, k = cnt / S;
+          if (k >= 1) um_wait(wprod ? &bar_wempty[st] : &bar_bfree[st], (k - 1) & 1u, a.err, abort);
           fence_proxy_async();
-          mbar_expect_tx(&bar_wfull[st], bytes);
+          if (wprod) {
+            mbar_expect_tx(&full[st], bytes);
 #pragma unroll
-          for (uint32_t tl = 0; tl < UM_TILES; tl++)
-            if (src[tl]) bulk_g2s(ring + (st * UM_TILES + tl) * UB, src[tl] + (size_t)(b0 + i) * UB, UB, &bar_wfull[st]);
+            for (uint32_t tl = 0; tl < UM_TILES; tl++)
+              if (src[tl]) bulk_g2s(ring + (st * UM_TILES + tl) * UB, src[tl] + (size_t)(b0 + i) * UB, UB, &full[st]);
+          } else {
+            mbar_expect_tx(&full[st], XB::BLK);
+            bulk_g2s(bring + st * XB::BLK, a.xblob + (size_t)(b0 + i) * XB::BLK, XB::BLK, &full[st]);
+          }
         }
       }
       // teardown: every copy issued has landed
-      for (uint32_t st = 0; st < UM_ST && st < wc; st++) {
-        const uint32_t uses = (wc - st + UM_ST - 1) / UM_ST;
-        um_drain(&bar_wfull[st], (uses - 1) & 1u, a.err);
-      }
+      for (uint32_t st = 0; st < S && st < cnt; st++) um_drain(&full[st], ((cnt - st + S - 1) / S - 1) & 1u, a.err);
     }
   } else if (warp == UM_MMAW) {
     // ------------------------------------------------------ MMA issuer
@@ -337,25 +448,27 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
         const uint32_t ks = unit % p.ksplit, nblk = min(p.slice, nb - ks * p.slice);
         for (uint32_t i = 0; i < nblk; i++, gb++) {
+          const uint32_t slot = gb % BS;
+#pragma unroll
           for (uint32_t h = 0; h < 2; h++) {
             const uint32_t hb = 2 * gb + h;
             um_wait(&bar_afull[hb & 1], (hb >> 1) & 1u, a.err, abort);
-            if (h == 0) um_wait(&bar_bfull[gb & 1], (gb >> 1) & 1u, a.err, abort);
+            if (h == 0) um_wait(&bar_bfull[slot], (gb / BS) & 1u, a.err, abort);
             if (*abort) continue;
             tc_fence_after();
             const uint32_t ta = tb + UM_TA + 128u * (hb & 1), td = tb + UM_TD + 64u * (gb & 1);
-            const uint32_t bs = smem_u32(bbuf + (gb & 1) * L::BBLK + h * 8 * L::KSTEP);
+            const uint32_t bs = smem_u32(bring + slot * XB::BLK) + h * 8 * XB::KSTEP;
 #pragma unroll
             for (uint32_t t = 0; t < 8; t++)
-              umma_ts(td, ta + 8 * t, umma_desc_k(bs + t * L::KSTEP, 128, 256), idesc, (h | t) != 0);
+              umma_ts(td, ta + 8 * t, umma_desc_k(bs + t * XB::KSTEP, 128, 256), idesc, (h | t) != 0);
             if constexpr (QT == 14) {
 #pragma unroll
               for (uint32_t t = 0; t < 8; t++)
-                umma_ts(td, ta + 64 + 8 * t, umma_desc_k(bs + t * L::KSTEP, 128, 256), idesc, 1u);
+                umma_ts(td, ta + 64 + 8 * t, umma_desc_k(bs + t * XB::KSTEP, 128, 256), idesc, 1u);
             }
             if (h == 0)
               umma_ss(tb + UM_TD2 + 64u * (gb & 1), umma_desc_k(smem_u32(a2buf + (gb & 1) * L::A2), 128, 256),
-                      umma_desc_k(smem_u32(b2buf + (gb & 1) * L::B2), 128, 256), idesc, 0u);
+                      umma_desc_k(smem_u32(bring + slot * XB::BLK + XB::OFF_B2), 128, 256), idesc, 0u);
             umma_commit(&bar_half[hb & 1]);
             if (h == 1) umma_commit(&bar_dfull[gb & 1]);
           }
@@ -365,114 +478,38 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       umma_commit(&bar_fin);
       um_drain(&bar_fin, 0, a.err);
     }
-  } else if (warp >= UM_RW) {
-    // -------------------------------------------- x warps: B and B2 operands
-    constexpr uint32_t LPC = 128 / NB, IPL = NB / 4;  // lanes per column, 8-value items per lane and block
-    constexpr uint32_t IPS = QT == 12 ? 4 : 2;        // items per sub-block
-    const uint32_t xt = threadIdx.x - UM_RW * 32, c = xt / LPC, u = xt % LPC;
-    pdl_wait();
-    for (uint32_t cc = warp - UM_RW; cc < a.batch; cc += UM_XW) {
-      const float v = input_scale(a, cc);
-      if (lane == 0) s_in[cc] = v;
-    }
-    uint32_t gb = 0;
-    for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
-      const uint32_t ks = unit % p.ksplit, b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
-      for (uint32_t i = 0; i < nblk; i++, gb++) {
-        if (gb >= 2) um_wait(&bar_dfull[gb & 1], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 done
-        float v[IPL][8];
-        const bool live = c < a.batch;
-        const float* xp = a.x + (size_t)c * a.ldx + (size_t)(b0 + i) * 256 + 8 * IPL * u;
-        float mx = 0.f;
-#pragma unroll
-        for (uint32_t j = 0; j < IPL; j++) {
-          float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
-          if (live) {
-            lo = ldg4(xp + 8 * j);
-            hi = ldg4(xp + 8 * j + 4);
-          }
-          v[j][0] = lo.x; v[j][1] = lo.y; v[j][2] = lo.z; v[j][3] = lo.w;
-          v[j][4] = hi.x; v[j][5] = hi.y; v[j][6] = hi.z; v[j][7] = hi.w;
-#pragma unroll
-          for (int k = 0; k < 8; k++) mx = fmaxf(mx, fabsf(v[j][k]));
-        }
-#pragma unroll
-        for (uint32_t o = 1; o < LPC; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        // the power of two that puts max|x| in [2^14, 2^15)
-        const uint32_t E = (__float_as_uint(mx) >> 23) & 0xFFu;
-        const float scl = E >= 15u ? __uint_as_float((268u - E) << 23) : 1.f;
-        const float inv = E >= 15u ? __uint_as_float((E - 14u) << 23) : 1.f;
-        if (u == 0) xs[(gb & 3) * UM_MAXB + c] = inv;
-        uint8_t* bb = bbuf + (gb & 1) * L::BBLK;
-        uint8_t* b2 = b2buf + (gb & 1) * L::B2;
-        float xsum[IPL / IPS > 0 ? IPL / IPS : 1];
-#pragma unroll
-        for (uint32_t s = 0; s < (IPL / IPS > 0 ? IPL / IPS : 1); s++) xsum[s] = 0.f;
-        float xpart = 0.f;
-#pragma unroll
-        for (uint32_t j = 0; j < IPL; j++) {
-          const uint32_t it = IPL * u + j, T = it >> 1, kc = it & 1;
-          const float w[8] = {v[j][0] * scl, v[j][2] * scl, v[j][1] * scl, v[j][3] * scl,
-                              v[j][4] * scl, v[j][6] * scl, v[j][5] * scl, v[j][7] * scl};
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            const float ah = hi11(w[2 * q]), bh = hi11(w[2 * q + 1]);
-            hw[q] = h2u(__floats2half2_rn(ah, bh));
-            lw[q] = h2u(__floats2half2_rn(w[2 * q] - ah, w[2 * q + 1] - bh));
-          }
-          *reinterpret_cast<uint4*>(bb + T * L::KSTEP + um_core(2 * c, kc)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(bb + T * L::KSTEP + um_core(2 * c + 1, kc)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-          const float s8 = ((w[0] + w[1]) + (w[2] + w[3])) + ((w[4] + w[5]) + (w[6] + w[7]));
-          if constexpr (IPL >= IPS) xsum[j / IPS] += s8;
-          else xpart += s8;
-        }
-        // sub-block sums of the scaled x (times 2^-6) as hi / lo rows of B2, K position = sub-block
-        auto put_sum = [&](uint32_t s, float X) {
-          X *= 0.015625f;
-          const float Xh = hi11(X);
-          const uint32_t off = (s & 7u) * 2u;
-          *reinterpret_cast<__half*>(b2 + um_core(2 * c, s >> 3) + off) = __float2half_rn(Xh);
-          *reinterpret_cast<__half*>(b2 + um_core(2 * c + 1, s >> 3) + off) = __float2half_rn(X - Xh);
-        };
-        if constexpr (IPL >= IPS) {
-#pragma unroll
-          for (uint32_t s = 0; s < IPL / IPS; s++) put_sum((IPL * u) / IPS + s, xsum[s]);
-        } else {  // two lanes share a sub-block
-          xpart += __shfl_xor_sync(0xffffffffu, xpart, 1);
-          if (!(u & 1)) put_sum((IPL * u) / IPS, xpart);
-        }
-        fence_proxy_async();  // the operands are read by the tensor cores (async proxy)
-        mbar_arrive(&bar_bfull[gb & 1]);
-        mbar_arrive(&bar_xs[gb & 3]);
-      }
-    }
   } else {
     // ---------------------------------- row warps: A operands, epilogues
     const uint32_t q = warp & 3, e = warp >> 2, m = 32 * q + lane, tl = m >> 4, rr = m & 15;
     const uint32_t tlane = (32u * q) << 16;
     pdl_wait();
-    uint32_t wc = 0, gb = 0;
+    const float* s_in = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK);
+    uint32_t gb = 0;
     float dcur = 0.f, mcur = 0.f;  // d, dmin (Q4_K) of the block being multiplied
-    // the accumulators of block g into y
+    // the accumulators of block g into y; then its B slot is free
     auto drain = [&](uint32_t g, float d, float dm, float (&y)[NH]) {
       um_wait(&bar_dfull[g & 1], (g >> 1) & 1u, a.err, abort);
-      um_wait(&bar_xs[g & 3], (g >> 2) & 1u, a.err, abort);
+      um_wait(&bar_bfull[g % BS], (g / BS) & 1u, a.err, abort);  // the slot's scales are visible
       tc_fence_after();
       uint32_t dr[NB], d2r[NB];
       tmem_ld<NB>(tb + tlane + UM_TD + 64u * (g & 1) + NB * e, dr);
       tmem_ld<NB>(tb + tlane + UM_TD2 + 64u * (g & 1) + NB * e, d2r);
+      const float* uu = reinterpret_cast<const float*>(bring + (g % BS) * XB::BLK + XB::OFF_U) + NH * e;
+      float us[NH];
+#pragma unroll
+      for (uint32_t i = 0; i < NH; i++) us[i] = uu[i];
       tmem_wait_ld();
-      const float* uu = xs + (g & 3) * UM_MAXB + NH * e;
 #pragma unroll
       for (uint32_t i = 0; i < NH; i++) {
         const float D = __uint_as_float(dr[2 * i]) + __uint_as_float(dr[2 * i + 1]);
         const float D2 = __uint_as_float(d2r[2 * i]) + __uint_as_float(d2r[2 * i + 1]);
-        if constexpr (QT == 12) y[i] = fmaf(uu[i], fmaf(d, D, -64.f * dm * D2), y[i]);
-        else y[i] = fmaf(uu[i] * d, fmaf(16.f, D, -2048.f * D2), y[i]);
+        if constexpr (QT == 12) y[i] = fmaf(us[i], fmaf(d, D, -64.f * dm * D2), y[i]);
+        else y[i] = fmaf(us[i] * d, fmaf(16.f, D, -2048.f * D2), y[i]);
       }
       tc_fence_before();
+      mbar_arrive(&bar_bfree[g % BS]);
     };
+    uint32_t wc = 0;
     for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
       const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
       const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0), tile = rg * UM_TILES + tl;
@@ -480,12 +517,12 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
 #pragma unroll
       for (uint32_t i = 0; i < NH; i++) y[i] = 0.f;
       for (uint32_t i = 0; i < nblk; i++, gb++, wc++) {
-        const uint32_t st = wc % UM_ST;
-        um_wait(&bar_wfull[st], (wc / UM_ST) & 1u, a.err, abort);
+        const uint32_t st = wc % WS;
+        um_wait(&bar_wfull[st], (wc / WS) & 1u, a.err, abort);
         const uint8_t* un = ring + (st * UM_TILES + tl) * UB;
         const uint4 hd = *reinterpret_cast<const uint4*>(un + 16 * rr);
         float dn, mn_ = 0.f;
-        uint4 W4[2][2];   // Q4_K: [half][p]
+        uint4 W4[2][2];     // Q4_K: [half][p]
         uint2 W6[2][3][2];  // Q6_K: [half][array][p]
         uint32_t d6 = 0;
         if constexpr (QT == 12) {
@@ -517,8 +554,21 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
           for (int s = 0; s < 16; s++) s6[s] = (int32_t)(int8_t)((hw[s >> 2] >> (8 * (s & 3))) & 0xFFu);
           dn = q6_d(d6);
         }
+#pragma unroll
         for (uint32_t h = 0; h < 2; h++) {
           const uint32_t hb = 2 * gb + h;
+          uint32_t A[32];
+          // sub-block scales of this warp's part (j = 2h + e, G = 2h + e), selected
+          // without a run-time array index
+          int32_t sc[4];
+          if constexpr (QT == 12) {
+            const uint32_t sc0 = e ? s4[4 * h + 2] : s4[4 * h], sc1 = e ? s4[4 * h + 3] : s4[4 * h + 1];
+            um_q4_a(W4[h], sc0, sc1, A);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) sc[k] = e ? s6[8 * h + 4 + k] : s6[8 * h + k];
+            um_q6_al(W6[h], sc, A);
+          }
           if (hb >= 2) um_wait(&bar_half[hb & 1], ((hb >> 1) + 1) & 1u, a.err, abort);  // half-block hb - 2 done
           const uint32_t ta = tb + tlane + UM_TA + 128u * (hb & 1) + 32u * e;
           if (h == 0 && e == 0) {  // per-block term operand A2 (row m)
@@ -537,16 +587,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             }
             fence_proxy_async();
           }
-          uint32_t A[32];
-          if constexpr (QT == 12) {
-            const uint32_t j = 2 * h + e;
-            um_q4_a(W4[h], s4[2 * j], s4[2 * j + 1], A);
-            tmem_st32(ta, A);
-          } else {
-            const uint32_t G = 2 * h + e;
-            const int32_t sc[4] = {s6[4 * G], s6[4 * G + 1], s6[4 * G + 2], s6[4 * G + 3]};
-            um_q6_al(W6[h], sc, A);
-            tmem_st32(ta, A);
+          tmem_st32(ta, A);
+          if constexpr (QT == 14) {
             um_q6_ah(W6[h], sc, A);
             tmem_st32(ta + 64, A);
           }
@@ -613,6 +655,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
 namespace {
 
 using UmKernel = void (*)(GemvArgs, UmPlan);
+using XpKernel = void (*)(GemvArgs, uint32_t);
 
 UmKernel um_kernel(uint32_t nb8, uint32_t qt) {
   switch (nb8 * 100 + qt) {
@@ -625,9 +668,31 @@ UmKernel um_kernel(uint32_t nb8, uint32_t qt) {
   }
   return nullptr;
 }
+XpKernel xp_kernel(uint32_t nb8, uint32_t qt) {
+  switch (nb8 * 100 + qt) {
+    case 812: return umma_xprep_kernel<8, 12>;
+    case 814: return umma_xprep_kernel<8, 14>;
+    case 1612: return umma_xprep_kernel<16, 12>;
+    case 1614: return umma_xprep_kernel<16, 14>;
+    case 3212: return umma_xprep_kernel<32, 12>;
+    case 3214: return umma_xprep_kernel<32, 14>;
+  }
+  return nullptr;
+}
 uint32_t um_nb8(uint32_t batch) { return batch <= 8 ? 8 : batch <= 16 ? 16 : 32; }
-uint32_t um_smem_for(uint32_t nb8, uint32_t ub) {
-  const uint32_t b = nb8 == 8 ? UmSmem<8>::bytes(ub) : nb8 == 16 ? UmSmem<16>::bytes(ub) : UmSmem<32>::bytes(ub);
+uint32_t um_blob_blk(uint32_t nb8) {
+  return nb8 == 8 ? UmBlob<8>::BLK : nb8 == 16 ? UmBlob<16>::BLK : UmBlob<32>::BLK;
+}
+uint32_t um_smem_for(uint32_t nb8, uint32_t qt) {
+  uint32_t b = 0;
+  switch (nb8 * 100 + qt) {
+    case 812: b = UmSmem<8, 12>::BYTES; break;
+    case 814: b = UmSmem<8, 14>::BYTES; break;
+    case 1612: b = UmSmem<16, 12>::BYTES; break;
+    case 1614: b = UmSmem<16, 14>::BYTES; break;
+    case 3212: b = UmSmem<32, 12>::BYTES; break;
+    default: b = UmSmem<32, 14>::BYTES; break;
+  }
   return std::max(b, UM_SMEM_MIN);
 }
 
@@ -655,14 +720,17 @@ cudaError_t um_setup(uint32_t* sms) {
   return cudaSuccess;
 }
 
-// One weight type for every segment, batch 2..32, whole 256-blocks.
+// One weight type for every segment, batch 2..32, whole 256-blocks, and room
+// for the B image.
 bool um_ok(const GemvArgs& a) {
   if (a.batch < 2 || a.batch > UM_MAXB || !a.nseg) return false;
   const uint32_t qt = a.seg[0].w.type;
   if (!tiled_type(qt)) return false;
   for (uint32_t i = 0; i < a.nseg; i++)
     if (a.seg[i].w.type != qt || a.seg[i].w.n_in != a.seg[0].w.n_in) return false;
-  return (a.ldx & 3u) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0;
+  if ((a.ldx & 3u) || (reinterpret_cast<uintptr_t>(a.x) & 15u)) return false;
+  return a.xblob && (reinterpret_cast<uintptr_t>(a.xblob) & 15u) == 0 &&
+         gemv_umma_blob_bytes(a.seg[0].w.n_in, a.batch) <= a.xblob_cap;
 }
 
 // CTA tiles of 128 rows and a K-split that minimizes rounds of units x
@@ -674,8 +742,7 @@ bool um_plan(GemvArgs& a, uint32_t sms, UmPlan* p) {
     tiles += (a.seg[i].w.n_out + 15) / 16;
   }
   const uint32_t nb = a.seg[0].w.n_in >> 8, groups = (tiles + UM_TILES - 1) / UM_TILES;
-  const uint32_t ub = tile_unit_bytes(a.seg[0].w.type);
-  const uint32_t smem = um_smem_for(um_nb8(a.batch), ub);
+  const uint32_t smem = um_smem_for(um_nb8(a.batch), a.seg[0].w.type);
   if (smem > UM_SMEM_MAX || nb == 0) return false;
   auto fits = [&](uint32_t k) {
     return k == 1 || (a.ks_part && a.ks_cnt && (uint64_t)k * tiles * 16u * a.batch <= a.ks_part_cap &&
@@ -705,6 +772,10 @@ bool um_plan(GemvArgs& a, uint32_t sms, UmPlan* p) {
 
 }  // namespace
 
+uint64_t gemv_umma_blob_bytes(uint32_t n_in, uint32_t batch) {
+  return (uint64_t)(n_in >> 8) * um_blob_blk(um_nb8(batch)) + UM_MAXB * 4;
+}
+
 cudaError_t gemv_umma_prepare() {
   uint32_t sms = 0;
   return um_setup(&sms);
@@ -720,7 +791,10 @@ cudaError_t launch_gemv_umma(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   UmPlan p;
   if (!um_plan(a, sms, &p)) return cudaErrorNotSupported;
   if (n_parts) *n_parts = p.tiles;
-  return launch_pdl(um_kernel(um_nb8(a.batch), a.seg[0].w.type), dim3(p.grid), dim3(UM_THREADS), p.smem, st, a, p);
+  const uint32_t nb8 = um_nb8(a.batch), qt = a.seg[0].w.type, nb = a.seg[0].w.n_in >> 8;
+  e = launch_pdl(xp_kernel(nb8, qt), dim3(nb), dim3(UM_XPREP_THREADS), 0, st, a, nb);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(um_kernel(nb8, qt), dim3(p.grid), dim3(UM_THREADS), p.smem, st, a, p);
 }
 
 void gemv_umma_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt) {
@@ -731,7 +805,7 @@ void gemv_umma_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* 
   *part = 0;
   *cnt = 0;
   UmPlan p;
-  if (!um_ok(a) || !um_plan(a, sms, &p) || p.ksplit == 1) return;
+  if (!tiled_type(a.seg[0].w.type) || !um_plan(a, sms, &p) || p.ksplit == 1) return;
   *part = (uint64_t)p.ksplit * p.tiles * 16u * a.batch;
   *cnt = p.groups;
 }

@@ -51,6 +51,9 @@ void gemv_tcb_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* c
 // uses for batches of 2..32 (gemv_tcb.cu when no plan of it fits).
 cudaError_t gemv_umma_prepare();
 void gemv_umma_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* cnt);
+// Bytes of the x image (GemvArgs::xblob) a launch of n_in inputs and `batch`
+// columns needs; without it launch_gemv runs the gemv_tcb.cu kernel.
+uint64_t gemv_umma_blob_bytes(uint32_t n_in, uint32_t batch);
 cudaError_t launch_record_tokens(const uint32_t* tok, uint32_t rows, uint32_t* hist, uint32_t* ctr,
                                  uint32_t cap_steps, cudaStream_t st);
 
