@@ -51,8 +51,9 @@ namespace sm {
 
 uint64_t gemv_umma_blob_bytes(uint32_t n_in, uint32_t batch);
 
-constexpr int UM_RW = 8;  // row warps
-constexpr int UM_BPW = UM_RW, UM_PROD = UM_RW + 1, UM_MMAW = UM_RW + 2, UM_WARPS = UM_RW + 3;
+constexpr int UM_RW = 8, UM_EW = 4;  // row warps (A operands), epilogue warps (accumulators)
+constexpr int UM_EW0 = UM_RW, UM_BPW = UM_RW + UM_EW, UM_PROD = UM_BPW + 1, UM_MMAW = UM_BPW + 2,
+              UM_WARPS = UM_BPW + 3;
 constexpr int UM_THREADS = UM_WARPS * 32;
 constexpr uint32_t UM_MAXB = 32;                // columns
 constexpr uint32_t UM_TILES = 8;                // 16-row weight tiles per CTA tile
@@ -220,11 +221,11 @@ __device__ __forceinline__ void um_q6_ah(const uint2 (&w)[3][2], const int32_t (
     }
 }
 
-// Epilogue of the calling row for its half of the columns (y[i]: column
-// NB / 2 * e + i, already times the input-norm scale). Every lane calls it.
-template <int NB>
+// Epilogue of the calling row (y[i]: column c0 + i, already times the
+// input-norm scale). Every lane of the warp calls it.
+template <int NC>
 __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, uint32_t n_parts, bool valid,
-                                            uint32_t rr, uint32_t e, const float (&y)[NB / 2]) {
+                                            uint32_t rr, uint32_t c0, const float (&y)[NC]) {
   const int lane = threadIdx.x & 31;
   uint32_t si = 0;
   if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
@@ -234,8 +235,8 @@ __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, ui
   const bool any_resid = a.seg[0].epi == EPI_RESID || (a.nseg > 1 && a.seg[1].epi == EPI_RESID) ||
                          (a.nseg > 2 && a.seg[2].epi == EPI_RESID);
 #pragma unroll
-  for (int i = 0; i < NB / 2; i++) {
-    const uint32_t col = (NB / 2) * e + i;
+  for (int i = 0; i < NC; i++) {
+    const uint32_t col = c0 + i;
     const float v = y[i], nv = __shfl_xor_sync(0xffffffffu, v, 1);
     const bool ok = valid && col < a.batch && o < sg.w.n_out;
     float xv = 0.f;
@@ -350,10 +351,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   using XB = UmBlob<NB>;
   using W = UmW<QT>;
   using L = UmSmem<NB, QT>;
-  constexpr uint32_t N = XB::N, UB = W::UB, WS = W::STAGES, BS = XB::SLOTS, NH = NB / 2;
+  constexpr uint32_t N = XB::N, UB = W::UB, WS = W::STAGES, BS = XB::SLOTS;
+  constexpr uint32_t NA = QT == 12 ? 4 : 2, ACOLS = QT == 12 ? 64 : 128;  // A buffers (half-blocks), columns each
   extern __shared__ __align__(1024) uint8_t um_smem[];
-  __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[2],
-      bar_half[2], bar_dfull[2], bar_fin;
+  __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[NA],
+      bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_fin;
   __shared__ uint32_t s_tmem, s_last;
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
@@ -366,16 +368,19 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   if (threadIdx.x == 0) {
     for (uint32_t k = 0; k < WS; k++) {
       mbar_init(&bar_wfull[k], 1);
-      mbar_init(&bar_wempty[k], UM_RW * 32);
+      mbar_init(&bar_wempty[k], (UM_RW + UM_EW) * 32);
     }
     for (uint32_t k = 0; k < BS; k++) {
       mbar_init(&bar_bfull[k], 1);
-      mbar_init(&bar_bfree[k], UM_RW * 32);
+      mbar_init(&bar_bfree[k], UM_EW * 32);
+    }
+    for (uint32_t k = 0; k < NA; k++) {
+      mbar_init(&bar_afull[k], UM_RW * 32);
+      mbar_init(&bar_afree[k], 1);
     }
     for (uint32_t k = 0; k < 2; k++) {
-      mbar_init(&bar_afull[k], UM_RW * 32);
-      mbar_init(&bar_half[k], 1);
       mbar_init(&bar_dfull[k], 1);
+      mbar_init(&bar_dfree[k], UM_EW * 32);
     }
     mbar_init(&bar_fin, 1);
     *abort = 0u;
@@ -451,12 +456,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
           const uint32_t slot = gb % BS;
 #pragma unroll
           for (uint32_t h = 0; h < 2; h++) {
-            const uint32_t hb = 2 * gb + h;
-            um_wait(&bar_afull[hb & 1], (hb >> 1) & 1u, a.err, abort);
-            if (h == 0) um_wait(&bar_bfull[slot], (gb / BS) & 1u, a.err, abort);
+            const uint32_t hb = 2 * gb + h, ab = hb % NA;
+            um_wait(&bar_afull[ab], (hb / NA) & 1u, a.err, abort);
+            if (h == 0) {
+              um_wait(&bar_bfull[slot], (gb / BS) & 1u, a.err, abort);
+              if (gb >= 2) um_wait(&bar_dfree[gb & 1], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 read
+            }
             if (*abort) continue;
             tc_fence_after();
-            const uint32_t ta = tb + UM_TA + 128u * (hb & 1), td = tb + UM_TD + 64u * (gb & 1);
+            const uint32_t ta = tb + UM_TA + ACOLS * ab, td = tb + UM_TD + 64u * (gb & 1);
             const uint32_t bs = smem_u32(bring + slot * XB::BLK) + h * 8 * XB::KSTEP;
 #pragma unroll
             for (uint32_t t = 0; t < 8; t++)
@@ -469,7 +477,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             if (h == 0)
               umma_ss(tb + UM_TD2 + 64u * (gb & 1), umma_desc_k(smem_u32(a2buf + (gb & 1) * L::A2), 128, 256),
                       umma_desc_k(smem_u32(bring + slot * XB::BLK + XB::OFF_B2), 128, 256), idesc, 0u);
-            umma_commit(&bar_half[hb & 1]);
+            umma_commit(&bar_afree[ab]);
             if (h == 1) umma_commit(&bar_dfull[gb & 1]);
           }
         }
@@ -478,53 +486,20 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       umma_commit(&bar_fin);
       um_drain(&bar_fin, 0, a.err);
     }
-  } else {
-    // ---------------------------------- row warps: A operands, epilogues
+  } else if (warp < UM_RW) {
+    // --------------------------------------------- row warps: A operands
     const uint32_t q = warp & 3, e = warp >> 2, m = 32 * q + lane, tl = m >> 4, rr = m & 15;
     const uint32_t tlane = (32u * q) << 16;
-    pdl_wait();
-    const float* s_in = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK);
-    uint32_t gb = 0;
-    float dcur = 0.f, mcur = 0.f;  // d, dmin (Q4_K) of the block being multiplied
-    // the accumulators of block g into y; then its B slot is free
-    auto drain = [&](uint32_t g, float d, float dm, float (&y)[NH]) {
-      um_wait(&bar_dfull[g & 1], (g >> 1) & 1u, a.err, abort);
-      um_wait(&bar_bfull[g % BS], (g / BS) & 1u, a.err, abort);  // the slot's scales are visible
-      tc_fence_after();
-      uint32_t dr[NB], d2r[NB];
-      tmem_ld<NB>(tb + tlane + UM_TD + 64u * (g & 1) + NB * e, dr);
-      tmem_ld<NB>(tb + tlane + UM_TD2 + 64u * (g & 1) + NB * e, d2r);
-      const float* uu = reinterpret_cast<const float*>(bring + (g % BS) * XB::BLK + XB::OFF_U) + NH * e;
-      float us[NH];
-#pragma unroll
-      for (uint32_t i = 0; i < NH; i++) us[i] = uu[i];
-      tmem_wait_ld();
-#pragma unroll
-      for (uint32_t i = 0; i < NH; i++) {
-        const float D = __uint_as_float(dr[2 * i]) + __uint_as_float(dr[2 * i + 1]);
-        const float D2 = __uint_as_float(d2r[2 * i]) + __uint_as_float(d2r[2 * i + 1]);
-        if constexpr (QT == 12) y[i] = fmaf(us[i], fmaf(d, D, -64.f * dm * D2), y[i]);
-        else y[i] = fmaf(us[i] * d, fmaf(16.f, D, -2048.f * D2), y[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&bar_bfree[g % BS]);
-    };
-    uint32_t wc = 0;
+    uint32_t gb = 0, wc = 0;
     for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
-      const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
-      const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0), tile = rg * UM_TILES + tl;
-      float y[NH];
-#pragma unroll
-      for (uint32_t i = 0; i < NH; i++) y[i] = 0.f;
+      const uint32_t ks = unit % p.ksplit, nblk = min(p.slice, nb - ks * p.slice);
       for (uint32_t i = 0; i < nblk; i++, gb++, wc++) {
         const uint32_t st = wc % WS;
         um_wait(&bar_wfull[st], (wc / WS) & 1u, a.err, abort);
         const uint8_t* un = ring + (st * UM_TILES + tl) * UB;
         const uint4 hd = *reinterpret_cast<const uint4*>(un + 16 * rr);
-        float dn, mn_ = 0.f;
         uint4 W4[2][2];     // Q4_K: [half][p]
         uint2 W6[2][3][2];  // Q6_K: [half][array][p]
-        uint32_t d6 = 0;
         if constexpr (QT == 12) {
 #pragma unroll
           for (int h = 0; h < 2; h++)
@@ -539,39 +514,40 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
 #pragma unroll
               for (int pp = 0; pp < 2; pp++)
                 W6[h][ar][pp] = *reinterpret_cast<const uint2*>(un + q6t_word_off(rr, ar, 2 * h + e, 0, pp));
-          d6 = *reinterpret_cast<const unsigned short*>(un + 256 + 2 * rr);
         }
         mbar_arrive(&bar_wempty[st]);  // the stage's bytes this row needs are in registers
         uint32_t s4[8], m4[8];
         int32_t s6[16];
         if constexpr (QT == 12) {
           um_q4_scales(hd, s4, m4);
-          dn = h2f_ref(hd.x & 0xFFFFu);
-          mn_ = h2f_ref(hd.x >> 16);
         } else {
           const uint32_t hw[4] = {hd.x, hd.y, hd.z, hd.w};
 #pragma unroll
           for (int s = 0; s < 16; s++) s6[s] = (int32_t)(int8_t)((hw[s >> 2] >> (8 * (s & 3))) & 0xFFu);
-          dn = q6_d(d6);
         }
+        uint32_t A[2][32];
 #pragma unroll
         for (uint32_t h = 0; h < 2; h++) {
-          const uint32_t hb = 2 * gb + h;
-          uint32_t A[32];
+          const uint32_t hb = 2 * gb + h, ab = hb % NA;
           // sub-block scales of this warp's part (j = 2h + e, G = 2h + e), selected
           // without a run-time array index
           int32_t sc[4];
           if constexpr (QT == 12) {
             const uint32_t sc0 = e ? s4[4 * h + 2] : s4[4 * h], sc1 = e ? s4[4 * h + 3] : s4[4 * h + 1];
-            um_q4_a(W4[h], sc0, sc1, A);
+            um_q4_a(W4[h], sc0, sc1, A[h]);
           } else {
 #pragma unroll
             for (int k = 0; k < 4; k++) sc[k] = e ? s6[8 * h + 4 + k] : s6[8 * h + k];
-            um_q6_al(W6[h], sc, A);
+            um_q6_al(W6[h], sc, A[h]);
           }
-          if (hb >= 2) um_wait(&bar_half[hb & 1], ((hb >> 1) + 1) & 1u, a.err, abort);  // half-block hb - 2 done
-          const uint32_t ta = tb + tlane + UM_TA + 128u * (hb & 1) + 32u * e;
-          if (h == 0 && e == 0) {  // per-block term operand A2 (row m)
+          if (h == 1) {  // half 0's stores have had the half-1 work to complete
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bar_afull[(hb - 1) % NA]);
+          }
+          if (hb >= NA) um_wait(&bar_afree[ab], ((hb / NA) + 1) & 1u, a.err, abort);  // its last MMAs are done
+          const uint32_t ta = tb + tlane + UM_TA + ACOLS * ab + 32u * e;
+          if (h == 0 && e == 0) {  // per-block term operand A2 (row m); its MMA of block gb - 2 is done
             uint8_t* a2 = a2buf + (gb & 1) * L::A2;
             if constexpr (QT == 12) {
               uint32_t pk[4];
@@ -587,57 +563,113 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             }
             fence_proxy_async();
           }
-          tmem_st32(ta, A);
+          tmem_st32(ta, A[h]);
           if constexpr (QT == 14) {
-            um_q6_ah(W6[h], sc, A);
-            tmem_st32(ta + 64, A);
+            uint32_t Ah[32];
+            um_q6_ah(W6[h], sc, Ah);
+            tmem_st32(ta + 64, Ah);
           }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&bar_afull[hb & 1]);
         }
-        if (i >= 1) drain(gb - 1, dcur, mcur, y);
-        dcur = dn;
-        mcur = mn_;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bar_afull[(2 * gb + 1) % NA]);
       }
-      drain(gb - 1, dcur, mcur, y);
+    }
+  } else {
+    // ------------------------------ epilogue warps: accumulators, results
+    const uint32_t q = warp & 3, m = 32 * q + lane, tl = m >> 4, rr = m & 15;
+    const uint32_t tlane = (32u * q) << 16;
+    pdl_wait();
+    const float* s_in = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK);
+    uint32_t gb = 0, wc = 0;
+    // the accumulators of block g into y; then its D and B slot are free
+    auto drain = [&](uint32_t g, float d, float dm, float (&y)[NB]) {
+      um_wait(&bar_dfull[g & 1], (g >> 1) & 1u, a.err, abort);
+      um_wait(&bar_bfull[g % BS], (g / BS) & 1u, a.err, abort);  // the slot's scales are visible
+      tc_fence_after();
+      const float* uu = reinterpret_cast<const float*>(bring + (g % BS) * XB::BLK + XB::OFF_U);
+      constexpr uint32_t CH = NB < 16 ? NB : 16;  // columns per read-back chunk (2 CH accumulator columns)
+#pragma unroll
+      for (uint32_t c0 = 0; c0 < NB; c0 += CH) {
+        uint32_t dr[2 * CH], d2r[2 * CH];
+        tmem_ld<2 * CH>(tb + tlane + UM_TD + 64u * (g & 1) + 2 * c0, dr);
+        tmem_ld<2 * CH>(tb + tlane + UM_TD2 + 64u * (g & 1) + 2 * c0, d2r);
+        float us[CH];
+#pragma unroll
+        for (uint32_t i = 0; i < CH; i++) us[i] = uu[c0 + i];
+        tmem_wait_ld();
+#pragma unroll
+        for (uint32_t i = 0; i < CH; i++) {
+          const float D = __uint_as_float(dr[2 * i]) + __uint_as_float(dr[2 * i + 1]);
+          const float D2 = __uint_as_float(d2r[2 * i]) + __uint_as_float(d2r[2 * i + 1]);
+          if constexpr (QT == 12) y[c0 + i] = fmaf(us[i], fmaf(d, D, -64.f * dm * D2), y[c0 + i]);
+          else y[c0 + i] = fmaf(us[i] * d, fmaf(16.f, D, -2048.f * D2), y[c0 + i]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_dfree[g & 1]);
+      mbar_arrive(&bar_bfree[g % BS]);
+    };
+    for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
+      const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
+      const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0), tile = rg * UM_TILES + tl;
+      float y[NB];
+#pragma unroll
+      for (uint32_t i = 0; i < NB; i++) y[i] = 0.f;
+      float dprev = 0.f, mprev = 0.f;  // d, dmin (Q4_K) of the previous block
+      for (uint32_t i = 0; i < nblk; i++, gb++, wc++) {
+        // this row's block scales, read while the weight stage is held
+        const uint32_t st = wc % WS;
+        um_wait(&bar_wfull[st], (wc / WS) & 1u, a.err, abort);
+        const uint8_t* un = ring + (st * UM_TILES + tl) * UB;
+        float dn, mn_ = 0.f;
+        if constexpr (QT == 12) {
+          const uint32_t dw = *reinterpret_cast<const uint32_t*>(un + 16 * rr);
+          dn = h2f_ref(dw & 0xFFFFu);
+          mn_ = h2f_ref(dw >> 16);
+        } else {
+          dn = q6_d(*reinterpret_cast<const unsigned short*>(un + 256 + 2 * rr));
+        }
+        mbar_arrive(&bar_wempty[st]);
+        if (i >= 1) drain(gb - 1, dprev, mprev, y);
+        dprev = dn;
+        mprev = mn_;
+      }
+      drain(gb - 1, dprev, mprev, y);
       // input-norm scale of each column
 #pragma unroll
-      for (uint32_t i = 0; i < NH; i++) {
-        const uint32_t col = NH * e + i;
-        y[i] *= col < a.batch ? s_in[col] : 0.f;
-      }
+      for (uint32_t i = 0; i < NB; i++) y[i] *= i < a.batch ? s_in[i] : 0.f;
       const bool valid = tile < p.tiles;
       if (p.ksplit == 1) {
-        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, e, y);
+        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
         continue;
       }
       // K-split: publish this slice; the last CTA of the group sums the slices in order
       const size_t stride = (size_t)p.tiles * 16u * a.batch;
+      float* mine = a.ks_part + ((size_t)tile * 16u + rr) * a.batch;
       if (valid) {
 #pragma unroll
-        for (uint32_t i = 0; i < NH; i++) {
-          const uint32_t col = NH * e + i;
-          if (col < a.batch) a.ks_part[ks * stride + ((size_t)tile * 16u + rr) * a.batch + col] = y[i];
-        }
+        for (uint32_t i = 0; i < NB; i++)
+          if (i < a.batch) mine[ks * stride + i] = y[i];
       }
       __threadfence();
-      named_bar(1, UM_RW * 32);
-      if (threadIdx.x == 0) s_last = atomicAdd(&a.ks_cnt[rg], 1u) == p.ksplit - 1;
-      named_bar(1, UM_RW * 32);
+      named_bar(1, UM_EW * 32);
+      if (threadIdx.x == UM_EW0 * 32) s_last = atomicAdd(&a.ks_cnt[rg], 1u) == p.ksplit - 1;
+      named_bar(1, UM_EW * 32);
       if (s_last) {
         __threadfence();
 #pragma unroll
-        for (uint32_t i = 0; i < NH; i++) {
-          const uint32_t col = NH * e + i;
-          float s = 0.f;
-          if (valid && col < a.batch)
-            for (uint32_t k = 0; k < p.ksplit; k++)
-              s += __ldcg(a.ks_part + k * stride + ((size_t)tile * 16u + rr) * a.batch + col);
-          y[i] = s;
-        }
-        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, e, y);
-        if (threadIdx.x == 0) a.ks_cnt[rg] = 0;  // ready for the next launch
+        for (uint32_t i = 0; i < NB; i++) y[i] = 0.f;
+        if (valid)
+          for (uint32_t k = 0; k < p.ksplit; k++) {  // in slice order; the columns' loads are independent
+            float t[NB];
+#pragma unroll
+            for (uint32_t i = 0; i < NB; i++) t[i] = i < a.batch ? __ldcg(mine + k * stride + i) : 0.f;
+#pragma unroll
+            for (uint32_t i = 0; i < NB; i++) y[i] += t[i];
+          }
+        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
+        if (threadIdx.x == UM_EW0 * 32) a.ks_cnt[rg] = 0;  // ready for the next launch
       }
     }
   }
@@ -734,7 +766,8 @@ bool um_ok(const GemvArgs& a) {
 }
 
 // CTA tiles of 128 rows and a K-split that minimizes rounds of units x
-// (blocks per unit + 2 blocks of per-unit cost), bounded by the scratch.
+// (blocks per unit + 2 blocks of per-unit cost) plus the fixup's reads (a
+// quarter block per slice), bounded by the scratch.
 bool um_plan(GemvArgs& a, uint32_t sms, UmPlan* p) {
   uint32_t tiles = 0;
   for (uint32_t i = 0; i < a.nseg; i++) {
@@ -754,8 +787,9 @@ bool um_plan(GemvArgs& a, uint32_t sms, UmPlan* p) {
     const uint32_t sl = (nb + k - 1) / k, kk = (nb + sl - 1) / sl;
     if (!fits(kk)) continue;
     const uint64_t rounds = ((uint64_t)groups * kk + sms - 1) / sms;
-    if (rounds * (sl + 2) < best) {
-      best = rounds * (sl + 2);
+    const uint64_t cost = rounds * (4 * sl + 8) + (kk > 1 ? kk : 0);  // quarter blocks; + the slices' fixup
+    if (cost < best) {
+      best = cost;
       ks = kk;
     }
   }
