@@ -79,7 +79,6 @@ struct UmBlob {
   static constexpr uint32_t N = 2 * NB;  // MMA N: a hi and a lo row per column
   static constexpr uint32_t KSTEP = N * 32, B2 = N * 32;
   static constexpr uint32_t OFF_B2 = 16 * KSTEP, OFF_U = OFF_B2 + B2, BLK = OFF_U + UM_MAXB * 4;
-  static constexpr uint32_t SLOTS = NB == 32 ? 3 : 4;  // shared-memory ring
 };
 // Weight stages in flight per type.
 template <int QT>
@@ -87,13 +86,16 @@ struct UmW {
   static constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT, STAGES = QT == 12 ? 4 : 3;
   static constexpr uint32_t BYTES = STAGES * UM_TILES * UB;
 };
-// Shared memory: weight stages | B slots | A2[2] (128 rows x 16 K f16)
+// Shared memory: weight stages | B slots | A2[2] (128 rows x 16 K f16) |
+// the rows' (d, dmin) of the last 4 blocks
 template <int NB, int QT>
 struct UmSmem {
+  static constexpr uint32_t SLOTS = QT == 12 ? (NB == 32 ? 4 : NB == 16 ? 6 : 8) : (NB == 32 ? 3 : NB == 16 ? 5 : 8);
   static constexpr uint32_t OFF_B = (UmW<QT>::BYTES + 1023u) / 1024u * 1024u;
-  static constexpr uint32_t OFF_A2 = OFF_B + UmBlob<NB>::SLOTS * UmBlob<NB>::BLK;
+  static constexpr uint32_t OFF_A2 = OFF_B + SLOTS * UmBlob<NB>::BLK;
   static constexpr uint32_t A2 = 128 * 32;
-  static constexpr uint32_t BYTES = OFF_A2 + 2 * A2;
+  static constexpr uint32_t OFF_DD = OFF_A2 + 2 * A2;
+  static constexpr uint32_t BYTES = OFF_DD + 4 * 128 * 8;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
@@ -351,11 +353,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   using XB = UmBlob<NB>;
   using W = UmW<QT>;
   using L = UmSmem<NB, QT>;
-  constexpr uint32_t N = XB::N, UB = W::UB, WS = W::STAGES, BS = XB::SLOTS;
+  constexpr uint32_t N = XB::N, UB = W::UB, WS = W::STAGES, BS = L::SLOTS;
   constexpr uint32_t NA = QT == 12 ? 4 : 2, ACOLS = QT == 12 ? 64 : 128;  // A buffers (half-blocks), columns each
   extern __shared__ __align__(1024) uint8_t um_smem[];
   __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[NA],
-      bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_fin;
+      bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_hdr[4], bar_fin;
   __shared__ uint32_t s_tmem, s_last;
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
@@ -363,13 +365,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   uint8_t* ring = um_smem;
   uint8_t* bring = um_smem + L::OFF_B;
   uint8_t* a2buf = um_smem + L::OFF_A2;
+  float2* dd = reinterpret_cast<float2*>(um_smem + L::OFF_DD);  // [block & 3][row]
   const uint32_t nb = a.seg[0].w.n_in >> 8;
 
   if (threadIdx.x == 0) {
     for (uint32_t k = 0; k < WS; k++) {
       mbar_init(&bar_wfull[k], 1);
-      mbar_init(&bar_wempty[k], (UM_RW + UM_EW) * 32);
+      mbar_init(&bar_wempty[k], UM_RW * 32);
     }
+    for (uint32_t k = 0; k < 4; k++) mbar_init(&bar_hdr[k], 4 * 32);
     for (uint32_t k = 0; k < BS; k++) {
       mbar_init(&bar_bfull[k], 1);
       mbar_init(&bar_bfree[k], UM_EW * 32);
@@ -431,14 +435,17 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
           const uint32_t st = cnt % S, k = cnt / S;
           if (k >= 1) um_wait(wprod ? &bar_wempty[st] : &bar_bfree[st], (k - 1) & 1u, a.err, abort);
           fence_proxy_async();
+          // row groups start their K walk at different blocks, so that the CTAs
+          // read different B images at a time
+          const uint32_t blk = b0 + (i + rg) % nblk;
           if (wprod) {
             mbar_expect_tx(&full[st], bytes);
 #pragma unroll
             for (uint32_t tl = 0; tl < UM_TILES; tl++)
-              if (src[tl]) bulk_g2s(ring + (st * UM_TILES + tl) * UB, src[tl] + (size_t)(b0 + i) * UB, UB, &full[st]);
+              if (src[tl]) bulk_g2s(ring + (st * UM_TILES + tl) * UB, src[tl] + (size_t)blk * UB, UB, &full[st]);
           } else {
             mbar_expect_tx(&full[st], XB::BLK);
-            bulk_g2s(bring + st * XB::BLK, a.xblob + (size_t)(b0 + i) * XB::BLK, XB::BLK, &full[st]);
+            bulk_g2s(bring + st * XB::BLK, a.xblob + (size_t)blk * XB::BLK, XB::BLK, &full[st]);
           }
         }
       }
@@ -465,14 +472,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             if (*abort) continue;
             tc_fence_after();
             const uint32_t ta = tb + UM_TA + ACOLS * ab, td = tb + UM_TD + 64u * (gb & 1);
-            const uint32_t bs = smem_u32(bring + slot * XB::BLK) + h * 8 * XB::KSTEP;
+            // K step t of the half-block: B descriptor start address advances by KSTEP (in 16-byte units)
+            const uint64_t bd = umma_desc_k(smem_u32(bring + slot * XB::BLK) + h * 8 * XB::KSTEP, 128, 256);
 #pragma unroll
             for (uint32_t t = 0; t < 8; t++)
-              umma_ts(td, ta + 8 * t, umma_desc_k(bs + t * XB::KSTEP, 128, 256), idesc, (h | t) != 0);
+              umma_ts(td, ta + 8 * t, bd + t * (XB::KSTEP >> 4), idesc, (h | t) != 0);
             if constexpr (QT == 14) {
 #pragma unroll
-              for (uint32_t t = 0; t < 8; t++)
-                umma_ts(td, ta + 64 + 8 * t, umma_desc_k(bs + t * XB::KSTEP, 128, 256), idesc, 1u);
+              for (uint32_t t = 0; t < 8; t++) umma_ts(td, ta + 64 + 8 * t, bd + t * (XB::KSTEP >> 4), idesc, 1u);
             }
             if (h == 0)
               umma_ss(tb + UM_TD2 + 64u * (gb & 1), umma_desc_k(smem_u32(a2buf + (gb & 1) * L::A2), 128, 256),
@@ -515,6 +522,11 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
               for (int pp = 0; pp < 2; pp++)
                 W6[h][ar][pp] = *reinterpret_cast<const uint2*>(un + q6t_word_off(rr, ar, 2 * h + e, 0, pp));
         }
+        float2 dmn = make_float2(0.f, 0.f);  // this row's block scales for the epilogue warps
+        if (e == 0) {
+          if constexpr (QT == 12) dmn = make_float2(h2f_ref(hd.x & 0xFFFFu), h2f_ref(hd.x >> 16));
+          else dmn.x = q6_d(*reinterpret_cast<const unsigned short*>(un + 256 + 2 * rr));
+        }
         mbar_arrive(&bar_wempty[st]);  // the stage's bytes this row needs are in registers
         uint32_t s4[8], m4[8];
         int32_t s6[16];
@@ -548,6 +560,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
           if (hb >= NA) um_wait(&bar_afree[ab], ((hb / NA) + 1) & 1u, a.err, abort);  // its last MMAs are done
           const uint32_t ta = tb + tlane + UM_TA + ACOLS * ab + 32u * e;
           if (h == 0 && e == 0) {  // per-block term operand A2 (row m); its MMA of block gb - 2 is done
+            // (d, dmin) for the epilogue warps: block gb - 4 has been read back (MMA gb - 2 waited for it)
+            dd[(gb & 3) * 128 + m] = dmn;
+            mbar_arrive(&bar_hdr[gb & 3]);
             uint8_t* a2 = a2buf + (gb & 1) * L::A2;
             if constexpr (QT == 12) {
               uint32_t pk[4];
@@ -581,11 +596,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     const uint32_t tlane = (32u * q) << 16;
     pdl_wait();
     const float* s_in = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK);
-    uint32_t gb = 0, wc = 0;
+    uint32_t gb = 0;
     // the accumulators of block g into y; then its D and B slot are free
-    auto drain = [&](uint32_t g, float d, float dm, float (&y)[NB]) {
+    auto drain = [&](uint32_t g, float (&y)[NB]) {
       um_wait(&bar_dfull[g & 1], (g >> 1) & 1u, a.err, abort);
       um_wait(&bar_bfull[g % BS], (g / BS) & 1u, a.err, abort);  // the slot's scales are visible
+      um_wait(&bar_hdr[g & 3], (g >> 2) & 1u, a.err, abort);
+      const float2 dmn = dd[(g & 3) * 128 + m];
+      const float d = dmn.x, dm = dmn.y;
       tc_fence_after();
       const float* uu = reinterpret_cast<const float*>(bring + (g % BS) * XB::BLK + XB::OFF_U);
       constexpr uint32_t CH = NB < 16 ? NB : 16;  // columns per read-back chunk (2 CH accumulator columns)
@@ -616,26 +634,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       float y[NB];
 #pragma unroll
       for (uint32_t i = 0; i < NB; i++) y[i] = 0.f;
-      float dprev = 0.f, mprev = 0.f;  // d, dmin (Q4_K) of the previous block
-      for (uint32_t i = 0; i < nblk; i++, gb++, wc++) {
-        // this row's block scales, read while the weight stage is held
-        const uint32_t st = wc % WS;
-        um_wait(&bar_wfull[st], (wc / WS) & 1u, a.err, abort);
-        const uint8_t* un = ring + (st * UM_TILES + tl) * UB;
-        float dn, mn_ = 0.f;
-        if constexpr (QT == 12) {
-          const uint32_t dw = *reinterpret_cast<const uint32_t*>(un + 16 * rr);
-          dn = h2f_ref(dw & 0xFFFFu);
-          mn_ = h2f_ref(dw >> 16);
-        } else {
-          dn = q6_d(*reinterpret_cast<const unsigned short*>(un + 256 + 2 * rr));
-        }
-        mbar_arrive(&bar_wempty[st]);
-        if (i >= 1) drain(gb - 1, dprev, mprev, y);
-        dprev = dn;
-        mprev = mn_;
-      }
-      drain(gb - 1, dprev, mprev, y);
+      for (uint32_t i = 0; i < nblk; i++, gb++) drain(gb, y);
       // input-norm scale of each column
 #pragma unroll
       for (uint32_t i = 0; i < NB; i++) y[i] *= i < a.batch ? s_in[i] : 0.f;
