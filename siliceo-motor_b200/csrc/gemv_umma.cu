@@ -52,8 +52,11 @@ namespace sm {
 uint64_t gemv_umma_blob_bytes(uint32_t n_in, uint32_t batch);
 
 constexpr int UM_RW = 8, UM_EW = 4;  // row warps (A operands), epilogue warps (accumulators)
+// Two MMA warps take alternate blocks (one thread issues at ~50 cycles per
+// MMA, two keep the tensor pipe busy at N = 64); the first also owns the
+// tensor-memory allocation.
 constexpr int UM_EW0 = UM_RW, UM_BPW = UM_RW + UM_EW, UM_PROD = UM_BPW + 1, UM_MMAW = UM_BPW + 2,
-              UM_WARPS = UM_BPW + 3;
+              UM_WARPS = UM_BPW + 4;
 constexpr int UM_THREADS = UM_WARPS * 32;
 constexpr uint32_t UM_MAXB = 32;                // columns
 constexpr uint32_t UM_TILES = 8;                // 16-row weight tiles per CTA tile
@@ -357,7 +360,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   constexpr uint32_t NA = QT == 12 ? 4 : 2, ACOLS = QT == 12 ? 64 : 128;  // A buffers (half-blocks), columns each
   extern __shared__ __align__(1024) uint8_t um_smem[];
   __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[NA],
-      bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_hdr[4], bar_fin;
+      bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_hdr[4], bar_fin[2];
   __shared__ uint32_t s_tmem, s_last;
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
@@ -386,7 +389,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       mbar_init(&bar_dfull[k], 1);
       mbar_init(&bar_dfree[k], UM_EW * 32);
     }
-    mbar_init(&bar_fin, 1);
+    mbar_init(&bar_fin[0], 1);
+    mbar_init(&bar_fin[1], 1);
     *abort = 0u;
     fence_mbar_init();
   }
@@ -452,46 +456,58 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       // teardown: every copy issued has landed
       for (uint32_t st = 0; st < S && st < cnt; st++) um_drain(&full[st], ((cnt - st + S - 1) / S - 1) & 1u, a.err);
     }
-  } else if (warp == UM_MMAW) {
-    // ------------------------------------------------------ MMA issuer
+  } else if (warp >= UM_MMAW) {
+    // ----------------------------- MMA issuers: blocks gb with gb % 2 == me
+    const uint32_t me = warp - UM_MMAW;
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(128, N);
       uint32_t gb = 0;
       for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
         const uint32_t ks = unit % p.ksplit, nblk = min(p.slice, nb - ks * p.slice);
         for (uint32_t i = 0; i < nblk; i++, gb++) {
-          const uint32_t slot = gb % BS;
+          if ((gb & 1) != me) continue;
+          const uint32_t slot = gb % BS, td = tb + UM_TD + 64u * me, td2 = tb + UM_TD2 + 64u * me;
 #pragma unroll
           for (uint32_t h = 0; h < 2; h++) {
             const uint32_t hb = 2 * gb + h, ab = hb % NA;
             um_wait(&bar_afull[ab], (hb / NA) & 1u, a.err, abort);
             if (h == 0) {
               um_wait(&bar_bfull[slot], (gb / BS) & 1u, a.err, abort);
-              if (gb >= 2) um_wait(&bar_dfree[gb & 1], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 read
+              if (gb >= 2) um_wait(&bar_dfree[me], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 read
             }
             if (*abort) continue;
-            tc_fence_after();
-            const uint32_t ta = tb + UM_TA + ACOLS * ab, td = tb + UM_TD + 64u * (gb & 1);
-            // K step t of the half-block: B descriptor start address advances by KSTEP (in 16-byte units)
+            // operands first, then the MMAs back to back: K step t of the half-block
+            // is A columns ta + 8t and a B descriptor KSTEP bytes further per step
+            const uint32_t ta = tb + UM_TA + ACOLS * ab;
             const uint64_t bd = umma_desc_k(smem_u32(bring + slot * XB::BLK) + h * 8 * XB::KSTEP, 128, 256);
+            uint64_t bds[8];
+            uint32_t tas[8];
 #pragma unroll
-            for (uint32_t t = 0; t < 8; t++)
-              umma_ts(td, ta + 8 * t, bd + t * (XB::KSTEP >> 4), idesc, (h | t) != 0);
+            for (uint32_t t = 0; t < 8; t++) {
+              bds[t] = bd + t * (XB::KSTEP >> 4);
+              tas[t] = ta + 8 * t;
+            }
+            uint64_t a2d = 0, b2d = 0;
+            if (h == 0) {
+              a2d = umma_desc_k(smem_u32(a2buf + me * L::A2), 128, 256);
+              b2d = umma_desc_k(smem_u32(bring + slot * XB::BLK + XB::OFF_B2), 128, 256);
+            }
+            tc_fence_after();
+#pragma unroll
+            for (uint32_t t = 0; t < 8; t++) umma_ts(td, tas[t], bds[t], idesc, (h | t) != 0);
             if constexpr (QT == 14) {
 #pragma unroll
-              for (uint32_t t = 0; t < 8; t++) umma_ts(td, ta + 64 + 8 * t, bd + t * (XB::KSTEP >> 4), idesc, 1u);
+              for (uint32_t t = 0; t < 8; t++) umma_ts(td, tas[t] + 64, bds[t], idesc, 1u);
             }
-            if (h == 0)
-              umma_ss(tb + UM_TD2 + 64u * (gb & 1), umma_desc_k(smem_u32(a2buf + (gb & 1) * L::A2), 128, 256),
-                      umma_desc_k(smem_u32(bring + slot * XB::BLK + XB::OFF_B2), 128, 256), idesc, 0u);
+            if (h == 0) umma_ss(td2, a2d, b2d, idesc, 0u);
             umma_commit(&bar_afree[ab]);
-            if (h == 1) umma_commit(&bar_dfull[gb & 1]);
+            if (h == 1) umma_commit(&bar_dfull[me]);
           }
         }
       }
       // teardown: every MMA issued is complete
-      umma_commit(&bar_fin);
-      um_drain(&bar_fin, 0, a.err);
+      umma_commit(&bar_fin[me]);
+      um_drain(&bar_fin[me], 0, a.err);
     }
   } else if (warp < UM_RW) {
     // --------------------------------------------- row warps: A operands
