@@ -457,23 +457,29 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       for (uint32_t st = 0; st < S && st < cnt; st++) um_drain(&full[st], ((cnt - st + S - 1) / S - 1) & 1u, a.err);
     }
   } else if (warp >= UM_MMAW) {
-    // ----------------------------- MMA issuers: blocks gb with gb % 2 == me
+    // ---------------------- MMA issuers: blocks gb with gb % NIS == me.
+    // Every barrier an issuer waits on must see each of its phases: with two
+    // issuers (Q4_K) block parity selects the issuer's own A buffers, B slots
+    // (an even number of them), D and D2. Q6_K's two A buffers are shared by
+    // consecutive blocks, whose MMAs cannot overlap anyway: one issuer.
+    constexpr uint32_t NIS = QT == 12 ? 2 : 1;
+    static_assert(NIS == 1 || (NA % 4 == 0 && BS % 2 == 0), "per-issuer barriers");
     const uint32_t me = warp - UM_MMAW;
-    if (lane == 0) {
+    if (lane == 0 && me < NIS) {
       const uint32_t idesc = umma_idesc_f16(128, N);
       uint32_t gb = 0;
       for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
         const uint32_t ks = unit % p.ksplit, nblk = min(p.slice, nb - ks * p.slice);
         for (uint32_t i = 0; i < nblk; i++, gb++) {
-          if ((gb & 1) != me) continue;
-          const uint32_t slot = gb % BS, td = tb + UM_TD + 64u * me, td2 = tb + UM_TD2 + 64u * me;
+          if (gb % NIS != me) continue;
+          const uint32_t db = gb & 1, slot = gb % BS, td = tb + UM_TD + 64u * db, td2 = tb + UM_TD2 + 64u * db;
 #pragma unroll
           for (uint32_t h = 0; h < 2; h++) {
             const uint32_t hb = 2 * gb + h, ab = hb % NA;
             um_wait(&bar_afull[ab], (hb / NA) & 1u, a.err, abort);
             if (h == 0) {
               um_wait(&bar_bfull[slot], (gb / BS) & 1u, a.err, abort);
-              if (gb >= 2) um_wait(&bar_dfree[me], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 read
+              if (gb >= 2) um_wait(&bar_dfree[db], ((gb >> 1) + 1) & 1u, a.err, abort);  // block gb - 2 read
             }
             if (*abort) continue;
             // operands first, then the MMAs back to back: K step t of the half-block
@@ -489,7 +495,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             }
             uint64_t a2d = 0, b2d = 0;
             if (h == 0) {
-              a2d = umma_desc_k(smem_u32(a2buf + me * L::A2), 128, 256);
+              a2d = umma_desc_k(smem_u32(a2buf + db * L::A2), 128, 256);
               b2d = umma_desc_k(smem_u32(bring + slot * XB::BLK + XB::OFF_B2), 128, 256);
             }
             tc_fence_after();
@@ -501,7 +507,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             }
             if (h == 0) umma_ss(td2, a2d, b2d, idesc, 0u);
             umma_commit(&bar_afree[ab]);
-            if (h == 1) umma_commit(&bar_dfull[me]);
+            if (h == 1) umma_commit(&bar_dfull[db]);
           }
         }
       }
