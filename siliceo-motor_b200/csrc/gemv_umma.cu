@@ -665,13 +665,15 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
         um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
         continue;
       }
-      // K-split: publish this slice; the last CTA of the group sums the slices in order
-      const size_t stride = (size_t)p.tiles * 16u * a.batch;
-      float* mine = a.ks_part + ((size_t)tile * 16u + rr) * a.batch;
+      // K-split: publish this slice ([slice][column][row]: a warp's rows are
+      // consecutive); the last CTA of the group sums the slices in order
+      const uint32_t R = p.tiles * 16u;
+      const size_t stride = (size_t)R * a.batch;
+      float* mine = a.ks_part + (size_t)tile * 16u + rr;
       if (valid) {
 #pragma unroll
         for (uint32_t i = 0; i < NB; i++)
-          if (i < a.batch) mine[ks * stride + i] = y[i];
+          if (i < a.batch) mine[ks * stride + (size_t)i * R] = y[i];
       }
       __threadfence();
       named_bar(1, UM_EW * 32);
@@ -685,9 +687,9 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
           for (uint32_t k = 0; k < p.ksplit; k++) {  // in slice order; the columns' loads are independent
             float t[NB];
 #pragma unroll
-            for (uint32_t i = 0; i < NB; i++) t[i] = i < a.batch ? __ldcg(mine + k * stride + i) : 0.f;
+            for (uint32_t i = 0; i < NB; i++) t[i] = __ldcg(mine + k * stride + (size_t)min(i, a.batch - 1) * R);
 #pragma unroll
-            for (uint32_t i = 0; i < NB; i++) y[i] += t[i];
+            for (uint32_t i = 0; i < NB; i++) y[i] += i < a.batch ? t[i] : 0.f;
           }
         um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
         if (threadIdx.x == UM_EW0 * 32) a.ks_cnt[rg] = 0;  // ready for the next launch
@@ -695,6 +697,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     }
   }
   // ------------------------------------------------------------ teardown
+  // (each warp reconverges first: the roles above leave lanes 1..31 of the
+  // producer and MMA warps idle while lane 0 works, and the CTA barrier
+  // must count whole warps that have all finished)
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == UM_MMAW) {
