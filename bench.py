@@ -356,6 +356,7 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     e2e_s = allmax(time.perf_counter() - t0)
     barrier()
     h2d, d2h = model.step_io_bytes()
+    step_kernels = model.step_launches(batch)  # kernel nodes of the decode-step graph
     model.free()  # every rank at the same point (tensor parallel: the group's teardown barrier)
     if rank != 0:
         return
@@ -375,7 +376,6 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     achieved = kbytes / (kus / 1e6) / 1e9
     tokens = batch * args.steps * (1 if split else world)
     value = tokens / (ms / 1e3)
-    L_ = L
     line = {
         "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -401,7 +401,7 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
         # per step and rank: embed+norm; per layer QKV (batched: one launch per weight type, 2), attention
         # split, combine, O, gate/up, down; head, sampler, record; tensor parallel adds 2 all-reduce
         # kernels per layer and the logit gather
-        "gpu_launches": world * args.steps * (L_ * (6 + (batch > 1) + 2 * split) + 4 + split),
+        "gpu_launches": world * args.steps * step_kernels,
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline and args.workload not in TP_WORKLOADS:

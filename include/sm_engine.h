@@ -120,6 +120,10 @@ int sm_model_stream(const sm_model* m, void** stream);
  * sampler state of every row, one pinned block) and device->host (tokens,
  * RNG states). */
 int sm_model_step_io_bytes(const sm_model* m, uint64_t* h2d, uint64_t* d2h);
+/* Kernels one sm_decode_run step of n_rows sequences launches (the kernel
+ * nodes of its CUDA graph; available after such a run). No reference
+ * counterpart. */
+int sm_model_step_launches(const sm_model* m, uint64_t n_rows, uint64_t* out);
 
 /* ------------------------------------------------------------------------
  * Sequence state. Replaces `s_models::state::SeqState` for dense models

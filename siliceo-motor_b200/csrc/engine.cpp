@@ -273,6 +273,7 @@ struct sm_model {
   std::unordered_map<float*, uint32_t> page_refs;
   std::map<uint32_t, cudaGraphExec_t> graphs;       // one step, state from the host
   std::map<uint32_t, cudaGraphExec_t> run_graphs;   // one step, state carried on the device
+  std::map<uint32_t, uint64_t> run_graph_kernels;    // kernel launches in each of them
   uint32_t* hist = nullptr;  // [HIST_TOKENS] tokens recorded by decode runs
   uint32_t* hist_ctr = nullptr;
   std::mutex mu;
@@ -1028,6 +1029,17 @@ int run_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
     set_error(std::string("cuda: decode-run graph capture failed: ") + cudaGetErrorString(e != cudaSuccess ? e : e2));
     return SM_ERR_CUDA;
   }
+  size_t n_nodes = 0;
+  uint64_t n_kernels = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n_nodes) == cudaSuccess && n_nodes) {
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (cudaGraphGetNodes(g, nodes.data(), &n_nodes) == cudaSuccess)
+      for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) n_kernels++;
+      }
+  }
+  cudaGetLastError();
   cudaGraphExec_t ex = nullptr;
   e = cudaGraphInstantiate(&ex, g, 0);
   cudaGraphDestroy(g);
@@ -1035,6 +1047,7 @@ int run_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
     set_error(std::string("cuda: graph instantiate: ") + cudaGetErrorString(e));
     return SM_ERR_CUDA;
   }
+  m->run_graph_kernels[B] = n_kernels;
   m->run_graphs[B] = ex;
   *out = ex;
   return SM_OK;
@@ -1182,6 +1195,17 @@ int sm_model_step_io_bytes(const sm_model* m, uint64_t* h2d, uint64_t* d2h) {
   return SM_OK;
 }
 
+int sm_model_step_launches(const sm_model* m, uint64_t n_rows, uint64_t* out) {
+  if (!m || !out) { set_error("null argument"); return SM_ERR_ARG; }
+  std::lock_guard<std::mutex> lk(const_cast<sm_model*>(m)->mu);
+  auto it = m->run_graph_kernels.find((uint32_t)n_rows);
+  if (n_rows > 0xFFFFFFFFull || it == m->run_graph_kernels.end()) {
+    set_error("sm_model_step_launches: no decode run of that many sequences has been made");
+    return SM_ERR_STATE;
+  }
+  *out = it->second;
+  return SM_OK;
+}
 int sm_model_stream(const sm_model* m, void** stream) {
   if (guard_model(m) || !stream) return SM_ERR_ARG;
   *stream = (void*)m->stream;

@@ -112,6 +112,7 @@ SIGNATURES = {
     "sm_model_weight_bytes": (C.c_int, [P, PU64]),
     "sm_model_stream": (C.c_int, [P, C.POINTER(P)]),
     "sm_model_step_io_bytes": (C.c_int, [P, PU64, PU64]),
+    "sm_model_step_launches": (C.c_int, [P, U64, PU64]),
     "sm_cache_new": (C.c_int, [P, U64, C.POINTER(P)]),
     "sm_cache_free": (C.c_int, [P]),
     "sm_cache_len": (C.c_int, [P, PU64]),
@@ -363,6 +364,12 @@ class Model:
         h, a, b = C.c_uint64(), C.c_uint64(), C.c_uint64()
         _check(lib().sm_model_kv_pages(self.h, C.byref(h), C.byref(a), C.byref(b)))
         return h.value, a.value, b.value
+
+    def step_launches(self, n_rows: int) -> int:
+        """Kernels one decode_run step of n_rows sequences launches."""
+        v = C.c_uint64()
+        _check(lib().sm_model_step_launches(self.h, n_rows, C.byref(v)))
+        return v.value
 
     def stream(self) -> int:
         v = C.c_void_p()
