@@ -262,21 +262,23 @@ __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, ui
 }
 
 // ------------------------------------------------------- x prep kernel ----
-// One CTA per 256-block: the B image of x[:, 256 b .. 256 b + 255] for all
-// padded columns (column c: lanes c * LPC .. + LPC - 1, each IPL items of 8
-// consecutive values). CTA 0 also writes the input-norm scales.
+// One CTA per (256-block, 8 columns): the B image of x[c, 256 b .. 256 b +
+// 255] for those padded columns (column c: lanes (c % 8) * LPC .. + LPC - 1,
+// each IPL items of 8 consecutive values). CTA (0, 0) also writes the
+// input-norm scales.
+constexpr uint32_t UM_XPREP_COLS = 8;
 template <int NB, int QT>
 __global__ void __launch_bounds__(UM_XPREP_THREADS) umma_xprep_kernel(const __grid_constant__ GemvArgs a, uint32_t nb) {
   using L = UmBlob<NB>;
-  constexpr uint32_t LPC = UM_XPREP_THREADS / NB, IPL = NB / 4;  // lanes per column, items per lane
-  constexpr uint32_t IPS = QT == 12 ? 4 : 2;                    // items per sub-block
+  constexpr uint32_t LPC = UM_XPREP_THREADS / UM_XPREP_COLS, IPL = 32 / LPC;  // lanes per column, items per lane
+  constexpr uint32_t IPS = QT == 12 ? 4 : 2;                                 // items per sub-block
   constexpr uint32_t NXS = IPL / IPS > 0 ? IPL / IPS : 1;
   pdl_trigger();
   pdl_wait();
-  const uint32_t blk = blockIdx.x, xt = threadIdx.x, c = xt / LPC, u = xt % LPC;
+  const uint32_t blk = blockIdx.x, xt = threadIdx.x, c = blockIdx.y * UM_XPREP_COLS + xt / LPC, u = xt % LPC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* out = a.xblob + (size_t)blk * L::BLK;
-  if (blk == 0) {
+  if (blk == 0 && blockIdx.y == 0) {
     float* s_in = reinterpret_cast<float*>(a.xblob + (size_t)nb * L::BLK);
     for (uint32_t cc = warp; cc < a.batch; cc += UM_XPREP_THREADS / 32) {
       const float v = input_scale(a, cc);
@@ -853,7 +855,7 @@ cudaError_t launch_gemv_umma(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   if (!um_plan(a, sms, &p)) return cudaErrorNotSupported;
   if (n_parts) *n_parts = p.tiles;
   const uint32_t nb8 = um_nb8(a.batch), qt = a.seg[0].w.type, nb = a.seg[0].w.n_in >> 8;
-  e = launch_pdl(xp_kernel(nb8, qt), dim3(nb), dim3(UM_XPREP_THREADS), 0, st, a, nb);
+  e = launch_pdl(xp_kernel(nb8, qt), dim3(nb, nb8 / UM_XPREP_COLS), dim3(UM_XPREP_THREADS), 0, st, a, nb);
   if (e != cudaSuccess) return e;
   return launch_pdl(um_kernel(nb8, qt), dim3(p.grid), dim3(UM_THREADS), p.smem, st, a, p);
 }
