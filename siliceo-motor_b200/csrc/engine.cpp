@@ -590,7 +590,7 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
     uint64_t need_part = 0;
     uint32_t need_cnt = 0;
     // a launch of these segments: batch 1 (gemv_tc) and batches up to R
-    // (gemv_tcb, one launch per weight type)
+    // (gemv_umma, or gemv_tcb without its x image; one launch per weight type)
     auto need = [&](std::initializer_list<const DW*> ws) {
       GemvArgs a{};
       for (const DW* w : ws) a.seg[a.nseg++] = seg(*w, nullptr, 0, nullptr, EPI_STORE);

@@ -1,7 +1,7 @@
-// Device helpers of the tensor-core GEMVs (gemv_tc.cu: batch 1, gemv_tcb.cu:
-// batches of 2..32): mma.sync, shared-memory loads, the mbarrier-completed
-// bulk copies of the per-warp weight rings (with bounded waits), the
-// quantized-value -> f16 operand tricks, and the hi/lo f16 split of x.
+// Device helpers of the tensor-core GEMVs (gemv_tc.cu: batch 1; gemv_umma.cu
+// and gemv_tcb.cu: batches of 2..32): mma.sync, shared-memory loads, the
+// mbarrier-completed bulk copies of the weight rings (with bounded waits),
+// the quantized-value -> f16 operand tricks, and the hi/lo f16 split of x.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
