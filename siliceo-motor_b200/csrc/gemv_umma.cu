@@ -227,7 +227,9 @@ __device__ __forceinline__ void um_q6_ah(const uint2 (&w)[3][2], const int32_t (
 }
 
 // Epilogue of the calling row (y[i]: column c0 + i, already times the
-// input-norm scale). Every lane of the warp calls it.
+// input-norm scale). Every lane of the warp calls it. The segment and the
+// row's constants are read once into registers: read through the parameter
+// reference they would be reloaded after every store of the column loop.
 template <int NC>
 __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, uint32_t n_parts, bool valid,
                                             uint32_t rr, uint32_t c0, const float (&y)[NC]) {
@@ -235,28 +237,67 @@ __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, ui
   uint32_t si = 0;
   if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
   if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
-  const GemvSeg& sg = a.seg[si];
-  const uint32_t o = (tile - sg.cta_begin) * 16u + rr;
+  const GemvSeg sg = a.seg[si];
+  const uint32_t o = (tile - sg.cta_begin) * 16u + rr, batch = a.batch, epi = sg.epi;
+  const bool row_ok = valid && o < sg.w.n_out;
   const bool any_resid = a.seg[0].epi == EPI_RESID || (a.nseg > 1 && a.seg[1].epi == EPI_RESID) ||
                          (a.nseg > 2 && a.seg[2].epi == EPI_RESID);
+  if (epi == EPI_STORE || epi == EPI_ADD || epi == EPI_RESID) {
+    // single-row epilogues of epi_single, with the loop-invariant loads hoisted
+    const float bo = (sg.bias && row_ok) ? sg.bias[o] : 0.f;
+    float* const yb = sg.y + o;
+    const uint32_t ldy = sg.ldy;
+    float* const xnb = epi == EPI_RESID ? a.xn + o : nullptr;
+    const uint32_t ldxn = a.ldxn;
+    const float nwo = (epi == EPI_RESID && row_ok) ? a.nw[o] : 0.f;
+    float* const parts = a.out_parts;
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+      const uint32_t col = c0 + i;
+      const bool ok = row_ok && col < batch;
+      float xv = 0.f;
+      if (ok) {
+        const float v = sg.bias ? y[i] + bo : y[i];
+        float* yy = yb + (size_t)col * ldy;
+        if (epi == EPI_STORE) {
+          *yy = v;
+        } else if (epi == EPI_ADD) {
+          *yy = *yy + v;
+        } else {  // EPI_RESID: x += v (qwen2.rs:536-538, 549-551)
+          xv = *yy + v;
+          *yy = xv;
+          xnb[(size_t)col * ldxn] = xv * nwo;
+        }
+      }
+      if (any_resid) {  // partial sum of x^2 over the tile's 16 rows, per column
+        float s2 = xv * xv;
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 8);
+        if ((lane & 15) == 0 && valid && col < batch && epi == EPI_RESID) parts[(size_t)col * n_parts + tile] = s2;
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < NC; i++) {
     const uint32_t col = c0 + i;
     const float v = y[i], nv = __shfl_xor_sync(0xffffffffu, v, 1);
-    const bool ok = valid && col < a.batch && o < sg.w.n_out;
+    const bool ok = row_ok && col < batch;
     float xv = 0.f;
-    if (epi_is_pair(sg.epi)) {
+    if (epi_is_pair(epi)) {
       if (ok && !(lane & 1)) epi_pair(a, sg, o, col, v, nv);
     } else if (ok) {
       xv = epi_single(a, sg, o, col, v);
     }
-    if (any_resid) {  // partial sum of x^2 over the tile's 16 rows, per column
+    if (any_resid) {
       float s2 = xv * xv;
       s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
       s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
       s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
       s2 += __shfl_xor_sync(0xffffffffu, s2, 8);
-      if ((lane & 15) == 0 && valid && col < a.batch && sg.epi == EPI_RESID) a.out_parts[(size_t)col * n_parts + tile] = s2;
+      if ((lane & 15) == 0 && valid && col < batch && epi == EPI_RESID) a.out_parts[(size_t)col * n_parts + tile] = s2;
     }
   }
 }
