@@ -295,23 +295,39 @@ __device__ __forceinline__ void tc_epilogue(const GemvArgs& a, uint32_t tile, fl
   uint32_t si = 0;
   if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
   if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
-  const GemvSeg& sg = a.seg[si];
-  const uint32_t row0 = (tile - sg.cta_begin) * 16u;
-  if (epi_is_pair(sg.epi)) {
+  // the segment by value, and the residual epilogue's pointers read before any
+  // store: read through the parameter reference after a store they are
+  // fetched again
+  const GemvSeg sg = a.seg[si];
+  const uint32_t row0 = (tile - sg.cta_begin) * 16u, epi = sg.epi;
+  if (epi_is_pair(epi)) {
     const float ng = __shfl_down_sync(0xffffffffu, vg, 4), nh = __shfl_down_sync(0xffffffffu, vh, 4);
     if (!(g & 1) && t < 2) {
       const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
       if (o < sg.w.n_out) epi_pair(a, sg, o, 0, t ? vh : vg, t ? nh : ng);
     }
   } else {
+    float* const parts = a.out_parts;
+    float* const xnp = a.xn;
     float xn = 0.f;
     if (t < 2) {
       const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
-      if (o < sg.w.n_out) xn = epi_single(a, sg, o, 0, t ? vh : vg);
+      if (o < sg.w.n_out) {
+        if (epi == EPI_RESID) {  // x += v, then the next RMSNorm's x * w (epi_single, column 0)
+          const float nwo = a.nw[o];
+          float v = t ? vh : vg;
+          if (sg.bias) v = v + sg.bias[o];
+          xn = sg.y[o] + v;
+          sg.y[o] = xn;
+          xnp[o] = xn * nwo;
+        } else {
+          xn = epi_single(a, sg, o, 0, t ? vh : vg);
+        }
+      }
     }
-    if (sg.epi == EPI_RESID) {  // partial sum of x^2 over the tile's rows
+    if (epi == EPI_RESID) {  // partial sum of x^2 over the tile's rows
       const float s2 = warp_sum(xn * xn);
-      if (lane == 0) a.out_parts[tile] = s2;
+      if (lane == 0) parts[tile] = s2;
     }
   }
 }
