@@ -18,14 +18,17 @@
 //             their sum is sc_s * v / 16 for the stored v = q + 32 = ql +
 //             16 qh, and each stays exact in f16 where sc_s * v would not)
 //     with one LOP3 (mask | 0x6400 exponent) and one HFMA2 per two weights;
-//   * one thread issues the MMAs, and per block one more with both operands
-//     in shared memory for the per-sub-block term: A2 = the Q4_K mins m_s or
-//     the Q6_K scales sc_s, B2 = sum of x over sub-block s (times 2^-6);
-//   * after each block the row warps read both accumulators and apply the
-//     block's d / dmin in f32 (dequant.rs:98-126, 178-206):
+//   * two MMA warps (one for Q6_K) take alternate blocks: one thread each
+//     issues the block's MMAs, and one more with both operands in shared
+//     memory for the per-sub-block term: A2 = the Q4_K mins m_s or the Q6_K
+//     scales sc_s, B2 = sum of x over sub-block s (times 2^-6);
+//   * four epilogue warps (one row per thread) read both accumulators after
+//     each block and apply the block's d / dmin in f32 (dequant.rs:98-126,
+//     178-206):
 //       Q4_K: y += u * (d * D - 64 * dmin * D2)
 //       Q6_K: y += u * d * (16 * D - 2048 * D2)
-//     with u = 1 / (the block's x scale of the column).
+//     with u = 1 / (the block's x scale of the column), then run the K-split
+//     fixup and the fused epilogue.
 // K orders of A and B agree: item i of a block (weights 8i .. 8i + 7) is K
 // step i / 2 (16 wide), core-matrix half i % 2, in the order 0 2 1 3 4 6 5 7
 // that one mask of a 32-bit quant word yields (weights e, e + 2 per f16x2).
@@ -34,8 +37,8 @@
 // sets the launch's error word and a CTA-wide abort flag after which the
 // other waits return at once; the CTA then waits (bounded) for its own MMAs
 // and copies, frees its tensor memory and exits. K-splits end in the
-// deterministic last-arriver fixup of the other GEMVs; epilogues are the
-// fused ones of gemv_common.cuh.
+// deterministic last-arriver fixup of the other GEMVs (slices summed in
+// order); epilogues are the fused ones of gemv_common.cuh.
 #include <cuda_fp16.h>
 
 #include <algorithm>
