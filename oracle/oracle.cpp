@@ -8,10 +8,14 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <immintrin.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <condition_variable>
 #include <functional>
+#include <mutex>
 #include <thread>
 
 namespace orc {
@@ -180,17 +184,20 @@ void dequant_q6_k(const uint8_t* b, float* out) {  // dequant.rs:178-206
   int yoff = 0;
   for (int n = 0; n < 2; n++) {
     int qloff = n * 64, qhoff = n * 32, scoff = n * 8;
-    for (int l = 0; l < 32; l++) {
-      int is = l / 16;
-      int32_t q1 = (int32_t)((ql[qloff + l] & 0x0F) | (((qh[qhoff + l] >> 0) & 3) << 4)) - 32;
-      int32_t q2 = (int32_t)((ql[qloff + l + 32] & 0x0F) | (((qh[qhoff + l] >> 2) & 3) << 4)) - 32;
-      int32_t q3 = (int32_t)((ql[qloff + l] >> 4) | (((qh[qhoff + l] >> 4) & 3) << 4)) - 32;
-      int32_t q4 = (int32_t)((ql[qloff + l + 32] >> 4) | (((qh[qhoff + l] >> 6) & 3) << 4)) - 32;
+    for (int is = 0; is < 2; is++) {  // is = l / 16: the scale is fixed over 16 values of l
       // (d * sc) * q, left to right as written in the reference
-      out[yoff + l] = d * (float)(int8_t)sc[scoff + is] * (float)q1;
-      out[yoff + l + 32] = d * (float)(int8_t)sc[scoff + is + 2] * (float)q2;
-      out[yoff + l + 64] = d * (float)(int8_t)sc[scoff + is + 4] * (float)q3;
-      out[yoff + l + 96] = d * (float)(int8_t)sc[scoff + is + 6] * (float)q4;
+      const float s1 = d * (float)(int8_t)sc[scoff + is], s2 = d * (float)(int8_t)sc[scoff + is + 2];
+      const float s3 = d * (float)(int8_t)sc[scoff + is + 4], s4 = d * (float)(int8_t)sc[scoff + is + 6];
+      for (int l = 16 * is; l < 16 * is + 16; l++) {
+        int32_t q1 = (int32_t)((ql[qloff + l] & 0x0F) | (((qh[qhoff + l] >> 0) & 3) << 4)) - 32;
+        int32_t q2 = (int32_t)((ql[qloff + l + 32] & 0x0F) | (((qh[qhoff + l] >> 2) & 3) << 4)) - 32;
+        int32_t q3 = (int32_t)((ql[qloff + l] >> 4) | (((qh[qhoff + l] >> 4) & 3) << 4)) - 32;
+        int32_t q4 = (int32_t)((ql[qloff + l + 32] >> 4) | (((qh[qhoff + l] >> 6) & 3) << 4)) - 32;
+        out[yoff + l] = s1 * (float)q1;
+        out[yoff + l + 32] = s2 * (float)q2;
+        out[yoff + l + 64] = s3 * (float)q3;
+        out[yoff + l + 96] = s4 * (float)q4;
+      }
     }
     yoff += 128;
   }
@@ -399,17 +406,78 @@ std::unique_ptr<Gguf> gguf_open(const std::string& path, std::string* err) {  //
 }
 
 // ---------------------------------------------------------------- model ----
+// A persistent pool of worker threads: parallel_for splits [0, n) into
+// contiguous chunks, one per thread, and returns when all are done. Which
+// thread computes a chunk never changes a result (chunks are independent
+// output elements).
+namespace {
+class Pool {
+ public:
+  ~Pool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  void run(size_t parts, const std::function<void(size_t)>& fn) {
+    std::lock_guard<std::mutex> serial(run_mu_);  // one parallel_for at a time
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      while (workers_.size() + 1 < parts) {
+        const size_t id = workers_.size() + 1;
+        workers_.emplace_back([this, id] { loop(id); });
+      }
+      fn_ = &fn;
+      parts_ = parts;
+      pending_ = parts - 1;
+      gen_++;
+    }
+    cv_.notify_all();
+    fn(0);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_.wait(lk, [this] { return pending_ == 0; });
+    fn_ = nullptr;
+  }
+
+ private:
+  void loop(size_t id) {
+    uint64_t seen = 0;
+    for (;;) {
+      const std::function<void(size_t)>* fn = nullptr;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+        if (id >= parts_) continue;
+        fn = fn_;
+      }
+      (*fn)(id);
+      std::lock_guard<std::mutex> lk(mu_);
+      if (--pending_ == 0) done_.notify_one();
+    }
+  }
+  std::mutex run_mu_, mu_;
+  std::condition_variable cv_, done_;
+  std::vector<std::thread> workers_;
+  const std::function<void(size_t)>* fn_ = nullptr;
+  size_t parts_ = 0, pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+Pool& pool() {
+  static Pool p;
+  return p;
+}
+}  // namespace
+
 static void parallel_for(int threads, size_t n, const std::function<void(size_t, size_t)>& fn) {
   if (threads <= 1 || n < 2) { fn(0, n); return; }
-  size_t t = std::min<size_t>((size_t)threads, n);
-  std::vector<std::thread> pool;
-  size_t chunk = (n + t - 1) / t;
-  for (size_t i = 0; i < t; i++) {
-    size_t b = i * chunk, e = std::min(n, b + chunk);
-    if (b >= e) break;
-    pool.emplace_back(fn, b, e);
-  }
-  for (auto& th : pool) th.join();
+  const size_t t = std::min<size_t>((size_t)threads, n), chunk = (n + t - 1) / t;
+  const size_t parts = (n + chunk - 1) / chunk;
+  pool().run(parts, [&](size_t i) { fn(i * chunk, std::min(n, (i + 1) * chunk)); });
 }
 
 void QWeight::row(size_t o, float* out) const {
@@ -419,6 +487,23 @@ void QWeight::row(size_t o, float* out) const {
   block_layout(type, &bs, &tb);
   size_t row_bytes = n_in / bs * tb;
   dequantize(type, n_in, raw + o * row_bytes, row_bytes, out, nullptr);
+}
+
+// Elements [d0, d0 + n) of row o: whole quant blocks (d0 and n multiples of
+// the block size, which tile_width() guarantees).
+void QWeight::row_range(size_t o, size_t d0, size_t n, float* out) const {
+  if (!dense.empty()) { std::memcpy(out, dense.data() + o * n_in + d0, n * 4); return; }
+  if (type == T_F32) { std::memcpy(out, raw + (o * n_in + d0) * 4, n * 4); return; }
+  uint32_t bs, tb;
+  block_layout(type, &bs, &tb);
+  const size_t row_bytes = n_in / bs * tb;
+  dequantize(type, n, raw + o * row_bytes + d0 / bs * tb, n / bs * tb, out, nullptr);
+}
+size_t QWeight::tile_width() const {
+  if (!dense.empty() || type == T_F32) return 256;
+  uint32_t bs, tb;
+  block_layout(type, &bs, &tb);
+  return bs >= 256 ? bs : 256 / bs * bs;
 }
 
 static bool load_weight(Gguf& g, const std::string& name, QWeight& w, std::string* err) {
@@ -568,40 +653,148 @@ int SeqState::truncate(size_t new_len, std::string* err) {  // state.rs:341-360 
 }
 
 // y(seq×n_out) = x(seq×n_in) @ W^T, each sum sequential over d (qwen2.rs:663-674).
-// Rows are dequantized once and applied to every token; 8 tokens are
-// accumulated side by side, each in its own sequential accumulator.
+// Every output element is its own running sum, updated as sum = sum + w*x
+// (a rounded product, then a rounded add) for d = 0, 1, ... in order, as the
+// reference's loop does. The work is vectorized ACROSS independent sums: a
+// lane of an 8-wide vector holds one row's sum (decode: 32 rows side by
+// side, weights transposed so that one load brings w[o..o+7][d]) or one
+// token's sum (prefill: one row, 32 tokens side by side, x transposed).
+// Lanes never mix, so each result is bit-identical to the scalar loop.
+typedef float v8f __attribute__((vector_size(32)));
+
+static inline v8f v8_load(const float* p) {
+  v8f v;
+  std::memcpy(&v, p, sizeof(v));
+  return v;
+}
+static inline v8f v8_splat(float f) { return v8f{f, f, f, f, f, f, f, f}; }
+
+// wt[d][32] = rows[r][d] for r < 32, d < dl (dl a multiple of 8), by 8x8
+// register transposes (pure data movement).
+static void transpose_tile(const float* rows, size_t ld, size_t dl, float* wt) {
+  for (size_t rb = 0; rb < 32; rb += 8)
+    for (size_t d0 = 0; d0 < dl; d0 += 8) {
+      __m256 r0 = _mm256_loadu_ps(rows + (rb + 0) * ld + d0), r1 = _mm256_loadu_ps(rows + (rb + 1) * ld + d0);
+      __m256 r2 = _mm256_loadu_ps(rows + (rb + 2) * ld + d0), r3 = _mm256_loadu_ps(rows + (rb + 3) * ld + d0);
+      __m256 r4 = _mm256_loadu_ps(rows + (rb + 4) * ld + d0), r5 = _mm256_loadu_ps(rows + (rb + 5) * ld + d0);
+      __m256 r6 = _mm256_loadu_ps(rows + (rb + 6) * ld + d0), r7 = _mm256_loadu_ps(rows + (rb + 7) * ld + d0);
+      __m256 t0 = _mm256_unpacklo_ps(r0, r1), t1 = _mm256_unpackhi_ps(r0, r1);
+      __m256 t2 = _mm256_unpacklo_ps(r2, r3), t3 = _mm256_unpackhi_ps(r2, r3);
+      __m256 t4 = _mm256_unpacklo_ps(r4, r5), t5 = _mm256_unpackhi_ps(r4, r5);
+      __m256 t6 = _mm256_unpacklo_ps(r6, r7), t7 = _mm256_unpackhi_ps(r6, r7);
+      __m256 u0 = _mm256_shuffle_ps(t0, t2, 0x44), u1 = _mm256_shuffle_ps(t0, t2, 0xEE);
+      __m256 u2 = _mm256_shuffle_ps(t1, t3, 0x44), u3 = _mm256_shuffle_ps(t1, t3, 0xEE);
+      __m256 u4 = _mm256_shuffle_ps(t4, t6, 0x44), u5 = _mm256_shuffle_ps(t4, t6, 0xEE);
+      __m256 u6 = _mm256_shuffle_ps(t5, t7, 0x44), u7 = _mm256_shuffle_ps(t5, t7, 0xEE);
+      float* o = wt + d0 * 32 + rb;
+      _mm256_storeu_ps(o + 0 * 32, _mm256_permute2f128_ps(u0, u4, 0x20));
+      _mm256_storeu_ps(o + 1 * 32, _mm256_permute2f128_ps(u1, u5, 0x20));
+      _mm256_storeu_ps(o + 2 * 32, _mm256_permute2f128_ps(u2, u6, 0x20));
+      _mm256_storeu_ps(o + 3 * 32, _mm256_permute2f128_ps(u3, u7, 0x20));
+      _mm256_storeu_ps(o + 4 * 32, _mm256_permute2f128_ps(u0, u4, 0x31));
+      _mm256_storeu_ps(o + 5 * 32, _mm256_permute2f128_ps(u1, u5, 0x31));
+      _mm256_storeu_ps(o + 6 * 32, _mm256_permute2f128_ps(u2, u6, 0x31));
+      _mm256_storeu_ps(o + 7 * 32, _mm256_permute2f128_ps(u3, u7, 0x31));
+    }
+}
+
 static void matmul_rows(const QWeight& w, const float* x, size_t seq, float* y, int threads) {
   const size_t n_in = w.n_in, n_out = w.n_out;
-  parallel_for(threads, n_out, [&](size_t b, size_t e) {
-    std::vector<float> row(n_in);
-    for (size_t o = b; o < e; o++) {
-      w.row(o, row.data());
-      const float* r = row.data();
-      size_t s = 0;
-      for (; s + 8 <= seq; s += 8) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f, a5 = 0.f, a6 = 0.f, a7 = 0.f;
-        const float* x0 = x + s * n_in;
-        for (size_t d = 0; d < n_in; d++) {
-          float wd = r[d];
-          a0 += wd * x0[d];
-          a1 += wd * x0[n_in + d];
-          a2 += wd * x0[2 * n_in + d];
-          a3 += wd * x0[3 * n_in + d];
-          a4 += wd * x0[4 * n_in + d];
-          a5 += wd * x0[5 * n_in + d];
-          a6 += wd * x0[6 * n_in + d];
-          a7 += wd * x0[7 * n_in + d];
+  if (seq < 8) {
+    // decode-sized: groups of 32 rows; K in tiles of (up to) 256 weights: the
+    // tile of all 32 rows is dequantized, transposed to wt[d][32] and applied
+    // to every token, each lane's running sum carried across tiles in d order.
+    const size_t groups = (n_out + 31) / 32, TW = w.tile_width();
+    parallel_for(threads, groups, [&](size_t gb, size_t ge) {
+      std::vector<float> rows(32 * TW, 0.f), wt(32 * TW), acc(32 * seq);
+      for (size_t gi = gb; gi < ge; gi++) {
+        const size_t o0 = gi * 32, nr = std::min<size_t>(32, n_out - o0);
+        std::fill(acc.begin(), acc.end(), 0.f);
+        for (size_t d0 = 0; d0 < n_in; d0 += TW) {
+          const size_t dl = std::min(TW, n_in - d0);
+          for (size_t r = 0; r < nr; r++) w.row_range(o0 + r, d0, dl, rows.data() + r * TW);
+          transpose_tile(rows.data(), TW, dl, wt.data());
+          for (size_t s = 0; s < seq; s++) {
+            const float* xs = x + s * n_in + d0;
+            float* as = acc.data() + s * 32;
+            v8f a0 = v8_load(as), a1 = v8_load(as + 8), a2 = v8_load(as + 16), a3 = v8_load(as + 24);
+            const float* t = wt.data();
+            for (size_t d = 0; d < dl; d++, t += 32) {
+              const v8f xv = v8_splat(xs[d]);
+              a0 = a0 + v8_load(t) * xv;
+              a1 = a1 + v8_load(t + 8) * xv;
+              a2 = a2 + v8_load(t + 16) * xv;
+              a3 = a3 + v8_load(t + 24) * xv;
+            }
+            std::memcpy(as, &a0, 32);
+            std::memcpy(as + 8, &a1, 32);
+            std::memcpy(as + 16, &a2, 32);
+            std::memcpy(as + 24, &a3, 32);
+          }
         }
-        y[(s + 0) * n_out + o] = a0; y[(s + 1) * n_out + o] = a1;
-        y[(s + 2) * n_out + o] = a2; y[(s + 3) * n_out + o] = a3;
-        y[(s + 4) * n_out + o] = a4; y[(s + 5) * n_out + o] = a5;
-        y[(s + 6) * n_out + o] = a6; y[(s + 7) * n_out + o] = a7;
+        for (size_t s = 0; s < seq; s++)
+          for (size_t r = 0; r < nr; r++) y[s * n_out + o0 + r] = acc[s * 32 + r];
       }
-      for (; s < seq; s++) {
+    });
+    return;
+  }
+  // prefill-sized: x transposed per group of 8 tokens (xt[g][d][8]); rows in
+  // groups of 4 against pairs of token groups (8 independent vectors).
+  const size_t ng = seq / 8, tail = seq - 8 * ng;
+  std::vector<float> xt(ng * n_in * 8);
+  for (size_t g = 0; g < ng; g++)
+    for (size_t d = 0; d < n_in; d++)
+      for (size_t l = 0; l < 8; l++) xt[(g * n_in + d) * 8 + l] = x[(8 * g + l) * n_in + d];
+  const size_t rgroups = (n_out + 3) / 4;
+  parallel_for(threads, rgroups, [&](size_t b, size_t e) {
+    std::vector<float> rowbuf(4 * n_in, 0.f);
+    for (size_t rg = b; rg < e; rg++) {
+      const size_t o0 = rg * 4, nr = std::min<size_t>(4, n_out - o0);
+      for (size_t r = 0; r < nr; r++) w.row(o0 + r, rowbuf.data() + r * n_in);
+      const float* r0 = rowbuf.data();
+      const float* r1 = r0 + n_in;
+      const float* r2 = r1 + n_in;
+      const float* r3 = r2 + n_in;
+      auto store = [&](size_t g, size_t r, const v8f& a) {
+        if (r < nr)
+          for (size_t l = 0; l < 8; l++) y[(8 * g + l) * n_out + o0 + r] = a[l];
+      };
+      size_t g = 0;
+      for (; g + 2 <= ng; g += 2) {
+        v8f a00 = v8_splat(0.f), a01 = a00, a10 = a00, a11 = a00, a20 = a00, a21 = a00, a30 = a00, a31 = a00;
+        const float* t0 = xt.data() + g * n_in * 8;
+        const float* t1 = t0 + n_in * 8;
+        for (size_t d = 0; d < n_in; d++) {
+          const v8f x0 = v8_load(t0 + 8 * d), x1 = v8_load(t1 + 8 * d);
+          const v8f w0 = v8_splat(r0[d]), w1 = v8_splat(r1[d]), w2 = v8_splat(r2[d]), w3 = v8_splat(r3[d]);
+          a00 = a00 + w0 * x0; a01 = a01 + w0 * x1;
+          a10 = a10 + w1 * x0; a11 = a11 + w1 * x1;
+          a20 = a20 + w2 * x0; a21 = a21 + w2 * x1;
+          a30 = a30 + w3 * x0; a31 = a31 + w3 * x1;
+        }
+        store(g, 0, a00); store(g + 1, 0, a01); store(g, 1, a10); store(g + 1, 1, a11);
+        store(g, 2, a20); store(g + 1, 2, a21); store(g, 3, a30); store(g + 1, 3, a31);
+      }
+      for (; g < ng; g++) {
+        v8f a0 = v8_splat(0.f), a1 = a0, a2 = a0, a3 = a0;
+        const float* t0 = xt.data() + g * n_in * 8;
+        for (size_t d = 0; d < n_in; d++) {
+          const v8f x0 = v8_load(t0 + 8 * d);
+          a0 = a0 + v8_splat(r0[d]) * x0;
+          a1 = a1 + v8_splat(r1[d]) * x0;
+          a2 = a2 + v8_splat(r2[d]) * x0;
+          a3 = a3 + v8_splat(r3[d]) * x0;
+        }
+        store(g, 0, a0); store(g, 1, a1); store(g, 2, a2); store(g, 3, a3);
+      }
+      for (size_t s = 8 * ng; s < 8 * ng + tail; s++) {
         const float* xs = x + s * n_in;
-        float sum = 0.f;
-        for (size_t d = 0; d < n_in; d++) sum += r[d] * xs[d];
-        y[s * n_out + o] = sum;
+        for (size_t r = 0; r < nr; r++) {
+          const float* rr = rowbuf.data() + r * n_in;
+          float sum = 0.f;
+          for (size_t d = 0; d < n_in; d++) sum += rr[d] * xs[d];
+          y[s * n_out + o0 + r] = sum;
+        }
       }
     }
   });

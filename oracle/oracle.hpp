@@ -104,6 +104,8 @@ struct QWeight {
   size_t n_out = 0, n_in = 0;
   std::vector<float> dense;  // used when rows do not fall on block boundaries
   void row(size_t o, float* out) const;
+  void row_range(size_t o, size_t d0, size_t n, float* out) const;  // whole blocks
+  size_t tile_width() const;  // a multiple of the block size, about 256
 };
 
 struct LayerW {
