@@ -63,8 +63,9 @@ def peaks():
 
 
 def model_file(preset: int, local_rank: int, barrier) -> str:
-    """The synthetic GGUF of a preset, generated once per machine and reused."""
-    import smotor
+    """The synthetic GGUF of a preset, generated once per machine and reused.
+    It is written by a child process, so that the calling process (the
+    reference arm among them) never loads the engine's library."""
     d = os.environ.get("SM_CACHE_DIR", os.path.join(tempfile.gettempdir(), "smotor_cache"))
     os.makedirs(d, exist_ok=True)
     path = os.path.join(d, f"preset{preset}_seed0_v1.gguf")
@@ -72,7 +73,11 @@ def model_file(preset: int, local_rank: int, barrier) -> str:
         with open(path + ".lock", "w") as lk:
             fcntl.flock(lk, fcntl.LOCK_EX)
             if not os.path.exists(path):
-                smotor.synth_write(smotor.synth_preset(preset), path)
+                code = ("import sys; sys.path.insert(0, %r); import smotor; "
+                        "smotor.synth_write(smotor.synth_preset(%d), %r)" % (os.path.join(ROOT, "siliceo-motor_b200"),
+                                                                             preset, path + ".part"))
+                subprocess.run([sys.executable, "-c", code], check=True)
+                os.replace(path + ".part", path)
             fcntl.flock(lk, fcntl.LOCK_UN)
     barrier()
     return path
@@ -152,23 +157,48 @@ def setup_sequences(model, V, batch, prompt_len, kind, extra):
     return caches, toks
 
 
-def cpu_baseline(path, budget_s=15.0):
-    """The oracle (C++ port of the reference CPU path) on all host cores: a
-    short prompt, then as many decode steps as fit in the budget."""
+def cpu_decode(path, prompt_len, steps, warmup, single_steps):
+    """The oracle (the reference's CPU path restated in C++: the same f32
+    operations in the same order) decoding greedily at the workload's context:
+    the prompt prefilled on all host cores, then `warmup` untimed and `steps`
+    timed decode steps on all cores, then `single_steps` timed steps on one
+    core (the reference's own execution model: it has no threading)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle as orc
     threads = os.cpu_count() or 1
     m = orc.Model(path, threads=threads)
-    c = m.new_cache(64)
-    m.forward_cached(c, [1, 2, 3, 4])
-    tok, n, t0 = 5, 0, time.perf_counter()
-    while n < 2 or (time.perf_counter() - t0 < budget_s and n < 48):
+    V = m.config.vocab_size
+    prompt = np.random.default_rng(0).integers(0, V, prompt_len).tolist()
+    c = m.new_cache(prompt_len + warmup + steps + single_steps + 8)
+    tok = int(np.argmax(m.forward_cached(c, prompt)))
+    for _ in range(warmup):
         tok = int(np.argmax(m.forward_cached(c, [tok])))
-        n += 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = int(np.argmax(m.forward_cached(c, [tok])))
     dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n} greedy decode steps of the same model after a 4-token prompt "
-                      f"(context 5..{4 + n}; attention is <0.5% of a step's work at 1k context)"}
+    single = None
+    if single_steps:
+        m.set_threads(1)
+        t1 = time.perf_counter()
+        for _ in range(single_steps):
+            tok = int(np.argmax(m.forward_cached(c, [tok])))
+        ds = (time.perf_counter() - t1) / single_steps
+        single = {"s_per_token": ds, "value": 1.0 / ds, "unit": "tok/s", "cores": 1,
+                  "sample": f"{single_steps} greedy decode steps on one core, context {prompt_len + warmup + steps + 1}"
+                            f"..{prompt_len + warmup + steps + single_steps}"}
+    return steps / dt, threads, single
+
+
+def cpu_baseline(path, prompt_len):
+    """Bounded CPU-baseline leg of the engine's line (rank 0, N = 1)."""
+    val, threads, single = cpu_decode(path, prompt_len, steps=6, warmup=1, single_steps=2)
+    out = {"value": val, "unit": "tok/s", "cores": threads, "kind": "port",
+           "sample": f"6 greedy decode steps on {threads} threads after the workload's {prompt_len}-token prompt "
+                     f"(context {prompt_len + 2}..{prompt_len + 7})"}
+    if single:
+        out["single_thread"] = single
+    return out
 
 
 def run_reference(args, rank, world, local_rank, barrier):
@@ -176,28 +206,19 @@ def run_reference(args, rank, world, local_rank, barrier):
     if rank != 0:
         return
     path = model_file(preset, 0, lambda: None)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import pyoracle as orc
-    threads = os.cpu_count() or 1
-    m = orc.Model(path, threads=threads)
-    V = m.config.vocab_size
-    c = m.new_cache(16 + args.warmup + args.steps)
-    tok = int(np.argmax(m.forward_cached(c, [1, 2, 3, 4])))
-    for _ in range(args.warmup):
-        tok = int(np.argmax(m.forward_cached(c, [tok])))
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        tok = int(np.argmax(m.forward_cached(c, [tok])))
-    dt = time.perf_counter() - t0
-    val = args.steps * 1 / dt
-    sample = (f"{args.steps} greedy decode steps (batch 1) after a 4-token prompt; the reference's f32 "
+    val, threads, single = cpu_decode(path, prompt_len, args.steps, args.warmup, 2 if preset != 4 else 0)
+    sample = (f"{args.steps} greedy decode steps (batch 1) after a {prompt_len}-token prompt (context "
+              f"{prompt_len + args.warmup + 1}..{prompt_len + args.warmup + args.steps}); the reference's f32 "
               f"forward_cached restated in C++ and threaded over independent outputs")
+    base = {"value": val, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+    if single:
+        base["single_thread"] = single
     print(json.dumps({
         "impl": "reference", "metric": "decode_tok_per_s", "value": val, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / val,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "description": desc + " (reference CPU path, batch 1)"},
-        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": base,
         "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -405,7 +426,7 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline and args.workload not in TP_WORKLOADS:
-        line["cpu_baseline"] = cpu_baseline(path)
+        line["cpu_baseline"] = cpu_baseline(path, prompt_len)
     print(json.dumps(line), flush=True)
 
 

@@ -151,6 +151,10 @@ int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_o
  * reference's SeqState owns contiguous vectors. */
 int sm_model_kv_pages(const sm_model* m, uint64_t* held, uint64_t* allocated, uint64_t* kv_page_bytes);
 
+/* Row `token` of the embedding table (n_embd floats, host) as the forward's
+ * first kernel gathers it: the exact dequantized row (qwen2.rs:468-472). */
+int sm_model_embedding(sm_model* m, uint32_t token, float* out);
+
 /* ------------------------------------------------------------------------
  * Forward. Device::forward_cached (crates/s-models/src/device.rs:33,
  * crates/s-models/src/qwen2.rs:460-561): processes `n` tokens at absolute
@@ -160,13 +164,33 @@ int sm_model_kv_pages(const sm_model* m, uint64_t* held, uint64_t* allocated, ui
 int sm_forward_cached(sm_model* m, sm_cache* c, const uint32_t* tokens, uint64_t n, float* logits_out);
 
 /* Sampler (crates/s-models/src/sampling.rs:43-60, 94-144). temperature <= 0
- * is greedy (lowest index wins ties); top_k < 0 and top_p < 0 mean None.
+ * is greedy (lowest index wins ties); top_k < 0 and top_p < 0 mean None;
+ * every combination is sampled on the device.
  * The splitmix64 state (sampling.rs:12-41) is passed in and returned. */
 typedef struct {
   float temperature;
   int64_t top_k;
   float top_p;
 } sm_sampler;
+
+/* Sampler::sample / sample_masked (crates/s-models/src/sampling.rs:66-144)
+ * on the device, for logits in host memory: row i (i < n_rows) samples the
+ * `vocab` logits at logits + i * ld with samplers[i] and rng_states[i]
+ * (updated); ld = 0: every row samples the same logits. mask (may be NULL)
+ * has the same layout, 0 = forbidden. The kernel the decode steps run, bit
+ * for bit the reference's result (the reference's f32 rounding at every step,
+ * glibc's expf). Uses the current device; allocates its buffers per call. */
+int sm_sample(const float* logits, uint64_t n_rows, uint64_t ld, uint64_t vocab, const uint8_t* mask,
+              const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens);
+/* softmax (crates/s-models/src/sampling.rs:157-172) of `rows` rows of n
+ * device floats into probs_dev (device, not aliasing x_dev): the sampler's
+ * probabilities, bit for bit the reference's (max, glibc expf, the
+ * left-to-right f32 sum, IEEE division). */
+int sm_softmax(const float* x_dev, uint64_t rows, uint64_t n, float* probs_dev, void* stream);
+/* The sampler's exp on n floats in device memory: glibc's expf (Rust's
+ * f32::exp on x86-64 Linux) for x <= 0 and NaN, bit for bit. No reference
+ * counterpart; exposed so its exactness can be checked. */
+int sm_expf_ref(const float* x_dev, float* y_dev, uint64_t n, void* stream);
 
 /* Initial splitmix64 state for Rng::new(seed). */
 uint64_t sm_rng_seed(uint64_t seed);
@@ -180,6 +204,11 @@ int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* tokens, uint64_t
  * cache advances by one). samplers and rng_states have n entries. */
 int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* tokens,
                     const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens);
+/* sm_decode_batch that also copies the logits its sampler drew from to
+ * logits_out (host, n x vocab floats): forward_cached's return value for each
+ * sequence of the batch (device.rs:33) next to the on-device sample. */
+int sm_decode_batch_logits(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* tokens,
+                           const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens, float* logits_out);
 
 /* n_steps decode steps for each of n sequences entirely on the device: the
  * token sampled at step i is the input of step i+1 (no stop checks; the
@@ -258,18 +287,33 @@ int sm_dequant(const sm_dweight* w, float* out_dev, void* stream);
 /* Dequant-fused GEMV: y_dev[b][o] = sum_d W[o][d] * x_dev[b][d] for b < batch
  * (batch 1..32; qwen2.rs:663-674, kernels/src/lib.rs:709-876). */
 int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream);
+/* Reports whether a bounded wait inside an sm_gemv on this weight gave up
+ * (a weight copy into shared memory did not complete) since the last call:
+ * waits for `stream`, then returns SM_ERR_CUDA (that output is invalid) and
+ * clears the flag, or SM_OK. No reference counterpart: the reference's
+ * kernels have no bounded waits. */
+int sm_gemv_status(const sm_dweight* w, void* stream);
 /* sm_gemv for callers that cannot allocate device memory: hosts that hand out
  * all device memory from their own pool, and latency-critical paths that may
  * not call cudaMalloc (it can synchronize the device). No counterpart in the
- * reference. It allocates nothing: the K-split of the batch-1 kernel keeps
- * its partial sums and arrival counters in a fixed 260 KB device array of the
- * library instead of the scratch sm_dweight_upload allocates for sm_gemv; a
- * split that does not fit runs unsplit. Every call on a device shares that
- * array, so calls that overlap on the GPU race; each call leaves the counters
- * at zero, so nothing needs clearing between calls. The first call on a
- * device looks the array's address up (once per device, with the weight's
- * device current); make that first call before any stream capture. */
+ * reference. It allocates nothing: the K-split of the tensor-core kernels
+ * keeps its partial sums and arrival counters in a fixed 260 KB device array
+ * of the library instead of the scratch sm_dweight_upload allocates for
+ * sm_gemv. A Q4_K/Q6_K shape whose smallest K-split does not fit the array is
+ * refused with SM_ERR_ARG (roughly: ceil(n_in / 8192) * n_out floats, n_out
+ * rounded up to 16, at most 65536; 7168 instead of 8192 for Q6_K; rows of at
+ * most 8192 (Q4_K) or 7168 (Q6_K) inputs always fit). Every call on a device
+ * shares that array, so calls that overlap on the GPU race and their outputs
+ * are wrong; the arrival counters advance by wrapping increments, so every
+ * completed call (overlapping ones and ones whose bounded wait gave up
+ * included) leaves them at zero and later calls are unaffected; nothing
+ * needs clearing. The first call on a device looks the array's address up
+ * (once per device, with the weight's device current); make that first call
+ * before any stream capture. */
 int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batch, void* stream);
+/* sm_gemv_status for the sm_gemv_noalloc calls of the current device (one
+ * error word in fixed device memory, shared by those calls). */
+int sm_gemv_noalloc_status(void* stream);
 
 /* ------------------------------------------------------------------------
  * Synthetic GGUF models (the stand-in for real model files). Shapes and

@@ -9,6 +9,11 @@
 
 #include "oracle.hpp"
 
+#include <algorithm>
+#include <cmath>
+#include <thread>
+#include <vector>
+
 using namespace orc;
 
 namespace {
@@ -173,6 +178,45 @@ size_t orc_sample(const float* logits, const uint8_t* mask, size_t n, float temp
   size_t out = mask ? smp.sample_masked(logits, mask, n, r) : smp.sample(logits, n, r);
   *rng_state = r.s;
   return out;
+}
+
+// Many Sampler::sample[_masked] draws, threaded over rows (each draw is the
+// single-threaded reference computation): row i samples logits + i * ld
+// (ld = 0: every row the same logits) with its own sampler and RNG state.
+void orc_sample_batch(const float* logits, size_t ld, size_t n, const uint8_t* mask, size_t rows,
+                      const float* temperature, const long* top_k, const float* top_p, uint64_t* rng_state,
+                      uint64_t* out, int threads) {
+  std::vector<std::thread> pool;
+  const size_t nt = std::max<size_t>(1, std::min<size_t>((size_t)std::max(threads, 1), rows));
+  for (size_t t = 0; t < nt; t++)
+    pool.emplace_back([&, t] {
+      for (size_t i = t; i < rows; i += nt) {
+        Sampler smp;
+        smp.temperature = temperature[i];
+        smp.top_k = top_k[i];
+        smp.top_p = top_p[i];
+        Rng r(0);
+        r.s = rng_state[i];
+        const float* lg = logits + i * ld;
+        out[i] = mask ? smp.sample_masked(lg, mask + i * ld, n, r) : smp.sample(lg, n, r);
+        rng_state[i] = r.s;
+      }
+    });
+  for (auto& th : pool) th.join();
+}
+
+// The sampler's softmax (sampling.rs:157-172) of one row, in place.
+void orc_softmax(float* x, size_t n) { softmax_row_ref(x, n); }
+
+// glibc's expf (Rust's f32::exp on x86-64 Linux) on n values, threaded.
+void orc_expf_block(const float* x, float* y, size_t n, int threads) {
+  std::vector<std::thread> pool;
+  const size_t nt = std::max<size_t>(1, std::min<size_t>((size_t)std::max(threads, 1), n / 4096 + 1));
+  for (size_t t = 0; t < nt; t++)
+    pool.emplace_back([&, t] {
+      for (size_t i = n * t / nt; i < n * (t + 1) / nt; i++) y[i] = expf(x[i]);
+    });
+  for (auto& th : pool) th.join();
 }
 
 // generate_tokens_seeded (generate.rs:149-250) over the oracle model.

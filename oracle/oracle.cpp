@@ -848,6 +848,8 @@ static void softmax_row(float* x, size_t n) {  // qwen2.rs:726-741
   for (size_t i = 0; i < n; i++) x[i] /= sum;
 }
 
+void softmax_row_ref(float* x, size_t n) { softmax_row(x, n); }  // sampling.rs:157-172 (same steps)
+
 static inline float silu(float x) { return x / (1.0f + expf(-x)); }  // qwen2.rs:743-745
 
 void logits_from_hidden(const Model& m, const float* last_hidden, float* logits) {  // qwen2.rs:425-446

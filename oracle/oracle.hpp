@@ -158,5 +158,6 @@ struct Sampler {  // :43-60
   size_t sample_masked(const float* logits, const uint8_t* mask, size_t n, Rng& rng) const;  // :66-88
 };
 size_t argmax(const float* x, size_t n);  // :147-155
+void softmax_row_ref(float* x, size_t n);  // :157-172
 
 }  // namespace orc

@@ -81,6 +81,11 @@ def lib():
             "orc_rng_next_f32": (C.c_float, [C.POINTER(U64)]),
             "orc_sample": (SZ, [C.POINTER(C.c_float), C.POINTER(C.c_uint8), SZ, C.c_float, C.c_long, C.c_float,
                                 C.POINTER(U64)]),
+            "orc_sample_batch": (None, [C.POINTER(C.c_float), SZ, SZ, C.POINTER(C.c_uint8), SZ,
+                                         C.POINTER(C.c_float), C.POINTER(C.c_long), C.POINTER(C.c_float),
+                                         C.POINTER(U64), C.POINTER(U64), C.c_int]),
+            "orc_expf_block": (None, [C.POINTER(C.c_float), C.POINTER(C.c_float), SZ, C.c_int]),
+            "orc_softmax": (None, [C.POINTER(C.c_float), SZ]),
             "orc_generate": (C.c_int, [P, C.POINTER(C.c_uint32), SZ, C.POINTER(orc_gen_params),
                                        C.POINTER(C.c_uint32), SZ, ON_TOKEN, MASKER, STOP, ON_PREFILL, P, P, SZ,
                                        C.POINTER(C.c_uint32), C.POINTER(orc_gen_result), C.c_char_p, SZ]),
@@ -158,6 +163,43 @@ def sample(logits, temperature=0.0, top_k=None, top_p=None, rng_state: int = 0, 
     idx = lib().orc_sample(_f32p(lg), mk, lg.size, temperature, -1 if top_k is None else top_k,
                            -1.0 if top_p is None else top_p, C.byref(st))
     return int(idx), st.value
+
+
+def sample_batch(logits, samplers, rng_states, mask=None, shared=False):
+    """Many Sampler::sample[_masked] draws (threaded over draws): row i of
+    `logits` (or the single row when shared) with samplers[i] = (temperature,
+    top_k, top_p) (None allowed) and rng_states[i]; returns (ids, new states)."""
+    lg = np.ascontiguousarray(np.asarray(logits, np.float32))
+    n = lg.shape[-1]
+    rows = len(samplers)
+    T = np.array([s[0] for s in samplers], np.float32)
+    K = np.array([-1 if s[1] is None else s[1] for s in samplers], np.int64).astype(C.c_long)
+    Pp = np.array([-1.0 if s[2] is None else s[2] for s in samplers], np.float32)
+    st = np.ascontiguousarray(np.asarray(rng_states, np.uint64))
+    out = np.empty(rows, np.uint64)
+    mk = None
+    if mask is not None:
+        m8 = np.ascontiguousarray(np.asarray(mask, np.uint8))
+        mk = m8.ctypes.data_as(C.POINTER(C.c_uint8))
+    lib().orc_sample_batch(_f32p(lg), 0 if shared else n, n, mk, rows, _f32p(T),
+                           K.ctypes.data_as(C.POINTER(C.c_long)), _f32p(Pp), st.ctypes.data_as(C.POINTER(C.c_uint64)),
+                           out.ctypes.data_as(C.POINTER(C.c_uint64)), os.cpu_count() or 1)
+    return out.astype(np.int64), st
+
+
+def softmax(x):
+    """The sampler's softmax (sampling.rs:157-172) of one row."""
+    y = np.array(x, np.float32, copy=True)
+    lib().orc_softmax(_f32p(y), y.size)
+    return y
+
+
+def expf_glibc(x):
+    """glibc's expf on a float32 array (what Rust's f32::exp calls)."""
+    xx = np.ascontiguousarray(np.asarray(x, np.float32))
+    y = np.empty_like(xx)
+    lib().orc_expf_block(_f32p(xx), _f32p(y), xx.size, os.cpu_count() or 1)
+    return y
 
 
 class SeqState:

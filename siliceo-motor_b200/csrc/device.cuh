@@ -170,7 +170,9 @@ struct GemvArgs {
   const float* sin_t;
   uint32_t layer, hd, kvd;
   // Scratch of the tensor-core batch-1 GEMV when it splits K: per-slice
-  // partial dot products and per-group arrival counters (zero between launches).
+  // partial dot products and per-group arrival counters. A counter advances
+  // with a wrapping increment (atomicInc modulo the split), so it is zero
+  // again after every complete launch without a reset.
   float* ks_part;
   uint32_t* ks_cnt;
   uint32_t ks_part_cap, ks_cnt_cap;

@@ -203,6 +203,7 @@ struct StepIn {
   SampleParams* sp;     // [rows]
   uint64_t* rng;        // [rows]
   uint32_t* sel;        // [rows]
+  uint32_t* shared;     // [1]: leading KV pages all rows of a batched step share (attention reads them once)
 };
 struct StepOut {
   uint32_t* tok;  // [rows]
@@ -242,7 +243,7 @@ struct sm_model {
   float* cos_t = nullptr;
   float* sin_t = nullptr;
   uint32_t max_ctx = 0;
-  uint32_t rows_max = 0, max_splits = 32;
+  uint32_t rows_max = 0, max_splits = 32 + ATT_SHARED_SPLITS;  // attention partial slots per (row, head)
   // workspace
   float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *g = nullptr,
         *u = nullptr, *logits = nullptr, *part_o = nullptr, *part_ml = nullptr;
@@ -257,6 +258,7 @@ struct sm_model {
   float *parts_a = nullptr, *parts_b = nullptr;
   uint32_t parts_cap = 0;
   uint8_t* mask_dev = nullptr;
+  uint32_t* smp_scratch = nullptr;  // the sampler's per-row scratch (sample_scratch_words(V) words a row)
   void* in_dev = nullptr;   // StepIn block on the device
   void* in_host = nullptr;  // pinned
   void* out_dev = nullptr;  // StepOut block on the device
@@ -294,7 +296,7 @@ void carve(uint8_t*& p, T*& out, size_t n) {
 }
 
 size_t step_in_bytes(uint32_t R) {
-  return 6 * 256 + (size_t)R * (sizeof(uint32_t) * 2 + sizeof(RowDesc) + sizeof(SeqDesc) + sizeof(SampleParams) +
+  return 7 * 256 + (size_t)R * (sizeof(uint32_t) * 2 + sizeof(RowDesc) + sizeof(SeqDesc) + sizeof(SampleParams) +
                                 sizeof(uint64_t));
 }
 void layout_in(void* base, uint32_t R, StepIn& s) {
@@ -305,6 +307,7 @@ void layout_in(void* base, uint32_t R, StepIn& s) {
   carve(p, s.sp, R);
   carve(p, s.rng, R);
   carve(p, s.sel, R);
+  carve(p, s.shared, 1);
 }
 size_t step_out_bytes(uint32_t R) { return 3 * 256 + (size_t)R * (sizeof(uint32_t) + sizeof(uint64_t)) + 4; }
 void layout_out(void* base, uint32_t R, StepOut& s) {
@@ -581,7 +584,8 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
       (rc = dev_alloc(m, (void**)&m->logits, R * V * 4)) ||
       (rc = dev_alloc(m, (void**)&m->part_o, (size_t)R * sh.q_heads * m->max_splits * hd * 4)) ||
       (rc = dev_alloc(m, (void**)&m->part_ml, (size_t)R * sh.q_heads * m->max_splits * 2 * 4)) ||
-      (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)))
+      (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)) ||
+      (rc = dev_alloc(m, (void**)&m->smp_scratch, R * sample_scratch_words((uint32_t)V) * 4)))
     return rc;
   {
     // K-split scratch: the most any batch-1 GEMV of this model asks for
@@ -701,6 +705,8 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   const uint32_t H = (uint32_t)c.n_embd, F = m->fl, kvd = m->kvd, hd = (uint32_t)c.head_dim, qd = m->qd;
   const uint32_t Hq = (uint32_t)m->sh.q_heads, Hkv = (uint32_t)m->sh.kv_heads;
   TpGroup* tp = m->tp;
+  // a batched decode step (one row per sequence) may share prefix pages
+  const uint32_t* shared = nrows > 1 && nsel == nrows && hd % 32 == 0 ? m->din.shared : nullptr;
   cudaError_t e;
 #define RK(x) do { if ((e = (x)) != cudaSuccess) return e; } while (0)
   // A row-split GEMV (O or down) whose rank partials are all-reduced into the
@@ -750,7 +756,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     a.seg[2] = seg(L.wv, nullptr, 0, L.bv, EPI_V);
     RK(launch_gemv(a, st));
     RK(launch_attention(m->q, qd, m->din.rows, m->din.seqs, nrows, li, Hq, Hkv, hd, m->part_o, m->part_ml,
-                        m->max_splits, m->att, qd, st));
+                        m->max_splits, m->att, qd, st, nsel != nrows ? 1u : 0u, shared));
     GemvArgs o = base;
     o.layer = li;
     o.x = m->att; o.ldx = qd;
@@ -818,14 +824,9 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   return cudaSuccess;
 }
 
-int check_sampler(const sm_sampler* s) {
-  if (!s) return SM_OK;
-  if (s->temperature > 0.0f && (s->top_k < 1 || s->top_k > SAMPLER_MAX_TOP_K)) {
-    set_error("on-device sampling with temperature > 0 needs 1 <= top_k <= " + std::to_string(SAMPLER_MAX_TOP_K));
-    return SM_ERR_UNSUPPORTED;
-  }
-  return SM_OK;
-}
+// Every Sampler of the reference is accepted: any temperature, top_k None
+// (< 0) or any k (0 acts as 1, as k.max(1) does), top_p None (< 0) or any p.
+int check_sampler(const sm_sampler*) { return SM_OK; }
 
 SampleParams to_params(const sm_sampler* s) {
   SampleParams p{};
@@ -927,6 +928,22 @@ static int cache_resize(sm_model* m, sm_cache* c, uint64_t cap) {
   c->dirty = true;
   return cache_sync(m, c);
 }
+// Leading KV pages that every cache of a batch holds as the same physical
+// page, all of whose positions are below every cache's length (the shared
+// prefix of sequences cloned from one prefilled state: prefix.rs:59-109).
+static uint32_t shared_prefix_pages(const sm_model* m, sm_cache* const* caches, uint64_t n) {
+  if (n < 2 || m->c.head_dim % 32) return 0;
+  uint64_t minlen = caches[0]->len;
+  for (uint64_t i = 1; i < n; i++) minlen = std::min(minlen, caches[i]->len);
+  uint64_t t = 0;
+  for (; t < minlen / KV_PAGE; t++) {
+    const float* p0 = caches[0]->pages[t];
+    bool same = p0 != nullptr;
+    for (uint64_t i = 1; same && i < n; i++) same = caches[i]->pages[t] == p0;
+    if (!same) break;
+  }
+  return (uint32_t)t;
+}
 static SeqDesc seq_desc(const sm_model* m, const sm_cache* c) {
   return SeqDesc{c->pages_dev, (uint32_t)c->cap, m->kv_voff};
 }
@@ -969,7 +986,7 @@ int sample_rows(sm_model* m, uint32_t rows, const uint8_t* mask_host, bool advan
     mask = m->mask_dev;
   }
   CK(launch_sample(m->logits, (uint32_t)m->c.vocab_size, rows, mask, m->din.sp, m->din.rng, m->dout.tok,
-                   advance ? m->din.tok : nullptr, advance ? m->din.rows : nullptr, st));
+                   advance ? m->din.tok : nullptr, advance ? m->din.rows : nullptr, m->smp_scratch, st));
   CK(cudaMemcpyAsync(m->dout.rng, m->din.rng, rows * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
   CK(cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st));
   return SM_OK;
@@ -987,7 +1004,7 @@ int decode_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
   if (e == cudaSuccess) e = run_rows(m, B, B, st);
   if (e == cudaSuccess)
     e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
-                      m->din.rows, st);
+                      m->din.rows, m->smp_scratch, st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->dout.rng, m->din.rng, B * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st);
   cudaError_t e2 = cudaStreamEndCapture(st, &g);
@@ -1020,7 +1037,7 @@ int run_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
   cudaError_t e = run_rows(m, B, B, st);
   if (e == cudaSuccess)
     e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
-                      m->din.rows, st);
+                      m->din.rows, m->smp_scratch, st);
   if (e == cudaSuccess) e = launch_record_tokens(m->dout.tok, B, m->hist, m->hist_ctr, HIST_TOKENS / B, st);
   cudaError_t e2 = cudaStreamEndCapture(st, &g);
   if (e != cudaSuccess || e2 != cudaSuccess) {
@@ -1138,7 +1155,7 @@ static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* 
   m->device = opts ? opts->device : 0;
   if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
       gemv_tc_prepare() != cudaSuccess || gemv_tcb_prepare() != cudaSuccess ||
-      gemv_umma_prepare() != cudaSuccess) {
+      gemv_umma_prepare() != cudaSuccess || attention_prepare() != cudaSuccess) {
     cudaGetLastError();
     set_error("cannot use CUDA device " + std::to_string(m->device));
     delete m;
@@ -1342,6 +1359,24 @@ int sm_cache_read_kv(const sm_cache* c, uint64_t layer, uint64_t pos, float* k_o
   return SM_OK;
 }
 
+// Row `token` of the embedding table as the forward's first kernel produces it
+// (qwen2.rs:468-472: the row dequantized exactly).
+int sm_model_embedding(sm_model* m, uint32_t token, float* out) {
+  if (guard_model(m) || !out) { set_error("sm_model_embedding: bad arguments"); return SM_ERR_ARG; }
+  if (token >= m->c.vocab_size) { set_error("token id out of range"); return SM_ERR_ARG; }
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaSetDevice(m->device);
+  CK(cudaStreamSynchronize(m->stream));  // the pinned staging block is free
+  m->hin.tok[0] = token;
+  CK(cudaMemcpyAsync(m->din.tok, m->hin.tok, sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+  const uint32_t H = (uint32_t)m->c.n_embd;
+  CK(launch_embed_norm(m->tok_embd.d, m->din.tok, 1, m->x, H, m->layers[0].attn_norm, m->xn, H, m->parts_a,
+                       m->stream));
+  CK(cudaMemcpyAsync(out, m->x, (size_t)H * 4, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return SM_OK;
+}
+
 // ------------------------------------------------------------ forward ----
 int sm_forward_cached(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n, float* logits_out) {
   if (guard_model(m) || !c || !toks || c->m != m) { set_error("sm_forward_cached: bad arguments"); return SM_ERR_ARG; }
@@ -1406,8 +1441,9 @@ int sm_forward_sample(sm_model* m, sm_cache* c, const uint32_t* toks, uint64_t n
   return SM_OK;
 }
 
-int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks, const sm_sampler* samplers,
-                    uint64_t* rng_states, uint32_t* out_tokens) {
+static int decode_batch_impl(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks,
+                             const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens,
+                             float* logits_out) {
   if (guard_model(m) || !caches || !toks || !rng_states || !out_tokens || n == 0) {
     set_error("sm_decode_batch: bad arguments");
     return SM_ERR_ARG;
@@ -1440,7 +1476,10 @@ int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint
     m->hin.rng[i] = rng_states[i];
     m->hin.sel[i] = (uint32_t)i;
   }
+  m->hin.shared[0] = shared_prefix_pages(m, caches, n);
   CK(cudaGraphLaunch(ex, m->stream));
+  if (logits_out)  // the logits the step's sampler read (untouched until the next forward)
+    CK(cudaMemcpyAsync(logits_out, m->logits, n * m->c.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   if ((rc = check_waits(m, false))) return rc;
   for (uint64_t i = 0; i < n; i++) {
@@ -1449,6 +1488,17 @@ int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint
     rng_states[i] = m->hout.rng[i];
   }
   return SM_OK;
+}
+
+int sm_decode_batch(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks, const sm_sampler* samplers,
+                    uint64_t* rng_states, uint32_t* out_tokens) {
+  return decode_batch_impl(m, caches, n, toks, samplers, rng_states, out_tokens, nullptr);
+}
+
+int sm_decode_batch_logits(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks,
+                           const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens, float* logits_out) {
+  if (!logits_out) { set_error("sm_decode_batch_logits: null logits_out"); return SM_ERR_ARG; }
+  return decode_batch_impl(m, caches, n, toks, samplers, rng_states, out_tokens, logits_out);
 }
 
 int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32_t* toks, const sm_sampler* samplers,
@@ -1487,6 +1537,7 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
     m->hin.rng[i] = rng_states[i];
     m->hin.sel[i] = (uint32_t)i;
   }
+  m->hin.shared[0] = shared_prefix_pages(m, caches, n);  // pages below every length stay shared during the run
   CK(cudaMemcpyAsync(m->in_dev, m->in_host, m->in_bytes, cudaMemcpyHostToDevice, m->stream));
   if (ev_begin) CK(cudaEventRecord((cudaEvent_t)ev_begin, m->stream));
   for (uint64_t s0 = 0; s0 < n_steps; s0 += chunk) {
@@ -1507,6 +1558,74 @@ int sm_decode_run(sm_model* m, sm_cache* const* caches, uint64_t n, const uint32
 }
 
 // ------------------------------------------------- kernel-level entries ----
+// Sampler::sample[_masked] (sampling.rs:66-144) on host logits, on the current
+// device: rows of `vocab` logits at logits + i * ld (ld = 0: every row samples
+// the same logits), mask likewise (may be NULL).
+int sm_sample(const float* logits, uint64_t n_rows, uint64_t ld, uint64_t vocab, const uint8_t* mask,
+              const sm_sampler* samplers, uint64_t* rng_states, uint32_t* out_tokens) {
+  if (!logits || !samplers || !rng_states || !out_tokens || !n_rows || !vocab || vocab > 0xFFFFFFFFull ||
+      (ld && ld < vocab)) {
+    set_error("sm_sample: bad arguments");
+    return SM_ERR_ARG;
+  }
+  const uint64_t B = 64, uniq = ld ? std::min(n_rows, B) : 1, L = ld ? vocab : 0;
+  const uint64_t sw = sample_scratch_words((uint32_t)vocab);
+  struct Bufs {
+    std::vector<void*> p;
+    ~Bufs() { for (void* q : p) cudaFree(q); }
+  } bufs;
+  auto alloc = [&](size_t n, void** out) -> int {
+    if (cudaMalloc(out, std::max<size_t>(n, 16)) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("sm_sample: cudaMalloc failed");
+      return SM_ERR_OOM;
+    }
+    bufs.p.push_back(*out);
+    return SM_OK;
+  };
+  float* dl = nullptr;
+  uint8_t* dm = nullptr;
+  SampleParams* dp = nullptr;
+  uint64_t* dr = nullptr;
+  uint32_t *dt = nullptr, *ds = nullptr;
+  int rc;
+  if ((rc = alloc(uniq * vocab * 4, (void**)&dl)) || (mask && (rc = alloc(uniq * vocab, (void**)&dm))) ||
+      (rc = alloc(B * sizeof(SampleParams), (void**)&dp)) || (rc = alloc(B * 8, (void**)&dr)) ||
+      (rc = alloc(B * 4, (void**)&dt)) || (rc = alloc(B * sw * 4, (void**)&ds)))
+    return rc;
+  std::vector<SampleParams> hp(B);
+  for (uint64_t r0 = 0; r0 < n_rows; r0 += B) {
+    const uint64_t nb = std::min(B, n_rows - r0);
+    if (ld || r0 == 0) {
+      for (uint64_t i = 0; i < (ld ? nb : 1); i++) {
+        CK(cudaMemcpy(dl + i * vocab, logits + (r0 + i) * ld, vocab * 4, cudaMemcpyHostToDevice));
+        if (mask) CK(cudaMemcpy(dm + i * vocab, mask + (r0 + i) * ld, vocab, cudaMemcpyHostToDevice));
+      }
+    }
+    for (uint64_t i = 0; i < nb; i++) hp[i] = to_params(&samplers[r0 + i]);
+    CK(cudaMemcpy(dp, hp.data(), nb * sizeof(SampleParams), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dr, rng_states + r0, nb * 8, cudaMemcpyHostToDevice));
+    CK(launch_sample(dl, (uint32_t)vocab, (uint32_t)nb, dm, dp, dr, dt, nullptr, nullptr, ds, 0, L));
+    CK(cudaMemcpy(out_tokens + r0, dt, nb * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(rng_states + r0, dr, nb * 8, cudaMemcpyDeviceToHost));
+  }
+  return SM_OK;
+}
+
+// softmax (sampling.rs:157-172) of rows x n device values (stream order).
+int sm_softmax(const float* x_dev, uint64_t rows, uint64_t n, float* probs_dev, void* stream) {
+  if (!x_dev || !probs_dev || rows > 0x7FFFFFFFull || n > 0xFFFFFFFFull) { set_error("sm_softmax: bad arguments"); return SM_ERR_ARG; }
+  CK(launch_softmax(x_dev, (uint32_t)rows, (uint32_t)n, probs_dev, (cudaStream_t)stream));
+  return SM_OK;
+}
+
+// The sampler's exp on n device values (stream order).
+int sm_expf_ref(const float* x_dev, float* y_dev, uint64_t n, void* stream) {
+  if (!x_dev || !y_dev) { set_error("null argument"); return SM_ERR_ARG; }
+  CK(launch_expf_ref(x_dev, y_dev, n, (cudaStream_t)stream));
+  return SM_OK;
+}
+
 struct sm_dweight {
   DW w;
   int device;
@@ -1517,6 +1636,8 @@ struct sm_dweight {
   // x image of its batched tcgen05 GEMV (up to 32 columns)
   uint8_t* xblob = nullptr;
   uint64_t xblob_cap = 0;
+  // error word of the GEMVs' bounded waits (sm_gemv_status reads and clears it)
+  uint32_t* err = nullptr;
 };
 
 int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t n_in, sm_dweight** out) {
@@ -1559,6 +1680,13 @@ int sm_dweight_upload(uint32_t type, const void* bytes, uint64_t n_out, uint64_t
     w->ks_part_cap = (uint32_t)need_part;
     w->ks_cnt_cap = need_cnt;
   }
+  if (cudaMalloc((void**)&w->err, 256) != cudaSuccess || cudaMemset(w->err, 0, 256) != cudaSuccess) {
+    cudaGetLastError();
+    w->err = nullptr;
+    sm_dweight_free(w);
+    set_error("cudaMalloc failed for the GEMV error word");
+    return SM_ERR_OOM;
+  }
   if (tiled_type(w->w.d.type)) {
     w->xblob_cap = gemv_umma_blob_bytes(w->w.d.n_in, 32);
     if (cudaMalloc((void**)&w->xblob, w->xblob_cap) != cudaSuccess) {
@@ -1577,6 +1705,7 @@ int sm_dweight_free(sm_dweight* w) {
   if (w->ks_part) cudaFree(w->ks_part);
   if (w->ks_cnt) cudaFree(w->ks_cnt);
   if (w->xblob) cudaFree(w->xblob);
+  if (w->err) cudaFree(w->err);
   free_weight(w->w);
   delete w;
   return SM_OK;
@@ -1607,8 +1736,22 @@ int sm_gemv(const sm_dweight* w, const float* x_dev, float* y_dev, uint64_t batc
   a.ks_cnt_cap = w->ks_cnt_cap;
   a.xblob = w->xblob;
   a.xblob_cap = w->xblob_cap;
+  a.err = w->err;
   CK(launch_gemv(a, (cudaStream_t)stream));
   return SM_OK;
+}
+
+int sm_gemv_status(const sm_dweight* w, void* stream) {
+  if (!w) { set_error("null argument"); return SM_ERR_ARG; }
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t h = 0;
+  CK(cudaMemcpyAsync(&h, w->err, sizeof(h), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (!h) return SM_OK;
+  CK(cudaMemsetAsync(w->err, 0, sizeof(uint32_t), st));
+  CK(cudaStreamSynchronize(st));
+  set_error("a bounded wait in a GEMV on this weight gave up (a weight copy did not complete); its output is invalid");
+  return SM_ERR_CUDA;
 }
 
 // Same product as sm_gemv, for callers that cannot allocate device memory: the
@@ -1630,8 +1773,24 @@ int sm_gemv_noalloc(const sm_dweight* w, const float* x_dev, float* y_dev, uint6
   a.batch = (uint32_t)batch;
   a.nseg = 1;
   a.seg[0] = seg(w->w, y_dev, w->w.d.n_out, nullptr, EPI_STORE);
-  CK(launch_gemv_noalloc(a, (cudaStream_t)stream));
+  const cudaError_t e = launch_gemv_noalloc(a, (cudaStream_t)stream);
+  if (e == cudaErrorNotSupported) {  // nothing was launched
+    set_error("sm_gemv_noalloc: this shape's K-split needs more scratch than the fixed 256 KB array holds "
+              "(Q4_K/Q6_K: roughly ceil(n_in / 8192) * n_out floats, rounded up to 16 rows, must be at most "
+              "65536; 7168 for Q6_K); use sm_gemv");
+    return SM_ERR_ARG;
+  }
+  CK(e);
   return SM_OK;
+}
+
+int sm_gemv_noalloc_status(void* stream) {
+  uint32_t flag = 0;
+  CK(gemv_noalloc_status((cudaStream_t)stream, &flag));
+  if (!flag) return SM_OK;
+  set_error("a bounded wait in an sm_gemv_noalloc call on this device gave up (a weight copy did not "
+            "complete); that call's output is invalid");
+  return SM_ERR_CUDA;
 }
 
 }  // extern "C"

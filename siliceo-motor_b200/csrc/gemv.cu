@@ -408,20 +408,25 @@ cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows,
 
 // ------------------------------------------------- no-allocation GEMV ----
 // Scratch of sm_gemv_noalloc: the K-split partial sums and arrival counters of
-// the batch-1 tensor-core GEMV, in fixed device arrays instead of memory the
-// call allocates. Every call on a device shares them; a launch leaves the
-// counters at zero (device globals start at zero), so nothing needs clearing,
-// and calls that overlap on the GPU race on them. A launch whose split does
-// not fit runs with K unsplit.
+// the batch-1 and batched tensor-core GEMVs, in fixed device arrays instead of
+// memory the call allocates, and the error word of their bounded waits. Every
+// call on a device shares them. The counters advance with wrapping increments,
+// so each complete launch leaves them at zero (device globals start at zero)
+// and nothing needs clearing; calls that overlap on the GPU race on the
+// partial sums (their results are then wrong) but leave the counters at zero
+// once all of them have completed. A shape whose smallest K-split does not
+// fit NOALLOC_PART floats is refused (cudaErrorNotSupported, nothing runs).
 constexpr uint32_t NOALLOC_PART = 65536, NOALLOC_CNT = 1024;
 static __device__ __align__(256) float g_noalloc_part[NOALLOC_PART];
 static __device__ __align__(256) uint32_t g_noalloc_cnt[NOALLOC_CNT];
+static __device__ __align__(256) uint32_t g_noalloc_err[64];
 
 constexpr int NOALLOC_MAX_DEVICES = 64;
 static std::mutex g_noalloc_mu;
 struct NoallocPtrs {
   float* part;
   uint32_t* cnt;
+  uint32_t* err;
 };
 static NoallocPtrs g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
 
@@ -437,6 +442,7 @@ static cudaError_t noalloc_scratch(NoallocPtrs* out) {
     NoallocPtrs p{};
     e = cudaGetSymbolAddress((void**)&p.part, g_noalloc_part);
     if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&p.cnt, g_noalloc_cnt);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&p.err, g_noalloc_err);
     if (e != cudaSuccess) return e;
     g_noalloc_ptr[dev] = p;
   }
@@ -453,7 +459,24 @@ cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st) {
   a.ks_cnt = p.cnt;
   a.ks_part_cap = NOALLOC_PART;
   a.ks_cnt_cap = NOALLOC_CNT;
+  a.err = p.err;
   return launch_gemv(a, st, nullptr);
+}
+
+// Reads (and clears) the error word of the no-allocation GEMVs of the current
+// device after the work queued on `st` so far: *flag is non-zero if a bounded
+// wait of one of them gave up since the last query.
+cudaError_t gemv_noalloc_status(cudaStream_t st, uint32_t* flag) {
+  NoallocPtrs p{};
+  cudaError_t e = noalloc_scratch(&p);
+  if (e != cudaSuccess) return e;
+  uint32_t h = 0;
+  e = cudaMemcpyAsync(&h, p.err, sizeof(h), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && h) e = cudaMemsetAsync(p.err, 0, sizeof(uint32_t), st);
+  if (e == cudaSuccess && h) e = cudaStreamSynchronize(st);
+  *flag = h;
+  return e;
 }
 
 }  // namespace sm

@@ -24,10 +24,11 @@
 // per 16-row block unit, completion on an mbarrier); x is converted once per
 // unit into shared memory, already in each lane's B-fragment order.
 //
-// Work: a unit is (16 tiles of 16 rows, K-slice). Warp w of a CTA owns tile
+// Work: a unit is (8 tiles of 16 rows, K-slice). Warp w of a CTA owns tile
 // w of the unit. When there are too few tiles to fill the GPU, K is split and
 // the CTA that finishes a group last sums the slices in order (deterministic)
-// and runs the epilogue. Epilogues are the fused ones of gemv_common.cuh.
+// and runs the epilogue. Epilogues are the fused ones of gemv_common.cuh. The
+// grid has up to two CTAs an SM.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -41,16 +42,22 @@
 
 namespace sm {
 
-constexpr int TC_WARPS = 16, TC_THREADS = TC_WARPS * 32;
-// B fragments of one block, one type: [8 MMA positions][32 lanes][4 words]
-constexpr uint32_t TC_FRAG = 4096;
+// A CTA is 8 warps (one 16-row tile each) with at most TC_SMEM_MAX bytes of
+// shared memory, so that two CTAs fit on an SM (registers: 2 x 256 threads x
+// 128; shared memory: 2 x (110 KB + static)): a CTA of the NEXT kernel in the
+// stream (programmatic dependent launch) can then start on an SM while this
+// kernel's CTA still runs there, and fetch its weights into shared memory
+// before it waits for this kernel's output.
+constexpr int TC_WARPS = 8, TC_THREADS = TC_WARPS * 32;
+// B fragments of one block, one type: [8 MMA positions][32 lanes] of two words
+// (the l0|l1 and the l2 operand word; the other word of each MMA operand pair
+// is zero and is not stored)
+constexpr uint32_t TC_FRAG = 2048;
 // per block: (u_s, X_s) of the 8 Q4_K sub-blocks, then of the 16 Q6_K ones
 constexpr uint32_t TC_XS = 256;
-constexpr uint32_t TC_SMEM_MAX = 225u * 1024u;
-// Ring slots per warp: 16 warps x 2-4 slots of one block unit each (as many as
-// shared memory holds; 4 measured 4% faster than 3 on Q4_K with compute in the
-// loop, while a copy-only probe lost bandwidth beyond 3; L2 prefetches ahead
-// of the ring lost bandwidth too).
+constexpr uint32_t TC_SMEM_MAX = 110u * 1024u;
+// Ring slots per warp: 2-4 slots of one block unit each (as many as shared
+// memory holds).
 constexpr uint32_t TC_MAX_STAGES = 4;
 
 struct TcPlan {
@@ -96,7 +103,7 @@ __device__ __forceinline__ void limbs4(const float4& v, float f, uint32_t (&l)[3
 // lane (g, t) is (sub-block sigma = g >> 1, limb g & 1); its b0 (k = 4t ..
 // 4t + 3) holds sub-block t >> 1 and b1 (k = 4t + 16 ..) sub-block 2 + (t >> 1),
 // so a lane's word is non-zero only where that matches sigma.
-__device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* f4, uint4* f6, float2* xs, bool t4,
+__device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint2* f4, uint2* f6, float2* xs, bool t4,
                                            bool t6) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, sn = g >> 1, lim = g & 1;
   const bool active = (t >> 1) == (sn & 1);
@@ -106,7 +113,7 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
   const float sm = sum4(v0) + sum4(v1);
   // Each lane cuts its own 8 values into limbs (with its sub-block's scale);
   // the fragment words are then fetched from the owning lanes by shuffles.
-  auto frag = [&](uint4* f, int wsub, float scl_own) {
+  auto frag = [&](uint2* f, int wsub, float scl_own) {
     uint32_t L0[3], L1[3];  // limbs of values 8 lane + 0..3 and + 4..7
     limbs4(v0, scl_own, L0);
     limbs4(v1, scl_own, L1);
@@ -120,7 +127,7 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint4* 
       const uint32_t b0 = __shfl_sync(0xffffffffu, L0[2], src), b1 = __shfl_sync(0xffffffffu, L1[2], src);
       const uint32_t A = active ? (half ? (lim ? a11 : a10) : (lim ? a01 : a00)) : 0u;
       const uint32_t B = (active && !lim) ? (half ? b1 : b0) : 0u;
-      f[P * 32 + lane] = (sn >> 1) ? make_uint4(0, A, 0, B) : make_uint4(A, 0, B, 0);
+      f[P * 32 + lane] = make_uint2(A, B);  // b0 (sn < 2) or b1 (sn >= 2) of each MMA; the other is 0
     }
   };
   if (t4) {  // 32-wide sub-blocks: lanes 4s .. 4s + 3
@@ -161,9 +168,17 @@ __device__ __forceinline__ void q4_sc_m(const uint4& h, int G, int t, float& sc,
     m = (float)(((h.w >> (sh + 4)) & 0xFu) | (((h.z >> (sh + 6)) & 3u) << 4));
   }
 }
-__device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* f, const float2* xs, int lane, float& rg,
+// The B operand pair of an MMA from a compact fragment word w: (w, 0) for
+// lanes 0-15 (columns of sub-blocks 0, 1: k < 16), (0, w) for lanes 16-31.
+__device__ __forceinline__ void b_pair(uint32_t w, uint32_t keep_lo, uint32_t& b0, uint32_t& b1) {
+  b0 = w & keep_lo;
+  b1 = w & ~keep_lo;
+}
+
+__device__ __forceinline__ void q4_block(const uint8_t* st, const uint2* f, const float2* xs, int lane, float& rg,
                                          float& rh) {
   const int g = lane >> 2, t = lane & 3, p = t & 1;
+  const uint32_t keep_lo = (lane >> 4) ? 0u : 0xFFFFFFFFu;
   const uint32_t M = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;  // nibble of sub-blocks t >> 1, 2 + (t >> 1)
   uint4 Wg[4], Wh[4];
 #pragma unroll
@@ -179,11 +194,14 @@ __device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* f, cons
     int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-      const uint4 bf = f[(4 * G + c) * 32 + lane];
+      const uint2 bf = f[(4 * G + c) * 32 + lane];
+      uint32_t b0, b1, b2, b3;
+      b_pair(bf.x, keep_lo, b0, b1);
+      b_pair(bf.y, keep_lo, b2, b3);
       const uint32_t a0 = word_of(Wg[2 * G], c) & M, a2 = word_of(Wg[2 * G + 1], c) & M;
       const uint32_t a1 = word_of(Wh[2 * G], c) & M, a3 = word_of(Wh[2 * G + 1], c) & M;
-      mma_u8s8(A, a0, a1, a2, a3, bf.x, bf.y);
-      mma_u8s8(B, a0, a1, a2, a3, bf.z, bf.w);
+      mma_u8s8(A, a0, a1, a2, a3, b0, b1);
+      mma_u8s8(B, a0, a1, a2, a3, b2, b3);
     }
     float Sg, Sh;
     limb_sums(A, B, Sg, Sh);
@@ -203,9 +221,10 @@ __device__ __forceinline__ void q6_a(uint32_t w, uint32_t hbits, int h, uint32_t
   lo = (w & 0x0F0F0F0Fu) | (hs & 0x30303030u);
   hi = ((w >> 4) & 0x0F0F0F0Fu) | ((hs >> 2) & 0x30303030u);
 }
-__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, const float2* xs, int lane, float& rg,
+__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint2* f, const float2* xs, int lane, float& rg,
                                          float& rh) {
   const int g = lane >> 2, t = lane & 3, p = t & 1, h = t >> 1;
+  const uint32_t keep_lo = (lane >> 4) ? 0u : 0xFFFFFFFFu;
   // per row: W_h words (G, c) and H words (G, c), G = 0..3, c = 0..1
   const uint4 wg0 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, h, 0, 0, p));
   const uint4 wg1 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, h, 2, 0, p));
@@ -225,12 +244,15 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, co
 #pragma unroll
     for (int G = 0; G < 4; G++) {
       const int wi = 2 * (G & 1) + c;
-      const uint4 bf = f[(2 * G + c) * 32 + lane];
+      const uint2 bf = f[(2 * G + c) * 32 + lane];
+      uint32_t b0, b1, b2, b3;
+      b_pair(bf.x, keep_lo, b0, b1);
+      b_pair(bf.y, keep_lo, b2, b3);
       uint32_t a0, a1, a2, a3;
       q6_a(word_of(G < 2 ? wg0 : wg1, wi), word_of(G < 2 ? hg0 : hg1, wi), h, a0, a2);
       q6_a(word_of(G < 2 ? wh0 : wh1, wi), word_of(G < 2 ? hh0 : hh1, wi), h, a1, a3);
-      mma_u8s8(A[G], a0, a1, a2, a3, bf.x, bf.y);
-      mma_u8s8(B[G], a0, a1, a2, a3, bf.z, bf.w);
+      mma_u8s8(A[G], a0, a1, a2, a3, b0, b1);
+      mma_u8s8(B[G], a0, a1, a2, a3, b2, b3);
     }
 #pragma unroll
   for (int G = 0; G < 4; G++) {
@@ -256,7 +278,7 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, co
 template <int QT, int S>
 __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t pre, uint8_t* ring,
                                         uint32_t stage_bytes, uint64_t* bars, uint32_t& nuse, uint32_t* err,
-                                        const uint4* f, const float2* xs, float& rg, float& rh) {
+                                        const uint2* f, const float2* xs, float& rg, float& rh) {
   const int lane = threadIdx.x & 31;
   constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT;
   // ring slot of the next copy to start (ip) and of the next block to compute (cp, phase cph)
@@ -273,8 +295,8 @@ __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32
     mbar_wait(bars + cp, cph, err);
     const uint8_t* sp = ring + cp * stage_bytes;
     if (++cp == S) { cp = 0; cph ^= 1u; }
-    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
-    else q6_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
+    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * (TC_FRAG / 8), xs + 32 * i, lane, rg, rh);
+    else q6_block(sp, f + (size_t)i * (TC_FRAG / 8), xs + 32 * i, lane, rg, rh);
     __syncwarp();  // every lane is done with the slot before it is refilled
   }
   nuse += nblk;
@@ -332,16 +354,16 @@ __device__ __forceinline__ void tc_epilogue(const GemvArgs& a, uint32_t tile, fl
   }
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_constant__ GemvArgs a,
+__global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_constant__ GemvArgs a,
                                                                 const __grid_constant__ TcPlan p) {
   extern __shared__ __align__(16) uint8_t tc_smem[];
   __shared__ float s_in;
   __shared__ uint32_t s_last;
   __shared__ __align__(8) uint64_t s_bars[TC_WARPS * TC_MAX_STAGES];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint4* f4 = reinterpret_cast<uint4*>(tc_smem);
-  uint4* f6 = f4 + (p.t4 ? p.slice * (TC_FRAG / 16) : 0);
-  float2* xs = reinterpret_cast<float2*>(f6 + (p.t6 ? p.slice * (TC_FRAG / 16) : 0));
+  uint2* f4 = reinterpret_cast<uint2*>(tc_smem);
+  uint2* f6 = f4 + (p.t4 ? p.slice * (TC_FRAG / 8) : 0);
+  float2* xs = reinterpret_cast<float2*>(f6 + (p.t6 ? p.slice * (TC_FRAG / 8) : 0));
   uint8_t* ring = reinterpret_cast<uint8_t*>(xs + 32 * p.slice) + (size_t)warp * p.stages * p.stage_bytes;
   const uint32_t nb = a.seg[0].w.n_in >> 8;
   uint64_t* bars = s_bars + warp * TC_MAX_STAGES;
@@ -378,7 +400,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
     __syncthreads();  // the previous unit is done with the x fragments
     for (uint32_t i = warp; i < nblk; i += TC_WARPS)
-      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * (TC_FRAG / 16), f6 + i * (TC_FRAG / 16), xs + 32 * i, p.t4,
+      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * (TC_FRAG / 8), f6 + i * (TC_FRAG / 8), xs + 32 * i, p.t4,
                  p.t6);
     __syncthreads();
     const uint32_t tile = rg * TC_WARPS + warp;
@@ -417,7 +439,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     if (tile < p.tiles && t < 2) a.ks_part[ks * stride + tile * 16u + g + 8u * t] = t ? vh : vg;
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.ks_cnt[rg], 1u) == p.ksplit - 1;
+    // a wrapping increment: the group's counter is back at zero once its last
+    // slice arrives, so no later store resets it
+    if (threadIdx.x == 0) s_last = atomicInc(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
     __syncthreads();
     if (s_last) {
       __threadfence();
@@ -429,7 +453,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         }
         tc_epilogue(a, tile, sg * s_in, sh * s_in);
       }
-      if (threadIdx.x == 0) a.ks_cnt[rg] = 0;  // ready for the next launch
     }
   }
 }
@@ -450,6 +473,9 @@ static cudaError_t tc_setup(uint32_t* sms) {
     int n = 0;
     e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     g_tc_sms[dev] = n;
   }
@@ -478,8 +504,10 @@ static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
   const uint32_t nb = a.seg[0].w.n_in >> 8;
   const uint32_t per_blk = (t4 ? TC_FRAG : 0) + (t6 ? TC_FRAG : 0) + TC_XS;
   const uint32_t stage_bytes = t6 ? Q6T_UNIT : Q4T_UNIT;
-  // x fragments of up to 32 blocks per slice; the rest of shared memory is ring
+  // x fragments of up to 32 blocks per slice; the rest of shared memory is
+  // ring (at least two slots a warp)
   const uint32_t slice_max = std::max(1u, std::min(32u, (TC_SMEM_MAX - TC_WARPS * 2 * stage_bytes) / per_blk));
+  const uint32_t slots = 2 * sms;  // two CTAs an SM
   const uint32_t groups = (tiles + TC_WARPS - 1) / TC_WARPS;
   auto fits = [&](uint32_t k) {
     return k == 1 || (a.ks_part && a.ks_cnt && (uint64_t)k * tiles * 16u <= a.ks_part_cap && groups <= a.ks_cnt_cap);
@@ -492,7 +520,7 @@ static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
     const uint32_t sl = (nb + k - 1) / k;
     const uint32_t kk = (nb + sl - 1) / sl;
     if (sl > slice_max || !fits(kk)) continue;
-    const uint64_t rounds = ((uint64_t)groups * kk + sms - 1) / sms;
+    const uint64_t rounds = ((uint64_t)groups * kk + slots - 1) / slots;
     if (rounds * (2 * sl + 1) < best) {
       best = rounds * (2 * sl + 1);
       ks = kk;
@@ -508,7 +536,7 @@ static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
   p->ksplit = ks;
   p->slice = slice;
   p->units = groups * ks;
-  p->grid = std::min(p->units, sms);
+  p->grid = std::min(p->units, slots);
   p->smem = slice * per_blk + ring;
   p->stages = stages;
   p->stage_bytes = stage_bytes;

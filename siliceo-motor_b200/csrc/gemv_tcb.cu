@@ -403,7 +403,9 @@ __global__ void __launch_bounds__(TB_THREADS, 1) gemv_tcb_kernel(const __grid_co
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.ks_cnt[rg], 1u) == p.ksplit - 1;
+    // a wrapping increment: the group's counter is back at zero once its last
+    // slice arrives, so no later store resets it
+    if (threadIdx.x == 0) s_last = atomicInc(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
     __syncthreads();
     if (s_last) {
       __threadfence();
@@ -422,7 +424,6 @@ __global__ void __launch_bounds__(TB_THREADS, 1) gemv_tcb_kernel(const __grid_co
         }
         tb_epilogue<NT>(a, tile, p.tiles, yg, yh);
       }
-      if (threadIdx.x == 0) a.ks_cnt[rg] = 0;  // ready for the next launch
     }
   }
 }

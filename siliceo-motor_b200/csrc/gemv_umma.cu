@@ -723,7 +723,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       }
       __threadfence();
       named_bar(1, UM_EW * 32);
-      if (threadIdx.x == UM_EW0 * 32) s_last = atomicAdd(&a.ks_cnt[rg], 1u) == p.ksplit - 1;
+      // wrapping increment: the counter is back at zero when the last slice arrives
+      if (threadIdx.x == UM_EW0 * 32) s_last = atomicInc(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
       named_bar(1, UM_EW * 32);
       if (s_last) {
         __threadfence();
@@ -738,7 +739,6 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
             for (uint32_t i = 0; i < NB; i++) y[i] += i < a.batch ? t[i] : 0.f;
           }
         um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
-        if (threadIdx.x == UM_EW0 * 32) a.ks_cnt[rg] = 0;  // ready for the next launch
       }
     }
   }

@@ -16,7 +16,6 @@ struct SampleParams {
   int32_t pad;
 };
 
-constexpr int SAMPLER_MAX_TOP_K = 1024;
 
 uint32_t gemv_plan(GemvArgs& a);
 // n_parts: the number of out_parts entries per column an EPI_RESID launch writes.
@@ -29,15 +28,37 @@ cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows,
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
                            uint32_t rows, uint32_t n, float eps, cudaStream_t st);
 size_t attn_smem_bytes(uint32_t G, uint32_t hd);
+// one_seq: the rows are consecutive positions of one sequence (a prefill
+// chunk), so every row's K/V from rows[0].pos on is written by this pass.
+// shared_tiles (device, may be null): the number of leading KV pages that
+// every row holds as the same physical page (all their positions older than
+// every row's): attn_shared_kernel reads them once for all rows. Partials:
+// max_splits slots per (row, head), the first ATT_SHARED_SPLITS for the
+// shared tiles.
+constexpr uint32_t ATT_SHARED_SPLITS = 8;
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
-                             uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st);
+                             uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st, uint32_t one_seq,
+                             const uint32_t* shared_tiles);
+size_t attn_shared_smem_bytes(uint32_t hd);
+cudaError_t attention_prepare();
 cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, cudaStream_t st);
+// The on-device sampler (sampler.cu): rows CTAs, row r's logits at
+// logits + r * ldl (ldl = ~0: V), scratch of sample_scratch_words(V) words per
+// row (used when the row's temperature is > 0).
+uint64_t sample_scratch_words(uint32_t V);
 cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const uint8_t* mask,
                           const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
-                          RowDesc* advance, cudaStream_t st);
+                          RowDesc* advance, uint32_t* scratch, cudaStream_t st, uint64_t ldl = ~0ull);
+// softmax (sampling.rs:157-172) of `rows` rows of n values, bit for bit.
+cudaError_t launch_softmax(const float* x, uint32_t rows, uint32_t n, float* out, cudaStream_t st);
+// The sampler's exp (glibc's expf on x <= 0) applied to n values.
+cudaError_t launch_expf_ref(const float* x, float* y, size_t n, cudaStream_t st);
 
+// sm_gemv_noalloc: scratch in fixed device arrays; cudaErrorNotSupported when
+// the shape's smallest K-split does not fit them (nothing is launched).
 cudaError_t launch_gemv_noalloc(GemvArgs a, cudaStream_t st);
+cudaError_t gemv_noalloc_status(cudaStream_t st, uint32_t* flag);
 // Batch-1 Q4_K/Q6_K GEMVs run on the tensor cores (gemv_tc.cu); launch_gemv
 // dispatches to that kernel. Per-device set-up, and the K-split scratch
 // (floats, counters) a launch of this shape may use on a GPU with `sms` SMs:

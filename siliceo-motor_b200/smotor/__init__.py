@@ -129,6 +129,8 @@ SIGNATURES = {
     "sm_forward_sample": (C.c_int, [P, P, PU32, U64, C.POINTER(sm_sampler), PU64, C.POINTER(C.c_uint8), PU32]),
     "sm_decode_batch": (C.c_int, [P, C.POINTER(P), U64, PU32, C.POINTER(sm_sampler), PU64, PU32]),
     "sm_decode_run": (C.c_int, [P, C.POINTER(P), U64, PU32, C.POINTER(sm_sampler), PU64, U64, PU32, P, P]),
+    "sm_decode_batch_logits": (C.c_int, [P, C.POINTER(P), U64, PU32, C.POINTER(sm_sampler), PU64, PU32,
+                                         C.POINTER(C.c_float)]),
     "sm_generate_with": (C.c_int, [C.POINTER(sm_device_vtbl), P, U64, PU32, U64, C.POINTER(sm_gen_params),
                                    PU32, U64, ON_TOKEN, MASKER, STOP, ON_PREFILL, P, P, U64, PU32,
                                    C.POINTER(sm_gen_result)]),
@@ -140,6 +142,13 @@ SIGNATURES = {
     "sm_dequant": (C.c_int, [P, P, P]),
     "sm_gemv": (C.c_int, [P, P, P, U64, P]),
     "sm_gemv_noalloc": (C.c_int, [P, P, P, U64, P]),
+    "sm_sample": (C.c_int, [C.POINTER(C.c_float), U64, U64, U64, C.POINTER(C.c_uint8), C.POINTER(sm_sampler),
+                            PU64, PU32]),
+    "sm_expf_ref": (C.c_int, [P, P, U64, P]),
+    "sm_softmax": (C.c_int, [P, U64, U64, P, P]),
+    "sm_model_embedding": (C.c_int, [P, U32, C.POINTER(C.c_float)]),
+    "sm_gemv_status": (C.c_int, [P, P]),
+    "sm_gemv_noalloc_status": (C.c_int, [P]),
     "sm_synth_preset": (C.c_int, [C.c_int, C.POINTER(sm_synth_spec)]),
     "sm_synth_size": (C.c_int, [C.POINTER(sm_synth_spec), PU64]),
     "sm_synth_write": (C.c_int, [C.POINTER(sm_synth_spec), C.c_char_p, C.c_int]),
@@ -194,6 +203,35 @@ class Sampler:
     def c(self) -> sm_sampler:
         return sm_sampler(self.temperature, -1 if self.top_k is None else int(self.top_k),
                           -1.0 if self.top_p is None else float(self.top_p))
+
+
+def sample(logits, samplers, rng_states, mask=None, shared=False):
+    """Sampler::sample[_masked] on the device (the decode steps' kernel) for
+    host logits: row i (or the single row when shared) with samplers[i] and
+    rng_states[i]; returns (ids, new states)."""
+    lg = np.ascontiguousarray(np.asarray(logits, np.float32))
+    V = lg.shape[-1]
+    n = len(samplers)
+    sm = (sm_sampler * n)(*[s.c() for s in samplers])
+    st = np.ascontiguousarray(np.asarray(rng_states, dtype=np.uint64))
+    out = np.empty(n, np.uint32)
+    mk = None
+    if mask is not None:
+        m8 = np.ascontiguousarray(np.asarray(mask, dtype=np.uint8))
+        mk = _p(m8, C.c_uint8)
+    _check(lib().sm_sample(_p(lg, C.c_float), n, 0 if shared else V, V, mk, sm, _p(st, C.c_uint64),
+                           _p(out, C.c_uint32)))
+    return out, st
+
+
+def softmax(x_ptr: int, rows: int, n: int, out_ptr: int, stream: int = 0) -> None:
+    """The sampler's softmax (sampling.rs:157-172) of rows x n device floats."""
+    _check(lib().sm_softmax(C.c_void_p(x_ptr), rows, n, C.c_void_p(out_ptr), C.c_void_p(stream)))
+
+
+def expf_ref(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
+    """The sampler's exp (glibc's expf on x <= 0) over n device floats."""
+    _check(lib().sm_expf_ref(C.c_void_p(x_ptr), C.c_void_p(y_ptr), n, C.c_void_p(stream)))
 
 
 class Cache:
@@ -376,6 +414,12 @@ class Model:
         _check(lib().sm_model_stream(self.h, C.byref(v)))
         return v.value or 0
 
+    def embedding(self, token: int) -> np.ndarray:
+        """Row `token` of the embedding table as the engine's forward gathers it."""
+        out = np.empty(self.config.n_embd, np.float32)
+        _check(lib().sm_model_embedding(self.h, token, _p(out, C.c_float)))
+        return out
+
     def new_cache(self, max_seq: int) -> Cache:
         out = C.c_void_p()
         _check(lib().sm_cache_new(self.h, max_seq, C.byref(out)))
@@ -413,6 +457,20 @@ class Model:
         _check(lib().sm_decode_batch(self.h, hs, n, _p(t, C.c_uint32), sm, _p(st, C.c_uint64),
                                      _p(out, C.c_uint32)))
         return out, st
+
+    def decode_batch_logits(self, caches: Sequence[Cache], tokens: Sequence[int], samplers: Sequence[Sampler],
+                            rng_states: Sequence[int]):
+        """decode_batch, also returning the logits [n, vocab] the step's sampler drew from."""
+        n = len(caches)
+        hs = (C.c_void_p * n)(*[c.h for c in caches])
+        t = _u32(tokens)
+        sm = (sm_sampler * n)(*[s.c() for s in samplers])
+        st = np.ascontiguousarray(np.asarray(rng_states, dtype=np.uint64))
+        out = np.empty(n, np.uint32)
+        lg = np.empty((n, self.config.vocab_size), np.float32)
+        _check(lib().sm_decode_batch_logits(self.h, hs, n, _p(t, C.c_uint32), sm, _p(st, C.c_uint64),
+                                            _p(out, C.c_uint32), _p(lg, C.c_float)))
+        return out, st, lg
 
     def decode_run(self, caches: Sequence[Cache], tokens: Sequence[int], samplers: Sequence[Sampler],
                    rng_states: Sequence[int], n_steps: int, ev_begin: int = 0, ev_end: int = 0):
@@ -554,6 +612,15 @@ class DWeight:
     def gemv_noalloc(self, x_ptr: int, y_ptr: int, batch: int, stream: int = 0) -> None:
         """sm_gemv without allocating: its K-split scratch is a fixed library array."""
         _check(lib().sm_gemv_noalloc(self.h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), batch, C.c_void_p(stream)))
+
+    def gemv_status(self, stream: int = 0) -> None:
+        """Raises if a bounded wait in an earlier gemv() on this weight gave up."""
+        _check(lib().sm_gemv_status(self.h, C.c_void_p(stream)))
+
+
+def gemv_noalloc_status(stream: int = 0) -> None:
+    """Raises if a bounded wait in an earlier gemv_noalloc() on the current device gave up."""
+    _check(lib().sm_gemv_noalloc_status(C.c_void_p(stream)))
 
     def free(self) -> None:
         if self.h:

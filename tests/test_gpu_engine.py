@@ -71,12 +71,18 @@ def test_logits_prefill_and_decode_vs_oracle(models, name):
             assert rel_err(ke, ko) <= 1e-4 and rel_err(ve, vo) <= 1e-4
 
 
-def test_embedding_row_is_bit_exact(models):
-    eng, ora = models["qwen2_tiny"]
-    # the first K row of layer 0 depends on the embedding through one norm and a GEMV;
-    # check the embedding itself via the logits of a zero-layer path instead: the
-    # engine's gather is the dequant kernel, pinned bit-exact in test_gpu_kernels.
-    assert ora.embedding(7).shape == (eng.config.n_embd,)
+@pytest.mark.parametrize("name", list(SPECS))
+def test_embedding_row_is_bit_exact(models, name):
+    # Q6_K (qwen2_tiny, llama_tiny) and Q8_0 (qwen2_fallback) tables; the
+    # engine's embedding kernel must give the oracle's dequantized row bit for bit
+    eng, ora = models[name]
+    V = eng.config.vocab_size
+    for tok in (0, 1, 7, V // 2 + 3, V - 1):
+        got, want = eng.embedding(tok), ora.embedding(tok)
+        assert got.shape == want.shape == (eng.config.n_embd,)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), tok
+    with pytest.raises(smotor.EngineError):
+        eng.embedding(V)
 
 
 @pytest.mark.parametrize("name", list(SPECS))
@@ -96,7 +102,8 @@ def test_sampler_on_device_matches_reference(models):
     base = eng.new_cache(64)
     eng.forward_cached(base, prompt[:-1], logits=False)
     cases = [smotor.Sampler(1.0, 40, 0.9), smotor.Sampler(0.7, 5, None), smotor.Sampler(1.5, 1000, 0.5),
-             smotor.Sampler(0.0, None, None), smotor.Sampler(2.0, 200, None)]
+             smotor.Sampler(0.0, None, None), smotor.Sampler(2.0, 200, None), smotor.Sampler(1.0, None, 0.9),
+             smotor.Sampler(0.9, None, None), smotor.Sampler(1.2, 2500, 0.97)]
     for i, s in enumerate(cases):
         for seed in range(8):
             st = smotor.rng_seed(100 * i + seed)
@@ -265,3 +272,38 @@ def test_paged_prefix_sharing(models):
     for f in forks:
         f.free()
     assert eng.kv_pages()[0] == held0  # back to the source's three pages
+
+
+def test_batched_decode_over_a_shared_prefix(models):
+    """Forks of one prefilled state decoded as a batch: the leading KV pages
+    every fork holds are read once for all of them (shared-prefix attention);
+    each fork's logits must still match the oracle's deep-copied state."""
+    eng, ora = models["llama_tiny"]
+    V = eng.config.vocab_size
+    rng = np.random.default_rng(21)
+    prefix = rng.integers(0, V, 100).tolist()  # pages 0-2 full (shared), page 3 holds 96..99
+    base = eng.new_cache(256)
+    eng.forward_cached(base, prefix, logits=False)
+    ob = ora.new_cache(256)
+    ora.forward_cached(ob, prefix)
+    conts = [rng.integers(0, V, n).tolist() for n in (1, 5, 9, 30, 2)]
+    forks, oforks = [], []
+    for c in conts:  # own tokens before the batched steps (the last one is the first step's input)
+        f, of = base.clone(), ob.clone()
+        if len(c) > 1:
+            eng.forward_cached(f, c[:-1], logits=False)
+            ora.forward_cached(of, c[:-1])
+        forks.append(f)
+        oforks.append(of)
+    toks = [c[-1] for c in conts]
+    n = len(conts)
+    for step in range(6):
+        out, _, lg = eng.decode_batch_logits(forks, toks, [smotor.Sampler()] * n, [0] * n)
+        for i in range(n):
+            want = ora.forward_cached(oforks[i], [toks[i]])
+            assert rel_err(lg[i], want) <= LOGIT_TOL and top8(lg[i]) == top8(want), (step, i)
+            assert int(out[i]) == int(np.argmax(lg[i]))
+        toks = out.tolist()
+    for f in forks:
+        f.free()
+    base.free()
