@@ -9,10 +9,12 @@ achieved HBM bandwidth against the measured peak in `roofline`.
   python bench.py --impl reference ...   # the reference CPU path (oracle port)
 
 N > 1 (torchrun): every rank decodes its own replica (the single-sequence
-decode path has no partition, so this is weak scaling with no collective);
-the timed region is bracketed by barriers and the max over ranks is used.
---workload cfg4 / cfg4b16 split the 70B shape over the job's N GPUs instead
-(tensor parallelism, strong scaling: one model, N GPUs).
+decode path has no partition, so `value` is weak scaling with no
+collective); the timed region is bracketed by barriers and the max over
+ranks is used. The same job then splits the 70B shape (config 4) over its N
+GPUs (tensor parallelism, two all-reduces per layer) and adds that
+measurement as `tensor_parallel` to the line (--no-tp-leg skips it).
+--workload cfg4 / cfg4b16 make the split model the headline instead.
 """
 import argparse
 import fcntl
@@ -62,11 +64,27 @@ def peaks():
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def model_file(preset: int, local_rank: int, barrier) -> str:
+def cache_dir(size_hint=0):
+    """Where synthetic GGUFs are kept: SM_CACHE_DIR, else RAM-backed /dev/shm
+    for a file that fits there with room to spare (a 70B-shape file is written
+    at memory speed instead of disk speed), else the temp directory."""
+    if os.environ.get("SM_CACHE_DIR"):
+        return os.environ["SM_CACHE_DIR"]
+    if size_hint:
+        try:
+            st = os.statvfs("/dev/shm")
+            if st.f_bavail * st.f_frsize > 1.5 * size_hint:
+                return "/dev/shm/smotor_cache"
+        except OSError:
+            pass
+    return os.path.join(tempfile.gettempdir(), "smotor_cache")
+
+
+def model_file(preset: int, local_rank: int, barrier, size_hint=0) -> str:
     """The synthetic GGUF of a preset, generated once per machine and reused.
     It is written by a child process, so that the calling process (the
     reference arm among them) never loads the engine's library."""
-    d = os.environ.get("SM_CACHE_DIR", os.path.join(tempfile.gettempdir(), "smotor_cache"))
+    d = cache_dir(size_hint)
     os.makedirs(d, exist_ok=True)
     path = os.path.join(d, f"preset{preset}_seed0_v1.gguf")
     if local_rank == 0:
@@ -320,6 +338,67 @@ def kernel_roofline(steps, warmup, shape=DOMINANT):
     return nbytes, us, traffic
 
 
+def tensor_parallel_leg(args, rank, world, local_rank, barrier, allmax):
+    """Config 4 (Llama-3-70B shape) split over the job's ranks (tensor
+    parallelism with the engine's peer-memory exchanges): batch 1, 1024-token
+    prompt, greedy, K timed decode steps. Run by every rank after the replica
+    measurement of a multi-GPU job; returns the summary on rank 0."""
+    import torch
+    import smotor
+    preset, batch, prompt_len, kind, desc = WORKLOADS["cfg4"]
+    size = smotor.synth_size(smotor.synth_preset(preset))
+    path = model_file(preset, local_rank, barrier, size_hint=size)
+    extra = args.warmup + 2 * args.steps + 8
+    tp = smotor.TensorParallel.from_process_group()
+    model = smotor.Model.load(path, device=local_rank, max_batch=32, max_context=prompt_len + extra + 64, tp=tp)
+    cfg = model.config
+    caches, toks = setup_sequences(model, cfg.vocab_size, 1, prompt_len, kind, extra)
+    samplers, states = [smotor.Sampler()], [0]
+    ext = torch.cuda.ExternalStream(model.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out, states = model.decode_run(caches, toks, samplers, states, max(args.warmup, 1))
+    toks = out[-1].tolist()
+    pos0 = len(caches[0])
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks() if rank == 0 else None
+    if clocks:
+        clocks.start()
+    out, states = model.decode_run(caches, toks, samplers, states, args.steps, ev0.cuda_event, ev1.cuda_event)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop(set(range(world))) if clocks else None
+    ms = allmax(ev0.elapsed_time(ev1))
+    toks = out[-1].tolist()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        t, states[0] = model.forward_sample(caches[0], [toks[0]], samplers[0], int(states[0]))
+        toks = [t]
+    torch.cuda.synchronize()
+    e2e_s = allmax(time.perf_counter() - t0)
+    wbytes = int(allsum(model.weight_bytes()))
+    step_kernels = model.step_launches(1)
+    model.free()  # every rank at the same point (the group's teardown barrier)
+    if rank != 0:
+        return None
+    kv_bytes = 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 4 * sum(pos0 + i + 1 for i in range(args.steps))
+    alg = args.steps * wbytes + kv_bytes
+    peak, peak_kind = peaks()
+    achieved = alg / (ms / 1e3) / 1e9
+    return {"workload": "cfg4", "description": desc, "tp": world, "value": args.steps / (ms / 1e3),
+            "unit": "tok/s", "ms_per_step": ms / args.steps, "steps": args.steps,
+            "e2e": {"value": args.steps / e2e_s, "unit": "tok/s", "api": "sm_forward_sample"},
+            "exchanges": "peer-memory pushes from the row-split GEMV epilogues (2 all-reduces per layer, one "
+                         "logit gather per step)",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+                         "frac": achieved / (peak * world), "bytes_per_step": alg / args.steps,
+                         "peak_source": peak_kind, "note": "all ranks' weight shards + KV per step / step time, "
+                                                           "against %d x the per-GPU peak" % world},
+            "gpu_launches": world * args.steps * step_kernels, "clocks": clk}
+
+
 def run_ours(args, rank, world, local_rank, barrier, allmax):
     import torch
     import smotor
@@ -379,6 +458,11 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     h2d, d2h = model.step_io_bytes()
     step_kernels = model.step_launches(batch)  # kernel nodes of the decode-step graph
     model.free()  # every rank at the same point (tensor parallel: the group's teardown barrier)
+    for c in caches:
+        c.free()
+    tp_line = None
+    if world > 1 and not split and not args.no_tp_leg:  # the 70B shape split over this job's GPUs
+        tp_line = tensor_parallel_leg(args, rank, world, local_rank, barrier, allmax)
     if rank != 0:
         return
     # KV bytes read by attention over the timed steps: positions 0..pos per layer, K and V, f32
@@ -427,6 +511,8 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     }
     if world == 1 and not args.no_cpu_baseline and args.workload not in TP_WORKLOADS:
         line["cpu_baseline"] = cpu_baseline(path, prompt_len)
+    if tp_line is not None:
+        line["tensor_parallel"] = tp_line
     print(json.dumps(line), flush=True)
 
 
@@ -441,6 +527,8 @@ def main():
     ap.add_argument("--only", default="", help="gemv workload: one MxK:TYPE:batch case, e.g. 3584x18944:Q4_K:1")
     ap.add_argument("--tp-nccl", action="store_true", help="tensor parallel: NCCL collectives instead of the "
                                                             "engine's peer-memory exchange kernels")
+    ap.add_argument("--no-tp-leg", action="store_true", help="multi-GPU jobs: skip the tensor-parallel config-4 "
+                                                              "measurement added to the replica line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = env_int("WORLD_SIZE", 1)

@@ -183,8 +183,24 @@ struct GemvArgs {
   // Set non-zero by a kernel whose bounded wait gave up (the launch's results
   // are then not valid); may be null.
   uint32_t* err;
+  // Batch-1 EPI_STORE launches (the output head): per 16-row tile, the key of
+  // its largest value, lowest row first (argmax_key); may be null.
+  uint64_t* amax;
   TpPush push;  // EPI_PUSH
 };
+
+// Greedy-sampling key of logit v at index i: larger value first, then lower
+// index (argmax, sampling.rs:147-155); a NaN never wins (key 0).
+SM_HD uint64_t argmax_key(float v, uint32_t i) {
+  union {
+    float f;
+    uint32_t u;
+  } b;
+  b.f = v;
+  if (v != v) return 0;
+  const uint32_t k = (b.u & 0x80000000u) ? ~b.u : (b.u | 0x80000000u);
+  return ((uint64_t)k << 32) | (0xFFFFFFFFu - i);
+}
 
 #ifdef __CUDACC__
 // fp16 bit pattern -> f32 as the reference decodes it (dequant.rs:12-33):

@@ -259,6 +259,8 @@ struct sm_model {
   uint32_t parts_cap = 0;
   uint8_t* mask_dev = nullptr;
   uint32_t* smp_scratch = nullptr;  // the sampler's per-row scratch (sample_scratch_words(V) words a row)
+  uint64_t* amax = nullptr;         // the batch-1 output head's per-tile argmax keys
+  uint32_t amax_n = 0;
   void* in_dev = nullptr;   // StepIn block on the device
   void* in_host = nullptr;  // pinned
   void* out_dev = nullptr;  // StepOut block on the device
@@ -587,6 +589,10 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
       (rc = dev_alloc(m, (void**)&m->mask_dev, R * V)) ||
       (rc = dev_alloc(m, (void**)&m->smp_scratch, R * sample_scratch_words((uint32_t)V) * 4)))
     return rc;
+  if (!m->tp && tiled_type(m->output.d.type)) {  // batch-1 heads run on gemv_tc: one key per 16-row tile
+    m->amax_n = (uint32_t)((V + 15) / 16);
+    if ((rc = dev_alloc(m, (void**)&m->amax, (size_t)m->amax_n * 8))) return rc;
+  }
   {
     // K-split scratch: the most any batch-1 GEMV of this model asks for
     int sms = 0;
@@ -814,6 +820,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     } else {  // a selection (prefill): normalize the selected rows here (qwen2.rs:555-560)
       RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
     }
+    if (nsel == 1 && m->amax) hd_.amax = m->amax;  // greedy candidates per tile (the sampler's fast path)
     RK(launch_gemv(hd_, st));
     if (tp) {  // the full logits on every rank
       if (gx.send) RK(tp_gather_issue(tp, nsel, st));
@@ -986,7 +993,8 @@ int sample_rows(sm_model* m, uint32_t rows, const uint8_t* mask_host, bool advan
     mask = m->mask_dev;
   }
   CK(launch_sample(m->logits, (uint32_t)m->c.vocab_size, rows, mask, m->din.sp, m->din.rng, m->dout.tok,
-                   advance ? m->din.tok : nullptr, advance ? m->din.rows : nullptr, m->smp_scratch, st));
+                   advance ? m->din.tok : nullptr, advance ? m->din.rows : nullptr, m->smp_scratch, st, ~0ull,
+                   rows == 1 ? m->amax : nullptr, m->amax_n));
   CK(cudaMemcpyAsync(m->dout.rng, m->din.rng, rows * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
   CK(cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st));
   return SM_OK;
@@ -1004,7 +1012,7 @@ int decode_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
   if (e == cudaSuccess) e = run_rows(m, B, B, st);
   if (e == cudaSuccess)
     e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
-                      m->din.rows, m->smp_scratch, st);
+                      m->din.rows, m->smp_scratch, st, ~0ull, B == 1 ? m->amax : nullptr, m->amax_n);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->dout.rng, m->din.rng, B * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st);
   cudaError_t e2 = cudaStreamEndCapture(st, &g);
@@ -1037,7 +1045,7 @@ int run_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
   cudaError_t e = run_rows(m, B, B, st);
   if (e == cudaSuccess)
     e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
-                      m->din.rows, m->smp_scratch, st);
+                      m->din.rows, m->smp_scratch, st, ~0ull, B == 1 ? m->amax : nullptr, m->amax_n);
   if (e == cudaSuccess) e = launch_record_tokens(m->dout.tok, B, m->hist, m->hist_ctr, HIST_TOKENS / B, st);
   cudaError_t e2 = cudaStreamEndCapture(st, &g);
   if (e != cudaSuccess || e2 != cudaSuccess) {

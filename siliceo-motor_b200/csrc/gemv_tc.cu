@@ -351,6 +351,17 @@ __device__ __forceinline__ void tc_epilogue(const GemvArgs& a, uint32_t tile, fl
       const float s2 = warp_sum(xn * xn);
       if (lane == 0) parts[tile] = s2;
     }
+    if (a.amax) {  // the tile's greedy candidate (the stored values, bias included)
+      const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
+      uint64_t key = 0;
+      if (t < 2 && o < sg.w.n_out) key = argmax_key(sg.y[o], o);
+#pragma unroll
+      for (int of = 16; of > 0; of >>= 1) {
+        const uint64_t k2 = __shfl_xor_sync(0xffffffffu, key, of);
+        key = k2 > key ? k2 : key;
+      }
+      if (lane == 0) a.amax[tile] = key;
+    }
   }
 }
 

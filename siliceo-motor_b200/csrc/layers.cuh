@@ -45,11 +45,14 @@ cudaError_t attention_prepare();
 cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, cudaStream_t st);
 // The on-device sampler (sampler.cu): rows CTAs, row r's logits at
 // logits + r * ldl (ldl = ~0: V), scratch of sample_scratch_words(V) words per
-// row (used when the row's temperature is > 0).
+// row (used when the row's temperature is > 0). amax (may be null): n_amax
+// per-tile argmax keys of row 0's logits written by the output head's
+// epilogue; a greedy row 0 without a mask reduces those instead.
 uint64_t sample_scratch_words(uint32_t V);
 cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const uint8_t* mask,
                           const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
-                          RowDesc* advance, uint32_t* scratch, cudaStream_t st, uint64_t ldl = ~0ull);
+                          RowDesc* advance, uint32_t* scratch, cudaStream_t st, uint64_t ldl = ~0ull,
+                          const uint64_t* amax = nullptr, uint32_t n_amax = 0);
 // softmax (sampling.rs:157-172) of `rows` rows of n values, bit for bit.
 cudaError_t launch_softmax(const float* x, uint32_t rows, uint32_t n, float* out, cudaStream_t st);
 // The sampler's exp (glibc's expf on x <= 0) applied to n values.

@@ -356,7 +356,8 @@ __device__ void radix_sort_stable(uint32_t* ka, uint32_t* ia, uint32_t* kb, uint
 __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits, uint32_t V, const uint8_t* mask,
                                                              const SampleParams* params, uint64_t* rng,
                                                              uint32_t* out_tok, uint32_t* next_tok, RowDesc* advance,
-                                                             uint32_t* scratch, uint64_t scratch_words, uint64_t ldl) {
+                                                             uint32_t* scratch, uint64_t scratch_words, uint64_t ldl,
+                                                             const uint64_t* amax, uint32_t n_amax) {
   pdl_trigger();
   pdl_wait();  // the logits come from the output-head GEMV
   const uint32_t r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -376,7 +377,27 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits
   unsigned long long* cand = reinterpret_cast<unsigned long long*>(big);
   auto logit = [&](uint32_t i) -> float { return (mr && !mr[i]) ? -INFINITY : lr[i]; };
 
-  if (P.temperature <= 0.0f) {  // greedy (sampling.rs:96-98, 147-155); a NaN temperature samples
+  if (P.temperature <= 0.0f && amax && !mr && r == 0) {
+    // greedy from the output head's per-tile candidates (argmax_key)
+    unsigned long long best = 0;
+    for (uint32_t i = tid; i < n_amax; i += SMP_THREADS) best = max(best, (unsigned long long)amax[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    __shared__ unsigned long long wk[32];
+    if (lane == 0) wk[warp] = best;
+    __syncthreads();
+    if (warp == 0) {
+      best = wk[lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+      if (lane == 0) {
+        const float l0 = lr[0];
+        // x[i] > NaN is false for every i: a NaN at index 0 is the answer
+        s_choice = (l0 != l0 || best == 0) ? 0u : 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+      }
+    }
+    __syncthreads();
+  } else if (P.temperature <= 0.0f) {  // greedy (sampling.rs:96-98, 147-155); a NaN temperature samples
     Best b{-INFINITY, 0xFFFFFFFFu};
     for (uint32_t i = tid; i < V; i += SMP_THREADS) b = better(b, Best{logit(i), i});
 #pragma unroll
@@ -629,10 +650,12 @@ uint64_t sample_scratch_words(uint32_t V) { return 5ull * V + 64; }
 
 cudaError_t launch_sample(const float* logits, uint32_t V, uint32_t rows, const uint8_t* mask,
                           const SampleParams* params, uint64_t* rng, uint32_t* out_tok, uint32_t* next_tok,
-                          RowDesc* advance, uint32_t* scratch, cudaStream_t st, uint64_t ldl) {
+                          RowDesc* advance, uint32_t* scratch, cudaStream_t st, uint64_t ldl, const uint64_t* amax,
+                          uint32_t n_amax) {
   if (!rows) return cudaSuccess;
   return launch_pdl(sample_kernel, dim3(rows), dim3(SMP_THREADS), 0, st, logits, V, mask, params, rng, out_tok,
-                    next_tok, advance, scratch, sample_scratch_words(V), ldl == ~0ull ? (uint64_t)V : ldl);
+                    next_tok, advance, scratch, sample_scratch_words(V), ldl == ~0ull ? (uint64_t)V : ldl, amax,
+                    n_amax);
 }
 
 cudaError_t launch_expf_ref(const float* x, float* y, size_t n, cudaStream_t st) {

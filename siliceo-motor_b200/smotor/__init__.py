@@ -618,10 +618,6 @@ class DWeight:
         _check(lib().sm_gemv_status(self.h, C.c_void_p(stream)))
 
 
-def gemv_noalloc_status(stream: int = 0) -> None:
-    """Raises if a bounded wait in an earlier gemv_noalloc() on the current device gave up."""
-    _check(lib().sm_gemv_noalloc_status(C.c_void_p(stream)))
-
     def free(self) -> None:
         if self.h:
             lib().sm_dweight_free(self.h)
@@ -632,6 +628,11 @@ def gemv_noalloc_status(stream: int = 0) -> None:
             self.free()
         except Exception:
             pass
+
+
+def gemv_noalloc_status(stream: int = 0) -> None:
+    """Raises if a bounded wait in an earlier gemv_noalloc() on the current device gave up."""
+    _check(lib().sm_gemv_noalloc_status(C.c_void_p(stream)))
 
 
 # ------------------------------------------------------------- synthetic ----

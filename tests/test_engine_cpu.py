@@ -121,3 +121,15 @@ def test_model_load_errors(tmp_path):
     with pytest.raises(smotor.EngineError) as e:
         smotor.Model.load(str(bad))
     assert e.value.status == 3 and "magic" in str(e.value)
+
+
+def test_binding_classes_keep_their_methods():
+    import smotor
+    for cls, names in ((smotor.DWeight, ("gemv", "gemv_noalloc", "gemv_status", "dequant", "nbytes", "free")),
+                       (smotor.Model, ("forward_cached", "forward_sample", "decode_batch", "decode_batch_logits",
+                                       "decode_run", "embedding", "generate", "free")),
+                       (smotor.Cache, ("clone", "truncate", "read_kv", "free"))):
+        for n in names:
+            assert callable(getattr(cls, n, None)), (cls.__name__, n)
+    for n in ("sample", "softmax", "expf_ref", "gemv_noalloc_status", "synth_write", "quantize"):
+        assert callable(getattr(smotor, n, None)), n
