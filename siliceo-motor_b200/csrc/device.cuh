@@ -186,6 +186,13 @@ struct GemvArgs {
   // Batch-1 EPI_STORE launches (the output head): per 16-row tile, the key of
   // its largest value, lowest row first (argmax_key); may be null.
   uint64_t* amax;
+  // Batch-1 launches whose input is the attention output (the O projection):
+  // when att_o is set, x is merged from the attention kernel's per-split
+  // partials (o, and (m, l) in att_ml; att_slots slots per head, the row's
+  // own splits from slot att_first on) instead of being read from x.
+  const float* att_o;
+  const float* att_ml;
+  uint32_t att_slots, att_first;
   TpPush push;  // EPI_PUSH
 };
 

@@ -749,7 +749,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
   base.xblob_cap = m->xblob_cap;
   base.err = m->dout.err;
   RK(launch_embed_norm(m->tok_embd.d, m->din.tok, nrows, m->x, H, m->layers[0].attn_norm, m->xn, H, m->parts_a, st));
-  uint32_t np_a = 1, np_b = 0;
+  uint32_t np_a = embed_norm_parts(H), np_b = 0;
   for (uint32_t li = 0; li < c.n_layers; li++) {
     const Layer& L = m->layers[li];
     GemvArgs a = base;
@@ -761,12 +761,20 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     a.seg[1] = seg(L.wk, nullptr, 0, L.bk, EPI_ROPE_K);
     a.seg[2] = seg(L.wv, nullptr, 0, L.bv, EPI_V);
     RK(launch_gemv(a, st));
+    // one row whose O projection runs on gemv_tc: the O GEMV merges the attention partials itself
+    const bool merge = nrows == 1 && tiled_type(L.wo.d.type);
     RK(launch_attention(m->q, qd, m->din.rows, m->din.seqs, nrows, li, Hq, Hkv, hd, m->part_o, m->part_ml,
-                        m->max_splits, m->att, qd, st, nsel != nrows ? 1u : 0u, shared));
+                        m->max_splits, merge ? nullptr : m->att, qd, st, nsel != nrows ? 1u : 0u, shared));
     GemvArgs o = base;
     o.layer = li;
     o.x = m->att; o.ldx = qd;
     o.nseg = 1;
+    if (merge) {
+      o.att_o = m->part_o;
+      o.att_ml = m->part_ml;
+      o.att_slots = m->max_splits;
+      o.att_first = ATT_SHARED_SPLITS;
+    }
     if (tp) {
       RK(split_gemv(o, L.wo, L.ffn_norm, m->parts_b, &np_b));
     } else {

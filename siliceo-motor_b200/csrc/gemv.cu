@@ -298,28 +298,32 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(const __grid_cons
 }
 
 // Embedding lookup (qwen2.rs:468-472) fused with the first layer's RMSNorm
-// input: x = row tok of the table (exact dequant), xn = x * nw, parts[r] =
-// sum(x^2) (one partial per row).
+// input: x = row tok of the table (exact dequant), xn = x * nw, and per chunk
+// of EMB_CHUNK elements (blockIdx.y) the partial sum(x^2) at
+// parts[r * gridDim.y + chunk] (summed by the next GEMV in chunk order).
+constexpr uint32_t EMB_CHUNK = 512;
 __global__ void embed_norm_kernel(DWDesc w, const uint32_t* tokens, float* x, uint32_t ldx, const float* nw, float* xn,
                                   uint32_t ldxn, float* parts) {
   const uint32_t r = blockIdx.x, tok = tokens[r], n = w.n_in;
-  float ss = 0.f;
-  for (uint32_t e = threadIdx.x; e < n; e += blockDim.x) {
-    const float v = dequant_elem(w, tok, e);
+  const uint32_t e = blockIdx.y * EMB_CHUNK + threadIdx.x;
+  float v = 0.f;
+  if (e < n) {
+    v = dequant_elem(w, tok, e);
     x[(size_t)r * ldx + e] = v;
     xn[(size_t)r * ldxn + e] = v * nw[e];
-    ss += v * v;
   }
-  __shared__ float red[32];
-  ss = warp_sum(ss);
+  float ss = warp_sum(v * v);
+  __shared__ float red[EMB_CHUNK / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    v = warp_sum(v);
-    if (threadIdx.x == 0) parts[r] = v;
+    float s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) parts[(size_t)r * gridDim.y + blockIdx.y] = s;
   }
 }
+
+uint32_t embed_norm_parts(uint32_t n) { return (n + EMB_CHUNK - 1) / EMB_CHUNK; }
 
 // ------------------------------------------------------------ launch ----
 // Fills cta_begin of each segment; returns the total CTA count along y.
@@ -396,7 +400,7 @@ cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st) {
 cudaError_t launch_embed_norm(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
                               const float* nw, float* xn, uint32_t ldxn, float* parts, cudaStream_t st) {
   if (!rows) return cudaSuccess;
-  embed_norm_kernel<<<rows, 512, 0, st>>>(w, tokens, x, ldx, nw, xn, ldxn, parts);
+  embed_norm_kernel<<<dim3(rows, embed_norm_parts(w.n_in)), EMB_CHUNK, 0, st>>>(w, tokens, x, ldx, nw, xn, ldxn, parts);
   return cudaGetLastError();
 }
 

@@ -49,10 +49,9 @@ namespace sm {
 // kernel's CTA still runs there, and fetch its weights into shared memory
 // before it waits for this kernel's output.
 constexpr int TC_WARPS = 8, TC_THREADS = TC_WARPS * 32;
-// B fragments of one block, one type: [8 MMA positions][32 lanes] of two words
-// (the l0|l1 and the l2 operand word; the other word of each MMA operand pair
-// is zero and is not stored)
-constexpr uint32_t TC_FRAG = 2048;
+// B fragments of one block, one type: [8 MMA positions][32 lanes][4 words]
+// (b0, b1 of the l0|l1 MMA, b0, b1 of the l2 MMA; one word of each pair is 0)
+constexpr uint32_t TC_FRAG = 4096;
 // per block: (u_s, X_s) of the 8 Q4_K sub-blocks, then of the 16 Q6_K ones
 constexpr uint32_t TC_XS = 256;
 constexpr uint32_t TC_SMEM_MAX = 110u * 1024u;
@@ -61,7 +60,7 @@ constexpr uint32_t TC_SMEM_MAX = 110u * 1024u;
 constexpr uint32_t TC_MAX_STAGES = 4;
 
 struct TcPlan {
-  uint32_t tiles, groups, ksplit, slice, units, grid, smem, t4, t6;
+  uint32_t tiles, groups, ksplit, slice, units, grid, smem, t4, t6, mixed;
   uint32_t stages, stage_bytes;  // per-warp cp.async ring of weight units
 };
 
@@ -70,6 +69,13 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
   asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// d = A B (a zero accumulator, without zeroing registers first)
+__device__ __forceinline__ void mma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int c) { return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w; }
 
@@ -96,24 +102,57 @@ __device__ __forceinline__ void limbs4(const float4& v, float f, uint32_t (&l)[3
   }
 }
 
-// Converts one block of x (256 values at xb) into shared memory, one warp per
+// Converts block blk of x (256 values) into shared memory, one warp per
 // block: per type the B fragments of its 8 MMA positions (f4, f6: [position]
 // [lane] uint4 = b0, b1 of the l0/l1 MMA, b0, b1 of the l2 MMA), and per
 // sub-block (u_s, X_s) (xs: 8 for Q4_K, then 16 for Q6_K). Column n = g of
 // lane (g, t) is (sub-block sigma = g >> 1, limb g & 1); its b0 (k = 4t ..
 // 4t + 3) holds sub-block t >> 1 and b1 (k = 4t + 16 ..) sub-block 2 + (t >> 1),
 // so a lane's word is non-zero only where that matches sigma.
-__device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint2* f4, uint2* f6, float2* xs, bool t4,
+// The attention output x[e0 .. e0 + 7] of head e0 / hd, merged from the
+// attention split kernel's partials: sum_s o_s e_s / sum_s l_s e_s with
+// e_s = exp(m_s - max m) (the merge of attn_combine_kernel, layers.cu).
+__device__ __forceinline__ void att_merge8(const GemvArgs& a, uint32_t e0, float4& v0, float4& v1) {
+  const uint32_t hd = a.hd, h = e0 / hd, d0 = e0 - h * hd;
+  const uint32_t L = a.rows[0].pos + 1, tiles = (L + 31) / 32, np = a.att_slots - a.att_first;
+  const uint32_t tps = (tiles + np - 1) / np, ns = (tiles + tps - 1) / tps;
+  const float* ml = a.att_ml + ((size_t)h * a.att_slots + a.att_first) * 2;
+  const float* po = a.att_o + ((size_t)h * a.att_slots + a.att_first) * hd + d0;
+  float M = -INFINITY;
+  for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, ml[2 * s]);
+  float den = 0.f;
+  float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+  for (uint32_t s = 0; s < ns; s++) {
+    const float es = expf(ml[2 * s] - M);
+    den = fmaf(ml[2 * s + 1], es, den);
+    const float4 o0 = ldg4(po + (size_t)s * hd), o1 = ldg4(po + (size_t)s * hd + 4);
+    acc0.x = fmaf(o0.x, es, acc0.x); acc0.y = fmaf(o0.y, es, acc0.y);
+    acc0.z = fmaf(o0.z, es, acc0.z); acc0.w = fmaf(o0.w, es, acc0.w);
+    acc1.x = fmaf(o1.x, es, acc1.x); acc1.y = fmaf(o1.y, es, acc1.y);
+    acc1.z = fmaf(o1.z, es, acc1.z); acc1.w = fmaf(o1.w, es, acc1.w);
+  }
+  v0 = make_float4(acc0.x / den, acc0.y / den, acc0.z / den, acc0.w / den);
+  v1 = make_float4(acc1.x / den, acc1.y / den, acc1.z / den, acc1.w / den);
+}
+
+__device__ __forceinline__ void tc_build_x(const GemvArgs& a, uint32_t blk, uint4* f4, uint4* f6, float2* xs, bool t4,
                                            bool t6) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, sn = g >> 1, lim = g & 1;
   const bool active = (t >> 1) == (sn & 1);
-  const float4 v0 = ldg4(xb + 8 * lane), v1 = ldg4(xb + 8 * lane + 4);
+  float4 v0, v1;
+  if (a.att_o) {
+    att_merge8(a, blk * 256u + 8u * lane, v0, v1);
+  } else {
+    const float* xb = a.x + (size_t)blk * 256;
+    v0 = ldg4(xb + 8 * lane);
+    v1 = ldg4(xb + 8 * lane + 4);
+  }
   const float mx = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
                          fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
   const float sm = sum4(v0) + sum4(v1);
   // Each lane cuts its own 8 values into limbs (with its sub-block's scale);
   // the fragment words are then fetched from the owning lanes by shuffles.
-  auto frag = [&](uint2* f, int wsub, float scl_own) {
+  auto frag = [&](uint4* f, int wsub, float scl_own) {
     uint32_t L0[3], L1[3];  // limbs of values 8 lane + 0..3 and + 4..7
     limbs4(v0, scl_own, L0);
     limbs4(v1, scl_own, L1);
@@ -127,7 +166,7 @@ __device__ __forceinline__ void tc_build_x(const float* __restrict__ xb, uint2* 
       const uint32_t b0 = __shfl_sync(0xffffffffu, L0[2], src), b1 = __shfl_sync(0xffffffffu, L1[2], src);
       const uint32_t A = active ? (half ? (lim ? a11 : a10) : (lim ? a01 : a00)) : 0u;
       const uint32_t B = (active && !lim) ? (half ? b1 : b0) : 0u;
-      f[P * 32 + lane] = make_uint2(A, B);  // b0 (sn < 2) or b1 (sn >= 2) of each MMA; the other is 0
+      f[P * 32 + lane] = (sn >> 1) ? make_uint4(0, A, 0, B) : make_uint4(A, 0, B, 0);
     }
   };
   if (t4) {  // 32-wide sub-blocks: lanes 4s .. 4s + 3
@@ -168,17 +207,9 @@ __device__ __forceinline__ void q4_sc_m(const uint4& h, int G, int t, float& sc,
     m = (float)(((h.w >> (sh + 4)) & 0xFu) | (((h.z >> (sh + 6)) & 3u) << 4));
   }
 }
-// The B operand pair of an MMA from a compact fragment word w: (w, 0) for
-// lanes 0-15 (columns of sub-blocks 0, 1: k < 16), (0, w) for lanes 16-31.
-__device__ __forceinline__ void b_pair(uint32_t w, uint32_t keep_lo, uint32_t& b0, uint32_t& b1) {
-  b0 = w & keep_lo;
-  b1 = w & ~keep_lo;
-}
-
-__device__ __forceinline__ void q4_block(const uint8_t* st, const uint2* f, const float2* xs, int lane, float& rg,
+__device__ __forceinline__ void q4_block(const uint8_t* st, const uint4* f, const float2* xs, int lane, float& rg,
                                          float& rh) {
   const int g = lane >> 2, t = lane & 3, p = t & 1;
-  const uint32_t keep_lo = (lane >> 4) ? 0u : 0xFFFFFFFFu;
   const uint32_t M = (t >> 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;  // nibble of sub-blocks t >> 1, 2 + (t >> 1)
   uint4 Wg[4], Wh[4];
 #pragma unroll
@@ -187,21 +218,24 @@ __device__ __forceinline__ void q4_block(const uint8_t* st, const uint2* f, cons
     Wh[j] = *reinterpret_cast<const uint4*>(st + q4t_word_off(g + 8, j, 0, p));
   }
   const uint4 hg = reinterpret_cast<const uint4*>(st)[g], hh = reinterpret_cast<const uint4*>(st)[g + 8];
-  const float dg = h2f_ref(hg.x & 0xFFFFu), dmg = h2f_ref(hg.x >> 16);
-  const float dh = h2f_ref(hh.x & 0xFFFFu), dmh = h2f_ref(hh.x >> 16);
+  // per row: sum over the lane's two sub-blocks of sc*u*S and of m*X; d and
+  // dmin are applied once
+  float sg_ = 0.f, sh_ = 0.f, mg_ = 0.f, mh_ = 0.f;
 #pragma unroll
   for (int G = 0; G < 2; G++) {
-    int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0};
+    int A[4], B[4];
 #pragma unroll
     for (int c = 0; c < 4; c++) {
-      const uint2 bf = f[(4 * G + c) * 32 + lane];
-      uint32_t b0, b1, b2, b3;
-      b_pair(bf.x, keep_lo, b0, b1);
-      b_pair(bf.y, keep_lo, b2, b3);
+      const uint4 bf = f[(4 * G + c) * 32 + lane];
       const uint32_t a0 = word_of(Wg[2 * G], c) & M, a2 = word_of(Wg[2 * G + 1], c) & M;
       const uint32_t a1 = word_of(Wh[2 * G], c) & M, a3 = word_of(Wh[2 * G + 1], c) & M;
-      mma_u8s8(A, a0, a1, a2, a3, b0, b1);
-      mma_u8s8(B, a0, a1, a2, a3, b2, b3);
+      if (c == 0) {
+        mma_u8s8_z(A, a0, a1, a2, a3, bf.x, bf.y);
+        mma_u8s8_z(B, a0, a1, a2, a3, bf.z, bf.w);
+      } else {
+        mma_u8s8(A, a0, a1, a2, a3, bf.x, bf.y);
+        mma_u8s8(B, a0, a1, a2, a3, bf.z, bf.w);
+      }
     }
     float Sg, Sh;
     limb_sums(A, B, Sg, Sh);
@@ -209,9 +243,15 @@ __device__ __forceinline__ void q4_block(const uint8_t* st, const uint2* f, cons
     float scg, mg, sch, mh;
     q4_sc_m(hg, G, t, scg, mg);
     q4_sc_m(hh, G, t, sch, mh);
-    rg += (dg * scg) * (ux.x * Sg) - (dmg * mg) * ux.y;
-    rh += (dh * sch) * (ux.x * Sh) - (dmh * mh) * ux.y;
+    sg_ = fmaf(scg, ux.x * Sg, sg_);
+    sh_ = fmaf(sch, ux.x * Sh, sh_);
+    mg_ = fmaf(mg, ux.y, mg_);
+    mh_ = fmaf(mh, ux.y, mh_);
   }
+  const float dg = h2f_ref(hg.x & 0xFFFFu), dmg = h2f_ref(hg.x >> 16);
+  const float dh = h2f_ref(hh.x & 0xFFFFu), dmh = h2f_ref(hh.x >> 16);
+  rg += dg * sg_ - dmg * mg_;
+  rh += dh * sh_ - dmh * mh_;
 }
 
 // ------------------------------------------------------------- Q6_K ----
@@ -221,10 +261,9 @@ __device__ __forceinline__ void q6_a(uint32_t w, uint32_t hbits, int h, uint32_t
   lo = (w & 0x0F0F0F0Fu) | (hs & 0x30303030u);
   hi = ((w >> 4) & 0x0F0F0F0Fu) | ((hs >> 2) & 0x30303030u);
 }
-__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint2* f, const float2* xs, int lane, float& rg,
+__device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, const float2* xs, int lane, float& rg,
                                          float& rh) {
   const int g = lane >> 2, t = lane & 3, p = t & 1, h = t >> 1;
-  const uint32_t keep_lo = (lane >> 4) ? 0u : 0xFFFFFFFFu;
   // per row: W_h words (G, c) and H words (G, c), G = 0..3, c = 0..1
   const uint4 wg0 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, h, 0, 0, p));
   const uint4 wg1 = *reinterpret_cast<const uint4*>(unit + q6t_word_off(g, h, 2, 0, p));
@@ -238,22 +277,25 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint2* f, co
   const float dg = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g]);
   const float dh = q6_d(reinterpret_cast<const unsigned short*>(unit + 256)[g + 8]);
   // eight independent accumulator chains (groups x limb sets) hide the MMA latency
-  int A[4][4] = {}, B[4][4] = {};
+  int A[4][4], B[4][4];
 #pragma unroll
   for (int c = 0; c < 2; c++)
 #pragma unroll
     for (int G = 0; G < 4; G++) {
       const int wi = 2 * (G & 1) + c;
-      const uint2 bf = f[(2 * G + c) * 32 + lane];
-      uint32_t b0, b1, b2, b3;
-      b_pair(bf.x, keep_lo, b0, b1);
-      b_pair(bf.y, keep_lo, b2, b3);
+      const uint4 bf = f[(2 * G + c) * 32 + lane];
       uint32_t a0, a1, a2, a3;
       q6_a(word_of(G < 2 ? wg0 : wg1, wi), word_of(G < 2 ? hg0 : hg1, wi), h, a0, a2);
       q6_a(word_of(G < 2 ? wh0 : wh1, wi), word_of(G < 2 ? hh0 : hh1, wi), h, a1, a3);
-      mma_u8s8(A[G], a0, a1, a2, a3, b0, b1);
-      mma_u8s8(B[G], a0, a1, a2, a3, b2, b3);
+      if (c == 0) {
+        mma_u8s8_z(A[G], a0, a1, a2, a3, bf.x, bf.y);
+        mma_u8s8_z(B[G], a0, a1, a2, a3, bf.z, bf.w);
+      } else {
+        mma_u8s8(A[G], a0, a1, a2, a3, bf.x, bf.y);
+        mma_u8s8(B[G], a0, a1, a2, a3, bf.z, bf.w);
+      }
     }
+  float ag = 0.f, ah = 0.f;  // per row: sum over the lane's sub-blocks of sc*(u*S - 32*X); d applied once
 #pragma unroll
   for (int G = 0; G < 4; G++) {
     float Sg, Sh;
@@ -261,9 +303,11 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint2* f, co
     const float2 ux = xs[8 + 4 * G + t];
     const float sg = (float)(int8_t)((word_of(scg, G) >> (8 * t)) & 0xFFu);
     const float sh = (float)(int8_t)((word_of(sch, G) >> (8 * t)) & 0xFFu);
-    rg += (dg * sg) * fmaf(ux.x, Sg, -32.f * ux.y);
-    rh += (dh * sh) * fmaf(ux.x, Sh, -32.f * ux.y);
+    ag = fmaf(sg, fmaf(ux.x, Sg, -32.f * ux.y), ag);
+    ah = fmaf(sh, fmaf(ux.x, Sh, -32.f * ux.y), ah);
   }
+  rg += dg * ag;
+  rh += dh * ah;
 }
 
 // One warp: tile rows g, g+8 over blocks b0 .. b0+nblk-1 (x fragments of
@@ -278,27 +322,35 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint2* f, co
 template <int QT, int S>
 __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t pre, uint8_t* ring,
                                         uint32_t stage_bytes, uint64_t* bars, uint32_t& nuse, uint32_t* err,
-                                        const uint2* f, const float2* xs, float& rg, float& rh) {
+                                        const uint4* f, const float2* xs, float& rg, float& rh) {
   const int lane = threadIdx.x & 31;
   constexpr uint32_t UB = QT == 12 ? Q4T_UNIT : Q6T_UNIT;
+  auto next = [](uint32_t i) -> uint32_t { return (S & (S - 1)) == 0 ? (i + 1) & (S - 1) : (i + 1 == S ? 0 : i + 1); };
   // ring slot of the next copy to start (ip) and of the next block to compute (cp, phase cph)
   uint32_t ip = nuse % S, cp = ip, cph = (nuse / S) & 1u;
-  for (uint32_t k = 0; k < pre; k++) ip = ip + 1 == S ? 0 : ip + 1;
-  auto issue = [&](uint32_t i) {
-    if (i >= nblk) return;
-    if (lane == 0) tc_issue(tile + (size_t)(b0 + i) * UB, UB, ring, stage_bytes, bars, ip);
-    ip = ip + 1 == S ? 0 : ip + 1;
-  };
-  for (uint32_t k = pre; k + 1 < S; k++) issue(k);
-  for (uint32_t i = 0; i < nblk; i++) {
-    issue(i + S - 1);
+  for (uint32_t k = 0; k < pre; k++) ip = next(ip);
+  const uint8_t* src = tile + (size_t)b0 * UB;
+  const uint32_t npro = min((uint32_t)S - 1, nblk);
+  for (uint32_t k = pre; k < npro; k++) {  // the first S - 1 copies
+    if (lane == 0) tc_issue(src + (size_t)k * UB, UB, ring, stage_bytes, bars, ip);
+    ip = next(ip);
+  }
+  auto compute = [&](uint32_t i) {
     mbar_wait(bars + cp, cph, err);
     const uint8_t* sp = ring + cp * stage_bytes;
-    if (++cp == S) { cp = 0; cph ^= 1u; }
-    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * (TC_FRAG / 8), xs + 32 * i, lane, rg, rh);
-    else q6_block(sp, f + (size_t)i * (TC_FRAG / 8), xs + 32 * i, lane, rg, rh);
+    cp = next(cp);
+    cph ^= cp == 0 ? 1u : 0u;
+    if constexpr (QT == 12) q4_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
+    else q6_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
     __syncwarp();  // every lane is done with the slot before it is refilled
+  };
+  uint32_t i = 0;
+  for (; i + S - 1 < nblk; i++) {  // steady state: the copy S - 1 blocks ahead, then this block
+    if (lane == 0) tc_issue(src + (size_t)(i + S - 1) * UB, UB, ring, stage_bytes, bars, ip);
+    ip = next(ip);
+    compute(i);
   }
+  for (; i < nblk; i++) compute(i);
   nuse += nblk;
 }
 
@@ -308,6 +360,14 @@ __device__ __forceinline__ uint32_t tc_seg(const GemvArgs& a, uint32_t tile) {
   if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
   if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
   return si;
+}
+
+// Whether launch tile `tile` holds rows (padding tiles of a mixed launch do
+// not), and its segment.
+__device__ __forceinline__ bool tc_tile_at(const GemvArgs& a, uint32_t tile, uint32_t tiles, uint32_t& si) {
+  if (tile >= tiles) return false;
+  si = tc_seg(a, tile);
+  return tile - a.seg[si].cta_begin < (a.seg[si].w.n_out + 15) / 16;
 }
 
 // Epilogue of one tile: vg / vh are the full dot products of rows g, g + 8
@@ -372,9 +432,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
   __shared__ uint32_t s_last;
   __shared__ __align__(8) uint64_t s_bars[TC_WARPS * TC_MAX_STAGES];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint2* f4 = reinterpret_cast<uint2*>(tc_smem);
-  uint2* f6 = f4 + (p.t4 ? p.slice * (TC_FRAG / 8) : 0);
-  float2* xs = reinterpret_cast<float2*>(f6 + (p.t6 ? p.slice * (TC_FRAG / 8) : 0));
+  // x fragments per type (a mixed launch: one region, of the CTA's type)
+  uint4* f4 = reinterpret_cast<uint4*>(tc_smem);
+  uint4* f6 = f4 + ((p.t4 && !p.mixed) ? p.slice * (TC_FRAG / 16) : 0);
+  float2* xs = reinterpret_cast<float2*>(f6 + (p.t6 ? p.slice * (TC_FRAG / 16) : 0));
   uint8_t* ring = reinterpret_cast<uint8_t*>(xs + 32 * p.slice) + (size_t)warp * p.stages * p.stage_bytes;
   const uint32_t nb = a.seg[0].w.n_in >> 8;
   uint64_t* bars = s_bars + warp * TC_MAX_STAGES;
@@ -391,8 +452,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
   if (blockIdx.x < p.units) {
     const uint32_t rg = blockIdx.x / p.ksplit, ks = blockIdx.x - rg * p.ksplit;
     const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0), tile = rg * TC_WARPS + warp;
-    if (tile < p.tiles) {
-      const uint32_t si = tc_seg(a, tile);
+    uint32_t si = 0;
+    if (tc_tile_at(a, tile, p.tiles, si)) {
       const DWDesc& w = a.seg[si].w;
       const uint32_t UB = tile_unit_bytes(w.type);
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
@@ -410,16 +471,21 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
     const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
     __syncthreads();  // the previous unit is done with the x fragments
+    // the types this CTA's tiles have (a mixed launch: the type of its group)
+    bool b4 = p.t4, b6 = p.t6;
+    if (p.mixed) {
+      const bool q4 = a.seg[tc_seg(a, rg * TC_WARPS)].w.type == 12;
+      b4 = q4;
+      b6 = !q4;
+    }
     for (uint32_t i = warp; i < nblk; i += TC_WARPS)
-      tc_build_x(a.x + (size_t)(b0 + i) * 256, f4 + i * (TC_FRAG / 8), f6 + i * (TC_FRAG / 8), xs + 32 * i, p.t4,
-                 p.t6);
+      tc_build_x(a, b0 + i, f4 + i * (TC_FRAG / 16), f6 + i * (TC_FRAG / 16), xs + 32 * i, b4, b6);
     __syncthreads();
     const uint32_t tile = rg * TC_WARPS + warp;
     float vg = 0.f, vh = 0.f;
-    if (tile < p.tiles) {
-      uint32_t si = 0;
-      if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
-      if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
+    uint32_t si = 0;
+    const bool valid = tc_tile_at(a, tile, p.tiles, si);
+    if (valid) {
       const DWDesc& w = a.seg[si].w;
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
 #define TC_TILE(QT, S, F) \
@@ -441,7 +507,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     vg += __shfl_xor_sync(0xffffffffu, vg, 2);
     vh += __shfl_xor_sync(0xffffffffu, vh, 2);
     if (p.ksplit == 1) {
-      if (tile < p.tiles) tc_epilogue(a, tile, vg * s_in, vh * s_in);
+      if (valid) tc_epilogue(a, tile, vg * s_in, vh * s_in);
       continue;
     }
     // K-split: publish this slice, the last CTA of the group sums the slices in order.
@@ -456,7 +522,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     __syncthreads();
     if (s_last) {
       __threadfence();
-      if (tile < p.tiles) {
+      if (valid) {
         float sg = 0.f, sh = 0.f;
         for (uint32_t k = 0; k < p.ksplit; k++) {
           sg += __ldcg(a.ks_part + k * stride + tile * 16u + g);
@@ -505,15 +571,19 @@ cudaError_t gemv_tc_prepare() {
 // (a split that does not fit falls back to one slice when the x fragments of
 // all of K fit in shared memory). Returns false when no plan fits.
 static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
-  uint32_t tiles = 0;
   bool t4 = false, t6 = false;
+  for (uint32_t i = 0; i < a.nseg; i++) (a.seg[i].w.type == 12 ? t4 : t6) = true;
+  // A launch of both types starts every segment on a CTA's first tile, so
+  // that a CTA converts x for one type only (padding tiles do nothing).
+  const bool mixed = t4 && t6;
+  uint32_t tiles = 0;
   for (uint32_t i = 0; i < a.nseg; i++) {
+    if (mixed) tiles = (tiles + TC_WARPS - 1) / TC_WARPS * TC_WARPS;
     a.seg[i].cta_begin = tiles;
     tiles += (a.seg[i].w.n_out + 15) / 16;
-    (a.seg[i].w.type == 12 ? t4 : t6) = true;
   }
   const uint32_t nb = a.seg[0].w.n_in >> 8;
-  const uint32_t per_blk = (t4 ? TC_FRAG : 0) + (t6 ? TC_FRAG : 0) + TC_XS;
+  const uint32_t per_blk = (mixed ? TC_FRAG : (t4 ? TC_FRAG : 0) + (t6 ? TC_FRAG : 0)) + TC_XS;
   const uint32_t stage_bytes = t6 ? Q6T_UNIT : Q4T_UNIT;
   // x fragments of up to 32 blocks per slice; the rest of shared memory is
   // ring (at least two slots a warp)
@@ -524,13 +594,16 @@ static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
     return k == 1 || (a.ks_part && a.ks_cnt && (uint64_t)k * tiles * 16u <= a.ks_part_cap && groups <= a.ks_cnt_cap);
   };
   // the split with the least work on the busiest SM: rounds of units x (blocks
-  // per unit + about half a block of per-unit cost: x conversion, epilogue)
+  // per unit + about half a block of per-unit cost: x conversion, epilogue).
+  // (Splitting further to deepen the copy rings measured slower in a chain of
+  // launches: 23.8 against 18.1 us for the 7B gate/up shape.)
   uint32_t ks = 0;
   uint64_t best = ~0ull;
   for (uint32_t k = 1; k <= std::min(nb, 64u); k++) {
     const uint32_t sl = (nb + k - 1) / k;
     const uint32_t kk = (nb + sl - 1) / sl;
     if (sl > slice_max || !fits(kk)) continue;
+    if ((TC_SMEM_MAX - sl * per_blk) / (TC_WARPS * stage_bytes) < 2) continue;  // at least two ring slots
     const uint64_t rounds = ((uint64_t)groups * kk + slots - 1) / slots;
     if (rounds * (2 * sl + 1) < best) {
       best = rounds * (2 * sl + 1);
@@ -553,6 +626,7 @@ static bool tc_plan(GemvArgs& a, uint32_t sms, TcPlan* p) {
   p->stage_bytes = stage_bytes;
   p->t4 = t4;
   p->t6 = t6;
+  p->mixed = mixed;
   return true;
 }
 

@@ -465,7 +465,7 @@ cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, 
   }
   e = launch_pdl(attn_split_kernel, dim3(nrows * Hkv, max_splits - ATT_SHARED_SPLITS), dim3(ATT_THREADS), sm, st, q,
                  ldq, rows, seqs, layer, Hq, Hkv, hd, scale, part_o, part_ml, max_splits, one_seq, shared_tiles);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || !out) return e;  // no out: the consumer merges the partials itself
   return launch_pdl(attn_combine_kernel, dim3(nrows * Hq), dim3(hd), 0, st, part_o, part_ml, rows, Hq, hd, max_splits,
                     out, ldo, shared_tiles);
 }

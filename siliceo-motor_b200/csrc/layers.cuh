@@ -21,8 +21,10 @@ uint32_t gemv_plan(GemvArgs& a);
 // n_parts: the number of out_parts entries per column an EPI_RESID launch writes.
 cudaError_t launch_gemv(GemvArgs a, cudaStream_t st, uint32_t* n_parts = nullptr);
 cudaError_t launch_dequant(const DWDesc& w, float* out, cudaStream_t st);
+// Writes embed_norm_parts(n_in) partial sums of x^2 per row into parts.
 cudaError_t launch_embed_norm(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
                               const float* nw, float* xn, uint32_t ldxn, float* parts, cudaStream_t st);
+uint32_t embed_norm_parts(uint32_t n);
 cudaError_t launch_embed(const DWDesc& w, const uint32_t* tokens, uint32_t rows, float* x, uint32_t ldx,
                          cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, uint32_t ldx, const uint32_t* sel, const float* w, float* out, uint32_t ldo,
@@ -34,7 +36,8 @@ size_t attn_smem_bytes(uint32_t G, uint32_t hd);
 // every row holds as the same physical page (all their positions older than
 // every row's): attn_shared_kernel reads them once for all rows. Partials:
 // max_splits slots per (row, head), the first ATT_SHARED_SPLITS for the
-// shared tiles.
+// shared tiles. out = null: only the partials are written (a batch-1 O GEMV
+// merges them as it reads its input: GemvArgs::att_o).
 constexpr uint32_t ATT_SHARED_SPLITS = 8;
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
