@@ -151,14 +151,33 @@ def sampler_for(kind):
     return smotor.Sampler() if kind == "greedy" else smotor.Sampler(1.0, 40, 0.9)
 
 
-def setup_sequences(model, V, batch, prompt_len, kind, extra):
-    """Prefill the workload's prompts; returns (caches, next tokens)."""
+def setup_sequences(model, V, batch, prompt_len, kind, extra, prefill=None):
+    """Prefill the workload's prompts; returns (caches, next tokens). With
+    `prefill` (a dict), a batch-1 prompt's prefill is timed: one untimed pass
+    on a scratch cache first, then the measured one (CUDA events on the
+    engine's stream around sm_forward_cached)."""
     rng = np.random.default_rng(0)
     cap = prompt_len + extra
     if batch == 1:
         prompt = rng.integers(0, V, prompt_len).tolist()
+        if prefill is not None:
+            import torch
+            scratch = model.new_cache(cap)
+            model.forward_cached(scratch, prompt[:-1], logits=False)  # warm-up (kernel set-up, page pool)
+            scratch.free()
+            ext = torch.cuda.ExternalStream(model.stream())
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c = model.new_cache(cap)
+        if prefill is not None:
+            torch.cuda.synchronize()
+            e0.record(ext)
         model.forward_cached(c, prompt[:-1], logits=False)
+        if prefill is not None:
+            e1.record(ext)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            prefill.update({"tokens": prompt_len - 1, "ms": ms, "tok_per_s": (prompt_len - 1) / (ms / 1e3),
+                            "api": "sm_forward_cached (32-row chunks on the batched tcgen05 GEMV)"})
         return [c], [prompt[-1]]
     # shared 1024-token prefix prefilled once, cloned per sequence (prefix cache)
     shared = rng.integers(0, V, prompt_len // 2).tolist()
@@ -413,7 +432,8 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
                               tp=tp)
     cfg = model.config
     V, L, kvd = cfg.vocab_size, cfg.n_layers, cfg.n_kv_heads * cfg.head_dim
-    caches, toks = setup_sequences(model, V, batch, prompt_len, kind, extra)
+    prefill = {} if batch == 1 and not split else None
+    caches, toks = setup_sequences(model, V, batch, prompt_len, kind, extra, prefill)
     samplers = [sampler_for(kind)] * batch
     states = [smotor.rng_seed(i) for i in range(batch)]
     ext = torch.cuda.ExternalStream(model.stream())
@@ -511,6 +531,8 @@ def run_ours(args, rank, world, local_rank, barrier, allmax):
     }
     if world == 1 and not args.no_cpu_baseline and args.workload not in TP_WORKLOADS:
         line["cpu_baseline"] = cpu_baseline(path, prompt_len)
+    if prefill:
+        line["prefill"] = prefill
     if tp_line is not None:
         line["tensor_parallel"] = tp_line
     print(json.dumps(line), flush=True)

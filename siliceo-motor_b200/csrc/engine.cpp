@@ -228,6 +228,7 @@ struct sm_cache {
 struct sm_model {
   int device = 0;
   cudaStream_t stream = nullptr;
+  SideStream side{nullptr, nullptr, nullptr};  // the shared-prefix attention pass of batched steps
   sm_config c{};
   uint32_t kvd = 0;  // this rank's KV width (kv heads x head_dim)
   // Tensor parallelism (sh.world == 1: none): the shard plan, the group, and
@@ -689,6 +690,10 @@ void destroy_model(sm_model* m) {
   for (void* p : m->page_chunks) cudaFree(p);
   if (m->in_host) cudaFreeHost(m->in_host);
   if (m->out_host) cudaFreeHost(m->out_host);
+  if (m->side.st) cudaStreamSynchronize(m->side.st);
+  if (m->side.st) cudaStreamDestroy(m->side.st);
+  if (m->side.fork) cudaEventDestroy(m->side.fork);
+  if (m->side.join) cudaEventDestroy(m->side.join);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -764,7 +769,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     // one row whose O projection runs on gemv_tc: the O GEMV merges the attention partials itself
     const bool merge = nrows == 1 && tiled_type(L.wo.d.type);
     RK(launch_attention(m->q, qd, m->din.rows, m->din.seqs, nrows, li, Hq, Hkv, hd, m->part_o, m->part_ml,
-                        m->max_splits, merge ? nullptr : m->att, qd, st, nsel != nrows ? 1u : 0u, shared));
+                        m->max_splits, merge ? nullptr : m->att, qd, st, nsel != nrows ? 1u : 0u, shared, m->side));
     GemvArgs o = base;
     o.layer = li;
     o.x = m->att; o.ldx = qd;
@@ -1170,11 +1175,15 @@ static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* 
   auto* m = new sm_model();
   m->device = opts ? opts->device : 0;
   if (cudaSetDevice(m->device) != cudaSuccess || cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&m->side.st, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->side.fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->side.join, cudaEventDisableTiming) != cudaSuccess ||
       gemv_tc_prepare() != cudaSuccess || gemv_tcb_prepare() != cudaSuccess ||
       gemv_umma_prepare() != cudaSuccess || attention_prepare() != cudaSuccess) {
     cudaGetLastError();
-    set_error("cannot use CUDA device " + std::to_string(m->device));
-    delete m;
+    const std::string msg = "cannot use CUDA device " + std::to_string(m->device);
+    destroy_model(m);  // releases the streams and events made so far
+    set_error(msg);
     return SM_ERR_CUDA;
   }
   int rc = load_model(*r, opts, m);

@@ -203,7 +203,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(const float* q,
 // ASH_Q of them, a query group. Its partial (o, m, l) per query goes to split
 // slot sp of that (row, head), merged by attn_combine_kernel with the row's
 // own tiles. Scores and P.V in f32 (4 queries x 4 positions and 4 queries x
-// hd/8 dims per thread), online softmax per query across the CTA's tiles.
+// hd/8 dims per thread; a quarter-warp's lanes read consecutive K rows and
+// consecutive V float4s, so their shared-memory loads hit distinct banks),
+// online softmax per query across the CTA's tiles.
 constexpr int ASH_THREADS = 256, ASH_Q = 128;
 
 size_t attn_shared_smem_bytes(uint32_t hd) {
@@ -270,15 +272,15 @@ __global__ void __launch_bounds__(ASH_THREADS) attn_shared_kernel(const float* q
     }
     cp_async_wait<0>();
     __syncthreads();
-    {  // scores of queries i0..i0+3 at positions 4*c8 .. 4*c8+3
+    {  // scores of queries i0..i0+3 at positions c8 + 8b (consecutive lanes read
+       // consecutive K rows: distinct banks)
       float sc[4][4] = {};
-      const uint32_t p0 = 4 * c8;
       for (uint32_t d4 = 0; d4 < hd4; d4++) {
         float4 qv[4], kv[4];
 #pragma unroll
         for (int a = 0; a < 4; a++) qv[a] = reinterpret_cast<const float4*>(qs + (i0 + a) * hs)[d4];
 #pragma unroll
-        for (int b = 0; b < 4; b++) kv[b] = reinterpret_cast<const float4*>(kt + (p0 + b) * hs)[d4];
+        for (int b = 0; b < 4; b++) kv[b] = reinterpret_cast<const float4*>(kt + (c8 + 8 * b) * hs)[d4];
 #pragma unroll
         for (int a = 0; a < 4; a++)
 #pragma unroll
@@ -292,7 +294,7 @@ __global__ void __launch_bounds__(ASH_THREADS) attn_shared_kernel(const float* q
 #pragma unroll
       for (int a = 0; a < 4; a++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) ps[(i0 + a) * (ATT_T + 1) + p0 + b] = sc[a][b] * scale;
+        for (int b = 0; b < 4; b++) ps[(i0 + a) * (ATT_T + 1) + c8 + 8 * b] = sc[a][b] * scale;
     }
     __syncthreads();
     for (uint32_t i = warp; i < nq; i += ASH_THREADS / 32) {  // online softmax, one warp per query
@@ -312,7 +314,8 @@ __global__ void __launch_bounds__(ASH_THREADS) attn_shared_kernel(const float* q
       }
     }
     __syncthreads();
-    {  // acc[a] (dims c8*dpt ..) = acc * alpha + sum_p P[i0+a][p] V[p]
+    {  // acc[a][b] (dims 4 (c8 + 8b) ..: consecutive lanes, consecutive float4s)
+       //   = acc * alpha + sum_p P[i0+a][p] V[p]
       float al[4];
 #pragma unroll
       for (int a = 0; a < 4; a++) al[a] = alpha[i0 + a];
@@ -329,7 +332,7 @@ __global__ void __launch_bounds__(ASH_THREADS) attn_shared_kernel(const float* q
 #pragma unroll
         for (int b = 0; b < 4; b++) {
           if (4 * b >= (int)dpt) break;
-          const float4 v = reinterpret_cast<const float4*>(vt + pp * hs + c8 * dpt)[b];
+          const float4 v = reinterpret_cast<const float4*>(vt + pp * hs)[c8 + 8 * b];
 #pragma unroll
           for (int a = 0; a < 4; a++) {
             acc[a][b].x = fmaf(pw[a], v.x, acc[a][b].x);
@@ -346,10 +349,10 @@ __global__ void __launch_bounds__(ASH_THREADS) attn_shared_kernel(const float* q
     const uint32_t qi = i0 + a;
     if (qi >= nq) continue;
     const uint32_t gq = q0 + qi, r = gq / G, h = g * G + (gq - r * G);
-    float* po = part_o + (((size_t)r * Hq + h) * max_splits + sp) * hd + c8 * dpt;
+    float* po = part_o + (((size_t)r * Hq + h) * max_splits + sp) * hd;
 #pragma unroll
     for (int b = 0; b < 4; b++)
-      if (4 * b < (int)dpt) reinterpret_cast<float4*>(po)[b] = acc[a][b];
+      if (4 * b < (int)dpt) reinterpret_cast<float4*>(po)[c8 + 8 * b] = acc[a][b];
     if (c8 == 0) {
       float* ml = part_ml + (((size_t)r * Hq + h) * max_splits + sp) * 2;
       ml[0] = mrun[qi];
@@ -450,22 +453,37 @@ size_t attn_smem_bytes(uint32_t G, uint32_t hd) {
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
                              uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st, uint32_t one_seq,
-                             const uint32_t* shared_tiles) {
+                             const uint32_t* shared_tiles, SideStream side) {
   if (!nrows) return cudaSuccess;
   const uint32_t G = Hq / Hkv;
   const size_t sm = attn_smem_bytes(G, hd);
   const float scale = 1.0f / sqrtf((float)hd);  // qwen2.rs:505
   cudaError_t e;
+  const bool fork = shared_tiles && side.st;
   if (shared_tiles) {  // the batch's shared prefix, once for all rows
     const uint32_t nqg = (nrows * G + ASH_Q - 1) / ASH_Q;
-    e = launch_pdl(attn_shared_kernel, dim3(Hkv * nqg, ATT_SHARED_SPLITS), dim3(ASH_THREADS),
-                   attn_shared_smem_bytes(hd), st, q, ldq, seqs, shared_tiles, nrows, layer, Hq, Hkv, hd, scale,
-                   part_o, part_ml, max_splits);
-    if (e != cudaSuccess) return e;
+    const dim3 grid(Hkv * nqg, ATT_SHARED_SPLITS), blk(ASH_THREADS);
+    if (fork) {  // on the side stream, concurrent with the split kernel: both need only the QKV GEMV
+      if ((e = cudaEventRecord(side.fork, st)) != cudaSuccess || (e = cudaStreamWaitEvent(side.st, side.fork, 0)))
+        return e;
+      attn_shared_kernel<<<grid, blk, attn_shared_smem_bytes(hd), side.st>>>(
+          q, ldq, seqs, shared_tiles, nrows, layer, Hq, Hkv, hd, scale, part_o, part_ml, max_splits);
+      if ((e = cudaGetLastError()) != cudaSuccess || (e = cudaEventRecord(side.join, side.st)) != cudaSuccess)
+        return e;
+    } else {
+      e = launch_pdl(attn_shared_kernel, grid, blk, attn_shared_smem_bytes(hd), st, q, ldq, seqs, shared_tiles, nrows,
+                     layer, Hq, Hkv, hd, scale, part_o, part_ml, max_splits);
+      if (e != cudaSuccess) return e;
+    }
   }
   e = launch_pdl(attn_split_kernel, dim3(nrows * Hkv, max_splits - ATT_SHARED_SPLITS), dim3(ATT_THREADS), sm, st, q,
                  ldq, rows, seqs, layer, Hq, Hkv, hd, scale, part_o, part_ml, max_splits, one_seq, shared_tiles);
   if (e != cudaSuccess || !out) return e;  // no out: the consumer merges the partials itself
+  if (fork) {  // the merge needs both passes: an ordinary launch after the join
+    if ((e = cudaStreamWaitEvent(st, side.join, 0)) != cudaSuccess) return e;
+    attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo, shared_tiles);
+    return cudaGetLastError();
+  }
   return launch_pdl(attn_combine_kernel, dim3(nrows * Hq), dim3(hd), 0, st, part_o, part_ml, rows, Hq, hd, max_splits,
                     out, ldo, shared_tiles);
 }

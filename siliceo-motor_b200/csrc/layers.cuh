@@ -38,11 +38,18 @@ size_t attn_smem_bytes(uint32_t G, uint32_t hd);
 // max_splits slots per (row, head), the first ATT_SHARED_SPLITS for the
 // shared tiles. out = null: only the partials are written (a batch-1 O GEMV
 // merges them as it reads its input: GemvArgs::att_o).
-constexpr uint32_t ATT_SHARED_SPLITS = 8;
+// side.st (optional): a second stream on which the shared pass runs
+// concurrently with the split kernel (fork and join through the two events;
+// they become graph edges when the launches are captured).
+constexpr uint32_t ATT_SHARED_SPLITS = 32;
+struct SideStream {
+  cudaStream_t st;
+  cudaEvent_t fork, join;
+};
 cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, const SeqDesc* seqs, uint32_t nrows,
                              uint32_t layer, uint32_t Hq, uint32_t Hkv, uint32_t hd, float* part_o, float* part_ml,
                              uint32_t max_splits, float* out, uint32_t ldo, cudaStream_t st, uint32_t one_seq,
-                             const uint32_t* shared_tiles);
+                             const uint32_t* shared_tiles, SideStream side = SideStream{nullptr, nullptr, nullptr});
 size_t attn_shared_smem_bytes(uint32_t hd);
 cudaError_t attention_prepare();
 cudaError_t launch_silu_mul(float* gate, const float* up, uint32_t F, size_t n, cudaStream_t st);

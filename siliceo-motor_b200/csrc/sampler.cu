@@ -219,29 +219,27 @@ __device__ float exact_seq_sum(const float* v, uint32_t n, float stop, uint32_t*
     if (hi - lo < SUM_NE) {
       r.e_lo = lo;
       r.ok = 1;
-      uint64_t D[SUM_NE][2] = {};
-      uint32_t par[SUM_NE][2];
+      // only the binades the running sum can reach in this chunk (usually 1-2)
 #pragma unroll
-      for (int k = 0; k < SUM_NE; k++) par[k][0] = 0, par[k][1] = 1;
-      for (uint32_t i = b; i < e; i++) {
-        const uint32_t tb = __float_as_uint(__ldcg(v + i));
-#pragma unroll
-        for (int k = 0; k < SUM_NE; k++) {
+      for (int k = 0; k < SUM_NE; k++) r.d[k][0] = r.d[k][1] = SUM_SAT;
+      for (int k = 0; k <= hi - lo; k++) {
+        uint64_t D0 = 0, D1 = 0;
+        uint32_t par0 = 0, par1 = 1;
+        const int E = lo + k;
+        for (uint32_t i = b; i < e; i++) {
           uint64_t q;
           bool up, tie;
-          grid_term(tb, lo + k, q, up, tie);
-#pragma unroll
-          for (int p = 0; p < 2; p++) {
-            const uint64_t rr = q + (tie ? ((par[k][p] + (uint32_t)q) & 1u) : (uint32_t)up);
-            D[k][p] += rr;
-            par[k][p] = (par[k][p] + (uint32_t)rr) & 1u;
-          }
+          grid_term(__float_as_uint(__ldcg(v + i)), E, q, up, tie);
+          const uint64_t r0 = q + (tie ? ((par0 + (uint32_t)q) & 1u) : (uint32_t)up);
+          const uint64_t r1 = q + (tie ? ((par1 + (uint32_t)q) & 1u) : (uint32_t)up);
+          D0 += r0;
+          D1 += r1;
+          par0 = (par0 + (uint32_t)r0) & 1u;
+          par1 = (par1 + (uint32_t)r1) & 1u;
         }
+        r.d[k][0] = D0 >= (1u << 24) ? SUM_SAT : (uint32_t)D0;
+        r.d[k][1] = D1 >= (1u << 24) ? SUM_SAT : (uint32_t)D1;
       }
-#pragma unroll
-      for (int k = 0; k < SUM_NE; k++)
-#pragma unroll
-        for (int p = 0; p < 2; p++) r.d[k][p] = D[k][p] >= (1u << 24) ? SUM_SAT : (uint32_t)D[k][p];
     }
   }
   recs[tid] = r;
@@ -306,7 +304,12 @@ __device__ void radix_sort_stable(uint32_t* ka, uint32_t* ia, uint32_t* kb, uint
     uint32_t* di = pass & 1 ? ia : ib;
     for (uint32_t i = tid; i < 256; i += SMP_THREADS) base[i] = 0;
     __syncthreads();
-    for (uint32_t i = tid; i < n; i += SMP_THREADS) atomicAdd(&base[(__ldcg(sk + i) >> shift) & 255u], 1u);
+    for (uint32_t i0 = 0; i0 < n; i0 += SMP_THREADS) {  // lanes with the same digit add once
+      const uint32_t i = i0 + tid;
+      const uint32_t dg = i < n ? (__ldcg(sk + i) >> shift) & 255u : 256u + lane;
+      const uint32_t peers = __match_any_sync(0xffffffffu, dg);
+      if (i < n && __ffs(peers) - 1 == (int)lane) atomicAdd(&base[dg], (uint32_t)__popc(peers));
+    }
     __syncthreads();
     if (tid == 0) {  // exclusive prefix of the digit counts
       uint32_t run = 0;
@@ -456,9 +459,14 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits
         const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (32 - 8 * pass));
         for (uint32_t i = tid; i < 256; i += SMP_THREADS) hist[i] = 0;
         __syncthreads();
-        for (uint32_t i = tid; i < V; i += SMP_THREADS) {
-          const uint32_t kk = key[i];
-          if ((kk & hmask) == prefix) atomicAdd(&hist[(kk >> shift) & 0xFF], 1u);
+        // keys concentrate on a few bins: lanes with the same bin add once
+        for (uint32_t i0 = 0; i0 < V; i0 += SMP_THREADS) {
+          const uint32_t i = i0 + tid;
+          const uint32_t kk = i < V ? key[i] : 0u;
+          const bool in = i < V && (kk & hmask) == prefix;
+          const uint32_t bin = in ? (kk >> shift) & 0xFF : 256u + lane;
+          const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+          if (in && __ffs(peers) - 1 == (int)lane) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
         }
         __syncthreads();
         if (tid == 0) {
