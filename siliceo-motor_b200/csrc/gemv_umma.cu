@@ -64,7 +64,7 @@ constexpr int UM_THREADS = UM_WARPS * 32;
 constexpr uint32_t UM_MAXB = 32;                // columns
 constexpr uint32_t UM_TILES = 8;                // 16-row weight tiles per CTA tile
 constexpr uint32_t UM_SMEM_MIN = 116u * 1024u;  // one CTA per SM: it holds all of tensor memory
-constexpr uint32_t UM_SMEM_MAX = 225u * 1024u;  // with the static part, within the 227 KB opt-in
+constexpr uint32_t UM_SMEM_MAX = 224u * 1024u;  // with the static part (2 KB), within the 227 KB opt-in
 // tensor-memory columns: A operands of two half-blocks, D and D2 of two blocks
 constexpr uint32_t UM_TA = 0, UM_TD = 256, UM_TD2 = 384, UM_TCOLS = 512;
 constexpr uint32_t UM_XPREP_THREADS = 128;
@@ -229,13 +229,67 @@ __device__ __forceinline__ void um_q6_ah(const uint2 (&w)[3][2], const int32_t (
     }
 }
 
+// Per-column constants of a decode launch, read once per CTA into shared
+// memory by the epilogue warps while the blocks stream: the RoPE rows at the
+// column's position and its K / V cache rows for this layer. Read inside the
+// column loop they would be chains of dependent loads (row -> sequence ->
+// page) per column, and the loop's stores keep the compiler from overlapping
+// the loads of one column with another's.
+struct UmCol {
+  const float* cs;
+  const float* sn;
+  float* kc;
+  float* vc;
+};
+
+// Column t's entry (t < batch; called by one thread per column).
+__device__ __forceinline__ void um_col_fill(const GemvArgs& a, uint32_t t, UmCol* cols) {
+  UmCol c{nullptr, nullptr, nullptr, nullptr};
+  bool rope = false, kv = false;
+  for (uint32_t i = 0; i < a.nseg; i++) {
+    const uint32_t e = a.seg[i].epi;
+    rope |= e == EPI_ROPE_Q || e == EPI_ROPE_K;
+    kv |= e == EPI_ROPE_K || e == EPI_V;
+  }
+  if (a.rows && (rope || kv)) {
+    const RowDesc rd = a.rows[t];
+    if (rope) {
+      const size_t r = (size_t)rd.pos * (a.hd >> 1);
+      c.cs = a.cos_t + r;
+      c.sn = a.sin_t + r;
+    }
+    if (kv) {
+      const SeqDesc sd = a.seqs[rd.seq];
+      c.kc = sd.pages[rd.pos / KV_PAGE] + kv_page_off(a.layer, rd.pos, a.kvd);
+      c.vc = c.kc + sd.voff;
+    }
+  }
+  cols[t] = c;
+}
+
+// Partial sum of x^2 over the tile's 16 rows for one column (EPI_RESID
+// launches); every lane of the warp calls it.
+__device__ __forceinline__ void um_resid_part(const GemvArgs& a, float xv, bool write, uint32_t col,
+                                              uint32_t n_parts, uint32_t tile) {
+  const int lane = threadIdx.x & 31;
+  float s2 = xv * xv;
+  s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+  s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+  s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
+  s2 += __shfl_xor_sync(0xffffffffu, s2, 8);
+  if ((lane & 15) == 0 && write) a.out_parts[(size_t)col * n_parts + tile] = s2;
+}
+
 // Epilogue of the calling row (y[i]: column c0 + i, already times the
-// input-norm scale). Every lane of the warp calls it. The segment and the
-// row's constants are read once into registers: read through the parameter
-// reference they would be reloaded after every store of the column loop.
+// input-norm scale): the fused epilogues of gemv_common.cuh (epi_single,
+// epi_pair) with the same arithmetic, organized for 32 columns a thread. The
+// segment's and the row's constants are read once into registers (read
+// through the parameter reference they would be reloaded after every output
+// store); columns go in chunks of 8 whose loads (residuals, RoPE rows) are
+// all issued before the chunk's stores. Every lane of the warp calls it.
 template <int NC>
-__device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, uint32_t n_parts, bool valid,
-                                            uint32_t rr, uint32_t c0, const float (&y)[NC]) {
+__device__ __forceinline__ void um_epilogue(const GemvArgs& a, const UmCol* cols, uint32_t tile, uint32_t n_parts,
+                                            bool valid, uint32_t rr, uint32_t c0, const float (&y)[NC]) {
   const int lane = threadIdx.x & 31;
   uint32_t si = 0;
   if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
@@ -245,71 +299,124 @@ __device__ __forceinline__ void um_epilogue(const GemvArgs& a, uint32_t tile, ui
   const bool row_ok = valid && o < sg.w.n_out;
   const bool any_resid = a.seg[0].epi == EPI_RESID || (a.nseg > 1 && a.seg[1].epi == EPI_RESID) ||
                          (a.nseg > 2 && a.seg[2].epi == EPI_RESID);
+  const bool has_bias = sg.bias != nullptr;
+  const float bo = (has_bias && row_ok) ? sg.bias[o] : 0.f;
+  float* const yb = sg.y + o;
+  const uint32_t ldy = sg.ldy;
+  constexpr int CH = NC < 8 ? NC : 8;
   if (epi == EPI_STORE || epi == EPI_ADD || epi == EPI_RESID) {
-    // single-row epilogues of epi_single, with the loop-invariant loads hoisted
-    const float bo = (sg.bias && row_ok) ? sg.bias[o] : 0.f;
-    float* const yb = sg.y + o;
-    const uint32_t ldy = sg.ldy;
+    // y = v, y += v, or x = y += v; xn = x * nw (qwen2.rs:536-538, 549-551)
     float* const xnb = epi == EPI_RESID ? a.xn + o : nullptr;
     const uint32_t ldxn = a.ldxn;
     const float nwo = (epi == EPI_RESID && row_ok) ? a.nw[o] : 0.f;
-    float* const parts = a.out_parts;
+    const bool reads = epi != EPI_STORE;
 #pragma unroll
-    for (int i = 0; i < NC; i++) {
-      const uint32_t col = c0 + i;
-      const bool ok = row_ok && col < batch;
-      float xv = 0.f;
-      if (ok) {
-        const float v = sg.bias ? y[i] + bo : y[i];
-        float* yy = yb + (size_t)col * ldy;
-        if (epi == EPI_STORE) {
-          *yy = v;
-        } else if (epi == EPI_ADD) {
-          *yy = *yy + v;
-        } else {  // EPI_RESID: x += v (qwen2.rs:536-538, 549-551)
-          xv = *yy + v;
-          *yy = xv;
-          xnb[(size_t)col * ldxn] = xv * nwo;
-        }
+    for (int g = 0; g < NC; g += CH) {
+      float old[CH];
+#pragma unroll
+      for (int i = 0; i < CH; i++) {
+        const uint32_t col = c0 + g + i;
+        old[i] = (reads && row_ok && col < batch) ? yb[(size_t)col * ldy] : 0.f;
       }
-      if (any_resid) {  // partial sum of x^2 over the tile's 16 rows, per column
-        float s2 = xv * xv;
-        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, 8);
-        if ((lane & 15) == 0 && valid && col < batch && epi == EPI_RESID) parts[(size_t)col * n_parts + tile] = s2;
+#pragma unroll
+      for (int i = 0; i < CH; i++) {
+        const uint32_t col = c0 + g + i;
+        const bool ok = row_ok && col < batch;
+        const float v = has_bias ? y[g + i] + bo : y[g + i];
+        float xv = 0.f;
+        if (ok) {
+          float* yy = yb + (size_t)col * ldy;
+          if (epi == EPI_STORE) {
+            *yy = v;
+          } else if (epi == EPI_ADD) {
+            *yy = old[i] + v;
+          } else {
+            xv = old[i] + v;
+            *yy = xv;
+            xnb[(size_t)col * ldxn] = xv * nwo;
+          }
+        }
+        if (any_resid) um_resid_part(a, xv, valid && col < batch && epi == EPI_RESID, col, n_parts, tile);
       }
     }
     return;
   }
+  if (epi_is_pair(epi)) {
+    // rows (o, o + 1), o even, on lanes (2j, 2j + 1): the even lane finishes the pair
+    const bool even = !(lane & 1), rope = epi != EPI_SILU;
+    uint32_t half = 0, hoff = 0, m = 0;
+    if (rope) {  // NEOX RoPE of (dim m, dim m + hd/2) of head h (qwen2.rs:708-724)
+      const uint32_t hd = a.hd, h = o / hd;
+      half = hd >> 1;
+      m = (o - h * hd) >> 1;
+      hoff = h * hd + m;
+    }
+    float* const hb = a.h + (o >> 1);
+    const uint32_t ldh = a.ldh;
+#pragma unroll
+    for (int g = 0; g < NC; g += CH) {
+      float cc[CH], ss[CH];
+#pragma unroll
+      for (int i = 0; i < CH; i++) {
+        const uint32_t col = c0 + g + i;
+        const bool ld = rope && even && row_ok && col < batch;
+        cc[i] = ld ? cols[col].cs[m] : 0.f;
+        ss[i] = ld ? cols[col].sn[m] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < CH; i++) {
+        const uint32_t col = c0 + g + i;
+        const bool ok = row_ok && col < batch;
+        const float v = has_bias ? y[g + i] + bo : y[g + i];
+        const float nv = __shfl_xor_sync(0xffffffffu, v, 1);  // row o + 1, bias included
+        if (ok && even) {
+          if (epi == EPI_SILU) {  // gate = silu(gate) * up (qwen2.rs:546-548, 743-745)
+            hb[(size_t)col * ldh] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), nv);
+          } else {
+            const float r0 = __fsub_rn(__fmul_rn(v, cc[i]), __fmul_rn(nv, ss[i]));
+            const float r1 = __fadd_rn(__fmul_rn(v, ss[i]), __fmul_rn(nv, cc[i]));
+            // EPI_ROPE_Q: q (natural order); EPI_ROPE_K: the K cache (qwen2.rs:497)
+            float* d = epi == EPI_ROPE_Q ? sg.y + (size_t)col * ldy + hoff : cols[col].kc + hoff;
+            d[0] = r0;
+            d[half] = r1;
+          }
+        }
+        if (any_resid) um_resid_part(a, 0.f, false, col, n_parts, tile);
+      }
+    }
+    return;
+  }
+  // EPI_V (the V cache row, qwen2.rs:498) and EPI_PUSH (tensor parallel: this
+  // rank's partial to every rank's receive area, tp.cu; the row's epoch read once)
+  uint32_t pe = 0;
+  if (epi == EPI_PUSH && row_ok) pe = __ldcg(a.push.epoch + (a.push.base + o) / a.push.per) + 1u;
 #pragma unroll
   for (int i = 0; i < NC; i++) {
     const uint32_t col = c0 + i;
-    const float v = y[i], nv = __shfl_xor_sync(0xffffffffu, v, 1);
     const bool ok = row_ok && col < batch;
-    float xv = 0.f;
-    if (epi_is_pair(epi)) {
-      if (ok && !(lane & 1)) epi_pair(a, sg, o, col, v, nv);
-    } else if (ok) {
-      xv = epi_single(a, sg, o, col, v);
+    const float v = has_bias ? y[i] + bo : y[i];
+    if (ok) {
+      if (epi == EPI_V) {
+        cols[col].vc[o] = v;
+      } else if (epi == EPI_PUSH) {
+        const TpPush& P = a.push;
+        const uint64_t pk = ((uint64_t)pe << 32) | __float_as_uint(v);
+        const uint64_t off = (pe & 1u) * P.parity_stride + P.rank * P.src_stride + (uint64_t)col * P.ld + o;
+        for (uint32_t k = 0; k < P.world; k++)
+          asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(P.dst[k] + off), "l"(pk) : "memory");
+      } else {
+        epi_single(a, sg, o, col, v);
+      }
     }
-    if (any_resid) {
-      float s2 = xv * xv;
-      s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
-      s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
-      s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
-      s2 += __shfl_xor_sync(0xffffffffu, s2, 8);
-      if ((lane & 15) == 0 && valid && col < batch && epi == EPI_RESID) a.out_parts[(size_t)col * n_parts + tile] = s2;
-    }
+    if (any_resid) um_resid_part(a, 0.f, false, col, n_parts, tile);
   }
 }
 
 // ------------------------------------------------------- x prep kernel ----
 // One CTA per (256-block, 8 columns): the B image of x[c, 256 b .. 256 b +
 // 255] for those padded columns (column c: lanes (c % 8) * LPC .. + LPC - 1,
-// each IPL items of 8 consecutive values). CTA (0, 0) also writes the
-// input-norm scales.
+// each IPL items of 8 consecutive values). The first CTAs of each column
+// group also write its columns' input-norm scales, one warp a column.
 constexpr uint32_t UM_XPREP_COLS = 8;
 template <int NB, int QT>
 __global__ void __launch_bounds__(UM_XPREP_THREADS) umma_xprep_kernel(const __grid_constant__ GemvArgs a, uint32_t nb) {
@@ -322,11 +429,15 @@ __global__ void __launch_bounds__(UM_XPREP_THREADS) umma_xprep_kernel(const __gr
   const uint32_t blk = blockIdx.x, xt = threadIdx.x, c = blockIdx.y * UM_XPREP_COLS + xt / LPC, u = xt % LPC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* out = a.xblob + (size_t)blk * L::BLK;
-  if (blk == 0 && blockIdx.y == 0) {
+  {  // the input-norm scales of this CTA row's columns: one warp a column
     float* s_in = reinterpret_cast<float*>(a.xblob + (size_t)nb * L::BLK);
-    for (uint32_t cc = warp; cc < a.batch; cc += UM_XPREP_THREADS / 32) {
-      const float v = input_scale(a, cc);
-      if (lane == 0) s_in[cc] = v;
+    constexpr uint32_t NW = UM_XPREP_THREADS / 32;
+    for (uint32_t cc = blk * NW + warp; cc < UM_XPREP_COLS; cc += nb * NW) {
+      const uint32_t col = blockIdx.y * UM_XPREP_COLS + cc;
+      if (col < a.batch) {
+        const float v = input_scale(a, col);
+        if (lane == 0) s_in[col] = v;
+      }
     }
   }
   float v[IPL][8];
@@ -408,6 +519,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[NA],
       bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_hdr[4], bar_fin[2];
   __shared__ uint32_t s_tmem, s_last;
+  __shared__ UmCol s_cols[UM_MAXB];
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -663,6 +775,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     const uint32_t q = warp & 3, m = 32 * q + lane, tl = m >> 4, rr = m & 15;
     const uint32_t tlane = (32u * q) << 16;
     pdl_wait();
+    if (threadIdx.x - UM_EW0 * 32 < a.batch) um_col_fill(a, threadIdx.x - UM_EW0 * 32, s_cols);
+    named_bar(1, UM_EW * 32);
     const float* s_in = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK);
     uint32_t gb = 0;
     // the accumulators of block g into y; then its D and B slot are free
@@ -708,7 +822,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       for (uint32_t i = 0; i < NB; i++) y[i] *= i < a.batch ? s_in[i] : 0.f;
       const bool valid = tile < p.tiles;
       if (p.ksplit == 1) {
-        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
+        um_epilogue<NB>(a, s_cols, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
         continue;
       }
       // K-split: publish this slice ([slice][column][row]: a warp's rows are
@@ -738,7 +852,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
 #pragma unroll
             for (uint32_t i = 0; i < NB; i++) y[i] += i < a.batch ? t[i] : 0.f;
           }
-        um_epilogue<NB>(a, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
+        um_epilogue<NB>(a, s_cols, valid ? tile : 0u, p.tiles, valid, rr, 0u, y);
       }
     }
   }

@@ -147,11 +147,11 @@ __device__ __forceinline__ float add_terms(float s, const float* v, uint32_t b, 
   for (; i + 8 <= e; i += 8) {
     float t[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) t[k] = __ldcg(v + i + k);
+    for (int k = 0; k < 8; k++) t[k] = v[i + k];
 #pragma unroll
     for (int k = 0; k < 8; k++) s = __fadd_rn(s, t[k]);
   }
-  for (; i < e; i++) s = __fadd_rn(s, __ldcg(v + i));
+  for (; i < e; i++) s = __fadd_rn(s, v[i]);
   return s;
 }
 
@@ -161,7 +161,7 @@ __device__ __forceinline__ uint32_t first_reach(float& s, const float* v, uint32
   for (uint32_t i = b; i < e; i += 8) {
     float t[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) t[k] = i + k < e ? __ldcg(v + i + k) : 0.0f;
+    for (int k = 0; k < 8; k++) t[k] = i + k < e ? v[i + k] : 0.0f;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
       if (i + k >= e) break;
@@ -174,6 +174,9 @@ __device__ __forceinline__ uint32_t first_reach(float& s, const float* v, uint32
 
 // The reference's left-to-right f32 sum of v[0..n) (non-negative terms or NaN)
 // computed by the whole CTA (SMP_THREADS threads, chunk c = [c*C, (c+1)*C)).
+// v was written by this CTA before the call; each thread walks its own chunk
+// with ordinary (L1-cached) loads, which see those writes after the CTA's
+// barrier.
 // With stop >= 0, instead returns in *cut the first index i at which the
 // running sum after v[i] is >= stop (n if none) and the sum up to it.
 // Called by all threads; the result is valid in every thread.
@@ -185,7 +188,7 @@ __device__ float exact_seq_sum(const float* v, uint32_t n, float stop, uint32_t*
   double d = 0.0;
   bool nan = false;
   for (uint32_t i = b; i < e; i++) {
-    const float t = __ldcg(v + i);
+    const float t = v[i];
     nan |= t != t;
     d += (double)t;
   }
@@ -229,7 +232,7 @@ __device__ float exact_seq_sum(const float* v, uint32_t n, float stop, uint32_t*
         for (uint32_t i = b; i < e; i++) {
           uint64_t q;
           bool up, tie;
-          grid_term(__float_as_uint(__ldcg(v + i)), E, q, up, tie);
+          grid_term(__float_as_uint(v[i]), E, q, up, tie);
           const uint64_t r0 = q + (tie ? ((par0 + (uint32_t)q) & 1u) : (uint32_t)up);
           const uint64_t r1 = q + (tie ? ((par1 + (uint32_t)q) & 1u) : (uint32_t)up);
           D0 += r0;
