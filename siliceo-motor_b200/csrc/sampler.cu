@@ -46,14 +46,9 @@ namespace sm {
 
 __constant__ double c_exp2_32[32] = SM_EXP2_32_TABLE;
 
-// glibc's expf(x) for x <= 0 (NaN passes through; x > 0 is outside the
-// sampler's domain and uses CUDA's expf).
-__device__ __forceinline__ float expf_ref(float x) {
-  if (x != x) return x;
-  if (x > 0.0f) return expf(x);
-  if (x < -104.0f) return 0.0f;
-  const ExpfEval ev = expf_eval(x, c_exp2_32);
-  if (!ev.check) return ev.f;
+// glibc's expf(x) for an input whose rounded double f may differ from it:
+// the table's value for x, else f.
+__device__ __forceinline__ float expf_lookup(float x, float f) {
   const uint32_t xb = __float_as_uint(x);
   int lo = 0, hi = SM_EXPF_EXC_N - 1;
   while (lo <= hi) {
@@ -63,12 +58,33 @@ __device__ __forceinline__ float expf_ref(float x) {
     if (v < xb) lo = mid + 1;
     else hi = mid - 1;
   }
-  return ev.f;
+  return f;
+}
+
+// glibc's expf(x) for x <= 0 (NaN passes through; x > 0 is outside the
+// sampler's domain and uses CUDA's expf). With `check`, an input that needs
+// the table is not looked up: *check is set and the rounded double returned,
+// for a later expf_lookup(x, it).
+// t32: the 2^(j/32) table (c_exp2_32, or its copy in shared memory: the
+// lanes of a warp index it with different j, which constant memory serves
+// one address at a time).
+__device__ __forceinline__ float expf_ref(float x, const double* t32, bool* check = nullptr) {
+  if (check) *check = false;
+  if (x != x) return x;
+  if (x > 0.0f) return expf(x);
+  if (x < -104.0f) return 0.0f;
+  const ExpfEval ev = expf_eval(x, t32);
+  if (!ev.check) return ev.f;
+  if (check) {
+    *check = true;
+    return ev.f;
+  }
+  return expf_lookup(x, ev.f);
 }
 
 __global__ void expf_ref_kernel(const float* x, float* y, size_t n) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    y[i] = expf_ref(x[i]);
+    y[i] = expf_ref(x[i], c_exp2_32);
 }
 
 constexpr int SMP_THREADS = 1024;
@@ -115,9 +131,12 @@ struct SumRec {
   uint32_t d[SUM_NE][2];
 };
 constexpr uint32_t SMP_SORT_COUNTS = 32 * 256, SMP_SORT_BASES = 512;
+constexpr uint32_t SMP_PATCH = 8192;  // terms whose exp is looked up after the terms pass
 constexpr size_t SMP_BIG = sizeof(SumRec) * SMP_THREADS;
 static_assert(SMP_BIG >= sizeof(unsigned long long) * SMP_KMAX, "candidates fit the shared buffer");
 static_assert(SMP_BIG >= 4 * (SMP_SORT_COUNTS + SMP_SORT_BASES), "sort counters fit the shared buffer");
+static_assert(SMP_BIG >= 4 * SMP_PATCH, "the exp patch list fits the shared buffer");
+static_assert(SMP_BIG >= 8 * SMP_KMAX + 4 * 32 * 8, "candidates and the selection counts fit the shared buffer");
 
 // The rounded increment of a non-negative finite float term (bits tb) on the
 // grid 2^(E-23): q = floor(term / u), and whether the remainder is above /
@@ -141,35 +160,61 @@ __device__ __forceinline__ void grid_term(uint32_t tb, int E, uint64_t& q, bool&
   tie = rem == half;
 }
 
-// s + the chunk's terms [b, e) of v, added one by one in f32.
-__device__ __forceinline__ float add_terms(float s, const float* v, uint32_t b, uint32_t e) {
-  uint32_t i = b;
-  for (; i + 8 <= e; i += 8) {
-    float t[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) t[k] = v[i + k];
-#pragma unroll
-    for (int k = 0; k < 8; k++) s = __fadd_rn(s, t[k]);
-  }
-  for (; i < e; i++) s = __fadd_rn(s, v[i]);
-  return s;
+// Increment from starting parity p of a run of chunks A (increment a from
+// p) followed by a run B (b0 / b1 from parity 0 / 1), or SUM_SAT when either
+// saturates or the total reaches 2^24.
+__device__ __forceinline__ uint32_t sum_cat(uint32_t a, uint32_t b0, uint32_t b1, uint32_t p) {
+  if (a == SUM_SAT) return SUM_SAT;
+  const uint32_t b = ((p + a) & 1u) ? b1 : b0;
+  if (b == SUM_SAT) return SUM_SAT;
+  const uint32_t t = a + b;
+  return t >= (1u << 24) ? SUM_SAT : t;
 }
 
-// The first i in [b, e) at which s + v[b] + ... + v[i] (added one by one in
-// f32) is >= stop, or e; s is updated to that running sum.
-__device__ __forceinline__ uint32_t first_reach(float& s, const float* v, uint32_t b, uint32_t e, float stop) {
-  for (uint32_t i = b; i < e; i += 8) {
-    float t[8];
+// v[i .. i + 8) with zeros past e: two 16-byte loads when v + i is 16-byte
+// aligned and all eight are in range, else eight 4-byte loads.
+__device__ __forceinline__ void load8(const float* v, uint32_t i, uint32_t e, float (&t)[8]) {
+  if (i + 8 <= e && (reinterpret_cast<uintptr_t>(v + i) & 15u) == 0) {
+    const float4 x = *reinterpret_cast<const float4*>(v + i), y = *reinterpret_cast<const float4*>(v + i + 4);
+    t[0] = x.x; t[1] = x.y; t[2] = x.z; t[3] = x.w;
+    t[4] = y.x; t[5] = y.y; t[6] = y.z; t[7] = y.w;
+  } else {
 #pragma unroll
-    for (int k = 0; k < 8; k++) t[k] = i + k < e ? v[i + k] : 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-      if (i + k >= e) break;
-      s = __fadd_rn(s, t[k]);
-      if (s >= stop) return i + k;
-    }
+    for (int q = 0; q < 8; q++) t[q] = i + q < e ? v[i + q] : 0.0f;
   }
-  return e;
+}
+
+// Sixteen 8-bit counters in four words (a thread counts at most 255 keys).
+__device__ __forceinline__ void pc_add(uint32_t (&pc)[4], uint32_t bin) {
+  const uint32_t inc = 1u << (8u * (bin & 3u)), w = bin >> 2;
+  pc[0] += w == 0 ? inc : 0u;
+  pc[1] += w == 1 ? inc : 0u;
+  pc[2] += w == 2 ? inc : 0u;
+  pc[3] += w == 3 ? inc : 0u;
+}
+// The CTA's sums of the sixteen counters: lane l < 16 of warp 0 gets bin l
+// (other threads get 0). wcnt: 32 x 8 words of shared memory. Called by all.
+__device__ __forceinline__ uint32_t pc_reduce(const uint32_t (&pc)[4], uint32_t* wcnt) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t u[8];  // 16-bit fields: word j holds bins 2j, 2j + 1
+#pragma unroll
+  for (int w = 0; w < 4; w++) {
+    u[2 * w] = (pc[w] & 0xFFu) | ((pc[w] & 0xFF00u) << 8);
+    u[2 * w + 1] = ((pc[w] >> 16) & 0xFFu) | ((pc[w] >> 8) & 0xFF0000u);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) u[j] += __shfl_xor_sync(0xffffffffu, u[j], o);
+  if (lane == 0)
+#pragma unroll
+    for (int j = 0; j < 8; j++) wcnt[warp * 8 + j] = u[j];
+  __syncthreads();
+  uint32_t c = 0;
+  if (warp == 0 && lane < 16)
+    for (uint32_t w = 0; w < SMP_THREADS / 32; w++) c += (wcnt[w * 8 + (lane >> 1)] >> (16 * (lane & 1))) & 0xFFFFu;
+  __syncthreads();
+  return c;
 }
 
 // The reference's left-to-right f32 sum of v[0..n) (non-negative terms or NaN)
@@ -187,10 +232,14 @@ __device__ float exact_seq_sum(const float* v, uint32_t n, float stop, uint32_t*
   // 1. approximate chunk sums (double) and their exclusive prefix
   double d = 0.0;
   bool nan = false;
-  for (uint32_t i = b; i < e; i++) {
-    const float t = v[i];
-    nan |= t != t;
-    d += (double)t;
+  for (uint32_t i = b; i < e; i += 8) {
+    float t[8];
+    load8(v, i, e, t);
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      nan |= t[q] != t[q];
+      d += (double)t[q];
+    }
   }
   double inc = d;
 #pragma unroll
@@ -229,16 +278,21 @@ __device__ float exact_seq_sum(const float* v, uint32_t n, float stop, uint32_t*
         uint64_t D0 = 0, D1 = 0;
         uint32_t par0 = 0, par1 = 1;
         const int E = lo + k;
-        for (uint32_t i = b; i < e; i++) {
-          uint64_t q;
-          bool up, tie;
-          grid_term(__float_as_uint(v[i]), E, q, up, tie);
-          const uint64_t r0 = q + (tie ? ((par0 + (uint32_t)q) & 1u) : (uint32_t)up);
-          const uint64_t r1 = q + (tie ? ((par1 + (uint32_t)q) & 1u) : (uint32_t)up);
-          D0 += r0;
-          D1 += r1;
-          par0 = (par0 + (uint32_t)r0) & 1u;
-          par1 = (par1 + (uint32_t)r1) & 1u;
+        for (uint32_t i = b; i < e; i += 8) {
+          float t[8];
+          load8(v, i, e, t);  // zeros past e add nothing
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            uint64_t q;
+            bool up, tie;
+            grid_term(__float_as_uint(t[j]), E, q, up, tie);
+            const uint64_t r0 = q + (tie ? ((par0 + (uint32_t)q) & 1u) : (uint32_t)up);
+            const uint64_t r1 = q + (tie ? ((par1 + (uint32_t)q) & 1u) : (uint32_t)up);
+            D0 += r0;
+            D1 += r1;
+            par0 = (par0 + (uint32_t)r0) & 1u;
+            par1 = (par1 + (uint32_t)r1) & 1u;
+          }
         }
         r.d[k][0] = D0 >= (1u << 24) ? SUM_SAT : (uint32_t)D0;
         r.d[k][1] = D1 >= (1u << 24) ? SUM_SAT : (uint32_t)D1;
@@ -247,42 +301,77 @@ __device__ float exact_seq_sum(const float* v, uint32_t n, float stop, uint32_t*
   }
   recs[tid] = r;
   __syncthreads();
-  // 3. one thread composes the chunks in order
-  if (tid == 0) {
+  // 3. warp 0 composes the chunks in order, 32 at a time. In the running
+  //    sum's binade, chunk summaries compose (the increment of A then B from
+  //    parity p is D_A[p] + D_B[(p + D_A[p]) & 1]), so a shuffle scan gives
+  //    the sum after each of the next 32 chunks; the first chunk that leaves
+  //    the binade, has no summary there, or reaches `stop` is added term by
+  //    term (its terms loaded by the whole warp at once, the adds done in
+  //    order by every lane alike).
+  if (warp == 0) {
+    const uint32_t nch = C ? (n + C - 1) / C : 0u;
     float s = 0.0f;
-    uint32_t where = n;
-    for (uint32_t c = 0; c < SMP_THREADS; c++) {
-      const uint32_t cb = min(n, c * C), ce = min(n, cb + C);
-      if (cb >= ce) break;
-      const SumRec rc = recs[c];
+    uint32_t where = n, c = 0;
+    while (c < nch) {
       const uint32_t sb = __float_as_uint(s), ex = sb >> 23;
-      bool done = false;
-      if ((rc.ok & 1u) && ex >= 1 && ex < 255) {
-        const int E = (int)ex - 127, k = E - rc.e_lo;
-        if (k >= 0 && k < SUM_NE) {
-          const uint32_t m = (sb & 0x7FFFFFu) | 0x800000u;
-          const uint32_t D = rc.d[k][m & 1u];
-          if (D != SUM_SAT && m + D < (1u << 24)) {
-            const float ns = __uint_as_float((ex << 23) | ((m + D) & 0x7FFFFFu));
-            if (!(stop >= 0.0f) || ns < stop) {  // a cut inside this chunk is found term by term
-              s = ns;
-              done = true;
+      const uint32_t m0 = (sb & 0x7FFFFFu) | 0x800000u;
+      const uint32_t cj = c + lane;
+      uint32_t q0 = SUM_SAT, q1 = SUM_SAT;
+      if (cj < nch && ex >= 1 && ex < 255) {
+        const SumRec& rc = recs[cj];
+        const int k = (int)ex - 127 - rc.e_lo;
+        if ((rc.ok & 1u) && k >= 0 && k < SUM_NE) {
+          q0 = rc.d[k][0];
+          q1 = rc.d[k][1];
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive scan: chunks c .. cj, per starting parity
+        const uint32_t a0 = __shfl_up_sync(0xffffffffu, q0, o), a1 = __shfl_up_sync(0xffffffffu, q1, o);
+        if (lane >= (uint32_t)o) {
+          const uint32_t n0 = sum_cat(a0, q0, q1, 0u), n1 = sum_cat(a1, q0, q1, 1u);
+          q0 = n0;
+          q1 = n1;
+        }
+      }
+      const uint32_t D = (m0 & 1u) ? q1 : q0;
+      const bool fits = D != SUM_SAT && m0 + D < (1u << 24);
+      const float sj = __uint_as_float((ex << 23) | ((m0 + D) & 0x7FFFFFu));
+      const bool okj = cj < nch && fits && !(stop >= 0.0f && sj >= stop);
+      const uint32_t bad = __ballot_sync(0xffffffffu, !okj);
+      const uint32_t f = bad ? (uint32_t)__ffs(bad) - 1u : 32u;
+      if (f > 0) s = __shfl_sync(0xffffffffu, sj, f - 1);
+      c += f;
+      if (f == 32) continue;
+      if (c >= nch) break;
+      const uint32_t cb = c * C, ce = min(n, cb + C);
+      bool hit = false;
+      for (uint32_t g0 = cb; g0 < ce && !hit; g0 += 256) {  // 256 terms' loads issued at once
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) t[q] = g0 + 32 * q + lane < ce ? v[g0 + 32 * q + lane] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          const uint32_t i0 = g0 + 32 * q;
+          if (hit || i0 >= ce) break;
+          const uint32_t cnt = min(32u, ce - i0);
+          for (uint32_t j = 0; j < cnt; j++) {
+            s = __fadd_rn(s, __shfl_sync(0xffffffffu, t[q], j));
+            if (stop >= 0.0f && s >= stop) {
+              where = i0 + j;
+              hit = true;
+              break;
             }
           }
         }
       }
-      if (!done) {
-        if (stop >= 0.0f) {
-          where = first_reach(s, v, cb, ce, stop);
-          if (where < ce) break;
-          where = n;
-        } else {
-          s = add_terms(s, v, cb, ce);
-        }
-      }
+      if (hit) break;
+      c += 1;
     }
-    scan[64] = (double)s;
-    scan[65] = (double)where;
+    if (lane == 0) {
+      scan[64] = (double)s;
+      scan[65] = (double)where;
+    }
   }
   __syncthreads();
   const float s = (float)scan[64];
@@ -376,6 +465,8 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits
   __shared__ uint32_t s_u[4];
   __shared__ uint32_t s_choice;
   __shared__ double scan[72];
+  __shared__ double s_t32[32];
+  if (tid < 32) s_t32[tid] = c_exp2_32[tid];  // read after the barriers below
   // one buffer, used in turn by: the exact sum's chunk records, the top-k
   // candidates, the radix sort's per-warp digit counts and digit bases
   __shared__ __align__(16) uint8_t big[SMP_BIG];
@@ -432,7 +523,13 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits
     uint32_t* key = reinterpret_cast<uint32_t*>(term);
     // 1. max of p = l/T (a NaN never replaces the running max)
     float m = -INFINITY;
-    for (uint32_t i = tid; i < V; i += SMP_THREADS) m = fmaxf(m, __fdiv_rn(logit(i), T));
+    for (uint32_t i0 = tid; i0 < V; i0 += 8 * SMP_THREADS) {  // eight loads in flight a thread
+      float l[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) l[q] = i0 + q * SMP_THREADS < V ? logit(i0 + q * SMP_THREADS) : -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 8; q++) m = fmaxf(m, __fdiv_rn(l[q], T));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[warp] = m;
@@ -446,89 +543,212 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits
     __syncthreads();
     m = red[0];
     // 2. terms exp(p - max) and their exact left-to-right f32 sum
-    for (uint32_t i = tid; i < V; i += SMP_THREADS) term[i] = expf_ref(__fsub_rn(__fdiv_rn(logit(i), T), m));
+    //    (inputs that need glibc's exception table are listed and looked up
+    //    after the pass by the whole CTA at once: a lookup is a chain of
+    //    dependent loads that would stall its warp inside the pass)
+    uint32_t* patch = reinterpret_cast<uint32_t*>(big);
+    if (tid == 0) s_u[3] = 0;
+    __syncthreads();
+    for (uint32_t i0 = tid; i0 < V; i0 += 4 * SMP_THREADS) {
+      float l[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) l[q] = i0 + q * SMP_THREADS < V ? logit(i0 + q * SMP_THREADS) : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint32_t i = i0 + q * SMP_THREADS;
+        if (i < V) {
+          const float x = __fsub_rn(__fdiv_rn(l[q], T), m);
+          bool chk;
+          float t = expf_ref(x, s_t32, &chk);
+          if (chk) {
+            const uint32_t slot = atomicAdd(&s_u[3], 1u);
+            if (slot < SMP_PATCH) patch[slot] = i;
+            else t = expf_lookup(x, t);  // list full: in place
+          }
+          term[i] = t;
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t npatch = min(s_u[3], SMP_PATCH);
+    for (uint32_t j = tid; j < npatch; j += SMP_THREADS) {
+      const uint32_t i = patch[j];
+      term[i] = expf_lookup(__fsub_rn(__fdiv_rn(logit(i), T), m), term[i]);
+    }
     __syncthreads();
     const float S = exact_seq_sum(term, V, -1.0f, nullptr, recs, scan);
-    // 3. probs, as order-preserving keys
-    for (uint32_t i = tid; i < V; i += SMP_THREADS) key[i] = fkey(__fdiv_rn(term[i], S));
+    // 3. probs, as order-preserving keys (in place of the terms)
+    for (uint32_t i0 = tid; i0 < V; i0 += 4 * SMP_THREADS) {
+      float t[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) t[q] = i0 + q * SMP_THREADS < V ? term[i0 + q * SMP_THREADS] : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        if (i0 + q * SMP_THREADS < V) key[i0 + q * SMP_THREADS] = fkey(__fdiv_rn(t[q], S));
+    }
     __syncthreads();
     const int64_t k64 = P.top_k < 0 ? (int64_t)V : min((int64_t)V, max((int64_t)P.top_k, (int64_t)1));
     const uint32_t k = (uint32_t)k64;
     if (k <= (uint32_t)SMP_KMAX) {
-      // 4a. the k largest keys (lowest indices among equal keys) by radix select
-      uint32_t prefix = 0, need = k;
-      for (int pass = 0; pass < 4; pass++) {
-        const int shift = 24 - 8 * pass;
-        const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (32 - 8 * pass));
-        for (uint32_t i = tid; i < 256; i += SMP_THREADS) hist[i] = 0;
-        __syncthreads();
-        // keys concentrate on a few bins: lanes with the same bin add once
-        for (uint32_t i0 = 0; i0 < V; i0 += SMP_THREADS) {
-          const uint32_t i = i0 + tid;
-          const uint32_t kk = i < V ? key[i] : 0u;
-          const bool in = i < V && (kk & hmask) == prefix;
-          const uint32_t bin = in ? (kk >> shift) & 0xFF : 256u + lane;
-          const uint32_t peers = __match_any_sync(0xffffffffu, bin);
-          if (in && __ffs(peers) - 1 == (int)lane) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
-        }
-        __syncthreads();
-        if (tid == 0) {
-          uint32_t acc = 0, bin = 0;
-          for (int bb = 255; bb >= 0; bb--) {
-            if (acc + hist[bb] >= need) { bin = (uint32_t)bb; break; }
-            acc += hist[bb];
-          }
-          s_u[0] = prefix | (bin << shift);
-          s_u[1] = need - acc;
-        }
-        __syncthreads();
-        prefix = s_u[0];
-        need = s_u[1];
-        __syncthreads();
-      }
-      // every key > prefix, and the first `need` keys == prefix in index order
-      const uint32_t per = (V + SMP_THREADS - 1) / SMP_THREADS;
-      const uint32_t i0 = min(V, tid * per), i1 = min(V, i0 + per);
-      uint32_t eq = 0;
-      for (uint32_t i = i0; i < i1; i++) eq += key[i] == prefix;
-      uint32_t incl = eq;
+      uint32_t nc = 0xFFFFFFFFu;  // candidates gathered; above SMP_KMAX: radix select
+      // 4a. a threshold with at least k and at most SMP_KMAX keys at or above
+      //     it, found without atomics: per-thread counts of the keys by their
+      //     distance below the largest key kmax = key(1 / S) (the largest term
+      //     is exp(0) = 1) in 16 bins of width 2^W (W = 23, a binade; the last
+      //     bin takes everything further), refined 16-fold inside the boundary
+      //     bin while too many keys remain. Those keys are then gathered.
+      if (m == m && fabsf(m) != INFINITY && S > 0.0f && S < INFINITY && V <= 255u * SMP_THREADS) {
+        const uint32_t kmax = fkey(__fdiv_rn(1.0f, S));
+        uint32_t* wcnt = reinterpret_cast<uint32_t*>(big + SMP_KMAX * 8);  // after the candidates
+        uint32_t hi = kmax, lo = 0, W = 23, above = 0;
+        for (;;) {
+          uint32_t pc[4] = {0u, 0u, 0u, 0u};
+          for (uint32_t i0 = tid; i0 < V; i0 += 4 * SMP_THREADS) {
+            uint32_t kk[4];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= (uint32_t)o) incl += t;
+            for (int q = 0; q < 4; q++) kk[q] = i0 + q * SMP_THREADS < V ? key[i0 + q * SMP_THREADS] : 0u;
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+              if (i0 + q * SMP_THREADS < V && kk[q] >= lo && kk[q] <= hi) pc_add(pc, min((hi - kk[q]) >> W, 15u));
+          }
+          const uint32_t cnt = pc_reduce(pc, wcnt);
+          if (warp == 0) {
+            uint32_t cum = cnt;  // inclusive scan over the bins, nearest kmax first
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t t = __shfl_up_sync(0xffffffffu, cum, o);
+              if (lane >= (uint32_t)o) cum += t;
+            }
+            const uint32_t hit = __ballot_sync(0xffffffffu, lane < 16 && above + cum >= k);
+            const uint32_t l = hit ? (uint32_t)__ffs(hit) - 1u : 16u;
+            const uint32_t cl = __shfl_sync(0xffffffffu, cum, l & 31u);
+            const uint32_t cp = __shfl_sync(0xffffffffu, cum, (l - 1u) & 31u);
+            if (lane == 0) {
+              s_u[0] = l;
+              s_u[1] = cl;
+              s_u[2] = l ? cp : 0u;
+            }
+          }
+          __syncthreads();
+          const uint32_t l = s_u[0], cl = s_u[1], cp = s_u[2];
+          __syncthreads();
+          if (l >= 16 || (W == 23 && l == 15)) break;  // no threshold this way
+          const uint32_t nhi = hi - (l << W), nlo = nhi - ((1u << W) - 1u);  // bin l: keys [nlo, nhi]
+          if (above + cl <= (uint32_t)SMP_KMAX) {
+            // 4b. gather every key >= nlo (warp-aggregated slots)
+            if (tid == 0) s_u[3] = 0;
+            __syncthreads();
+            for (uint32_t i0 = 0; i0 < V; i0 += 4 * SMP_THREADS) {
+              uint32_t kk[4];
+#pragma unroll
+              for (int q = 0; q < 4; q++) {
+                const uint32_t i = i0 + q * SMP_THREADS + tid;
+                kk[q] = i < V ? key[i] : 0u;
+              }
+#pragma unroll
+              for (int q = 0; q < 4; q++) {
+                const uint32_t i = i0 + q * SMP_THREADS + tid;
+                const bool take = i < V && kk[q] >= nlo;
+                const uint32_t bal = __ballot_sync(0xffffffffu, take);
+                if (!bal) continue;
+                const uint32_t lead = __ffs(bal) - 1;
+                uint32_t base = 0;
+                if (lane == lead) base = atomicAdd(&s_u[3], (uint32_t)__popc(bal));
+                base = __shfl_sync(0xffffffffu, base, lead);
+                if (take) cand[base + __popc(bal & ((1u << lane) - 1u))] = ((unsigned long long)kk[q] << 32) | (0xFFFFFFFFu - i);
+              }
+            }
+            __syncthreads();
+            nc = s_u[3];
+            break;
+          }
+          if (W < 4) break;  // ties beyond the candidate buffer
+          above += cp;
+          hi = nhi;
+          lo = nlo;
+          W -= 4;
+        }
       }
-      __shared__ uint32_t wsum[32];
-      if (lane == 31) wsum[warp] = incl;
-      if (tid == 0) s_u[2] = 0;
-      __syncthreads();
-      if (warp == 0) {
-        uint32_t v = wsum[lane], iv = v;
+      if (nc > (uint32_t)SMP_KMAX) {
+        // 4a'. otherwise the k largest keys (lowest indices among equal keys) by
+        //      radix select
+        uint32_t prefix = 0, need = k;
+        for (int pass = 0; pass < 4; pass++) {
+          const int shift = 24 - 8 * pass;
+          const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (32 - 8 * pass));
+          for (uint32_t i = tid; i < 256; i += SMP_THREADS) hist[i] = 0;
+          __syncthreads();
+          // keys concentrate on a few bins: lanes with the same bin add once
+          for (uint32_t i0 = 0; i0 < V; i0 += SMP_THREADS) {
+            const uint32_t i = i0 + tid;
+            const uint32_t kk = i < V ? key[i] : 0u;
+            const bool in = i < V && (kk & hmask) == prefix;
+            const uint32_t bin = in ? (kk >> shift) & 0xFF : 256u + lane;
+            const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+            if (in && __ffs(peers) - 1 == (int)lane) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+          }
+          __syncthreads();
+          if (tid == 0) {
+            uint32_t acc = 0, bin = 0;
+            for (int bb = 255; bb >= 0; bb--) {
+              if (acc + hist[bb] >= need) { bin = (uint32_t)bb; break; }
+              acc += hist[bb];
+            }
+            s_u[0] = prefix | (bin << shift);
+            s_u[1] = need - acc;
+          }
+          __syncthreads();
+          prefix = s_u[0];
+          need = s_u[1];
+          __syncthreads();
+        }
+        // every key > prefix, and the first `need` keys == prefix in index order
+        const uint32_t per = (V + SMP_THREADS - 1) / SMP_THREADS;
+        const uint32_t i0 = min(V, tid * per), i1 = min(V, i0 + per);
+        uint32_t eq = 0;
+        for (uint32_t i = i0; i < i1; i++) eq += key[i] == prefix;
+        uint32_t incl = eq;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t t = __shfl_up_sync(0xffffffffu, iv, o);
-          if (lane >= (uint32_t)o) iv += t;
+          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= (uint32_t)o) incl += t;
         }
-        wsum[lane] = iv - v;
-      }
-      __syncthreads();
-      uint32_t rank = wsum[warp] + incl - eq;
-      for (uint32_t i = i0; i < i1; i++) {
-        const uint32_t kk = key[i];
-        bool take = kk > prefix;
-        if (kk == prefix) { take = rank < need; rank++; }
-        if (take) {
-          const uint32_t slot = atomicAdd(&s_u[2], 1u);
-          if (slot < SMP_KMAX) cand[slot] = ((unsigned long long)kk << 32) | (0xFFFFFFFFu - i);
+        __shared__ uint32_t wsum[32];
+        if (lane == 31) wsum[warp] = incl;
+        if (tid == 0) s_u[2] = 0;
+        __syncthreads();
+        if (warp == 0) {
+          uint32_t v = wsum[lane], iv = v;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, iv, o);
+            if (lane >= (uint32_t)o) iv += t;
+          }
+          wsum[lane] = iv - v;
         }
+        __syncthreads();
+        uint32_t rank = wsum[warp] + incl - eq;
+        for (uint32_t i = i0; i < i1; i++) {
+          const uint32_t kk = key[i];
+          bool take = kk > prefix;
+          if (kk == prefix) { take = rank < need; rank++; }
+          if (take) {
+            const uint32_t slot = atomicAdd(&s_u[2], 1u);
+            if (slot < SMP_KMAX) cand[slot] = ((unsigned long long)kk << 32) | (0xFFFFFFFFu - i);
+          }
+        }
+        __syncthreads();
+        nc = min(s_u[2], (uint32_t)SMP_KMAX);
       }
+      // bitonic sort of the candidates (padded to a power of two), descending
+      // (key desc, index asc): the first k are the reference's sorted top-k
+      uint32_t np2 = 1;
+      while (np2 < nc) np2 <<= 1;
+      for (uint32_t i = nc + tid; i < np2; i += SMP_THREADS) cand[i] = 0ull;
       __syncthreads();
-      const uint32_t nc = min(s_u[2], (uint32_t)SMP_KMAX);
-      // bitonic sort, descending (key desc, index asc)
-      for (uint32_t i = nc + tid; i < SMP_KMAX; i += SMP_THREADS) cand[i] = 0ull;
-      __syncthreads();
-      for (uint32_t size = 2; size <= SMP_KMAX; size <<= 1)
+      for (uint32_t size = 2; size <= np2; size <<= 1)
         for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-          for (uint32_t i = tid; i < SMP_KMAX; i += SMP_THREADS) {
+          for (uint32_t i = tid; i < np2; i += SMP_THREADS) {
             const uint32_t j = i ^ stride;
             if (j > i) {
               const bool desc = (i & size) == 0;
@@ -541,7 +761,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* logits
       // 5-6. top-p, total, multinomial walk (one thread, the reference's order)
       if (tid == 0) {
         uint64_t st = rng[r];
-        uint32_t kept = nc;
+        uint32_t kept = k;
         auto prob = [&](uint32_t c) -> float { return fkey_inv((uint32_t)(cand[c] >> 32)); };
         auto index = [&](uint32_t c) -> uint32_t { return 0xFFFFFFFFu - (uint32_t)(cand[c] & 0xFFFFFFFFu); };
         if (P.top_p >= 0.0f) {
@@ -629,6 +849,8 @@ __global__ void __launch_bounds__(SMP_THREADS) softmax_kernel(const float* x, ui
   float* o = out + (size_t)r * n;
   __shared__ float red[32];
   __shared__ double scan[72];
+  __shared__ double s_t32[32];
+  if (tid < 32) s_t32[tid] = c_exp2_32[tid];  // read after the max's barriers
   __shared__ __align__(16) uint8_t big[SMP_BIG];
   SumRec* recs = reinterpret_cast<SumRec*>(big);
   float m = -INFINITY;
@@ -645,7 +867,7 @@ __global__ void __launch_bounds__(SMP_THREADS) softmax_kernel(const float* x, ui
   }
   __syncthreads();
   m = red[0];
-  for (uint32_t i = tid; i < n; i += SMP_THREADS) o[i] = expf_ref(__fsub_rn(xr[i], m));
+  for (uint32_t i = tid; i < n; i += SMP_THREADS) o[i] = expf_ref(__fsub_rn(xr[i], m), s_t32);
   __syncthreads();
   const float S = exact_seq_sum(o, n, -1.0f, nullptr, recs, scan);
   for (uint32_t i = tid; i < n; i += SMP_THREADS) o[i] = __fdiv_rn(o[i], S);
