@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
   extern __shared__ __align__(1024) uint8_t um_smem[];
   __shared__ __align__(8) uint64_t bar_wfull[WS], bar_wempty[WS], bar_bfull[BS], bar_bfree[BS], bar_afull[NA],
       bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_hdr[4], bar_fin[2];
-  __shared__ uint32_t s_tmem, s_last;
+  __shared__ uint32_t s_tmem, s_last, s_fix;
   __shared__ UmCol s_cols[UM_MAXB];
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
@@ -550,6 +550,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     mbar_init(&bar_fin[0], 1);
     mbar_init(&bar_fin[1], 1);
     *abort = 0u;
+    s_fix = 0u;
     fence_mbar_init();
   }
   if (warp == UM_MMAW) {
@@ -841,6 +842,10 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       if (threadIdx.x == UM_EW0 * 32) s_last = atomicInc(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
       named_bar(1, UM_EW * 32);
       if (s_last) {
+        if (p.units <= gridDim.x) {  // one unit per CTA: every warp joins the fixup after the CTA's last barrier
+          if (threadIdx.x == UM_EW0 * 32) s_fix = 1u;
+          continue;
+        }
         __threadfence();
 #pragma unroll
         for (uint32_t i = 0; i < NB; i++) y[i] = 0.f;
@@ -867,6 +872,41 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tb, UM_TCOLS);
+  }
+  if (s_fix) {
+    // The last CTA of a single-round K-split group: all UM_THREADS threads sum
+    // the slices (in slice order, as the epilogue warps would) and run the
+    // epilogue, as 128 rows x 4 groups of NB / 4 columns. A thread's loads and
+    // stores are a quarter of one epilogue thread's.
+    constexpr uint32_t CPG = NB / 4;
+    static_assert(UM_THREADS == 4 * 128, "four column groups");
+    const uint32_t m = threadIdx.x & 127u, g = threadIdx.x >> 7;
+    const uint32_t tile = (blockIdx.x / p.ksplit) * UM_TILES + (m >> 4), rr = m & 15u;
+    const bool valid = tile < p.tiles;
+    const uint32_t R = p.tiles * 16u;
+    const size_t stride = (size_t)R * a.batch;
+    const float* mine = a.ks_part + (size_t)tile * 16u + rr;
+    float y[CPG];
+#pragma unroll
+    for (uint32_t i = 0; i < CPG; i++) y[i] = 0.f;
+    __threadfence();  // the other slices' stores, published before the counter reached this CTA
+    if (valid)
+      for (uint32_t k0 = 0; k0 < p.ksplit; k0 += 4) {  // four slices' loads in flight, added in slice order
+        float t[4][CPG];
+#pragma unroll
+        for (uint32_t kk = 0; kk < 4; kk++)
+#pragma unroll
+          for (uint32_t i = 0; i < CPG; i++) {
+            const uint32_t col = g * CPG + i;
+            t[kk][i] = (k0 + kk < p.ksplit && col < a.batch) ? __ldcg(mine + (k0 + kk) * stride + (size_t)col * R) : 0.f;
+          }
+#pragma unroll
+        for (uint32_t kk = 0; kk < 4; kk++)
+#pragma unroll
+          for (uint32_t i = 0; i < CPG; i++)
+            if (k0 + kk < p.ksplit) y[i] += t[kk][i];
+      }
+    um_epilogue<CPG>(a, s_cols, valid ? tile : 0u, p.tiles, valid, rr, g * CPG, y);
   }
 }
 
