@@ -110,11 +110,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
-// Bounded wait that also gives up at once when the CTA has aborted.
+// Bounded wait that also gives up soon after the CTA has aborted (the flag is
+// read every 32nd try: read on every try, it costs the waiting warps a
+// shared-memory load per try, ~18% of a long launch).
 __device__ __forceinline__ bool um_wait(uint64_t* b, uint32_t parity, uint32_t* err, volatile uint32_t* abort) {
   for (uint32_t n = 0; n < TC_SPIN_MAX; n++) {
     if (mbar_try(b, parity)) return true;
-    if (*abort) return false;
+    if ((n & 31u) == 31u && *abort) return false;
   }
   *abort = 1u;
   if (err) atomicOr(err, 1u);
@@ -797,7 +799,13 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
         tmem_ld<2 * CH>(tb + tlane + UM_TD2 + 64u * (g & 1) + 2 * c0, d2r);
         float us[CH];
 #pragma unroll
-        for (uint32_t i = 0; i < CH; i++) us[i] = uu[c0 + i];
+        for (uint32_t i = 0; i < CH; i += 4) {  // 16-byte aligned (OFF_U and BLK are multiples of 16)
+          const float4 u4 = *reinterpret_cast<const float4*>(uu + c0 + i);
+          us[i] = u4.x;
+          if (i + 1 < CH) us[i + 1] = u4.y;
+          if (i + 2 < CH) us[i + 2] = u4.z;
+          if (i + 3 < CH) us[i + 3] = u4.w;
+        }
         tmem_wait_ld();
 #pragma unroll
         for (uint32_t i = 0; i < CH; i++) {
