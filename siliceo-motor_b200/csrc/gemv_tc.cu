@@ -370,58 +370,104 @@ __device__ __forceinline__ bool tc_tile_at(const GemvArgs& a, uint32_t tile, uin
   return tile - a.seg[si].cta_begin < (a.seg[si].w.n_out + 15) / 16;
 }
 
-// Epilogue of one tile: vg / vh are the full dot products of rows g, g + 8
-// (in every lane of the group).
-__device__ __forceinline__ void tc_epilogue(const GemvArgs& a, uint32_t tile, float vg, float vh) {
+// Operands of a tile's fused epilogue that do not depend on the dot
+// products, for the calling lane's row o (lanes t < 2; for pairs the even
+// rows): read at the start of the unit so that the loads overlap the weight
+// stream. Read after the dot products they would be chains of dependent
+// loads (row -> sequence -> page) on the launch's critical path.
+struct TcEpiIn {
+  float bias;    // bias[o] (0 without a bias)
+  float res, nw;  // EPI_RESID: the residual x[o] and the next norm's weight
+  float c, s;    // pair RoPE: cos / sin at the row's position (qwen2.rs:708-724)
+  float* dst;    // pair RoPE: q or the K cache at (head, m); EPI_V: the V cache at o
+};
+
+__device__ __forceinline__ TcEpiIn tc_epi_in(const GemvArgs& a, uint32_t tile) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  TcEpiIn e{0.f, 0.f, 0.f, 0.f, 0.f, nullptr};
+  const GemvSeg& sg = a.seg[tc_seg(a, tile)];
+  const uint32_t o = (tile - sg.cta_begin) * 16u + (uint32_t)g + 8u * (uint32_t)t, epi = sg.epi;
+  if (t >= 2 || o >= sg.w.n_out) return e;
+  if (sg.bias) e.bias = sg.bias[o];
+  if (epi == EPI_RESID) {
+    e.res = sg.y[o];
+    e.nw = a.nw[o];
+  } else if ((epi == EPI_ROPE_Q || epi == EPI_ROPE_K) && !(g & 1)) {
+    const RowDesc rd = a.rows[0];
+    const uint32_t half = a.hd >> 1, h = o / a.hd, m = (o - h * a.hd) >> 1;
+    e.c = a.cos_t[(size_t)rd.pos * half + m];
+    e.s = a.sin_t[(size_t)rd.pos * half + m];
+    if (epi == EPI_ROPE_Q) {
+      e.dst = sg.y + h * a.hd + m;
+    } else {
+      const SeqDesc sd = a.seqs[rd.seq];
+      e.dst = sd.pages[rd.pos / KV_PAGE] + kv_page_off(a.layer, rd.pos, a.kvd) + h * a.hd + m;
+    }
+  } else if (epi == EPI_V) {
+    const RowDesc rd = a.rows[0];
+    const SeqDesc sd = a.seqs[rd.seq];
+    e.dst = sd.pages[rd.pos / KV_PAGE] + sd.voff + kv_page_off(a.layer, rd.pos, a.kvd) + o;
+  }
+  return e;
+}
+
+// Epilogue of one tile (column 0): vg / vh are the full dot products of rows
+// g, g + 8 (in every lane of the group); `in` holds the lane's operands read
+// ahead (tc_epi_in). The arithmetic of epi_single / epi_pair (gemv_common.cuh).
+__device__ __forceinline__ void tc_epilogue(const GemvArgs& a, uint32_t tile, float vg, float vh, const TcEpiIn& in) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   uint32_t si = 0;
   if (a.nseg > 1 && tile >= a.seg[1].cta_begin) si = 1;
   if (a.nseg > 2 && tile >= a.seg[2].cta_begin) si = 2;
-  // the segment by value, and the residual epilogue's pointers read before any
-  // store: read through the parameter reference after a store they are
-  // fetched again
+  // the segment by value: read through the parameter reference after a store
+  // its fields are fetched again
   const GemvSeg sg = a.seg[si];
   const uint32_t row0 = (tile - sg.cta_begin) * 16u, epi = sg.epi;
+  const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
+  const bool mine = t < 2 && o < sg.w.n_out, has_bias = sg.bias != nullptr;
+  const float raw = t ? vh : vg;              // this lane's row o
+  const float v = has_bias ? raw + in.bias : raw;  // with its bias
   if (epi_is_pair(epi)) {
-    const float ng = __shfl_down_sync(0xffffffffu, vg, 4), nh = __shfl_down_sync(0xffffffffu, vh, 4);
-    if (!(g & 1) && t < 2) {
-      const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
-      if (o < sg.w.n_out) epi_pair(a, sg, o, 0, t ? vh : vg, t ? nh : ng);
-    }
-  } else {
-    float* const parts = a.out_parts;
-    float* const xnp = a.xn;
-    float xn = 0.f;
-    if (t < 2) {
-      const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
-      if (o < sg.w.n_out) {
-        if (epi == EPI_RESID) {  // x += v, then the next RMSNorm's x * w (epi_single, column 0)
-          const float nwo = a.nw[o];
-          float v = t ? vh : vg;
-          if (sg.bias) v = v + sg.bias[o];
-          xn = sg.y[o] + v;
-          sg.y[o] = xn;
-          xnp[o] = xn * nwo;
-        } else {
-          xn = epi_single(a, sg, o, 0, t ? vh : vg);
-        }
+    const float nv = __shfl_down_sync(0xffffffffu, v, 4);  // row o + 1, bias included
+    if (!(g & 1) && mine) {
+      if (epi == EPI_SILU) {  // gate = silu(gate) * up (qwen2.rs:546-548, 743-745)
+        a.h[o >> 1] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), nv);
+      } else {  // NEOX RoPE of the pair into q (natural order) or the K cache (qwen2.rs:497, 708-724)
+        const uint32_t half = a.hd >> 1;
+        in.dst[0] = __fsub_rn(__fmul_rn(v, in.c), __fmul_rn(nv, in.s));
+        in.dst[half] = __fadd_rn(__fmul_rn(v, in.s), __fmul_rn(nv, in.c));
       }
     }
-    if (epi == EPI_RESID) {  // partial sum of x^2 over the tile's rows
-      const float s2 = warp_sum(xn * xn);
-      if (lane == 0) parts[tile] = s2;
+    return;
+  }
+  float xn = 0.f, stored = 0.f;
+  if (mine) {
+    if (epi == EPI_RESID) {  // x += v, then the next RMSNorm's x * w (qwen2.rs:536-538, 549-551)
+      xn = in.res + v;
+      sg.y[o] = xn;
+      a.xn[o] = xn * in.nw;
+    } else if (epi == EPI_STORE) {
+      sg.y[o] = v;
+      stored = v;
+    } else if (epi == EPI_V) {  // the V cache row (qwen2.rs:498)
+      in.dst[0] = v;
+    } else {
+      xn = epi_single(a, sg, o, 0, raw);
     }
-    if (a.amax) {  // the tile's greedy candidate (the stored values, bias included)
-      const uint32_t o = row0 + (uint32_t)g + 8u * (uint32_t)t;
-      uint64_t key = 0;
-      if (t < 2 && o < sg.w.n_out) key = argmax_key(sg.y[o], o);
+  }
+  if (epi == EPI_RESID) {  // partial sum of x^2 over the tile's rows
+    const float s2 = warp_sum(xn * xn);
+    if (lane == 0) a.out_parts[tile] = s2;
+  }
+  if (a.amax) {  // the tile's greedy candidate (the stored values, bias included)
+    uint64_t key = 0;
+    if (mine) key = argmax_key(epi == EPI_STORE ? stored : sg.y[o], o);
 #pragma unroll
-      for (int of = 16; of > 0; of >>= 1) {
-        const uint64_t k2 = __shfl_xor_sync(0xffffffffu, key, of);
-        key = k2 > key ? k2 : key;
-      }
-      if (lane == 0) a.amax[tile] = key;
+    for (int of = 16; of > 0; of >>= 1) {
+      const uint64_t k2 = __shfl_xor_sync(0xffffffffu, key, of);
+      key = k2 > key ? k2 : key;
     }
+    if (lane == 0) a.amax[tile] = key;
   }
 }
 
@@ -485,6 +531,9 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     float vg = 0.f, vh = 0.f;
     uint32_t si = 0;
     const bool valid = tc_tile_at(a, tile, p.tiles, si);
+    // the epilogue's operands, read while the weights stream (only the
+    // group's last CTA uses them when K is split)
+    const TcEpiIn ein = valid ? tc_epi_in(a, tile) : TcEpiIn{0.f, 0.f, 0.f, 0.f, 0.f, nullptr};
     if (valid) {
       const DWDesc& w = a.seg[si].w;
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
@@ -507,7 +556,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     vg += __shfl_xor_sync(0xffffffffu, vg, 2);
     vh += __shfl_xor_sync(0xffffffffu, vh, 2);
     if (p.ksplit == 1) {
-      if (valid) tc_epilogue(a, tile, vg * s_in, vh * s_in);
+      if (valid) tc_epilogue(a, tile, vg * s_in, vh * s_in, ein);
       continue;
     }
     // K-split: publish this slice, the last CTA of the group sums the slices in order.
@@ -524,11 +573,22 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
       __threadfence();
       if (valid) {
         float sg = 0.f, sh = 0.f;
-        for (uint32_t k = 0; k < p.ksplit; k++) {
-          sg += __ldcg(a.ks_part + k * stride + tile * 16u + g);
-          sh += __ldcg(a.ks_part + k * stride + tile * 16u + g + 8u);
+        for (uint32_t k0 = 0; k0 < p.ksplit; k0 += 8) {  // eight slices' loads in flight, added in order
+          float lg[8], lh[8];
+#pragma unroll
+          for (uint32_t k = 0; k < 8; k++) {
+            const bool in = k0 + k < p.ksplit;
+            lg[k] = in ? __ldcg(a.ks_part + (k0 + k) * stride + tile * 16u + g) : 0.f;
+            lh[k] = in ? __ldcg(a.ks_part + (k0 + k) * stride + tile * 16u + g + 8u) : 0.f;
+          }
+#pragma unroll
+          for (uint32_t k = 0; k < 8; k++)
+            if (k0 + k < p.ksplit) {
+              sg += lg[k];
+              sh += lh[k];
+            }
         }
-        tc_epilogue(a, tile, sg * s_in, sh * s_in);
+        tc_epilogue(a, tile, sg * s_in, sh * s_in, ein);
       }
     }
   }
