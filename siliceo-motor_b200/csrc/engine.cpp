@@ -711,6 +711,12 @@ void destroy_model(sm_model* m) {
 // to every rank (EPI_PUSH) and tp_reduce_resid_kernel adds the sum over ranks
 // to the residual (and prepares the next norm's input); the output head
 // pushes this rank's vocab slice and tp_gather_kernel assembles the logits.
+// The batch-1 output head's per-tile argmax keys (the greedy sampler's fast
+// path), or null. Not with tensor parallelism: there the head's epilogue
+// sends each rank's vocab slice to the other ranks (it stores no logits to
+// read a key from), and a rank's keys would cover its slice only.
+static uint64_t* head_amax(const sm_model* m, uint32_t rows) { return rows == 1 && !m->tp ? m->amax : nullptr; }
+
 cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st) {
   const sm_config& c = m->c;
   const uint32_t H = (uint32_t)c.n_embd, F = m->fl, kvd = m->kvd, hd = (uint32_t)c.head_dim, qd = m->qd;
@@ -833,7 +839,7 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     } else {  // a selection (prefill): normalize the selected rows here (qwen2.rs:555-560)
       RK(launch_rmsnorm(m->x, H, m->din.sel, m->output_norm, m->xn, H, nsel, H, c.rms_eps, st));
     }
-    if (nsel == 1 && m->amax) hd_.amax = m->amax;  // greedy candidates per tile (the sampler's fast path)
+    hd_.amax = head_amax(m, nsel);  // greedy candidates per tile (the sampler's fast path)
     RK(launch_gemv(hd_, st));
     if (tp) {  // the full logits on every rank
       if (gx.send) RK(tp_gather_issue(tp, nsel, st));
@@ -1007,7 +1013,7 @@ int sample_rows(sm_model* m, uint32_t rows, const uint8_t* mask_host, bool advan
   }
   CK(launch_sample(m->logits, (uint32_t)m->c.vocab_size, rows, mask, m->din.sp, m->din.rng, m->dout.tok,
                    advance ? m->din.tok : nullptr, advance ? m->din.rows : nullptr, m->smp_scratch, st, ~0ull,
-                   rows == 1 ? m->amax : nullptr, m->amax_n));
+                   head_amax(m, rows), m->amax_n));
   CK(cudaMemcpyAsync(m->dout.rng, m->din.rng, rows * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
   CK(cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st));
   return SM_OK;
@@ -1025,7 +1031,7 @@ int decode_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
   if (e == cudaSuccess) e = run_rows(m, B, B, st);
   if (e == cudaSuccess)
     e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
-                      m->din.rows, m->smp_scratch, st, ~0ull, B == 1 ? m->amax : nullptr, m->amax_n);
+                      m->din.rows, m->smp_scratch, st, ~0ull, head_amax(m, B), m->amax_n);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->dout.rng, m->din.rng, B * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->out_host, m->out_dev, m->out_bytes, cudaMemcpyDeviceToHost, st);
   cudaError_t e2 = cudaStreamEndCapture(st, &g);
@@ -1058,7 +1064,7 @@ int run_graph(sm_model* m, uint32_t B, cudaGraphExec_t* out) {
   cudaError_t e = run_rows(m, B, B, st);
   if (e == cudaSuccess)
     e = launch_sample(m->logits, (uint32_t)m->c.vocab_size, B, nullptr, m->din.sp, m->din.rng, m->dout.tok, m->din.tok,
-                      m->din.rows, m->smp_scratch, st, ~0ull, B == 1 ? m->amax : nullptr, m->amax_n);
+                      m->din.rows, m->smp_scratch, st, ~0ull, head_amax(m, B), m->amax_n);
   if (e == cudaSuccess) e = launch_record_tokens(m->dout.tok, B, m->hist, m->hist_ctr, HIST_TOKENS / B, st);
   cudaError_t e2 = cudaStreamEndCapture(st, &g);
   if (e != cudaSuccess || e2 != cudaSuccess) {
