@@ -375,6 +375,11 @@ def tensor_parallel_leg(args, rank, world, local_rank, barrier, allmax):
     samplers, states = [smotor.Sampler()], [0]
     ext = torch.cuda.ExternalStream(model.stream())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # recorded once through torch, which otherwise refuses elapsed_time on
+    # events that only the engine records
+    ev0.record(ext)
+    ev1.record(ext)
+    torch.cuda.synchronize()
     out, states = model.decode_run(caches, toks, samplers, states, max(args.warmup, 1))
     toks = out[-1].tolist()
     pos0 = len(caches[0])
