@@ -180,6 +180,9 @@ struct GemvArgs {
   // the shared-memory image of its B operand (may be null: another kernel runs).
   uint8_t* xblob;
   uint64_t xblob_cap;  // bytes
+  // Host planning only: a tcgen05 batched launch uses at most this many CTAs
+  // (0: up to one per SM), so that a launch on another stream can run beside it.
+  uint32_t grid_cap;
   // Set non-zero by a kernel whose bounded wait gave up (the launch's results
   // are then not valid); may be null.
   uint32_t* err;

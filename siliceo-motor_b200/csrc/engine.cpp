@@ -255,6 +255,17 @@ struct sm_model {
   // x images of the tcgen05 batched GEMV (one launch at a time, stream order)
   uint8_t* xblob = nullptr;
   uint64_t xblob_cap = 0;
+  // Batched steps whose V weight has another type than Q and K run the V
+  // GEMV on the side stream beside the Q+K one (each launch's time is mostly
+  // its fixed latency): its own scratch, and how many CTAs each may use.
+  bool qkv_side = false;
+  uint32_t qk_cap = 0, v_cap = 0;
+  float* ks_part2 = nullptr;
+  uint32_t* ks_cnt2 = nullptr;
+  uint32_t ks_part2_cap = 0, ks_cnt2_cap = 0;
+  uint8_t* xblob2 = nullptr;
+  uint64_t xblob2_cap = 0;
+  cudaEvent_t qkv_join = nullptr;
   // partial sums of x^2 written by residual GEMVs, read by the next GEMV
   float *parts_a = nullptr, *parts_b = nullptr;
   uint32_t parts_cap = 0;
@@ -633,6 +644,45 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
       need({&L.wdown});
     }
     need({&m->output});
+    // Q+K and V side by side (see qkv_side): the SMs split by their rows
+    const Layer& L0 = m->layers[0];
+    const auto mixed = [](const Layer& L) {
+      return tiled_type(L.wq.d.type) && L.wk.d.type == L.wq.d.type && tiled_type(L.wv.d.type) &&
+             L.wv.d.type != L.wq.d.type;
+    };
+    bool any_mixed = false;
+    for (const Layer& L : m->layers) any_mixed |= mixed(L);
+    uint64_t need_part2 = 0;
+    uint32_t need_cnt2 = 0;
+    if (R >= 2 && any_mixed) {
+      const uint64_t qk_rows = (uint64_t)L0.wq.d.n_out + L0.wk.d.n_out, v_rows = L0.wv.d.n_out;
+      m->v_cap = (uint32_t)std::max<uint64_t>(8, ((uint64_t)sms * v_rows + qk_rows + v_rows - 1) / (qk_rows + v_rows));
+      m->qk_cap = (uint32_t)sms > m->v_cap + 8 ? (uint32_t)sms - m->v_cap : 0u;
+      m->qkv_side = m->qk_cap != 0;
+    }
+    if (m->qkv_side)
+      for (const Layer& L : m->layers) {
+        if (!mixed(L)) continue;
+        GemvArgs b{};
+        b.seg[b.nseg++] = seg(L.wq, nullptr, 0, nullptr, EPI_STORE);
+        b.seg[b.nseg++] = seg(L.wk, nullptr, 0, nullptr, EPI_STORE);
+        b.batch = R;
+        b.ldx = b.seg[0].w.n_in;
+        b.grid_cap = m->qk_cap;
+        uint64_t pp = 0;
+        uint32_t pc = 0;
+        gemv_umma_scratch_need(b, (uint32_t)sms, &pp, &pc);
+        need_part = std::max(need_part, pp);
+        need_cnt = std::max(need_cnt, pc);
+        GemvArgs v{};
+        v.seg[v.nseg++] = seg(L.wv, nullptr, 0, nullptr, EPI_STORE);
+        v.batch = R;
+        v.ldx = v.seg[0].w.n_in;
+        v.grid_cap = m->v_cap;
+        gemv_umma_scratch_need(v, (uint32_t)sms, &pp, &pc);
+        need_part2 = std::max(need_part2, pp);
+        need_cnt2 = std::max(need_cnt2, pc);
+      }
     m->ks_part_cap = (uint32_t)std::max<uint64_t>(need_part, 16);
     m->ks_cnt_cap = std::max<uint32_t>(need_cnt, 16);
     if ((rc = dev_alloc(m, (void**)&m->ks_part, (size_t)m->ks_part_cap * 4)) ||
@@ -642,6 +692,16 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
     for (uint32_t n_in : {(uint32_t)H, m->qd, m->fl})
       m->xblob_cap = std::max(m->xblob_cap, gemv_umma_blob_bytes(n_in, R));
     if ((rc = dev_alloc(m, (void**)&m->xblob, (size_t)m->xblob_cap))) return rc;
+    if (m->qkv_side) {
+      m->ks_part2_cap = (uint32_t)std::max<uint64_t>(need_part2, 16);
+      m->ks_cnt2_cap = std::max<uint32_t>(need_cnt2, 16);
+      m->xblob2_cap = gemv_umma_blob_bytes((uint32_t)H, R);
+      if ((rc = dev_alloc(m, (void**)&m->ks_part2, (size_t)m->ks_part2_cap * 4)) ||
+          (rc = dev_alloc(m, (void**)&m->ks_cnt2, (size_t)m->ks_cnt2_cap * 4)) ||
+          (rc = dev_alloc(m, (void**)&m->xblob2, (size_t)m->xblob2_cap)))
+        return rc;
+      CK(cudaMemset(m->ks_cnt2, 0, (size_t)m->ks_cnt2_cap * 4));
+    }
     m->parts_cap = (uint32_t)(H / 4 + 64);
     if ((rc = dev_alloc(m, (void**)&m->parts_a, (size_t)R * m->parts_cap * 4)) ||
         (rc = dev_alloc(m, (void**)&m->parts_b, (size_t)R * m->parts_cap * 4)))
@@ -694,6 +754,7 @@ void destroy_model(sm_model* m) {
   if (m->side.st) cudaStreamDestroy(m->side.st);
   if (m->side.fork) cudaEventDestroy(m->side.fork);
   if (m->side.join) cudaEventDestroy(m->side.join);
+  if (m->qkv_join) cudaEventDestroy(m->qkv_join);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -771,7 +832,31 @@ cudaError_t run_rows(sm_model* m, uint32_t nrows, uint32_t nsel, cudaStream_t st
     a.seg[0] = seg(L.wq, m->q, qd, L.bq, EPI_ROPE_Q);
     a.seg[1] = seg(L.wk, nullptr, 0, L.bk, EPI_ROPE_K);
     a.seg[2] = seg(L.wv, nullptr, 0, L.bv, EPI_V);
-    RK(launch_gemv(a, st));
+    if (nrows > 1 && m->qkv_side && tiled_type(L.wq.d.type) && L.wk.d.type == L.wq.d.type &&
+        tiled_type(L.wv.d.type) && L.wv.d.type != L.wq.d.type) {
+      // V on the side stream (own scratch, v_cap CTAs) beside Q+K (qk_cap CTAs);
+      // attention waits for both
+      GemvArgs v = a;
+      v.nseg = 1;
+      v.seg[0] = a.seg[2];
+      v.grid_cap = m->v_cap;
+      v.ks_part = m->ks_part2;
+      v.ks_cnt = m->ks_cnt2;
+      v.ks_part_cap = m->ks_part2_cap;
+      v.ks_cnt_cap = m->ks_cnt2_cap;
+      v.xblob = m->xblob2;
+      v.xblob_cap = m->xblob2_cap;
+      a.nseg = 2;
+      a.grid_cap = m->qk_cap;
+      RK(cudaEventRecord(m->side.fork, st));
+      RK(cudaStreamWaitEvent(m->side.st, m->side.fork, 0));
+      RK(launch_gemv(v, m->side.st));
+      RK(cudaEventRecord(m->qkv_join, m->side.st));
+      RK(launch_gemv(a, st));
+      RK(cudaStreamWaitEvent(st, m->qkv_join, 0));
+    } else {
+      RK(launch_gemv(a, st));
+    }
     // one row whose O projection runs on gemv_tc: the O GEMV merges the attention partials itself
     const bool merge = nrows == 1 && tiled_type(L.wo.d.type);
     RK(launch_attention(m->q, qd, m->din.rows, m->din.seqs, nrows, li, Hq, Hkv, hd, m->part_o, m->part_ml,
@@ -1184,6 +1269,7 @@ static int model_from_reader(std::unique_ptr<GgufReader> r, const sm_load_opts* 
       cudaStreamCreateWithFlags(&m->side.st, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&m->side.fork, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&m->side.join, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->qkv_join, cudaEventDisableTiming) != cudaSuccess ||
       gemv_tc_prepare() != cudaSuccess || gemv_tcb_prepare() != cudaSuccess ||
       gemv_umma_prepare() != cudaSuccess || attention_prepare() != cudaSuccess) {
     cudaGetLastError();

@@ -1057,6 +1057,7 @@ cudaError_t launch_gemv_umma(GemvArgs a, cudaStream_t st, uint32_t* n_parts) {
   uint32_t sms = 0;
   cudaError_t e = um_setup(&sms);
   if (e != cudaSuccess) return e;
+  if (a.grid_cap) sms = std::min(sms, a.grid_cap);
   UmPlan p;
   if (!um_plan(a, sms, &p)) return cudaErrorNotSupported;
   if (n_parts) *n_parts = p.tiles;
@@ -1073,6 +1074,7 @@ void gemv_umma_scratch_need(GemvArgs a, uint32_t sms, uint64_t* part, uint32_t* 
   a.ks_cnt_cap = 0xFFFFFFFFu;
   *part = 0;
   *cnt = 0;
+  if (a.grid_cap) sms = std::min(sms, a.grid_cap);
   UmPlan p;
   if (!tiled_type(a.seg[0].w.type) || !um_plan(a, sms, &p) || p.ksplit == 1) return;
   *part = (uint64_t)p.ksplit * p.tiles * 16u * a.batch;
