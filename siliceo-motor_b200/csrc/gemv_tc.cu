@@ -509,10 +509,6 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     }
   }
   pdl_wait();
-  if (warp == 0) {
-    const float v = input_scale(a, 0);
-    if (lane == 0) s_in = v;
-  }
   for (uint32_t unit = blockIdx.x; unit < p.units; unit += gridDim.x) {
     const uint32_t rg = unit / p.ksplit, ks = unit - rg * p.ksplit;
     const uint32_t b0 = ks * p.slice, nblk = min(p.slice, nb - b0);
@@ -523,6 +519,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
       const bool q4 = a.seg[tc_seg(a, rg * TC_WARPS)].w.type == 12;
       b4 = q4;
       b6 = !q4;
+    }
+    if (unit == blockIdx.x && warp == TC_WARPS - 1) {  // the input-norm scale, beside the other warps' x
+      const float v = input_scale(a, 0);
+      if (lane == 0) s_in = v;
     }
     for (uint32_t i = warp; i < nblk; i += TC_WARPS)
       tc_build_x(a, b0 + i, f4 + i * (TC_FRAG / 16), f6 + i * (TC_FRAG / 16), xs + 32 * i, b4, b6);

@@ -431,17 +431,6 @@ __global__ void __launch_bounds__(UM_XPREP_THREADS) umma_xprep_kernel(const __gr
   const uint32_t blk = blockIdx.x, xt = threadIdx.x, c = blockIdx.y * UM_XPREP_COLS + xt / LPC, u = xt % LPC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* out = a.xblob + (size_t)blk * L::BLK;
-  {  // the input-norm scales of this CTA row's columns: one warp a column
-    float* s_in = reinterpret_cast<float*>(a.xblob + (size_t)nb * L::BLK);
-    constexpr uint32_t NW = UM_XPREP_THREADS / 32;
-    for (uint32_t cc = blk * NW + warp; cc < UM_XPREP_COLS; cc += nb * NW) {
-      const uint32_t col = blockIdx.y * UM_XPREP_COLS + cc;
-      if (col < a.batch) {
-        const float v = input_scale(a, col);
-        if (lane == 0) s_in[col] = v;
-      }
-    }
-  }
   float v[IPL][8];
   const bool live = c < a.batch;
   const float* xp = a.x + (size_t)c * a.ldx + (size_t)blk * 256 + 8 * IPL * u;
@@ -455,9 +444,23 @@ __global__ void __launch_bounds__(UM_XPREP_THREADS) umma_xprep_kernel(const __gr
     }
     v[j][0] = lo.x; v[j][1] = lo.y; v[j][2] = lo.z; v[j][3] = lo.w;
     v[j][4] = hi.x; v[j][5] = hi.y; v[j][6] = hi.z; v[j][7] = hi.w;
+  }
+  {  // the input-norm scales of this CTA row's columns, one warp a column (after
+     // the x loads are issued: both sets of loads are then in flight together)
+    float* s_in = reinterpret_cast<float*>(a.xblob + (size_t)nb * L::BLK);
+    constexpr uint32_t NW = UM_XPREP_THREADS / 32;
+    for (uint32_t cc = blk * NW + warp; cc < UM_XPREP_COLS; cc += nb * NW) {
+      const uint32_t col = blockIdx.y * UM_XPREP_COLS + cc;
+      if (col < a.batch) {
+        const float sc = input_scale(a, col);
+        if (lane == 0) s_in[col] = sc;
+      }
+    }
+  }
+#pragma unroll
+  for (uint32_t j = 0; j < IPL; j++)
 #pragma unroll
     for (int k = 0; k < 8; k++) mx = fmaxf(mx, fabsf(v[j][k]));
-  }
 #pragma unroll
   for (uint32_t o = 1; o < LPC; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   // the power of two that puts max|x| in [2^14, 2^15)
@@ -522,6 +525,7 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
       bar_afree[NA], bar_dfull[2], bar_dfree[2], bar_hdr[4], bar_fin[2];
   __shared__ uint32_t s_tmem, s_last, s_fix;
   __shared__ UmCol s_cols[UM_MAXB];
+  __shared__ float s_scale[UM_MAXB];
   __shared__ uint32_t s_abort_word;
   volatile uint32_t* abort = &s_abort_word;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -778,9 +782,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     const uint32_t q = warp & 3, m = 32 * q + lane, tl = m >> 4, rr = m & 15;
     const uint32_t tlane = (32u * q) << 16;
     pdl_wait();
-    if (threadIdx.x - UM_EW0 * 32 < a.batch) um_col_fill(a, threadIdx.x - UM_EW0 * 32, s_cols);
+    if (threadIdx.x - UM_EW0 * 32 < a.batch) {
+      // the column's table entry and input-norm scale, read while the blocks stream
+      const uint32_t t = threadIdx.x - UM_EW0 * 32;
+      um_col_fill(a, t, s_cols);
+      s_scale[t] = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK)[t];
+    }
     named_bar(1, UM_EW * 32);
-    const float* s_in = reinterpret_cast<const float*>(a.xblob + (size_t)nb * XB::BLK);
+    const float* s_in = s_scale;
     uint32_t gb = 0;
     // the accumulators of block g into y; then its D and B slot are free
     auto drain = [&](uint32_t g, float (&y)[NB]) {
