@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(ASH_THREADS) attn_shared_kernel(const float* q
 // shared memory by one parallel load; the partial outputs are read eight
 // splits at a time.
 __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, const RowDesc* rows, uint32_t Hq,
-                                    uint32_t hd, uint32_t max_splits, float* out, uint32_t ldo,
+                                    uint32_t hd, uint32_t max_splits, uint32_t np, float* out, uint32_t ldo,
                                     const uint32_t* shared_tiles) {
   __shared__ float sm_m[64], sm_e[64];
   pdl_trigger();
@@ -377,8 +377,7 @@ __global__ void attn_combine_kernel(const float* part_o, const float* part_ml, c
   // splits with work: shared ones (slots 0..) and the row's own (slots ATT_SHARED_SPLITS..)
   const uint32_t tss = ts ? (ts + ATT_SHARED_SPLITS - 1) / ATT_SHARED_SPLITS : 1u;
   const uint32_t nsh = ts ? (ts + tss - 1) / tss : 0u;
-  const uint32_t np = max_splits - ATT_SHARED_SPLITS;
-  const uint32_t tps = (tiles - ts + np - 1) / np;
+  const uint32_t tps = (tiles - ts + np - 1) / np;  // np: the split kernel's private splits (its grid's y)
   const uint32_t npr = tiles > ts ? (tiles - ts + tps - 1) / tps : 0u;
   const uint32_t ns = nsh + npr;  // <= max_splits <= 64
   pdl_wait();  // the partials come from attn_split_kernel / attn_shared_kernel
@@ -460,6 +459,10 @@ cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, 
   const float scale = 1.0f / sqrtf((float)hd);  // qwen2.rs:505
   cudaError_t e;
   const bool fork = shared_tiles && side.st;
+  // the rows' own tiles in np splits: fewer for many rows (more tiles a CTA,
+  // fewer partials to merge), all of them for one row (its only parallelism)
+  const uint32_t np = nrows > 1 ? std::min(ATT_BATCH_SPLITS, max_splits - ATT_SHARED_SPLITS)
+                                : max_splits - ATT_SHARED_SPLITS;
   if (shared_tiles) {  // the batch's shared prefix, once for all rows
     const uint32_t nqg = (nrows * G + ASH_Q - 1) / ASH_Q;
     const dim3 grid(Hkv * nqg, ATT_SHARED_SPLITS), blk(ASH_THREADS);
@@ -476,16 +479,17 @@ cudaError_t launch_attention(const float* q, uint32_t ldq, const RowDesc* rows, 
       if (e != cudaSuccess) return e;
     }
   }
-  e = launch_pdl(attn_split_kernel, dim3(nrows * Hkv, max_splits - ATT_SHARED_SPLITS), dim3(ATT_THREADS), sm, st, q,
+  e = launch_pdl(attn_split_kernel, dim3(nrows * Hkv, np), dim3(ATT_THREADS), sm, st, q,
                  ldq, rows, seqs, layer, Hq, Hkv, hd, scale, part_o, part_ml, max_splits, one_seq, shared_tiles);
   if (e != cudaSuccess || !out) return e;  // no out: the consumer merges the partials itself
   if (fork) {  // the merge needs both passes: an ordinary launch after the join
     if ((e = cudaStreamWaitEvent(st, side.join, 0)) != cudaSuccess) return e;
-    attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, out, ldo, shared_tiles);
+    attn_combine_kernel<<<nrows * Hq, hd, 0, st>>>(part_o, part_ml, rows, Hq, hd, max_splits, np, out, ldo,
+                                                   shared_tiles);
     return cudaGetLastError();
   }
   return launch_pdl(attn_combine_kernel, dim3(nrows * Hq), dim3(hd), 0, st, part_o, part_ml, rows, Hq, hd, max_splits,
-                    out, ldo, shared_tiles);
+                    np, out, ldo, shared_tiles);
 }
 
 // Per-device set-up of the attention kernels (shared memory above 48 KB).

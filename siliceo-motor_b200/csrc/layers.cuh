@@ -41,7 +41,10 @@ size_t attn_smem_bytes(uint32_t G, uint32_t hd);
 // side.st (optional): a second stream on which the shared pass runs
 // concurrently with the split kernel (fork and join through the two events;
 // they become graph edges when the launches are captured).
-constexpr uint32_t ATT_SHARED_SPLITS = 32;
+constexpr uint32_t ATT_SHARED_SPLITS = 16;
+// Splits of the rows' own tiles in a step of several rows (one row: all the
+// remaining max_splits - ATT_SHARED_SPLITS slots).
+constexpr uint32_t ATT_BATCH_SPLITS = 16;
 struct SideStream {
   cudaStream_t st;
   cudaEvent_t fork, join;
