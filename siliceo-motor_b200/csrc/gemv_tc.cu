@@ -119,9 +119,11 @@ __device__ __forceinline__ void att_merge8(const GemvArgs& a, uint32_t e0, float
   const float* ml = a.att_ml + ((size_t)h * a.att_slots + a.att_first) * 2;
   const float* po = a.att_o + ((size_t)h * a.att_slots + a.att_first) * hd + d0;
   float M = -INFINITY;
+#pragma unroll 4
   for (uint32_t s = 0; s < ns; s++) M = fmaxf(M, ml[2 * s]);
   float den = 0.f;
   float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+#pragma unroll 4
   for (uint32_t s = 0; s < ns; s++) {
     const float es = expf(ml[2 * s] - M);
     den = fmaf(ml[2 * s + 1], es, den);
@@ -135,11 +137,10 @@ __device__ __forceinline__ void att_merge8(const GemvArgs& a, uint32_t e0, float
   v1 = make_float4(acc1.x / den, acc1.y / den, acc1.z / den, acc1.w / den);
 }
 
-__device__ __forceinline__ void tc_build_x(const GemvArgs& a, uint32_t blk, uint4* f4, uint4* f6, float2* xs, bool t4,
-                                           bool t6) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, sn = g >> 1, lim = g & 1;
-  const bool active = (t >> 1) == (sn & 1);
-  float4 v0, v1;
+// x[256 blk + 8 lane .. + 7] of the calling lane (or the merged attention
+// output, att_merge8).
+__device__ __forceinline__ void tc_load_x(const GemvArgs& a, uint32_t blk, float4& v0, float4& v1) {
+  const int lane = threadIdx.x & 31;
   if (a.att_o) {
     att_merge8(a, blk * 256u + 8u * lane, v0, v1);
   } else {
@@ -147,6 +148,12 @@ __device__ __forceinline__ void tc_build_x(const GemvArgs& a, uint32_t blk, uint
     v0 = ldg4(xb + 8 * lane);
     v1 = ldg4(xb + 8 * lane + 4);
   }
+}
+
+// The B fragments and scales of block blk from the lanes' x values (tc_load_x).
+__device__ __forceinline__ void tc_build_x(float4 v0, float4 v1, uint4* f4, uint4* f6, float2* xs, bool t4, bool t6) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, sn = g >> 1, lim = g & 1;
+  const bool active = (t >> 1) == (sn & 1);
   const float mx = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
                          fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
   const float sm = sum4(v0) + sum4(v1);
@@ -524,8 +531,14 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
       const float v = input_scale(a, 0);
       if (lane == 0) s_in = v;
     }
-    for (uint32_t i = warp; i < nblk; i += TC_WARPS)
-      tc_build_x(a, b0 + i, f4 + i * (TC_FRAG / 16), f6 + i * (TC_FRAG / 16), xs + 32 * i, b4, b6);
+    for (uint32_t i = warp; i < nblk; i += 2 * TC_WARPS) {  // two blocks' x loads in flight, then their fragments
+      const uint32_t j = i + TC_WARPS;
+      float4 u0, u1, w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
+      tc_load_x(a, b0 + i, u0, u1);
+      if (j < nblk) tc_load_x(a, b0 + j, w0, w1);
+      tc_build_x(u0, u1, f4 + i * (TC_FRAG / 16), f6 + i * (TC_FRAG / 16), xs + 32 * i, b4, b6);
+      if (j < nblk) tc_build_x(w0, w1, f4 + j * (TC_FRAG / 16), f6 + j * (TC_FRAG / 16), xs + 32 * j, b4, b6);
+    }
     __syncthreads();
     const uint32_t tile = rg * TC_WARPS + warp;
     float vg = 0.f, vh = 0.f;
@@ -563,14 +576,10 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
     const size_t stride = (size_t)p.tiles * 16u;
     const int g = lane >> 2, t = lane & 3;
     if (tile < p.tiles && t < 2) a.ks_part[ks * stride + tile * 16u + g + 8u * t] = t ? vh : vg;
-    __threadfence();
     __syncthreads();
-    // a wrapping increment: the group's counter is back at zero once its last
-    // slice arrives, so no later store resets it
-    if (threadIdx.x == 0) s_last = atomicInc(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
+    if (threadIdx.x == 0) s_last = ks_arrive(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
     __syncthreads();
     if (s_last) {
-      __threadfence();
       if (valid) {
         float sg = 0.f, sh = 0.f;
         for (uint32_t k0 = 0; k0 < p.ksplit; k0 += 8) {  // eight slices' loads in flight, added in order

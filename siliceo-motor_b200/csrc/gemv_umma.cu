@@ -853,17 +853,14 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
         for (uint32_t i = 0; i < NB; i++)
           if (i < a.batch) mine[ks * stride + (size_t)i * R] = y[i];
       }
-      __threadfence();
       named_bar(1, UM_EW * 32);
-      // wrapping increment: the counter is back at zero when the last slice arrives
-      if (threadIdx.x == UM_EW0 * 32) s_last = atomicInc(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
+      if (threadIdx.x == UM_EW0 * 32) s_last = ks_arrive(&a.ks_cnt[rg], p.ksplit - 1u) == p.ksplit - 1u;
       named_bar(1, UM_EW * 32);
       if (s_last) {
         if (p.units <= gridDim.x) {  // one unit per CTA: every warp joins the fixup after the CTA's last barrier
           if (threadIdx.x == UM_EW0 * 32) s_fix = 1u;
           continue;
         }
-        __threadfence();
 #pragma unroll
         for (uint32_t i = 0; i < NB; i++) y[i] = 0.f;
         if (valid)
@@ -906,7 +903,8 @@ __global__ void __launch_bounds__(UM_THREADS, 1) gemv_umma_kernel(const __grid_c
     float y[CPG];
 #pragma unroll
     for (uint32_t i = 0; i < CPG; i++) y[i] = 0.f;
-    __threadfence();  // the other slices' stores, published before the counter reached this CTA
+    // (the other slices' stores are visible: ks_arrive acquired them, and the
+    // CTA's barriers order these loads after it)
     if (valid)
       for (uint32_t k0 = 0; k0 < p.ksplit; k0 += 4) {  // four slices' loads in flight, added in slice order
         float t[4][CPG];

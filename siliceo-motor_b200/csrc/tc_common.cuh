@@ -86,6 +86,21 @@ __device__ __forceinline__ uint32_t hl_pair(float a, float b, bool lo) {
   return lo ? h2u(__floats2half2_rn(a - ah, b - bh)) : h2u(__floats2half2_rn(ah, bh));
 }
 
+// The arrival of one K-split slice at its group's counter, by one thread of a
+// CTA after a barrier that follows the slice's stores: a wrapping increment
+// (the counter is back at zero once the group's last slice arrives, so no
+// store ever resets it) with acquire-release semantics at GPU scope. The
+// release publishes the CTA's stores made before the barrier (cumulativity
+// through the barrier); for the last arriver the acquire makes the other
+// slices visible to the loads its threads make after the next barrier. One
+// GPU-scope ordering point a CTA instead of a fence in every thread. Returns
+// the counter's old value.
+__device__ __forceinline__ uint32_t ks_arrive(uint32_t* cnt, uint32_t wrap) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;" : "=r"(old) : "l"(cnt), "r"(wrap) : "memory");
+  return old;
+}
+
 // Lane 0: the bulk copy of one block unit (UB bytes) into ring slot st.
 __device__ __forceinline__ void tc_issue(const uint8_t* unit, uint32_t UB, uint8_t* ring, uint32_t stage_bytes,
                                          uint64_t* bars, uint32_t st) {
