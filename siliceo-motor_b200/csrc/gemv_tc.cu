@@ -319,13 +319,14 @@ __device__ __forceinline__ void q6_block(const uint8_t* unit, const uint4* f, co
 
 // One warp: tile rows g, g+8 over blocks b0 .. b0+nblk-1 (x fragments of
 // block b0 + i at slot i). The block units stream through the warp's ring of
-// S shared-memory slots: lane 0 starts one bulk copy per unit, S - 1 units
-// ahead of the one being computed, each completing on the slot's mbarrier
-// (use n of the ring waits for parity (n / S) & 1; nuse counts the warp's
-// uses across units). Returns the partial dot products in rg, rh (summed
-// over the lane's sub-blocks only).
-// The first `pre` copies may have been started by the caller already (ahead
-// of the previous kernel, pdl.cuh).
+// S shared-memory slots: lane 0 fills the whole ring first, then refills the
+// slot of each computed unit with the unit S further on, each copy
+// completing on the slot's mbarrier (use n of the ring waits for parity
+// (n / S) & 1; nuse counts the warp's uses across units). Returns the partial
+// dot products in rg, rh (summed over the lane's sub-blocks only).
+// The first `pre` copies (up to S) may have been started by the caller
+// already, ahead of the previous kernel (pdl.cuh): the whole ring lands while
+// the kernel waits for its input and converts x.
 template <int QT, int S>
 __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32_t nblk, uint32_t pre, uint8_t* ring,
                                         uint32_t stage_bytes, uint64_t* bars, uint32_t& nuse, uint32_t* err,
@@ -337,8 +338,8 @@ __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32
   uint32_t ip = nuse % S, cp = ip, cph = (nuse / S) & 1u;
   for (uint32_t k = 0; k < pre; k++) ip = next(ip);
   const uint8_t* src = tile + (size_t)b0 * UB;
-  const uint32_t npro = min((uint32_t)S - 1, nblk);
-  for (uint32_t k = pre; k < npro; k++) {  // the first S - 1 copies
+  const uint32_t npro = min((uint32_t)S, nblk);
+  for (uint32_t k = pre; k < npro; k++) {  // the first S copies: the whole ring
     if (lane == 0) tc_issue(src + (size_t)k * UB, UB, ring, stage_bytes, bars, ip);
     ip = next(ip);
   }
@@ -351,13 +352,13 @@ __device__ __forceinline__ void tc_tile(const uint8_t* tile, uint32_t b0, uint32
     else q6_block(sp, f + (size_t)i * (TC_FRAG / 16), xs + 32 * i, lane, rg, rh);
     __syncwarp();  // every lane is done with the slot before it is refilled
   };
-  uint32_t i = 0;
-  for (; i + S - 1 < nblk; i++) {  // steady state: the copy S - 1 blocks ahead, then this block
-    if (lane == 0) tc_issue(src + (size_t)(i + S - 1) * UB, UB, ring, stage_bytes, bars, ip);
-    ip = next(ip);
+  for (uint32_t i = 0; i < nblk; i++) {  // this block, then the copy S blocks ahead into its slot
     compute(i);
+    if (i + S < nblk) {
+      if (lane == 0) tc_issue(src + (size_t)(i + S) * UB, UB, ring, stage_bytes, bars, ip);
+      ip = next(ip);
+    }
   }
-  for (; i < nblk; i++) compute(i);
   nuse += nblk;
 }
 
@@ -510,7 +511,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemv_tc_kernel(const __grid_con
       const DWDesc& w = a.seg[si].w;
       const uint32_t UB = tile_unit_bytes(w.type);
       const uint8_t* tb = w.body + (size_t)(tile - a.seg[si].cta_begin) * w.body_stride;
-      pre = min(p.stages - 1, nblk);
+      pre = min(p.stages, nblk);
       if (lane == 0)
         for (uint32_t k = 0; k < pre; k++) tc_issue(tb + (size_t)(b0 + k) * UB, UB, ring, p.stage_bytes, bars, k);
     }
