@@ -21,15 +21,18 @@
 //     thread summarizes its chunk of the terms for the few float binades the
 //     running sum can be in while the chunk is added (the integer sum of the
 //     terms rounded to that binade's grid, for either parity of the running
-//     sum, because a term exactly halfway rounds to even), and one thread
-//     composes the chunks, adding a chunk term by term only where the running
-//     sum leaves its binade inside it;
+//     sum, because a term exactly halfway rounds to even), and one warp
+//     composes the chunks, 32 at a time by a shuffle scan of the summaries,
+//     adding a chunk term by term only where the running sum leaves its
+//     binade inside it;
 //   * probs = e / sum with IEEE division; the order is by the probs values,
 //     so terms that round to equal probs are ordered by index as in the
 //     reference, not by their logits;
 //   * cumulative, total and walk run in sorted order with f32 adds.
-// top_k in 1..1024 selects its candidates with a radix select and sorts
-// them in shared memory; otherwise (None, or larger) the whole vocabulary is
+// top_k in 1..1024 finds a threshold key from per-thread counters of the
+// keys' distance below the largest key, gathers the keys at or above it and
+// sorts them in shared memory (a radix select when ties overflow the
+// candidate buffer); otherwise (None, or larger) the whole vocabulary is
 // sorted with a stable least-significant-digit radix sort in the row's
 // scratch (four 8-bit passes) and scanned in order.
 #include <cfloat>
