@@ -644,7 +644,8 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
       need({&L.wdown});
     }
     need({&m->output});
-    // Q+K and V side by side (see qkv_side): the SMs split by their rows
+    // Q+K and V side by side (see qkv_side): the SMs split by their weight
+    // bytes (a Q6_K row streams 210 bytes a block, a Q4_K row 144)
     const Layer& L0 = m->layers[0];
     const auto mixed = [](const Layer& L) {
       return tiled_type(L.wq.d.type) && L.wk.d.type == L.wq.d.type && tiled_type(L.wv.d.type) &&
@@ -656,7 +657,9 @@ int load_model(const GgufReader& g, const sm_load_opts* opts, sm_model* m) {
     uint32_t need_cnt2 = 0;
     if (R >= 2 && any_mixed) {
       const uint64_t qk_rows = (uint64_t)L0.wq.d.n_out + L0.wk.d.n_out, v_rows = L0.wv.d.n_out;
-      m->v_cap = (uint32_t)std::max<uint64_t>(8, ((uint64_t)sms * v_rows + qk_rows + v_rows - 1) / (qk_rows + v_rows));
+      const auto row_bytes = [](uint32_t type) -> uint64_t { return type == QT_Q6K ? 210 : 144; };
+      const uint64_t vb = v_rows * row_bytes(L0.wv.d.type), qb = qk_rows * row_bytes(L0.wq.d.type);
+      m->v_cap = (uint32_t)std::max<uint64_t>(8, ((uint64_t)sms * vb + qb + vb - 1) / (qb + vb));
       m->qk_cap = (uint32_t)sms > m->v_cap + 8 ? (uint32_t)sms - m->v_cap : 0u;
       m->qkv_side = m->qk_cap != 0;
     }
